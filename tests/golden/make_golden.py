@@ -1,0 +1,141 @@
+"""Generate the golden fixtures by running the *reference* SparseFold modules.
+
+Run in a container that has the reference source tree (it is read-only and is
+never needed at test time):
+
+    python tests/golden/make_golden.py /path/to/SparseFold/src
+
+The reference is configured exactly as its own CPU tests do
+(tests/test_runtime_reference.py:22-29): backend "torch", device "cpu", math
+SDPA, no sharding/compile; fp32 matmuls at "highest" precision.  Weights come
+from ``sparsefold_b200.synth`` (keyed by parameter name), inputs from seeded
+generators.  Each fixture stores inputs, outputs and the parameter spec list
+(name, shape, kind, fan_in) so the weights can be regenerated without the
+reference.  ``weights/records.py`` imports ``zstandard``; it is unused without
+checkpoints, so a stub module is injected when the package is absent.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+from sparsefold_b200 import synth  # noqa: E402
+
+
+def _setup_reference(src: str):
+  sys.path.insert(0, src)
+  try:
+    import zstandard  # noqa: F401
+  except ImportError:
+    sys.modules["zstandard"] = types.ModuleType("zstandard")
+  from sparsefold.runtime import config
+  config.configure_runtime(backend="torch", device="cpu", sdpa_implementation="math",
+                           enable_sharding=False, enable_compile=False, logs=set())
+  from sparsefold import backends
+  backends.init()
+  torch.set_float32_matmul_precision("highest")
+
+
+def _spec(module) -> list:
+  out = []
+  for mod_name, mod in module.named_modules():
+    for pname, p in mod.named_parameters(recurse=False):
+      full = f"{mod_name}.{pname}" if mod_name else pname
+      if synth._is_layernorm(mod):
+        kind, fan = ("ln_weight" if pname == "weight" else "ln_bias"), 1
+      elif synth._is_linear(mod):
+        kind, fan = ("weight" if pname == "weight" else "bias"), int(math.prod(mod.input_shape))
+      else:
+        raise ValueError(full)
+      out.append([full, list(p.shape), kind, fan])
+  return out
+
+
+def _save(name, module_spec, seed, **arrays):
+  path = os.path.join(HERE, f"{name}.npz")
+  meta = json.dumps({"seed": seed, "params": module_spec})
+  np.savez_compressed(path, meta=np.array(meta), **{k: np.asarray(v) for k, v in arrays.items()})
+  print(f"wrote {path} ({os.path.getsize(path)} bytes)")
+
+
+def main(src: str):
+  _setup_reference(src)
+  from sparsefold.model.trunk import blocks, network
+  from sparsefold.model import config as mc
+  from sparsefold.backends.torch.attention import dot_product_attention
+
+  gc = mc.GlobalConfig()
+  pcfg = network.Evoformer.Config().pairformer
+  seed = 0
+
+  # 1. dot_product_attention semantics (tests/test_runtime_reference.py:117-138 shapes, seed 808)
+  arrays = {}
+  for bi, batch in enumerate([(), (2,), (2, 3)]):
+    for masked in (False, True):
+      g = torch.Generator().manual_seed(808)
+      q = torch.randn(*batch, 3, 2, 4, generator=g)
+      k = torch.randn(*batch, 5, 2, 4, generator=g)
+      v = torch.randn(*batch, 5, 2, 6, generator=g)
+      bias = torch.randn(*batch, 2, 3, 5, generator=g)
+      mq = torch.tensor([True, False, True]).expand(*batch, 3) if masked else None
+      mk = torch.tensor([True, False, True, True, False]).expand(*batch, 5) if masked else None
+      out = dot_product_attention(q, k, v, scale=0.4, mask_q=mq, mask_k=mk, bias=bias)
+      tag = f"b{bi}_m{int(masked)}"
+      arrays.update({f"{tag}_q": q, f"{tag}_k": k, f"{tag}_v": v, f"{tag}_bias": bias, f"{tag}_out": out})
+      if masked:
+        arrays.update({f"{tag}_mask_q": mq.contiguous(), f"{tag}_mask_k": mk.contiguous()})
+  # A larger case shaped like tests/test_runtime_gpu.py:28-41 (seed 610, scale 0.3).
+  g = torch.Generator().manual_seed(610)
+  q = torch.randn(2, 7, 3, 16, generator=g)
+  k = torch.randn(2, 9, 3, 16, generator=g)
+  v = torch.randn(2, 9, 3, 12, generator=g)
+  bias = torch.randn(2, 3, 7, 9, generator=g)
+  mk = torch.tensor([[True, False, True, True, True, False, True, False, True]]).expand(2, 9)
+  out = dot_product_attention(q, k, v, mask_k=mk, bias=bias, scale=0.3)
+  arrays.update({"g610_q": q, "g610_k": k, "g610_v": v, "g610_bias": bias,
+                 "g610_mask_k": mk.contiguous(), "g610_out": out})
+  _save("attention", [], 808, **arrays)
+
+  # 2. Per-op fixtures on a ragged pair (N=16, 13 real tokens) and a full one (N=8).
+  for n, n_real in ((16, 13), (8, 8)):
+    z, s, mask = synth.pair_inputs(n, n_real=n_real, seed=1)
+    tag = f"n{n}"
+    for name, make in (
+        ("tri_mult_out", lambda: blocks.TriangleMultiplication(pcfg.triangle_multiplication_outgoing, gc, num_channels=128, name="t")),
+        ("tri_mult_in", lambda: blocks.TriangleMultiplication(pcfg.triangle_multiplication_incoming, gc, num_channels=128, name="t")),
+        ("tri_att_start", lambda: blocks.GridSelfAttention(pcfg.pair_attention, gc, transpose=False, num_channels=128, name="g")),
+        ("tri_att_end", lambda: blocks.GridSelfAttention(pcfg.pair_attention, gc, transpose=True, num_channels=128, name="g")),
+        ("transition", lambda: blocks.TransitionBlock(pcfg.pair_transition, gc, num_channels=128, name="p")),
+    ):
+      mod = make()
+      synth.init_params(mod, seed)
+      with torch.no_grad():
+        out = mod(z, mask) if name != "transition" else mod(z)
+      _save(f"{name}_{tag}", _spec(mod), seed, z=z, mask=mask, out=out)
+    mod = blocks.SingleActUpdate(gc, 128, 384, pcfg.single_attention, pcfg.single_transition)
+    synth.init_params(mod, seed)
+    with torch.no_grad():
+      out = mod(z, s, mask)
+    _save(f"single_update_{tag}", _spec(mod), seed, z=z, s=s, mask=mask, out=out)
+
+  # 3. Full Pairformer block, ragged N=24 (21 real).
+  z, s, mask = synth.pair_inputs(24, n_real=21, seed=2)
+  blk = blocks.PairFormerIteration(pcfg, gc, with_single=True, num_channels=128, seq_channels=384)
+  synth.init_params(blk, seed)
+  with torch.no_grad():
+    zo, so = blk(z, seq_mask=mask, single_act=s)
+  _save("pairformer_n24", _spec(blk), seed, z=z, s=s, mask=mask, z_out=zo, s_out=so)
+
+
+if __name__ == "__main__":
+  main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
