@@ -1,0 +1,367 @@
+"""Pairformer trunk benchmark on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one forward pass of the full 48-block Pairformer trunk at
+N_token = 512 (475 real tokens, token mask zeroes the rest), c_z = 128,
+c_s = 384, bf16 activations with fp32 accumulation, random-init weights
+(seed 0), z ~ N(0,1), s ~ N(0,1) — synthetic data of the reference's shapes.
+``value`` is ms per Pairformer block (trunk time / 48), max over ranks.
+With --gpus N > 1 each rank runs an independent replica of the trunk
+(weak scaling); the row-sharded N = 2048 path is measured separately.
+
+``--impl reference`` times the reference's CPU algorithm (the oracle
+restatement in oracle/pairformer.py of the reference Torch CPU math path) on
+this host's cores, on a bounded sample, and prints the same JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+N_TOKEN, N_REAL, N_BLOCKS, C_Z, C_S = 512, 475, 48, 128, 384
+METRIC = "pairformer_ms_per_block"
+UNIT = "ms/block"
+
+
+def block_flops(n: int) -> float:
+  """Algorithmic FLOPs of one Pairformer block at padded N (1536 N^3 + 1,121,792 N^2 + 5,013,504 N)."""
+  return 1536.0 * n**3 + 1121792.0 * n**2 + 5013504.0 * n
+
+
+def tri_attention_core_flops(n: int, heads: int = 4, d: int = 32) -> float:
+  """4 * Nq * Nk * d * H * batch for one triangle attention (batch = N rows)."""
+  return 4.0 * n * n * d * heads * n
+
+
+def load_peaks() -> dict:
+  path = os.path.join(REPO, "MEASURED_PEAKS.json")
+  if os.path.exists(path):
+    with open(path) as f:
+      p = json.load(f)
+    return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+            "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]), "source": "measured"}
+  return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+  """nvidia-smi clocks and throttle reasons sampled every 200 ms while active."""
+
+  FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+            "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+            "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+  def __init__(self, index: int):
+    self.index = index
+    self.proc = None
+
+  def __enter__(self):
+    try:
+      self.proc = subprocess.Popen(
+          ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+    except OSError:
+      self.proc = None
+    return self
+
+  def __exit__(self, *exc):
+    self.lines = []
+    if self.proc is not None:
+      self.proc.terminate()
+      try:
+        out, _ = self.proc.communicate(timeout=5)
+      except subprocess.TimeoutExpired:
+        self.proc.kill()
+        out, _ = self.proc.communicate()
+      self.lines = [ln for ln in out.splitlines() if ln.strip()]
+    return False
+
+  def summary(self) -> dict:
+    sm, mx, reasons = [], None, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for ln in getattr(self, "lines", []):
+      parts = [p.strip() for p in ln.split(",")]
+      if len(parts) < 9:
+        continue
+      try:
+        sm.append(float(parts[1]))
+        mx = float(parts[2])
+      except ValueError:
+        continue
+      for name, flag in zip(names, parts[5:9]):
+        if flag.lower().startswith("active"):
+          reasons.add(name)
+    return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+            "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+  import datetime
+  import torch
+  import torch.distributed as dist
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  rank = int(os.environ.get("RANK", "0"))
+  local = int(os.environ.get("LOCAL_RANK", "0"))
+  if world != n_gpus:
+    raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+  if torch.cuda.is_available():
+    torch.cuda.set_device(local)
+  if world > 1:
+    dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo",
+                            timeout=datetime.timedelta(seconds=300))
+  return rank, world, local
+
+
+def barrier(world):
+  if world > 1:
+    import torch.distributed as dist
+    dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+  if world == 1:
+    return x
+  import torch
+  import torch.distributed as dist
+  t = torch.tensor([x], dtype=torch.float64, device="cuda")
+  dist.all_reduce(t, op=dist.ReduceOp.MAX)
+  return float(t.item())
+
+
+def build_trunk(device, n_blocks=N_BLOCKS, seed=0):
+  import torch
+  from sparsefold_b200 import modules, synth
+  trunk = modules.PairformerTrunk(n_blocks, C_Z, C_S)
+  synth.init_params(trunk, seed=seed)
+  trunk = trunk.to(device)
+  modules.prepare(trunk)
+  # the fp32 master parameters are not used by the bf16 kernels; drop them from HBM
+  for p in trunk.parameters():
+    p.data = torch.empty(0, device=device)
+  return trunk
+
+
+def flush_l2(buf):
+  buf.add_(1)
+
+
+def time_kernel_probe(n: int, dtype, iters: int = 10) -> float:
+  """Average device time (ms) of one triangle-attention core launch at [n rows, n, 4 heads x 32]."""
+  import torch
+  from sparsefold_b200 import ops
+  g = torch.Generator(device="cuda").manual_seed(3)
+  y = torch.randn(n, n, 4, 4, 32, device="cuda", generator=g).to(dtype)  # q, k, v, gate
+  bias = torch.randn(4, n, n, device="cuda", generator=g)
+  mask = torch.ones(n, dtype=torch.bool, device="cuda")
+  mask[N_REAL * n // N_TOKEN:] = False
+  q, k, v, gate = (y[:, :, i] for i in range(4))
+  run = lambda: ops.attention(q, k, v, bias=bias, mask_k=mask, mask_row=mask, gate=gate)
+  for _ in range(2):
+    run()
+  st = torch.cuda.current_stream()
+  ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+  torch.cuda.synchronize()
+  for a, b in ev:
+    a.record(st)
+    run()
+    b.record(st)
+  torch.cuda.synchronize()
+  return sum(a.elapsed_time(b) for a, b in ev) / iters
+
+
+def run_b200(args) -> None:
+  import torch
+  from sparsefold_b200 import _native, synth
+  rank, world, local = dist_setup(args.gpus)
+  if not torch.cuda.is_available():
+    raise SystemExit("bench.py --impl b200 needs a CUDA device")
+  _native.check(_native.load().sf_device_check(), "sf_device_check")
+  dev = torch.device("cuda", local)
+  dt = torch.bfloat16
+  trunk = build_trunk(dev)
+  z_h, s_h, m_h = synth.pair_inputs(N_TOKEN, C_Z, C_S, n_real=N_REAL, seed=rank)
+  z0 = z_h.to(dev, dt)
+  s0 = s_h.to(dev, dt)
+  mask = m_h.to(dev)
+  l2_flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # 2x the 126 MB L2
+  st = torch.cuda.current_stream()
+
+  with torch.no_grad():
+    for _ in range(args.warmup):
+      trunk(z0, s0, mask)
+    torch.cuda.synchronize()
+
+    # ---- device-resident timing: K trunk passes, L2 flushed between them ----
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    launches0 = _native.launch_count()
+    with ClockSampler(local) as clk:
+      for a, b in evs:
+        flush_l2(l2_flush)
+        a.record(st)
+        trunk(z0, s0, mask)
+        b.record(st)
+      torch.cuda.synchronize()
+    launches = _native.launch_count() - launches0
+    barrier(world)
+    ms_total = sum(a.elapsed_time(b) for a, b in evs)
+    ms_total = max_over_ranks(ms_total, world)
+    ms_step = ms_total / args.steps
+    ms_block = ms_step / N_BLOCKS
+
+    # ---- end to end through the public module API with host buffers ----
+    zp = z_h.to(dt).pin_memory()
+    sp = s_h.to(dt).pin_memory()
+    mp = m_h.pin_memory()
+    zo = torch.empty_like(zp).pin_memory()
+    so = torch.empty_like(sp).pin_memory()
+    e2e_steps = max(1, min(args.steps, 3))
+    eev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(e2e_steps)]
+    barrier(world)
+    torch.cuda.synchronize()
+    for a, b in eev:
+      flush_l2(l2_flush)
+      a.record(st)
+      zd = zp.to(dev, non_blocking=True)
+      sd = sp.to(dev, non_blocking=True)
+      md = mp.to(dev, non_blocking=True)
+      zr, sr = trunk(zd, sd, md)
+      zo.copy_(zr, non_blocking=True)
+      so.copy_(sr, non_blocking=True)
+      b.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in eev) / e2e_steps, world)
+    h2d = zp.numel() * zp.element_size() + sp.numel() * sp.element_size() + mp.numel()
+    d2h = zo.numel() * zo.element_size() + so.numel() * so.element_size()
+
+    # ---- dominant-kernel roofline: triangle attention core ----
+    probe_ms = time_kernel_probe(N_TOKEN, dt)
+
+  peaks = load_peaks()
+  flops = tri_attention_core_flops(N_TOKEN)
+  achieved = flops / (probe_ms * 1e-3) / 1e12
+  cpu = cpu_baseline_sample() if rank == 0 and world == 1 and not args.no_cpu_baseline else None
+  if rank == 0:
+    line = {
+        "metric": METRIC, "value": round(ms_block, 4), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) pair/single, random-init AF3-shaped weights)",
+        "config": {"workload": "configs[1]: 48-block Pairformer trunk, N_token=512 (475 real), c_z=128, c_s=384",
+                   "n_token": N_TOKEN, "n_real": N_REAL, "blocks": N_BLOCKS,
+                   "block_gflop": round(block_flops(N_TOKEN) / 1e9, 1),
+                   "trunk_tflop_per_s": round(block_flops(N_TOKEN) / (ms_block * 1e-3) / 1e12, 2),
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "parallelism": "replicas" if world > 1 else "single"},
+        "e2e": {"value": round(e2e_ms / N_BLOCKS, 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(launches),
+        "roofline": {"kernel": "triangle attention core (sf_attention, N=512 rows x 512 x 4 heads x 32)",
+                     "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "peak_source": peaks["source"], "launch_ms": round(probe_ms, 4), "traffic": None},
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+  if world > 1:
+    import torch.distributed as dist
+    dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the reference algorithm (oracle restatement of the Torch CPU math
+# path, oracle/pairformer.py) on this host's cores.
+# ---------------------------------------------------------------------------
+def _cpu_threads() -> int:
+  import torch
+  n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+  torch.set_num_threads(n)
+  return torch.get_num_threads()
+
+
+def _cpu_block_seconds(n: int, repeats: int = 1, warmup: int = 0) -> list:
+  import torch
+  from oracle import pairformer as orc
+  from sparsefold_b200 import modules, synth
+  dt = torch.bfloat16
+  blk = modules.PairFormerIteration(C_Z, C_S)
+  p = {k: v.to(dt) for k, v in synth.init_params(blk, seed=0).items()}
+  z, s, mask = synth.pair_inputs(n, C_Z, C_S, n_real=max(1, n * N_REAL // N_TOKEN), seed=0)
+  z, s = z.to(dt), s.to(dt)
+  out = []
+  with torch.no_grad():
+    for i in range(warmup + repeats):
+      t0 = time.perf_counter()
+      orc.pairformer_block(z, s, mask, p)
+      if i >= warmup:
+        out.append(time.perf_counter() - t0)
+  return out
+
+
+def cpu_baseline_sample() -> dict:
+  """One Pairformer block on the host; exact at N=512 when that fits ~30 s, else N=256 scaled by FLOPs."""
+  cores = _cpu_threads()
+  t256 = min(_cpu_block_seconds(256))
+  scale = block_flops(N_TOKEN) / block_flops(256)
+  if t256 * scale <= 30.0:
+    t = min(_cpu_block_seconds(N_TOKEN))
+    sample = "1 Pairformer block at N=512 (oracle port, bf16 tensors), timed exactly"
+  else:
+    t = t256 * scale
+    sample = f"1 Pairformer block at N=256 (oracle port, bf16 tensors), x{scale:.2f} FLOP ratio to N=512"
+  return {"value": round(t * 1e3, 2), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+
+def run_reference(args) -> None:
+  rank = int(os.environ.get("RANK", "0"))
+  world = int(os.environ.get("WORLD_SIZE", "1"))
+  if rank != 0:
+    return
+  cores = _cpu_threads()
+  n_sample = 256
+  times = _cpu_block_seconds(n_sample, repeats=args.steps, warmup=args.warmup)
+  scale = block_flops(N_TOKEN) / block_flops(n_sample)
+  ms_block = statistics.median(times) * scale * 1e3
+  sample = (f"per step 1 Pairformer block at N={n_sample} (oracle port of the reference Torch CPU math path, "
+            f"bf16 tensors), scaled x{scale:.2f} by FLOPs to N=512")
+  line = {
+      "metric": METRIC, "value": round(ms_block, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+      "warmup": args.warmup, "ms_per_step": round(ms_block * N_BLOCKS, 1), "higher_is_better": False,
+      "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+      "config": {"workload": "configs[1]: 48-block Pairformer trunk, N_token=512 (475 real)", "n_token": N_TOKEN},
+      "impl": "reference",
+      "cpu_baseline": {"value": round(ms_block, 2), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+      "e2e": {"value": round(ms_block, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+  }
+  print(json.dumps(line), flush=True)
+
+
+def main():
+  ap = argparse.ArgumentParser()
+  ap.add_argument("--gpus", type=int, default=1)
+  ap.add_argument("--steps", type=int, default=3)
+  ap.add_argument("--warmup", type=int, default=3)
+  ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+  ap.add_argument("--no-cpu-baseline", action="store_true")
+  args = ap.parse_args()
+  if args.warmup < 3 and args.impl == "b200":
+    raise SystemExit("--warmup must be >= 3")
+  if args.impl == "reference":
+    run_reference(args)
+  else:
+    run_b200(args)
+
+
+if __name__ == "__main__":
+  main()

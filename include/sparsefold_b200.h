@@ -1,0 +1,163 @@
+/*
+ * sparsefold_b200 — C ABI of the B200 (sm_100a) kernels for the AF3 trunk hot path.
+ *
+ * Every entry point is `extern "C"`, takes plain device pointers, element
+ * counts and a CUDA stream, returns an `int` status (SF_OK == 0), and never
+ * throws.  On failure `sf_last_error()` returns a message for the calling
+ * thread.  The caller allocates every input, output and workspace buffer; the
+ * library allocates and frees nothing and keeps no device state.  Work is
+ * enqueued asynchronously on `stream`.
+ *
+ * Conventions
+ *  - dtype (`SF_F32` / `SF_BF16`) is the element type of the activation
+ *    tensors (pair z, single s, intermediate buffers).  Weights passed as
+ *    `const void*` have the same dtype; LayerNorm scales/offsets and Linear
+ *    biases are always fp32.  Arithmetic accumulates in fp32.
+ *  - Weights are "out x in" matrices (`Wt[n_out][k_in]`, k contiguous), the
+ *    transpose of the reference's `x @ W` layout; the Python `prepare()` step
+ *    builds them.
+ *  - Pair tensors are position-major `[rows][n][c]` (channels contiguous).
+ *    Masks are `uint8_t` (0 / 1) per token.
+ *  - `rows` is the number of pair rows this call owns (all `n` on one device,
+ *    `n / P` on a row shard) and `row_offset` the global index of its first row.
+ *
+ * Reference interfaces replaced (paths in HenryRenYz/SparseFold src/sparsefold/):
+ *  sf_attention            backends/torch/attention/sdpa.py:22-121  dot_product_attention
+ *  sf_layernorm            model/layers/primitives.py:471-497       LayerNorm.forward
+ *  sf_tri_mult_*           model/trunk/blocks.py:484-566            TriangleMultiplication.forward
+ *  sf_tri_attention_*      model/trunk/blocks.py:270-366            GridSelfAttention.forward/_attention
+ *  sf_transition           model/trunk/blocks.py:79-96              TransitionBlock.forward
+ *  sf_linear               model/layers/primitives.py:328-372       Linear.forward (post_op, residual)
+ *  sf_pair_logits          model/trunk/blocks.py:745-749            SingleActUpdate pair-logit projection
+ */
+#ifndef SPARSEFOLD_B200_H_
+#define SPARSEFOLD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* sf_stream_t; /* == cudaStream_t */
+
+enum sf_dtype { SF_F32 = 0, SF_BF16 = 1 };
+
+enum sf_status {
+  SF_OK = 0,
+  SF_ERR_ARG = 1,         /* bad shape, null pointer, unsupported combination */
+  SF_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed */
+  SF_ERR_WORKSPACE = 3,   /* workspace too small */
+  SF_ERR_DEVICE = 4,      /* current device is not sm_100 */
+  SF_ERR_TIMEOUT = 5      /* a bounded device-side wait gave up (kernel set an error flag) */
+};
+
+enum sf_post_op { SF_POST_NONE = 0, SF_POST_RELU = 1, SF_POST_SILU = 2, SF_POST_SIGMOID = 3 };
+
+/* ---- runtime ------------------------------------------------------------ */
+const char* sf_version(void);
+/* Copies the calling thread's last error message into buf; returns its length. */
+int sf_last_error(char* buf, size_t len);
+/* SF_OK when the current device is an sm_100 part this build was compiled for. */
+int sf_device_check(void);
+/* Number of kernels this library launched since load (all threads). */
+uint64_t sf_launch_count(void);
+
+/* ---- generic attention: sdpa.py:22-121 ---------------------------------
+ * out[b,q,h,:] = softmax_k(scale * q.k + bias[b,h,q,k] + maskbias) @ v
+ * where maskbias = -FLT_MAX when !mask_q[b,q] or !mask_k[b,k] or !mask_row[b].
+ * Strides are in elements; the innermost (head-dim) axis is contiguous.
+ * `bias` may broadcast over batch (bias_sb == 0).  If `gate` is non-null the
+ * output is multiplied by sigmoid(gate) (same layout as out) — the gating of
+ * GridSelfAttention._attention (blocks.py:288-289).                      */
+typedef struct sf_attention_args {
+  int dtype;
+  int64_t batch, heads, q_len, k_len, head_dim;
+  const void* q; int64_t q_sb, q_sh, q_sq;
+  const void* k; int64_t k_sb, k_sh, k_sk;
+  const void* v; int64_t v_sb, v_sh, v_sk;
+  void* out; int64_t o_sb, o_sh, o_sq;
+  const void* bias; int bias_dtype; int64_t b_sb, b_sh, b_sq;
+  const uint8_t* mask_q; int64_t mq_sb;
+  const uint8_t* mask_k; int64_t mk_sb;
+  const uint8_t* mask_row;
+  const void* gate; int64_t g_sb, g_sh, g_sq;
+  float scale;
+} sf_attention_args;
+int sf_attention(const sf_attention_args* args, sf_stream_t stream);
+
+/* ---- LayerNorm over the last axis (primitives.py:471-497), eps per call. */
+int sf_layernorm(int dtype, const void* x, void* y, const float* weight, const float* bias,
+                 int64_t rows, int64_t cols, float eps, sf_stream_t stream);
+
+/* ---- Linear (primitives.py:328-372): y = post_op(x @ W + bias + residual).
+ * x [rows][k], wt [n][k], y/residual [rows][n]; bias/residual may be null. */
+int sf_linear(int dtype, const void* x, const void* wt, const float* bias, const void* residual,
+              void* y, int64_t rows, int64_t k, int64_t n, int post_op, sf_stream_t stream);
+
+/* ---- TriangleMultiplication (blocks.py:484-566) --------------------------
+ * w_glu: [4][C][C] rows = (gate of a-channels, value of a-channels,
+ *        gate of b-channels, value of b-channels); a-channel c is the
+ *        reference projection channel 2c, b-channel c is 2c+1 (blocks.py:538).
+ * w_out = output_projection^T, w_gate = gating_linear^T, both [C][C].        */
+typedef struct sf_tri_mult_weights {
+  const float* ln_w; const float* ln_b;          /* left_norm_input */
+  const void* w_glu;                              /* [4C][C] */
+  const float* center_w; const float* center_b;  /* center_norm */
+  const void* w_out;                              /* [C][C] */
+  const void* w_gate;                             /* [C][C] */
+} sf_tri_mult_weights;
+
+/* Phase 1: x = LN(z); proj = sigmoid(x Wg) * (x Wv) * mask; writes the two
+ * contraction operands so that phase 2 is always P[c,i,j] = sum_k A[c,i,k] B[c,j,k]:
+ *   outgoing: A[c][i][k] = a[c,i,k], B[c][j][k] = b[c,j,k]   (rows = i, cols = k)
+ *   incoming: A[c][i][k] = b[c,k,i], B[c][j][k] = a[c,k,j]   (stored transposed)
+ * a_op / b_op are [C][n][n] for the full device case. */
+int sf_tri_mult_project(int dtype, const void* z, const uint8_t* mask, int64_t n, int incoming,
+                        const sf_tri_mult_weights* w, void* a_op, void* b_op,
+                        void* ws, size_t ws_bytes, sf_stream_t stream);
+size_t sf_tri_mult_project_workspace(int dtype, int64_t n);
+/* Phase 2: P[c][i][j] = sum_k A[c][i][k] * B[c][j][k]; A [C][rows][kdim], B [C][cols][kdim]. */
+int sf_tri_mult_contract(int dtype, const void* a_op, const void* b_op, void* p,
+                         int64_t channels, int64_t rows, int64_t cols, int64_t kdim, sf_stream_t stream);
+/* Phase 3: z_out = z + (centerLN(P) W_out) * sigmoid(LN(z) W_gate); z_out may alias z. */
+int sf_tri_mult_output(int dtype, const void* z, const void* p, int64_t rows, int64_t n,
+                       const sf_tri_mult_weights* w, void* z_out,
+                       void* ws, size_t ws_bytes, sf_stream_t stream);
+size_t sf_tri_mult_output_workspace(int dtype, int64_t rows, int64_t n);
+
+/* ---- GridSelfAttention (blocks.py:270-366), H heads of D = C / H --------
+ * w_qkvg: [4][C][C] rows = q (h,d), k (h,d), v (h,d), gating_query;
+ * w_bias: [H][C] pair_bias_projection^T; w_out: output_projection^T [C][C]. */
+typedef struct sf_tri_attention_weights {
+  const float* ln_w;        /* act_norm scale (no offset) */
+  const void* w_qkvg;       /* [4C][C] */
+  const void* w_bias;       /* [H][C] */
+  const void* w_out;        /* [C][C] */
+  int64_t heads;
+} sf_tri_attention_weights;
+/* Whole op on one device: z_out = z + GridSelfAttention(z); z_out may alias z. */
+int sf_tri_attention(int dtype, const void* z, const uint8_t* mask, int64_t n, int transpose,
+                     const sf_tri_attention_weights* w, void* z_out,
+                     void* ws, size_t ws_bytes, sf_stream_t stream);
+size_t sf_tri_attention_workspace(int dtype, int64_t n, int64_t heads);
+
+/* ---- TransitionBlock (blocks.py:79-96): y = x + swish(LN(x) W1a) * (LN(x) W1b) W2
+ * w1: [2I][C] (first I rows = swish half), w2: [C][I]; y may alias x.        */
+int sf_transition(int dtype, const void* x, const float* ln_w, const float* ln_b,
+                  const void* w1, const void* w2, void* y, int64_t rows, int64_t c, int64_t inter,
+                  void* ws, size_t ws_bytes, sf_stream_t stream);
+size_t sf_transition_workspace(int dtype, int64_t rows, int64_t inter);
+
+/* ---- SingleActUpdate pair logits (blocks.py:745-749):
+ * logits[h][i][j] = LN(z[i,j]) . W[h]; w: [H][C] (single_pair_logits_projection^T). */
+int sf_pair_logits(int dtype, const void* z, const float* ln_w, const float* ln_b, const void* w,
+                   void* logits, int64_t rows, int64_t n, int64_t c, int64_t heads,
+                   void* ws, size_t ws_bytes, sf_stream_t stream);
+size_t sf_pair_logits_workspace(int dtype, int64_t rows, int64_t n, int64_t c);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPARSEFOLD_B200_H_ */

@@ -1,0 +1,106 @@
+"""The ``b200`` backend for SparseFold's plugin API (backends/__init__.py:25-137).
+
+Registration, as a user of the reference does it::
+
+    import sparsefold_b200.backend as b200
+    b200.register()                                   # backends.register_library(apply, "b200", hooks)
+    config.configure_runtime(backend="b200", device="cuda")
+    backends.init()                                   # runs apply(): factory replacement
+    model = ...construct...; load weights
+    backends.prepare(model)                           # prepare_native() on every B200 module
+
+``apply`` replaces the module factories exactly as vecops/backend.py:187-223
+does, with classes built as ``(Mixin, ReferenceClass)`` so the reference
+``__init__`` and parameter layout stay untouched (state_dict keys unchanged,
+tests/test_native_preparation.py:107-132).
+"""
+from __future__ import annotations
+
+from contextlib import nullcontext
+
+import torch
+
+from sparsefold_b200 import modules as _m
+
+_PATCHED: list[tuple[object, str, object]] = []
+_MADE: dict[str, type] = {}
+
+
+def _native_class(ref_cls: type, mixin: type) -> type:
+  key = f"{ref_cls.__module__}.{ref_cls.__qualname__}"
+  if key not in _MADE:
+    _MADE[key] = type(ref_cls.__name__ + "B200", (mixin, ref_cls), {"__module__": __name__})
+  return _MADE[key]
+
+
+def replacement_map():
+  """(module, attribute, replacement) for each reference factory this backend replaces."""
+  from sparsefold.model.trunk import blocks
+  from sparsefold.model.diffusion import transformer
+  orig = {name: getattr(blocks, name) for name in ("GridSelfAttention", "TriangleMultiplication",
+                                                     "TransitionBlock", "SingleActUpdate")}
+  for name, cls in list(orig.items()):
+    if issubclass(cls, _m.B200Module):   # already applied: recover the reference base
+      orig[name] = next(b for b in cls.__mro__[1:] if not issubclass(b, _m.B200Module))
+  sa = transformer.SelfAttention
+  if issubclass(sa, _m.B200Module):
+    sa = next(b for b in sa.__mro__[1:] if not issubclass(b, _m.B200Module))
+  return [
+      (blocks, "GridSelfAttention", _native_class(orig["GridSelfAttention"], _m.GridSelfAttentionB200)),
+      (blocks, "TriangleMultiplication", _native_class(orig["TriangleMultiplication"], _m.TriangleMultiplicationB200)),
+      (blocks, "TransitionBlock", _native_class(orig["TransitionBlock"], _m.TransitionBlockB200)),
+      (blocks, "SingleActUpdate", _native_class(orig["SingleActUpdate"], _m.SingleActUpdateB200)),
+      (transformer, "SelfAttention", _native_class(sa, _m.SelfAttentionB200)),
+  ]
+
+
+def apply() -> None:
+  """Swap the reference factories for B200 classes (construct models afterwards)."""
+  for module, name, repl in replacement_map():
+    current = getattr(module, name)
+    if current is repl:
+      continue
+    _PATCHED.append((module, name, current))
+    setattr(module, name, repl)
+
+
+def unapply() -> None:
+  for module, name, original in reversed(_PATCHED):
+    setattr(module, name, original)
+  _PATCHED.clear()
+
+
+def manual_seed(seed: int) -> None:
+  torch.manual_seed(seed)
+
+
+def prepare(module: torch.nn.Module) -> dict[str, int]:
+  return _m.prepare(module)
+
+
+def materialize(*, parallelism: int | None = None) -> int:
+  return 0
+
+
+def precompile(module, *args, **kwargs):
+  return None
+
+
+def is_precompiling() -> bool:
+  return False
+
+
+def execution_context():
+  return nullcontext()
+
+
+HOOKS = {"manual_seed": manual_seed, "prepare": prepare, "precompile": precompile,
+         "materialize": materialize, "is_precompiling": is_precompiling,
+         "execution_context": execution_context}
+
+
+def register(name: str = "b200") -> None:
+  """``backends.register_library(apply, name, hooks)`` on the reference package."""
+  from sparsefold import backends
+  if name not in backends._registered_impl:
+    backends.register_library(apply, name, dict(HOOKS))

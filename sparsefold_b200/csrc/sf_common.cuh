@@ -1,0 +1,97 @@
+// Shared helpers of the sparsefold_b200 kernels: element access, error state,
+// launch accounting.  Host-side errors are reported through a thread-local
+// message read by sf_last_error(); no C++ exception crosses the C ABI.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/sparsefold_b200.h"
+
+namespace sf {
+
+using bf16 = __nv_bfloat16;
+
+// ---- element access (fp32 arithmetic everywhere) ---------------------------
+__device__ __forceinline__ float ld(const float* p) { return *p; }
+__device__ __forceinline__ float ld(const bf16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void st(float* p, float v) { *p = v; }
+__device__ __forceinline__ void st(bf16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float swish_f(float x) { return x * sigmoid_f(x); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---- host-side error state --------------------------------------------------
+void set_error(const char* fmt, ...);
+void count_launch(uint64_t n = 1);
+int check_launch(const char* what);  // cudaGetLastError -> status
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Carves aligned sub-buffers out of a caller-provided workspace.
+struct Workspace {
+  char* base;
+  size_t size, used = 0;
+  Workspace(void* p, size_t n) : base(static_cast<char*>(p)), size(n) {}
+  template <typename T>
+  T* take(size_t count) {
+    size_t off = align_up(used, 256);
+    used = off + count * sizeof(T);
+    return used <= size ? reinterpret_cast<T*>(base + off) : nullptr;
+  }
+  bool ok() const { return used <= size; }
+};
+
+// Workspace size accounting that mirrors Workspace::take.
+struct WorkspaceSize {
+  size_t used = 0;
+  template <typename T>
+  void take(size_t count) { used = align_up(used, 256) + count * sizeof(T); }
+};
+
+}  // namespace sf
+
+#define SF_REQUIRE(cond, ...)           \
+  do {                                  \
+    if (!(cond)) {                      \
+      ::sf::set_error(__VA_ARGS__);     \
+      return SF_ERR_ARG;                \
+    }                                   \
+  } while (0)
+
+#define SF_TRY(expr)                    \
+  do {                                  \
+    int _st = (expr);                   \
+    if (_st != SF_OK) return _st;       \
+  } while (0)
+
+// Dispatch on the activation dtype: defines `T` inside the body.
+#define SF_DISPATCH(dtype, ...)                                         \
+  do {                                                                  \
+    if ((dtype) == SF_F32) {                                            \
+      using T = float;                                                  \
+      __VA_ARGS__                                                       \
+    } else if ((dtype) == SF_BF16) {                                    \
+      using T = ::sf::bf16;                                             \
+      __VA_ARGS__                                                       \
+    } else {                                                            \
+      ::sf::set_error("unsupported dtype %d", (int)(dtype));            \
+      return SF_ERR_ARG;                                                \
+    }                                                                   \
+  } while (0)

@@ -1,0 +1,201 @@
+"""Torch-facing wrappers of the C ABI: tensors in, tensors out, current stream.
+
+Each wrapper validates shapes/dtypes, allocates outputs and workspace with the
+torch caching allocator, and calls one entry point of libsparsefold_b200.so.
+Nothing here computes on the host; a missing library raises NativeError.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import torch
+
+from sparsefold_b200 import _native as N
+
+
+def _dt(t: torch.Tensor) -> int:
+  if t.dtype == torch.float32:
+    return N.SF_F32
+  if t.dtype == torch.bfloat16:
+    return N.SF_BF16
+  raise TypeError(f"unsupported dtype {t.dtype}; use float32 or bfloat16")
+
+
+def _stream() -> int:
+  return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t) -> int | None:
+  return None if t is None else t.data_ptr()
+
+
+def _cuda(*ts):
+  for t in ts:
+    if t is not None and not t.is_cuda:
+      raise ValueError("sparsefold_b200 ops take CUDA tensors only")
+
+
+def _ws(nbytes: int, device) -> torch.Tensor:
+  return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def mask_u8(mask: torch.Tensor) -> torch.Tensor:
+  return mask.to(torch.uint8).contiguous()
+
+
+# ---------------------------------------------------------------------------
+def layer_norm(x: torch.Tensor, weight, bias, eps: float = 1e-5) -> torch.Tensor:
+  _cuda(x)
+  x = x.contiguous()
+  y = torch.empty_like(x)
+  cols = x.shape[-1]
+  N.call("sf_layernorm", _dt(x), _p(x), _p(y), _p(weight), _p(bias), x.numel() // cols, cols,
+         C.c_float(eps), _stream())
+  return y
+
+
+def linear(x: torch.Tensor, wt: torch.Tensor, bias=None, residual=None, post_op=None) -> torch.Tensor:
+  """y = post_op(x @ wt.T + bias + residual); wt is [out, in] in x's dtype."""
+  _cuda(x, wt)
+  x = x.contiguous()
+  k = x.shape[-1]
+  n = wt.shape[0]
+  assert wt.shape[1] == k and wt.dtype == x.dtype
+  rows = x.numel() // k
+  y = torch.empty(*x.shape[:-1], n, dtype=x.dtype, device=x.device)
+  if residual is not None:
+    residual = residual.to(x.dtype).expand_as(y).contiguous()
+  N.call("sf_linear", _dt(x), _p(x), _p(wt), _p(bias), _p(residual), _p(y), rows, k, n,
+         N.POST_OPS[post_op], _stream())
+  return y
+
+
+def attention(q, k, v, *, scale=None, mask_q=None, mask_k=None, bias=None, gate=None,
+              mask_row=None) -> torch.Tensor:
+  """Drop-in for backends/torch/attention/sdpa.py:22 dot_product_attention.
+
+  q [..., Q, H, D], k/v [..., K, H, D], masks [..., Q] / [..., K] (broadcast),
+  bias broadcastable to [..., H, Q, K]; optional gate [..., Q, H, D] applies
+  sigmoid(gate) to the output.  Returns [..., Q, H, D] in q's dtype.
+  """
+  _cuda(q, k, v)
+  batch = q.shape[:-3]
+  Q, H, D = q.shape[-3:]
+  K = k.shape[-3]
+  if v.shape[-1] != D:
+    raise ValueError("sf_attention requires value dim == query dim")
+  B = math.prod(batch) if batch else 1
+  dt = _dt(q)
+  q3 = q.reshape(B, Q, H, D)
+  k3 = k.expand(*batch, K, H, D).reshape(B, K, H, D)
+  v3 = v.expand(*batch, K, H, D).reshape(B, K, H, D)
+  q3, k3, v3 = (t if t.stride(-1) == 1 else t.contiguous() for t in (q3, k3, v3))
+  out = torch.empty(B, Q, H, D, dtype=q.dtype, device=q.device)
+  a = N.AttentionArgs()
+  a.dtype = dt
+  a.batch, a.heads, a.q_len, a.k_len, a.head_dim = B, H, Q, K, D
+  a.q, a.q_sb, a.q_sh, a.q_sq = _p(q3), q3.stride(0), q3.stride(2), q3.stride(1)
+  a.k, a.k_sb, a.k_sh, a.k_sk = _p(k3), k3.stride(0), k3.stride(2), k3.stride(1)
+  a.v, a.v_sb, a.v_sh, a.v_sk = _p(v3), v3.stride(0), v3.stride(2), v3.stride(1)
+  a.out, a.o_sb, a.o_sh, a.o_sq = _p(out), out.stride(0), out.stride(2), out.stride(1)
+  keep = [q3, k3, v3, out]
+  if bias is not None:
+    b4 = bias.to(q.dtype) if bias.dtype not in (torch.float32, q.dtype) else bias
+    b4 = b4.expand(*batch, H, Q, K)
+    try:
+      b4 = b4.view(B, H, Q, K)
+    except RuntimeError:
+      b4 = b4.reshape(B, H, Q, K)
+    if b4.stride(-1) != 1:
+      b4 = b4.contiguous()
+    a.bias, a.bias_dtype = _p(b4), _dt(b4)
+    a.b_sb, a.b_sh, a.b_sq = b4.stride(0), b4.stride(1), b4.stride(2)
+    keep.append(b4)
+  if mask_q is not None:
+    mq = mask_u8(mask_q.expand(*batch, Q).reshape(B, Q))
+    a.mask_q, a.mq_sb = _p(mq), mq.stride(0)
+    keep.append(mq)
+  if mask_k is not None:
+    mk = mask_u8(mask_k.expand(*batch, K).reshape(B, K))
+    a.mask_k, a.mk_sb = _p(mk), mk.stride(0)
+    keep.append(mk)
+  if mask_row is not None:
+    mr = mask_u8(mask_row.reshape(B))
+    a.mask_row = _p(mr)
+    keep.append(mr)
+  if gate is not None:
+    g3 = gate.reshape(B, Q, H, D)
+    a.gate, a.g_sb, a.g_sh, a.g_sq = _p(g3), g3.stride(0), g3.stride(2), g3.stride(1)
+    keep.append(g3)
+  a.scale = float(1.0 / math.sqrt(D) if scale is None else scale)
+  N.call("sf_attention", C.byref(a), _stream())
+  return out.reshape(*batch, Q, H, D)
+
+
+# ---------------------------------------------------------------------------
+def tri_mult_weights(glu, ln_w, ln_b, center_w, center_b, w_out, w_gate) -> N.TriMultWeights:
+  return N.TriMultWeights(_p(ln_w), _p(ln_b), _p(glu), _p(center_w), _p(center_b), _p(w_out), _p(w_gate))
+
+
+def tri_mult(z: torch.Tensor, mask_u8_: torch.Tensor, w: N.TriMultWeights, incoming: bool,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+  """Whole TriangleMultiplication on one device: returns z + update."""
+  _cuda(z)
+  n, n2, c = z.shape
+  assert n == n2 and c == 128 and z.is_contiguous()
+  dt = _dt(z)
+  lib = N.load()
+  a_op = torch.empty(c, n, n, dtype=z.dtype, device=z.device)
+  b_op = torch.empty_like(a_op)
+  p = torch.empty_like(a_op)
+  ws = _ws(max(lib.sf_tri_mult_project_workspace(dt, n), lib.sf_tri_mult_output_workspace(dt, n, n)), z.device)
+  N.call("sf_tri_mult_project", dt, _p(z), _p(mask_u8_), n, int(incoming), C.byref(w), _p(a_op), _p(b_op),
+         _p(ws), ws.numel(), _stream())
+  N.call("sf_tri_mult_contract", dt, _p(a_op), _p(b_op), _p(p), c, n, n, n, _stream())
+  out = torch.empty_like(z) if out is None else out
+  N.call("sf_tri_mult_output", dt, _p(z), _p(p), n, n, C.byref(w), _p(out), _p(ws), ws.numel(), _stream())
+  return out
+
+
+def tri_attention_weights(ln_w, w_qkvg, w_bias, w_out, heads: int) -> N.TriAttentionWeights:
+  return N.TriAttentionWeights(_p(ln_w), _p(w_qkvg), _p(w_bias), _p(w_out), heads)
+
+
+def tri_attention(z: torch.Tensor, mask_u8_: torch.Tensor, w: N.TriAttentionWeights, transpose: bool,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+  _cuda(z)
+  n, n2, c = z.shape
+  assert n == n2 and c == 128 and z.is_contiguous()
+  dt = _dt(z)
+  ws = _ws(N.load().sf_tri_attention_workspace(dt, n, w.heads), z.device)
+  out = torch.empty_like(z) if out is None else out
+  N.call("sf_tri_attention", dt, _p(z), _p(mask_u8_), n, int(transpose), C.byref(w), _p(out), _p(ws),
+         ws.numel(), _stream())
+  return out
+
+
+def transition(x: torch.Tensor, ln_w, ln_b, w1, w2, out: torch.Tensor | None = None) -> torch.Tensor:
+  _cuda(x)
+  x = x.contiguous()
+  c = x.shape[-1]
+  inter = w1.shape[0] // 2
+  rows = x.numel() // c
+  dt = _dt(x)
+  ws = _ws(N.load().sf_transition_workspace(dt, rows, inter), x.device)
+  out = torch.empty_like(x) if out is None else out
+  N.call("sf_transition", dt, _p(x), _p(ln_w), _p(ln_b), _p(w1), _p(w2), _p(out), rows, c, inter,
+         _p(ws), ws.numel(), _stream())
+  return out
+
+
+def pair_logits(z: torch.Tensor, ln_w, ln_b, w, heads: int) -> torch.Tensor:
+  """[H, rows, n] logits of LN(z) @ W (SingleActUpdate, blocks.py:745-749)."""
+  _cuda(z)
+  rows, n, c = z.shape
+  dt = _dt(z)
+  out = torch.empty(heads, rows, n, dtype=z.dtype, device=z.device)
+  ws = _ws(N.load().sf_pair_logits_workspace(dt, rows, n, c), z.device)
+  N.call("sf_pair_logits", dt, _p(z.contiguous()), _p(ln_w), _p(ln_b), _p(w), _p(out), rows, n, c, heads,
+         _p(ws), ws.numel(), _stream())
+  return out

@@ -1,0 +1,81 @@
+"""Host-side contract of the B200 modules (no GPU): parameters, buffers, packing layouts.
+
+Mirrors the reference's native-preparation contract
+(tests/test_native_preparation.py:107-132): forward refuses to run before
+prepare, Parameters and state_dict keys are unchanged, only non-persistent
+buffers are added, and re-preparation is idempotent.  The packing tests
+recompute an op's first stage on the CPU from the *packed* weights and compare
+it with the oracle, which pins the row orders the kernels rely on.
+"""
+import pytest
+import torch
+
+from oracle import pairformer as orc
+from sparsefold_b200 import modules, synth
+
+
+def _block():
+  b = modules.PairFormerIteration()
+  synth.init_params(b, seed=0)
+  return b
+
+
+def test_forward_refuses_before_prepare():
+  b = _block()
+  z, s, mask = synth.pair_inputs(8)
+  with pytest.raises(RuntimeError, match="not prepared"):
+    b.triangle_multiplication_outgoing(z, mask)
+
+
+def test_prepare_keeps_parameters_and_state_dict():
+  b = _block()
+  keys = set(b.state_dict())
+  params = {k: v.detach().clone() for k, v in b.named_parameters()}
+  counts = modules.prepare(b)
+  assert counts["opaque"] == 8
+  assert set(b.state_dict()) == keys
+  for k, v in b.named_parameters():
+    torch.testing.assert_close(v, params[k], rtol=0, atol=0)
+  for m in b.modules():
+    assert set(m._buffers) <= m._non_persistent_buffers_set
+  modules.prepare(b)
+  assert set(b.state_dict()) == keys
+
+
+def test_tri_mult_glu_packing_matches_reference_channel_split():
+  b = _block()
+  modules.prepare(b)
+  t = b.triangle_multiplication_outgoing
+  p = {k: v for k, v in t.state_dict().items()}
+  z, _, mask = synth.pair_inputs(6, seed=3)
+  x = orc.layer_norm(z, p["left_norm_input.weight"], p["left_norm_input.bias"])
+  proj = torch.sigmoid(x @ p["gate_projection.weight"]) * (x @ p["projection.weight"])
+  y = x @ t._packed("glu", torch.float32).T
+  c = 128
+  a_pk = torch.sigmoid(y[..., :c]) * y[..., c:2 * c]
+  b_pk = torch.sigmoid(y[..., 2 * c:3 * c]) * y[..., 3 * c:]
+  torch.testing.assert_close(a_pk, proj[..., 0::2], rtol=1e-5, atol=1e-5)
+  torch.testing.assert_close(b_pk, proj[..., 1::2], rtol=1e-5, atol=1e-5)
+
+
+def test_grid_attention_qkvg_packing():
+  b = _block()
+  modules.prepare(b)
+  g = b.pair_attention1
+  p = g.state_dict()
+  z, _, _ = synth.pair_inputs(5, seed=4)
+  x = orc.layer_norm(z, p["act_norm.weight"], None)
+  y = x @ g._packed("qkvg", torch.float32).T
+  q = torch.einsum("bnc,hdc->bnhd", x, p["q_projection.weight"]).reshape(5, 5, 128)
+  v = torch.einsum("bnc,chd->bnhd", x, p["v_projection.weight"]).reshape(5, 5, 128)
+  gate = torch.einsum("bnc,oc->bno", x, p["gating_query.weight"])
+  torch.testing.assert_close(y[..., :128], q, rtol=1e-5, atol=1e-5)
+  torch.testing.assert_close(y[..., 256:384], v, rtol=1e-5, atol=1e-5)
+  torch.testing.assert_close(y[..., 384:], gate, rtol=1e-5, atol=1e-5)
+
+
+def test_ops_reject_host_tensors():
+  from sparsefold_b200 import ops
+  x = torch.zeros(4, 8)
+  with pytest.raises(ValueError, match="CUDA"):
+    ops.layer_norm(x, None, None)
