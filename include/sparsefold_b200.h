@@ -63,6 +63,9 @@ int sf_last_error(char* buf, size_t len);
 int sf_device_check(void);
 /* Number of kernels this library launched since load (all threads). */
 uint64_t sf_launch_count(void);
+/* Reads (and with clear != 0 resets) the current device's status word: 0, or
+ * SF_ERR_TIMEOUT when a kernel's bounded wait gave up.  Synchronises the device. */
+int sf_device_status(uint32_t* out, int clear);
 
 /* ---- generic attention: sdpa.py:22-121 ---------------------------------
  * out[b,q,h,:] = softmax_k(scale * q.k + bias[b,h,q,k] + maskbias) @ v

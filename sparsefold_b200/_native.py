@@ -52,6 +52,7 @@ _SIGNATURES = {
     "sf_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
     "sf_device_check": (C.c_int, []),
     "sf_launch_count": (C.c_uint64, []),
+    "sf_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
     "sf_attention": (C.c_int, [C.POINTER(AttentionArgs), _vp]),
     "sf_layernorm": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, C.c_float, _vp]),
     "sf_linear": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, C.c_int, _vp]),
@@ -113,6 +114,13 @@ def check(status: int, what: str) -> None:
 
 def call(name: str, *args) -> None:
   check(getattr(load(), name)(*args), name)
+
+
+def device_status(clear: bool = True) -> int:
+  """0, or SF_ERR_TIMEOUT if a kernel's bounded wait gave up since the last clear."""
+  v = C.c_uint32(0)
+  check(load().sf_device_status(C.byref(v), int(clear)), "sf_device_status")
+  return int(v.value)
 
 
 def launch_count() -> int:

@@ -67,7 +67,7 @@ def build(force: bool = False, jobs: int | None = None, verbose_ptxas: bool = Fa
     objs = list(ex.map(lambda s: _compile(s, extra), sources))
   if force or _stale(LIB, objs):
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcuda"]
+    cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
       raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -3,6 +3,7 @@
 // message read by sf_last_error(); no C++ exception crosses the C ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -41,6 +42,20 @@ __device__ __forceinline__ float warp_max(float v) {
 void set_error(const char* fmt, ...);
 void count_launch(uint64_t n = 1);
 int check_launch(const char* what);  // cudaGetLastError -> status
+// Device address of the library's status word on the current device (0 = ok;
+// a kernel whose bounded wait gave up stores SF_ERR_TIMEOUT).  nullptr on error.
+uint32_t* device_status_ptr();
+
+// tcgen05 kernels (bf16 track), host launchers defined in sf_*_tc.cu.
+int num_sms();
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn tensor_map_encoder();
+int make_pair_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t n, bool column_tile);
+int trimul_project_tc(const bf16* z, const uint8_t* mask, int64_t rows, int64_t n, int64_t row_offset, int incoming,
+                      const float* ln_w, const float* ln_b, const bf16* w_glu, bf16* a_op, bf16* b_op,
+                      cudaStream_t stream);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

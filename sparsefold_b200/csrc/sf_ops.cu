@@ -273,6 +273,9 @@ int sf_tri_mult_project(int dtype, const void* z, const uint8_t* mask, int64_t n
     set_error("sf_tri_mult_project: workspace %zu < %zu", ws_bytes, sf_tri_mult_project_workspace(dtype, n));
     return SF_ERR_WORKSPACE;
   }
+  if (dtype == SF_BF16)
+    return trimul_project_tc((const bf16*)z, mask, n, n, 0, incoming, w->ln_w, w->ln_b, (const bf16*)w->w_glu,
+                             (bf16*)a_op, (bf16*)b_op, stream);
   SF_DISPATCH(dtype, {
     Workspace ws(ws_p, ws_bytes);
     T* x = ws.take<T>(n * n * C);

@@ -8,6 +8,10 @@ namespace sf {
 
 static thread_local char g_err[1024] = {0};
 static std::atomic<uint64_t> g_launches{0};
+// One status word per device that loads the library; kernels with bounded
+// waits record a timeout here instead of hanging.
+static __device__ uint32_t g_device_status;
+static uint32_t* g_status_ptr[64] = {nullptr};
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -27,6 +31,21 @@ int check_launch(const char* what) {
   return SF_OK;
 }
 
+uint32_t* device_status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_device_status);
+    if (e != cudaSuccess) {
+      set_error("cudaGetSymbolAddress(status): %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_status_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
 }  // namespace sf
 
 extern "C" {
@@ -44,6 +63,21 @@ int sf_last_error(char* buf, size_t len) {
 }
 
 uint64_t sf_launch_count(void) { return sf::g_launches.load(); }
+
+int sf_device_status(uint32_t* out, int clear) {
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, sf::g_device_status, sizeof(v));
+  if (e == cudaSuccess && clear) {
+    uint32_t z = 0;
+    e = cudaMemcpyToSymbol(sf::g_device_status, &z, sizeof(z));
+  }
+  if (e != cudaSuccess) {
+    sf::set_error("sf_device_status: %s", cudaGetErrorString(e));
+    return SF_ERR_CUDA;
+  }
+  if (out) *out = v;
+  return SF_OK;
+}
 
 int sf_device_check(void) {
   int dev = 0;

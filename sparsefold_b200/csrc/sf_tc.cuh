@@ -1,0 +1,175 @@
+// Blackwell (sm_100a) primitives written as inline PTX: mbarriers with bounded
+// waits, TMA tile loads (no multicast), tcgen05 TMEM allocation, UMMA shared
+// memory / instruction descriptors, tcgen05.mma issue and commit, tcgen05.ld.
+//
+// Descriptor bit layouts (PTX ISA, tcgen05 matrix descriptors):
+//   smem descriptor: [0,14) start>>4, [16,30) LBO>>4, [32,46) SBO>>4,
+//                    [46,48) version = 1, [49,52) base offset, [61,64) layout
+//                    (2 = 128B swizzle, 4 = 64B swizzle, 6 = 32B swizzle).
+//   instr descriptor (kind::f16): [4,6) D format (1 = f32), [7,10) A format
+//                    (1 = bf16), [10,13) B format, [15] A MN-major, [16] B
+//                    MN-major, [17,23) N>>3, [24,29) M>>4.
+// K-major operands use the canonical swizzled layout: rows of one swizzle
+// atom width (128 B or 64 B), 8-row groups SBO bytes apart, and the 16-byte
+// chunk c of row r stored at chunk (c ^ f(r)), f(r) = r & 7 for 128B swizzle
+// and (r >> 1) & 3 for 64B swizzle.  Atoms start on 1024-byte boundaries.
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+#include "sf_common.cuh"
+
+namespace sf {
+namespace tc {
+
+// Every wait gives up after this many try_wait polls (each poll may suspend
+// the thread for a hardware-defined interval), records SF_ERR_TIMEOUT in the
+// caller's status word and lets the kernel run to its end.
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier ----------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait.  On timeout sets *status (first error wins) and returns false;
+// once this thread has timed out (`aborted`), later waits poll only once so the
+// kernel still reaches its end in bounded time.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, bool& aborted) {
+  const uint32_t limit = aborted ? 1u : kWaitLimit;
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try(bar, parity)) return true;
+  aborted = true;
+  if (status) atomicCAS(status, 0u, (uint32_t)SF_ERR_TIMEOUT);
+  return false;
+}
+
+// ---- fences --------------------------------------------------------------------
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---- TMA tiled loads (never multicast) -------------------------------------------
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- TMEM allocation (one full warp executes these) ---------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// ---- descriptors -----------------------------------------------------------------
+enum Swizzle : uint64_t { kSW128 = 2, kSW64 = 4, kSW32 = 6 };
+
+// K-major operand in the canonical swizzled layout: `sbo_bytes` apart per 8-row
+// group; LBO is unused for swizzled K-major layouts and set to 16 bytes.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t sbo_bytes, Swizzle sw) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(1u) << 16;                          // LBO = 16 B
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;  // SBO
+  d |= (uint64_t)1 << 46;                             // version
+  d |= (uint64_t)sw << 61;
+  return d;
+}
+
+// bf16 x bf16 -> fp32, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4)                       // D = f32
+         | (1u << 7)                     // A = bf16
+         | (1u << 10)                    // B = bf16
+         | ((uint32_t)(n >> 3) << 17)    // N
+         | ((uint32_t)(m >> 4) << 24);   // M
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate)
+      : "memory");
+}
+// Arrive on `bar` once all tcgen05.mma previously issued by this thread complete.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// ---- TMEM -> registers: lane = row (warp w reads lanes 32*(w%4)..+31) -----------------
+// The wait is in the same asm statement so no instruction can read the
+// destination registers before the load has landed.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- swizzled shared-memory addressing of a K-major bf16 tile -----------------------
+// Byte offset of 16-byte chunk `c` (8 bf16 along K) of row `r` inside one
+// 128B-swizzle atom column (rows of 128 bytes).
+__device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
+// Same for a 64B-swizzle atom column (rows of 64 bytes, 4 chunks).
+__device__ __forceinline__ uint32_t sw64_off(uint32_t r, uint32_t c) {
+  return r * 64u + ((c ^ ((r >> 1) & 3u)) << 4);
+}
+
+}  // namespace tc
+}  // namespace sf

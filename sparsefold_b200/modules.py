@@ -41,6 +41,11 @@ def _require_prepared(fn):
   def wrapped(self, *args, **kwargs):
     if not getattr(self, "_native_prepared", False):
       raise RuntimeError("Native buffers are not prepared; call backends.prepare(model) after weight loading")
+    dev = args[0].device if args and isinstance(args[0], torch.Tensor) else None
+    for name, buf in self._buffers.items():
+      if dev is not None and name.startswith("_sf_") and buf.device != dev:
+        raise RuntimeError(f"prepared buffer {name} is on {buf.device}, activation on {dev}; "
+                           "move the module before or after prepare, consistently")
     return fn(self, *args, **kwargs)
   return wrapped
 
@@ -184,7 +189,7 @@ class SelfAttentionB200(B200Module):
     wv = self.v_projection.weight.detach().float().reshape(c, h * d).T
     wg = self.gating_query.weight.detach().float().T
     self._pack("qkvg", torch.cat([wq, wk, wv, wg], 0))
-    bias = torch.zeros(4 * h * d)
+    bias = torch.zeros(4 * h * d, device=self.q_projection.weight.device)
     bias[: h * d] = self.q_projection.bias.detach().float().reshape(-1)
     self._keep("qkvg_bias", bias)
     self._pack("out", self.zero_init.transition2.weight.detach().float().T)

@@ -46,7 +46,7 @@ def mask_u8(mask: torch.Tensor) -> torch.Tensor:
 
 # ---------------------------------------------------------------------------
 def layer_norm(x: torch.Tensor, weight, bias, eps: float = 1e-5) -> torch.Tensor:
-  _cuda(x)
+  _cuda(x, weight, bias)
   x = x.contiguous()
   y = torch.empty_like(x)
   cols = x.shape[-1]
@@ -57,7 +57,7 @@ def layer_norm(x: torch.Tensor, weight, bias, eps: float = 1e-5) -> torch.Tensor
 
 def linear(x: torch.Tensor, wt: torch.Tensor, bias=None, residual=None, post_op=None) -> torch.Tensor:
   """y = post_op(x @ wt.T + bias + residual); wt is [out, in] in x's dtype."""
-  _cuda(x, wt)
+  _cuda(x, wt, bias, residual)
   x = x.contiguous()
   k = x.shape[-1]
   n = wt.shape[0]

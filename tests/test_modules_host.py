@@ -79,3 +79,11 @@ def test_ops_reject_host_tensors():
   x = torch.zeros(4, 8)
   with pytest.raises(ValueError, match="CUDA"):
     ops.layer_norm(x, None, None)
+
+
+def test_prepare_after_move_keeps_every_buffer_on_the_parameter_device():
+  """prepare() on an already-moved module must not leave any buffer behind on the host."""
+  b = modules.PairFormerIteration().to("meta")
+  modules.prepare(b)
+  for name, buf in b.named_buffers():
+    assert buf.device.type == "meta", name
