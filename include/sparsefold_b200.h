@@ -112,16 +112,21 @@ typedef struct sf_tri_mult_weights {
   const void* w_gate;                             /* [C][C] */
 } sf_tri_mult_weights;
 
+/* Row pitch of the channel-major buffers a_op, b_op and p: n rounded up to a
+ * multiple of 8 elements (16-byte aligned rows).  Padding columns are zero. */
+int64_t sf_pair_pitch(int64_t n);
+
 /* Phase 1: x = LN(z); proj = sigmoid(x Wg) * (x Wv) * mask; writes the two
  * contraction operands so that phase 2 is always P[c,i,j] = sum_k A[c,i,k] B[c,j,k]:
  *   outgoing: A[c][i][k] = a[c,i,k], B[c][j][k] = b[c,j,k]   (rows = i, cols = k)
  *   incoming: A[c][i][k] = b[c,k,i], B[c][j][k] = a[c,k,j]   (stored transposed)
- * a_op / b_op are [C][n][n] for the full device case. */
+ * a_op / b_op are [C][n][sf_pair_pitch(n)] for the full device case. */
 int sf_tri_mult_project(int dtype, const void* z, const uint8_t* mask, int64_t n, int incoming,
                         const sf_tri_mult_weights* w, void* a_op, void* b_op,
                         void* ws, size_t ws_bytes, sf_stream_t stream);
 size_t sf_tri_mult_project_workspace(int dtype, int64_t n);
-/* Phase 2: P[c][i][j] = sum_k A[c][i][k] * B[c][j][k]; A [C][rows][kdim], B [C][cols][kdim]. */
+/* Phase 2: P[c][i][j] = sum_k A[c][i][k] * B[c][j][k]; A [C][rows][pitch(kdim)],
+ * B [C][cols][pitch(kdim)], P [C][rows][pitch(cols)]. */
 int sf_tri_mult_contract(int dtype, const void* a_op, const void* b_op, void* p,
                          int64_t channels, int64_t rows, int64_t cols, int64_t kdim, sf_stream_t stream);
 /* Phase 3: z_out = z + (centerLN(P) W_out) * sigmoid(LN(z) W_gate); z_out may alias z. */

@@ -52,6 +52,7 @@ _SIGNATURES = {
     "sf_last_error": (C.c_int, [C.c_char_p, C.c_size_t]),
     "sf_device_check": (C.c_int, []),
     "sf_launch_count": (C.c_uint64, []),
+    "sf_pair_pitch": (C.c_int64, [_i64]),
     "sf_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
     "sf_attention": (C.c_int, [C.POINTER(AttentionArgs), _vp]),
     "sf_layernorm": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, C.c_float, _vp]),

@@ -53,9 +53,15 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn tensor_map_encoder();
 int make_pair_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t n, bool column_tile);
+int contract_tc(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
+                int64_t kdim, cudaStream_t stream);
 int trimul_project_tc(const bf16* z, const uint8_t* mask, int64_t rows, int64_t n, int64_t row_offset, int incoming,
                       const float* ln_w, const float* ln_b, const bf16* w_glu, bf16* a_op, bf16* b_op,
                       cudaStream_t stream);
+
+// Row pitch (elements) of the channel-major triangle-multiplication buffers:
+// rows are padded to a multiple of 8 elements so every row starts 16-byte aligned.
+__host__ __device__ inline int64_t pair_pitch(int64_t n) { return (n + 7) / 8 * 8; }
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

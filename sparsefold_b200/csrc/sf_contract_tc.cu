@@ -1,0 +1,204 @@
+// Triangle-multiplication contraction on tcgen05 (blocks.py:558):
+//   P[c][i][j] = sum_k A[c][i][k] * B[c][j][k]   (bf16 in, fp32 accumulate, bf16 out)
+// for each of the 128 channels c.  Both operands are K-major, which is how the
+// projection phase writes them for either equation.
+//
+// Persistent, warp-specialised: warp 4 streams 128x64 A and 256x64 B tiles by
+// TMA through a 4-stage shared-memory ring; one thread of warp 5 issues
+// tcgen05.mma (M=128, N=256, K=16) into one of two TMEM accumulators
+// (2 x 256 fp32 columns); warps 0-3 drain the other accumulator (tcgen05.ld,
+// one row per thread) and store bf16 rows of P while the next tile computes.
+#include "sf_pair_tc.cuh"
+
+namespace sf {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int SA_BYTES = BM * BK * 2;              // 16 KB
+constexpr int SB_BYTES = BN * BK * 2;              // 32 KB
+constexpr int STAGE_BYTES = SA_BYTES + SB_BYTES;   // 48 KB
+constexpr int SMEM_CONTRACT = STAGES * STAGE_BYTES + 1024 + 1024;
+
+struct ContractParams {
+  bf16* P;
+  int64_t channels, rows, cols, kdim;
+  uint32_t* status;
+};
+
+__global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ CUtensorMap tmA,
+                                                        const __grid_constant__ CUtensorMap tmB,
+                                                        ContractParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = pt::align1024(smem_raw);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* accf = empty + STAGES;
+  uint64_t* acce = accf + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const int64_t mt = (p.rows + BM - 1) / BM, nt = (p.cols + BN - 1) / BN;
+  const int64_t ntiles = p.channels * mt * nt;
+  const int nk = (int)((p.kdim + BK - 1) / BK);
+
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&accf[a], 1);
+      tc::mbar_init(&acce[a], 128);
+    }
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmA);
+    tc::prefetch_tmap(&tmB);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  bool aborted = false;
+
+  if (warp == 4 && lane == 0) {
+    // ---- TMA producer ----
+    uint32_t q = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const int64_t c = t / (mt * nt), rem = t % (mt * nt);
+      const int i0 = (int)((rem / nt) * BM), j0 = (int)((rem % nt) * BN);
+      for (int kb = 0; kb < nk; ++kb, ++q) {
+        const int s = q % STAGES;
+        tc::mbar_wait(&empty[s], ((q / STAGES) & 1) ^ 1, p.status, aborted);
+        uint8_t* st = smem + s * STAGE_BYTES;
+        tc::mbar_expect_tx(&full[s], STAGE_BYTES);
+        tc::tma_load_3d(st, &tmA, &full[s], kb * BK, i0, (int)c);
+        tc::tma_load_3d(st + SA_BYTES, &tmB, &full[s], kb * BK, j0, (int)c);
+      }
+    }
+  } else if (warp == 5 && lane == 0) {
+    // ---- MMA issuer ----
+    constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN);
+    const uint32_t sbase = tc::smem_u32(smem);
+    uint32_t q = 0, u = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++u) {
+      const uint32_t acc = u & 1;
+      tc::mbar_wait(&acce[acc], ((u >> 1) & 1) ^ 1, p.status, aborted);
+      tc::tc_fence_after();
+      for (int kb = 0; kb < nk; ++kb, ++q) {
+        const int s = q % STAGES;
+        tc::mbar_wait(&full[s], (q / STAGES) & 1, p.status, aborted);
+        tc::tc_fence_after();
+        const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + SA_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t ad = tc::smem_desc(sa + kk * 32, 1024, tc::kSW128);
+          const uint64_t bd = tc::smem_desc(sb + kk * 32, 1024, tc::kSW128);
+          tc::mma_bf16(tbase + acc * BN, ad, bd, IDESC, (kb | kk) != 0);
+        }
+        tc::mma_commit(&empty[s]);
+      }
+      tc::mma_commit(&accf[acc]);
+    }
+  } else if (warp < 4) {
+    // ---- epilogue ----
+    const int64_t cp = pair_pitch(p.cols);
+    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    uint32_t u = 0;
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++u) {
+      const uint32_t acc = u & 1;
+      const int64_t c = t / (mt * nt), rem = t % (mt * nt);
+      const int64_t i = (rem / nt) * BM + tid, j0 = (rem % nt) * BN;
+      tc::mbar_wait(&accf[acc], (u >> 1) & 1, p.status, aborted);
+      tc::tc_fence_after();
+      bf16* prow = p.P + (c * p.rows + i) * cp;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 16; ++ch) {
+        float v[16];
+        tc::tmem_ld16(lane_addr + acc * BN + ch * 16, v);
+        if (i < p.rows) {
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const int64_t j = j0 + ch * 16 + g * 8;
+            if (j + 8 <= cp) {
+              uint4 o;
+              o.x = pt::pack_bf2(v[g * 8 + 0], v[g * 8 + 1]);
+              o.y = pt::pack_bf2(v[g * 8 + 2], v[g * 8 + 3]);
+              o.z = pt::pack_bf2(v[g * 8 + 4], v[g * 8 + 5]);
+              o.w = pt::pack_bf2(v[g * 8 + 6], v[g * 8 + 7]);
+              *reinterpret_cast<uint4*>(prow + j) = o;
+            }
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&acce[acc]);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, 512);
+  }
+}
+
+// Tensor map over a channel-major operand [channels][rows][pitch(kdim)] bf16, box 64 (k) x box_rows.
+int make_operand_tmap(CUtensorMap* map, const void* base, int64_t channels, int64_t rows, int64_t kdim,
+                      uint32_t box_rows) {
+  auto encode = tensor_map_encoder();
+  if (!encode) return SF_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) {
+    set_error("contraction operand %p is not 16-byte aligned", base);
+    return SF_ERR_ARG;
+  }
+  const int64_t kp = pair_pitch(kdim);
+  cuuint64_t dims[3] = {(cuuint64_t)kp, (cuuint64_t)rows, (cuuint64_t)channels};
+  cuuint64_t strides[2] = {(cuuint64_t)kp * 2, (cuuint64_t)(rows * kp * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)BK, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for operand [%lld][%lld][%lld]", (int)r, (long long)channels,
+              (long long)rows, (long long)kp);
+    return SF_ERR_CUDA;
+  }
+  return SF_OK;
+}
+
+}  // namespace
+
+int contract_tc(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
+                int64_t kdim, cudaStream_t stream) {
+  if (channels == 0 || rows == 0 || cols == 0) return SF_OK;
+  SF_REQUIRE(rows < (1 << 30) && cols < (1 << 30) && kdim < (1 << 30) && channels < (1 << 30),
+             "contract_tc: size too large");
+  CUtensorMap ma, mb;
+  SF_TRY(make_operand_tmap(&ma, a_op, channels, rows, kdim, BM));
+  SF_TRY(make_operand_tmap(&mb, b_op, channels, cols, kdim, BN));
+  uint32_t* status = device_status_ptr();
+  if (!status) return SF_ERR_CUDA;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(k_contract_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_CONTRACT);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(contract): %s", cudaGetErrorString(e));
+      return SF_ERR_CUDA;
+    }
+    attr_set[dev & 63] = true;
+  }
+  ContractParams p{P, channels, rows, cols, kdim, status};
+  const int64_t ntiles = channels * ((rows + BM - 1) / BM) * ((cols + BN - 1) / BN);
+  const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
+  k_contract_tc<<<grid, 192, SMEM_CONTRACT, stream>>>(ma, mb, p);
+  count_launch();
+  return check_launch("contract_tc");
+}
+
+}  // namespace sf

@@ -55,10 +55,10 @@ struct EpiResidual {  // y = x + v (row-major, ld = c)
 // operands channel-major through a 32x32 shared-memory transpose.
 template <typename T>
 __global__ void k_tri_glu_scatter(const float* __restrict__ y, const uint8_t* __restrict__ mask,
-                                  int64_t n, int C, int incoming, T* __restrict__ a_op,
+                                  int64_t n, int64_t pitch, int C, int incoming, T* __restrict__ a_op,
                                   T* __restrict__ b_op) {
   __shared__ float ta[32][33], tb[32][33];
-  const int64_t M = n * n;
+  const int64_t M = n * n, plane = n * pitch;
   const int64_t m0 = (int64_t)blockIdx.x * 32;
   const int c0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
@@ -86,12 +86,13 @@ __global__ void k_tri_glu_scatter(const float* __restrict__ y, const uint8_t* __
     int64_t i = m / n, k = m % n;
     float va = ta[tx][r], vb = tb[tx][r];
     if (!incoming) {
-      st(a_op + (int64_t)c * M + m, va);   // A[c][i][k] = a[c,i,k]
-      st(b_op + (int64_t)c * M + m, vb);   // B[c][j][k] = b[c,j,k]
+      int64_t t = i * pitch + k;
+      st(a_op + (int64_t)c * plane + t, va);   // A[c][i][k] = a[c,i,k]
+      st(b_op + (int64_t)c * plane + t, vb);   // B[c][j][k] = b[c,j,k]
     } else {
-      int64_t t = k * n + i;               // transpose of position (i, k)
-      st(a_op + (int64_t)c * M + t, vb);   // A[c][i][k] = b[c,k,i]
-      st(b_op + (int64_t)c * M + t, va);   // B[c][j][k] = a[c,k,j]
+      int64_t t = k * pitch + i;               // transpose of position (i, k)
+      st(a_op + (int64_t)c * plane + t, vb);   // A[c][i][k] = b[c,k,i]
+      st(b_op + (int64_t)c * plane + t, va);   // B[c][j][k] = a[c,k,j]
     }
   }
 }
@@ -104,17 +105,18 @@ __global__ void __launch_bounds__(256) k_contract(const T* __restrict__ A, const
   __shared__ float As[GK][GM + 4];
   __shared__ float Bs[GK][GN + 4];
   const int64_t c = blockIdx.z;
-  const T* Ab = A + c * rows * K;
-  const T* Bb = B + c * cols * K;
-  T* Pb = P + c * rows * cols;
+  const int64_t kp = pair_pitch(K), cp = pair_pitch(cols);
+  const T* Ab = A + c * rows * kp;
+  const T* Bb = B + c * cols * kp;
+  T* Pb = P + c * rows * cp;
   const int tid = threadIdx.x, tm = tid / 16, tn = tid % 16;
   const int64_t m0 = (int64_t)blockIdx.y * GM, n0 = (int64_t)blockIdx.x * GN;
   float acc[4][4] = {};
   for (int64_t k0 = 0; k0 < K; k0 += GK) {
     for (int e = tid; e < GM * GK; e += 256) {
       int r = e / GK, kk = e % GK;
-      As[kk][r] = (m0 + r < rows && k0 + kk < K) ? ld(Ab + (m0 + r) * K + k0 + kk) : 0.f;
-      Bs[kk][r] = (n0 + r < cols && k0 + kk < K) ? ld(Bb + (n0 + r) * K + k0 + kk) : 0.f;
+      As[kk][r] = (m0 + r < rows && k0 + kk < K) ? ld(Ab + (m0 + r) * kp + k0 + kk) : 0.f;
+      Bs[kk][r] = (n0 + r < cols && k0 + kk < K) ? ld(Bb + (n0 + r) * kp + k0 + kk) : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -138,7 +140,7 @@ __global__ void __launch_bounds__(256) k_contract(const T* __restrict__ A, const
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       int64_t nn = n0 + tn * 4 + j;
-      if (nn < cols) st(Pb + m * cols + nn, acc[i][j]);
+      if (nn < cols) st(Pb + m * cp + nn, acc[i][j]);
     }
   }
 }
@@ -148,14 +150,16 @@ __global__ void __launch_bounds__(256) k_contract(const T* __restrict__ A, const
 template <typename T>
 __global__ void __launch_bounds__(256) k_center_ln(const T* __restrict__ p, T* __restrict__ y,
                                                    const float* __restrict__ w,
-                                                   const float* __restrict__ b, int64_t M, int C,
+                                                   const float* __restrict__ b, int64_t M, int64_t n, int C,
                                                    float eps) {
   extern __shared__ float tile[];  // [C][33]
   __shared__ float mean_s[32], rstd_s[32];
   const int64_t m0 = (int64_t)blockIdx.x * 32;
+  const int64_t pitch = pair_pitch(n), plane = (M / n) * pitch;
   for (int e = threadIdx.x; e < C * 32; e += blockDim.x) {
     int c = e / 32, r = e % 32;
-    tile[c * 33 + r] = (m0 + r < M) ? ld(p + (int64_t)c * M + m0 + r) : 0.f;
+    const int64_t m = m0 + r;
+    tile[c * 33 + r] = (m < M) ? ld(p + (int64_t)c * plane + (m / n) * pitch + m % n) : 0.f;
   }
   __syncthreads();
   if (threadIdx.x < 32) {
@@ -204,6 +208,7 @@ using namespace sf;
 
 static size_t dsize(int dtype) { return dtype == SF_F32 ? 4 : 2; }
 
+
 template <typename F>
 static size_t ws_of(F f) {
   WorkspaceSize w;
@@ -212,6 +217,8 @@ static size_t ws_of(F f) {
 }
 
 extern "C" {
+
+int64_t sf_pair_pitch(int64_t n) { return pair_pitch(n); }
 
 // ---------------------------------------------------------------------------
 int sf_layernorm(int dtype, const void* x, void* y, const float* weight, const float* bias,
@@ -273,6 +280,11 @@ int sf_tri_mult_project(int dtype, const void* z, const uint8_t* mask, int64_t n
     set_error("sf_tri_mult_project: workspace %zu < %zu", ws_bytes, sf_tri_mult_project_workspace(dtype, n));
     return SF_ERR_WORKSPACE;
   }
+  if (pair_pitch(n) != n) {  // zero the row padding the contraction reads as K
+    const size_t bytes = (size_t)C * n * pair_pitch(n) * dsize(dtype);
+    if (cudaMemsetAsync(a_op, 0, bytes, stream) != cudaSuccess || cudaMemsetAsync(b_op, 0, bytes, stream) != cudaSuccess)
+      return check_launch("tri_mult_project.memset");
+  }
   if (dtype == SF_BF16)
     return trimul_project_tc((const bf16*)z, mask, n, n, 0, incoming, w->ln_w, w->ln_b, (const bf16*)w->w_glu,
                              (bf16*)a_op, (bf16*)b_op, stream);
@@ -284,7 +296,8 @@ int sf_tri_mult_project(int dtype, const void* z, const uint8_t* mask, int64_t n
     SF_TRY(launch_gemm(n * n, (int)(4 * C), (int)C, RowMajor<T>{x, C}, (const T*)w->w_glu,
                        EpiStore<float>{y, 4 * C}, stream, "tri_mult_project.gemm"));
     dim3 grid((unsigned)((n * n + 31) / 32), (unsigned)(C / 32));
-    k_tri_glu_scatter<T><<<grid, dim3(32, 8), 0, stream>>>(y, mask, n, (int)C, incoming, (T*)a_op, (T*)b_op);
+    k_tri_glu_scatter<T><<<grid, dim3(32, 8), 0, stream>>>(y, mask, n, pair_pitch(n), (int)C, incoming, (T*)a_op,
+                                                           (T*)b_op);
     count_launch();
     return check_launch("tri_mult_project.scatter");
   });
@@ -296,6 +309,8 @@ int sf_tri_mult_contract(int dtype, const void* a_op, const void* b_op, void* p,
              "sf_tri_mult_contract: bad arguments");
   SF_REQUIRE(channels <= 65535, "sf_tri_mult_contract: too many channels");
   if (rows == 0 || cols == 0) return SF_OK;
+  if (dtype == SF_BF16)
+    return contract_tc((const bf16*)a_op, (const bf16*)b_op, (bf16*)p, channels, rows, cols, kdim, stream);
   SF_DISPATCH(dtype, {
     dim3 grid((unsigned)((cols + GN - 1) / GN), (unsigned)((rows + GM - 1) / GM), (unsigned)channels);
     k_contract<T><<<grid, 256, 0, stream>>>((const T*)a_op, (const T*)b_op, (T*)p, rows, cols, kdim);
@@ -333,7 +348,7 @@ int sf_tri_mult_output(int dtype, const void* z, const void* p, int64_t rows, in
     float* g = ws.take<float>(M * C);
     SF_TRY(launch_layernorm((const T*)z, x, w->ln_w, w->ln_b, M, (int)C, 1e-5f, stream));
     k_center_ln<T><<<(unsigned)((M + 31) / 32), 256, C * 33 * sizeof(float), stream>>>(
-        (const T*)p, yh, w->center_w, w->center_b, M, (int)C, 1e-5f);
+        (const T*)p, yh, w->center_w, w->center_b, M, n, (int)C, 1e-5f);
     count_launch();
     SF_TRY(check_launch("tri_mult_output.center_ln"));
     SF_TRY(launch_gemm(M, (int)C, (int)C, RowMajor<T>{x, C}, (const T*)w->w_gate, EpiStore<float>{g, C},

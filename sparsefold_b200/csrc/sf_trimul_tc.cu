@@ -76,7 +76,9 @@ __global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_const
 
   constexpr uint32_t IDESC = tc::idesc_bf16(128, 256);
   const uint32_t a_base = tc::smem_u32(A), w_base = tc::smem_u32(W);
-  const int64_t plane = p.n * p.rows;
+  // operand planes: outgoing [rows][pitch(n)], incoming (transposed) [n][pitch(rows)]
+  const int64_t pitch = pair_pitch(p.incoming ? p.rows : p.n);
+  const int64_t plane = (p.incoming ? p.n : p.rows) * pitch;
 
   int64_t tile = blockIdx.x;
   if (tid == 0 && tile < ntiles) issue(tile, 0);
@@ -115,7 +117,7 @@ __global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_const
     const int64_t r = p.incoming ? minor : major;     // local pair row
     const int64_t s = p.incoming ? major : minor;     // pair column
     const bool keep = valid && p.mask[p.row_offset + r] && p.mask[s];
-    const int64_t pos = p.incoming ? s * p.rows + r : r * p.n + s;
+    const int64_t pos = p.incoming ? s * pitch + r : r * pitch + s;
     bf16* ao = p.incoming ? p.b_op : p.a_op;          // incoming: A <- b, B <- a (transposed)
     bf16* bo = p.incoming ? p.a_op : p.b_op;
     const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);

@@ -146,7 +146,8 @@ def tri_mult(z: torch.Tensor, mask_u8_: torch.Tensor, w: N.TriMultWeights, incom
   assert n == n2 and c == 128 and z.is_contiguous()
   dt = _dt(z)
   lib = N.load()
-  a_op = torch.empty(c, n, n, dtype=z.dtype, device=z.device)
+  pitch = lib.sf_pair_pitch(n)
+  a_op = torch.empty(c, n, pitch, dtype=z.dtype, device=z.device)
   b_op = torch.empty_like(a_op)
   p = torch.empty_like(a_op)
   ws = _ws(max(lib.sf_tri_mult_project_workspace(dt, n), lib.sf_tri_mult_output_workspace(dt, n, n)), z.device)
