@@ -158,6 +158,19 @@ int sf_transition(int dtype, const void* x, const float* ln_w, const float* ln_b
                   void* ws, size_t ws_bytes, sf_stream_t stream);
 size_t sf_transition_workspace(int dtype, int64_t rows, int64_t inter);
 
+/* sf_transition for callers that cannot allocate device memory (no counterpart
+ * in the reference).  Same arguments as sf_transition minus the workspace: the
+ * scratch is a fixed array of sf_transition_noalloc_max_scratch() bytes
+ * (16 MiB) inside the library, reserved on every GPU that loads it until exit.
+ * Sizes whose sf_transition_workspace() exceeds it return SF_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address (make it
+ * before any stream capture).  All calls share the array, so calls that
+ * overlap on the GPU race; the array needs no clearing between calls. */
+int sf_transition_noalloc(int dtype, const void* x, const float* ln_w, const float* ln_b,
+                          const void* w1, const void* w2, void* y, int64_t rows, int64_t c,
+                          int64_t inter, sf_stream_t stream);
+size_t sf_transition_noalloc_max_scratch(void);
+
 /* ---- SingleActUpdate pair logits (blocks.py:745-749):
  * logits[h][i][j] = LN(z[i,j]) . W[h]; w: [H][C] (single_pair_logits_projection^T). */
 int sf_pair_logits(int dtype, const void* z, const float* ln_w, const float* ln_b, const void* w,

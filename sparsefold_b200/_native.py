@@ -69,6 +69,8 @@ _SIGNATURES = {
     "sf_tri_attention_workspace": (C.c_size_t, [C.c_int, _i64, _i64]),
     "sf_transition": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, C.c_size_t, _vp]),
     "sf_transition_workspace": (C.c_size_t, [C.c_int, _i64, _i64]),
+    "sf_transition_noalloc": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "sf_transition_noalloc_max_scratch": (C.c_size_t, []),
     "sf_pair_logits": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, C.c_size_t, _vp]),
     "sf_pair_logits_workspace": (C.c_size_t, [C.c_int, _i64, _i64, _i64]),
 }
