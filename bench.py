@@ -154,25 +154,31 @@ def flush_l2(buf):
   buf.add_(1)
 
 
+def tri_attention_op_flops(n: int) -> float:
+  """Algorithmic FLOPs of one GridSelfAttention call: core 512 N^3 + projections
+  (q, k, v, gate, bias: 2*128*(512+4) per position) + output projection (2*128*128)."""
+  return tri_attention_core_flops(n) + n * n * (2.0 * 128 * 516 + 2.0 * 128 * 128)
+
+
 def time_kernel_probe(n: int, dtype, iters: int = 10) -> float:
-  """Average device time (ms) of one triangle-attention core launch at [n rows, n, 4 heads x 32]."""
+  """Average device time (ms) of one triangle attention (starting node) on [n, n, 128]."""
   import torch
-  from sparsefold_b200 import ops
-  g = torch.Generator(device="cuda").manual_seed(3)
-  y = torch.randn(n, n, 4, 4, 32, device="cuda", generator=g).to(dtype)  # q, k, v, gate
-  bias = torch.randn(4, n, n, device="cuda", generator=g)
-  mask = torch.ones(n, dtype=torch.bool, device="cuda")
-  mask[N_REAL * n // N_TOKEN:] = False
-  q, k, v, gate = (y[:, :, i] for i in range(4))
-  run = lambda: ops.attention(q, k, v, bias=bias, mask_k=mask, mask_row=mask, gate=gate)
+  from sparsefold_b200 import modules, synth
+  m = modules.GridSelfAttention(128, 4, transpose=False)
+  synth.init_params(m, seed=3)
+  m = m.cuda()
+  modules.prepare(m)
+  z, _, mask = synth.pair_inputs(n, n_real=N_REAL * n // N_TOKEN, seed=3)
+  z = z.to("cuda", dtype)
+  mask = mask.cuda()
   for _ in range(2):
-    run()
+    m(z, mask)
   st = torch.cuda.current_stream()
   ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
   torch.cuda.synchronize()
   for a, b in ev:
     a.record(st)
-    run()
+    m(z, mask)
     b.record(st)
   torch.cuda.synchronize()
   return sum(a.elapsed_time(b) for a, b in ev) / iters
@@ -248,7 +254,7 @@ def run_b200(args) -> None:
     probe_ms = time_kernel_probe(N_TOKEN, dt)
 
   peaks = load_peaks()
-  flops = tri_attention_core_flops(N_TOKEN)
+  flops = tri_attention_op_flops(N_TOKEN)
   achieved = flops / (probe_ms * 1e-3) / 1e12
   cpu = cpu_baseline_sample() if rank == 0 and world == 1 and not args.no_cpu_baseline else None
   if rank == 0:
@@ -266,7 +272,8 @@ def run_b200(args) -> None:
         "e2e": {"value": round(e2e_ms / N_BLOCKS, 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
-        "roofline": {"kernel": "triangle attention core (sf_attention, N=512 rows x 512 x 4 heads x 32)",
+        "roofline": {"kernel": "triangle attention op (sf_tri_attention: projection + tcgen05 attention core "
+                               "with fused output projection), N=512, 4 heads x 32",
                      "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      "peak_source": peaks["source"], "launch_ms": round(probe_ms, 4), "traffic": None},

@@ -361,6 +361,7 @@ int sf_tri_mult_output(int dtype, const void* z, const void* p, int64_t rows, in
 // ---------------------------------------------------------------------------
 size_t sf_tri_attention_workspace(int dtype, int64_t n, int64_t heads) {
   const int64_t C = 128;
+  if (dtype == SF_BF16 && heads == 4) return triatt_tc_workspace(n);
   size_t ds = dsize(dtype);
   size_t used = n * n * C * ds;                                  // x
   used = align_up(used, 256) + heads * n * n * sizeof(float);    // bias
@@ -382,6 +383,9 @@ int sf_tri_attention(int dtype, const void* z, const uint8_t* mask, int64_t n, i
     return SF_ERR_WORKSPACE;
   }
   const int64_t H = w->heads, D = C / H, M = n * n;
+  if (dtype == SF_BF16 && H == 4)
+    return triatt_tc((const bf16*)z, mask, n, transpose, w->ln_w, (const bf16*)w->w_qkvg, (const bf16*)w->w_bias,
+                     (const bf16*)w->w_out, (bf16*)z_out, ws_p, ws_bytes, stream);
   SF_DISPATCH(dtype, {
     Workspace ws(ws_p, ws_bytes);
     T* x = ws.take<T>(M * C);

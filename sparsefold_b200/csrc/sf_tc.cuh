@@ -151,6 +151,7 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 // destination registers before the load has landed.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
+  __syncwarp();   // .sync.aligned: the whole warp must arrive converged
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
