@@ -340,6 +340,9 @@ int sf_tri_mult_output(int dtype, const void* z, const void* p, int64_t rows, in
     return SF_ERR_WORKSPACE;
   }
   if (rows == 0) return SF_OK;
+  if (dtype == SF_BF16)
+    return trimul_output_tc((const bf16*)z, (const bf16*)p, rows, n, w->ln_w, w->ln_b, w->center_w, w->center_b,
+                            (const bf16*)w->w_gate, (const bf16*)w->w_out, (bf16*)z_out, stream);
   SF_DISPATCH(dtype, {
     Workspace ws(ws_p, ws_bytes);
     const int64_t M = rows * n;
@@ -439,6 +442,8 @@ int sf_transition(int dtype, const void* x, const float* ln_w, const float* ln_b
     return SF_ERR_WORKSPACE;
   }
   if (rows == 0) return SF_OK;
+  if (dtype == SF_BF16 && c == 128 && inter == 512)   // the pair transition runs on tcgen05
+    return transition_tc((const bf16*)x, ln_w, ln_b, (const bf16*)w1, (const bf16*)w2, (bf16*)y, rows, stream);
   SF_DISPATCH(dtype, {
     Workspace ws(ws_p, ws_bytes);
     T* xn = ws.take<T>(rows * inter);

@@ -247,7 +247,8 @@ constexpr int OFF_P = 64 * 1024;           // [wg] x 128 x 128 B (128B swizzle)
 constexpr int OFF_O = 96 * 1024;           // 128 x 256 B gated outputs of all heads
 constexpr int OFF_W = 128 * 1024;          // 128 x 256 B output projection
 constexpr int OFF_BAR = 160 * 1024;
-constexpr int SMEM_CORE = OFF_BAR + 1024 + 1024;
+constexpr int OFF_KBITS = OFF_BAR + 1024;       // key-valid bits, qp/32 words (qp <= 65536)
+constexpr int SMEM_CORE = OFF_KBITS + 8192 + 1024;
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -297,6 +298,19 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
     for (int i = 0; i < 5; ++i) tc::mbar_init(&sdone[i], 1);
     tc::fence_mbar_init();
   }
+  // key k is attended iff mask[b] && mask[k] (pair mask, blocks.py:314)
+  uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
+  {
+    const bool rok = p.mask[b] != 0;
+    for (int w = tid; w < (int)(p.qp / 32); w += 256) {
+      uint32_t bits = 0;
+      for (int e = 0; e < 32; ++e) {
+        const int64_t key = (int64_t)w * 32 + e;
+        if (rok && key < p.n && p.mask[key]) bits |= 1u << e;
+      }
+      kbits[w] = bits;
+    }
+  }
   // Q of all four heads and the output projection, by all 256 threads.
   for (int e = tid; e < H * TILE * 4; e += 256) {
     const int h = e >> 9, q = (e >> 2) & 127, c = e & 3;
@@ -321,7 +335,6 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
   bool aborted = false;
 
   const int64_t q = q0 + t;
-  const bool row_ok = p.mask[b] != 0;
   const uint32_t sb = tc::smem_u32(smem);
   constexpr uint32_t IDESC_S = tc::idesc_bf16(128, KB), IDESC_O = tc::idesc_bf16(128, D);
   float m = -INFINITY, l = 0.f, o[D];
@@ -348,6 +361,12 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
                      tc::smem_desc(kvs + kk * 32, 512, tc::kSW64), IDESC_S, kk > 0);
       tc::mma_commit(&sdone[g]);
     }
+    // bias row of this key block, fetched while the S MMA runs
+    const uint4* brow = reinterpret_cast<const uint4*>(p.bias + ((int64_t)h * p.qp + q) * p.qp + (int64_t)kb * KB);
+    uint4 bias_raw[KB / 8];
+#pragma unroll
+    for (int c = 0; c < KB / 8; ++c) bias_raw[c] = __ldg(brow + c);
+    const uint64_t vbits = (uint64_t)kbits[kb * 2] | ((uint64_t)kbits[kb * 2 + 1] << 32);
     tc::mbar_wait(&sdone[g], j & 1, p.status, aborted);
     tc::tc_fence_after();
     if (kb == 0) {
@@ -365,20 +384,18 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) sv[16 * i + e] = v[e];
     }
-    const uint4* brow = reinterpret_cast<const uint4*>(p.bias + ((int64_t)h * p.qp + q) * p.qp + (int64_t)kb * KB);
     float mx = -INFINITY;
 #pragma unroll
     for (int c = 0; c < KB / 8; ++c) {
-      const uint4 bb = __ldg(brow + c);
-      const uint32_t* bu = reinterpret_cast<const uint32_t*>(&bb);
+      const uint32_t* bu = reinterpret_cast<const uint32_t*>(&bias_raw[c]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int kidx = c * 8 + e;
         const int64_t key = (int64_t)kb * KB + kidx;
         const float bv = (e & 1) ? bf_hi(bu[e >> 1]) : bf_lo(bu[e >> 1]);
         float x = sv[kidx] * p.scale_log2 + bv * kLog2e;
-        if (key >= p.n) x = -INFINITY;
-        else if (!(row_ok && p.mask[key])) x = -FLT_MAX;
+        if (key >= p.n) x = -INFINITY;                 // padding beyond the N keys: excluded
+        else if (!((vbits >> kidx) & 1)) x = -FLT_MAX;   // masked key: the reference's -finfo.max bias
         sv[kidx] = x;
         mx = fmaxf(mx, x);
       }
