@@ -354,6 +354,64 @@ def run_reference(args) -> None:
   print(json.dumps(line), flush=True)
 
 
+OPS = ("tri_attention_start", "tri_attention_end", "tri_mult_outgoing", "tri_mult_incoming", "pair_transition",
+       "single_update")
+
+
+def op_flops(op: str, n: int) -> float:
+  if op.startswith("tri_attention"):
+    return tri_attention_op_flops(n)
+  if op.startswith("tri_mult"):
+    return 256.0 * n**3 + n * n * 2.0 * 128 * (512 + 128 + 128)
+  if op == "pair_transition":
+    return n * n * 2.0 * 128 * (1024 + 512)
+  return 0.0
+
+
+def run_op(args) -> None:
+  """Time one hot-path op alone at N_token (for per-kernel rooflines and small ncu captures)."""
+  import torch
+  from sparsefold_b200 import _native, modules, synth
+  _native.check(_native.load().sf_device_check(), "sf_device_check")
+  n = args.n
+  make = {
+      "tri_attention_start": lambda: modules.GridSelfAttention(128, 4, transpose=False),
+      "tri_attention_end": lambda: modules.GridSelfAttention(128, 4, transpose=True),
+      "tri_mult_outgoing": lambda: modules.TriangleMultiplication(128, "...ikc,...jkc->...ijc"),
+      "tri_mult_incoming": lambda: modules.TriangleMultiplication(128, "...kjc,...kic->...ijc"),
+      "pair_transition": lambda: modules.TransitionBlock(128, 4),
+      "single_update": lambda: modules.SingleActUpdate(128, 384),
+  }[args.op]
+  m = make()
+  synth.init_params(m, seed=4)
+  m = m.cuda()
+  modules.prepare(m)
+  z, s, mask = synth.pair_inputs(n, n_real=max(1, N_REAL * n // N_TOKEN), seed=4)
+  z, s, mask = z.to("cuda", torch.bfloat16), s.to("cuda", torch.bfloat16), mask.cuda()
+  run = {
+      "pair_transition": lambda: m(z),
+      "single_update": lambda: m(z, s, mask),
+  }.get(args.op, lambda: m(z, mask))
+  with torch.no_grad():
+    for _ in range(args.warmup):
+      run()
+    st = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    for a, b in ev:
+      a.record(st)
+      run()
+      b.record(st)
+    torch.cuda.synchronize()
+  ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+  fl = op_flops(args.op, n)
+  peaks = load_peaks()
+  print(json.dumps({"op": args.op, "n_token": n, "ms": round(ms, 4),
+                    "tflop_per_s": round(fl / (ms * 1e-3) / 1e12, 2) if fl else None,
+                    "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4) if fl else None,
+                    "device_status": _native.device_status()}), flush=True)
+
+
 def main():
   ap = argparse.ArgumentParser()
   ap.add_argument("--gpus", type=int, default=1)
@@ -361,7 +419,12 @@ def main():
   ap.add_argument("--warmup", type=int, default=3)
   ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
   ap.add_argument("--no-cpu-baseline", action="store_true")
+  ap.add_argument("--op", choices=OPS, default=None, help="time one op alone instead of the trunk")
+  ap.add_argument("--n", type=int, default=N_TOKEN, help="N_token for --op")
   args = ap.parse_args()
+  if args.op:
+    run_op(args)
+    return
   if args.warmup < 3 and args.impl == "b200":
     raise SystemExit("--warmup must be >= 3")
   if args.impl == "reference":
