@@ -63,6 +63,8 @@ int transition_tc(const bf16* x, const float* ln_w, const float* ln_b, const bf1
 int trimul_output_tc(const bf16* z, const bf16* P, int64_t rows, int64_t n, const float* ln_w, const float* ln_b,
                      const float* center_w, const float* center_b, const bf16* w_gate, const bf16* w_out, bf16* z_out,
                      cudaStream_t stream);
+int linear_tc(const bf16* x, const bf16* wt, const float* bias, const bf16* residual, bf16* y, int64_t M, int64_t K,
+              int64_t N, int post_op, cudaStream_t stream);
 int contract_tc(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
                 int64_t kdim, cudaStream_t stream);
 int trimul_project_tc(const bf16* z, const uint8_t* mask, int64_t rows, int64_t n, int64_t row_offset, int incoming,

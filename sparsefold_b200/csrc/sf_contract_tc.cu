@@ -22,8 +22,18 @@ constexpr int SMEM_CONTRACT = STAGES * STAGE_BYTES + 1024 + 1024;
 struct ContractParams {
   bf16* P;
   int64_t channels, rows, cols, kdim;
+  const float* bias;        // [cols] or null
+  const bf16* residual;     // laid out like P, or null
+  int post_op;              // SF_POST_*
   uint32_t* status;
 };
+
+__device__ __forceinline__ float post(float v, int op) {
+  if (op == SF_POST_RELU) return fmaxf(v, 0.f);
+  if (op == SF_POST_SILU) return v * pt::fast_sigmoid(v);
+  if (op == SF_POST_SIGMOID) return pt::fast_sigmoid(v);
+  return v;
+}
 
 __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ CUtensorMap tmA,
                                                         const __grid_constant__ CUtensorMap tmB,
@@ -124,6 +134,16 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
           for (int g = 0; g < 2; ++g) {
             const int64_t j = j0 + ch * 16 + g * 8;
             if (j + 8 <= cp) {
+              if (p.bias || p.residual || p.post_op) {
+                const bf16* res = p.residual ? p.residual + (c * p.rows + i) * cp + j : nullptr;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  float x = v[g * 8 + e];
+                  if (p.bias && j + e < p.cols) x += __ldg(p.bias + j + e);
+                  if (res) x += __bfloat162float(res[e]);
+                  v[g * 8 + e] = post(x, p.post_op);
+                }
+              }
               uint4 o;
               o.x = pt::pack_bf2(v[g * 8 + 0], v[g * 8 + 1]);
               o.y = pt::pack_bf2(v[g * 8 + 2], v[g * 8 + 3]);
@@ -172,8 +192,22 @@ int make_operand_tmap(CUtensorMap* map, const void* base, int64_t channels, int6
 
 }  // namespace
 
+static int gemm_tc_impl(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
+                        int64_t kdim, const float* bias, const bf16* residual, int post_op, cudaStream_t stream);
+
 int contract_tc(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
                 int64_t kdim, cudaStream_t stream) {
+  return gemm_tc_impl(a_op, b_op, P, channels, rows, cols, kdim, nullptr, nullptr, SF_POST_NONE, stream);
+}
+
+// y[M][N] = post(x[M][K] . wt[N][K]^T + bias + residual); K and N multiples of 8.
+int linear_tc(const bf16* x, const bf16* wt, const float* bias, const bf16* residual, bf16* y, int64_t M, int64_t K,
+              int64_t N, int post_op, cudaStream_t stream) {
+  return gemm_tc_impl(x, wt, y, 1, M, N, K, bias, residual, post_op, stream);
+}
+
+static int gemm_tc_impl(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
+                        int64_t kdim, const float* bias, const bf16* residual, int post_op, cudaStream_t stream) {
   if (channels == 0 || rows == 0 || cols == 0) return SF_OK;
   SF_REQUIRE(rows < (1 << 30) && cols < (1 << 30) && kdim < (1 << 30) && channels < (1 << 30),
              "contract_tc: size too large");
@@ -193,7 +227,7 @@ int contract_tc(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, i
     }
     attr_set[dev & 63] = true;
   }
-  ContractParams p{P, channels, rows, cols, kdim, status};
+  ContractParams p{P, channels, rows, cols, kdim, bias, residual, post_op, status};
   const int64_t ntiles = channels * ((rows + BM - 1) / BM) * ((cols + BN - 1) / BN);
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
   k_contract_tc<<<grid, 192, SMEM_CONTRACT, stream>>>(ma, mb, p);

@@ -181,6 +181,52 @@ __global__ void __launch_bounds__(256) k_center_ln(const T* __restrict__ p, T* _
   }
 }
 
+// Pair logits of SingleActUpdate (blocks.py:745-749), bf16: logits[h][m] = LN(z[m]) . W[h].
+// 128 positions per block, staged by coalesced 16-byte loads into padded rows.
+constexpr int PL_ROW = 128 + 8;   // bf16 elements per staged row (16-byte pad, no bank conflicts)
+
+__global__ void __launch_bounds__(128) k_pair_logits_bf16(const bf16* __restrict__ z, const float* __restrict__ ln_w,
+                                                          const float* __restrict__ ln_b, const bf16* __restrict__ w,
+                                                          bf16* __restrict__ logits, int64_t M, int heads) {
+  __shared__ __align__(16) bf16 rows_s[128 * PL_ROW];
+  __shared__ float w_s[16 * 128];
+  const int tid = threadIdx.x;
+  const int64_t m0 = (int64_t)blockIdx.x * 128;
+  for (int e = tid; e < heads * 128; e += 128) w_s[e] = __bfloat162float(w[e]);
+  for (int e = tid; e < 128 * 16; e += 128) {
+    const int r = e >> 4, c = e & 15;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (m0 + r < M) v = __ldg(reinterpret_cast<const uint4*>(z + (m0 + r) * 128) + c);
+    *reinterpret_cast<uint4*>(rows_s + r * PL_ROW + c * 8) = v;
+  }
+  __syncthreads();
+  const bf16* row = rows_s + tid * PL_ROW;
+  float s = 0.f;
+  for (int c = 0; c < 128; ++c) s += __bfloat162float(row[c]);
+  const float mean = s * (1.0f / 128);
+  float q = 0.f;
+  for (int c = 0; c < 128; ++c) {
+    const float d = __bfloat162float(row[c]) - mean;
+    q += d * d;
+  }
+  const float rstd = rsqrtf(q * (1.0f / 128) + 1e-5f);
+  float acc[16];
+#pragma unroll
+  for (int h = 0; h < 16; ++h) acc[h] = 0.f;
+  for (int c = 0; c < 128; ++c) {
+    // the reference rounds LN(z) to the activation dtype before the projection
+    const float y = __bfloat162float(__float2bfloat16_rn((__bfloat162float(row[c]) - mean) * rstd * ln_w[c] + ln_b[c]));
+#pragma unroll
+    for (int h = 0; h < 16; ++h)
+      if (h < heads) acc[h] = fmaf(y, w_s[h * 128 + c], acc[h]);
+  }
+  if (m0 + tid < M) {
+#pragma unroll
+    for (int h = 0; h < 16; ++h)
+      if (h < heads) logits[(int64_t)h * M + m0 + tid] = __float2bfloat16_rn(acc[h]);
+  }
+}
+
 template <typename T>
 __global__ void k_swiglu(const float* __restrict__ h, T* __restrict__ out, int64_t rows, int64_t I) {
   int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -233,6 +279,11 @@ int sf_linear(int dtype, const void* x, const void* wt, const float* bias, const
               void* y, int64_t rows, int64_t k, int64_t n, int post_op, sf_stream_t stream) {
   SF_REQUIRE(x && wt && y && rows >= 0 && k > 0 && n > 0, "sf_linear: bad arguments");
   SF_REQUIRE(post_op >= SF_POST_NONE && post_op <= SF_POST_SIGMOID, "sf_linear: bad post_op %d", post_op);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(wt) |
+                         reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(residual)) & 15) == 0;
+  if (dtype == SF_BF16 && k % 8 == 0 && n % 8 == 0 && aligned && rows > 0)
+    return linear_tc((const bf16*)x, (const bf16*)wt, bias, (const bf16*)residual, (bf16*)y, rows, k, n, post_op,
+                     stream);
   SF_DISPATCH(dtype, {
     EpiLinear<T> epi{(T*)y, bias, (const T*)residual, n, post_op};
     return launch_gemm(rows, (int)n, (int)k, RowMajor<T>{(const T*)x, k}, (const T*)wt, epi, stream, "sf_linear");
@@ -248,12 +299,22 @@ int sf_attention(const sf_attention_args* a, sf_stream_t stream) {
   if (a->batch == 0 || a->q_len == 0) return SF_OK;
   SF_REQUIRE(a->k_len > 0, "sf_attention: k_len must be positive");
   SF_REQUIRE(!a->bias || a->bias_dtype == SF_F32 || a->bias_dtype == a->dtype, "sf_attention: bias dtype");
-  dim3 grid((unsigned)((a->q_len + ATT_Q - 1) / ATT_Q), (unsigned)a->heads, (unsigned)a->batch);
+  dim3 grid((unsigned)((a->q_len + ATT_WARPS - 1) / ATT_WARPS), (unsigned)a->heads, (unsigned)a->batch);
+  const size_t smem = attention_smem_bytes((int)a->head_dim);
   SF_DISPATCH(a->dtype, {
-    if (a->bias && a->bias_dtype == SF_F32)
-      k_attention<T, float><<<grid, ATT_Q, 0, stream>>>(*a);
-    else
-      k_attention<T, T><<<grid, ATT_Q, 0, stream>>>(*a);
+    const bool f32bias = a->bias && a->bias_dtype == SF_F32;
+    const bool small = a->head_dim <= 32;
+    auto kern = small ? (f32bias ? k_attention<T, float, 32> : k_attention<T, T, 32>)
+                      : (f32bias ? k_attention<T, float, 64> : k_attention<T, T, 64>);
+    static bool attr_done[64][4] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int slot = (small ? 2 : 0) + (f32bias ? 1 : 0);
+    if (!attr_done[dev & 63][slot]) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem_bytes(64));
+      attr_done[dev & 63][slot] = true;
+    }
+    kern<<<grid, ATT_WARPS * 32, smem, stream>>>(*a);
     count_launch();
     return check_launch("sf_attention");
   });
@@ -476,6 +537,13 @@ int sf_pair_logits(int dtype, const void* z, const float* ln_w, const float* ln_
     return SF_ERR_WORKSPACE;
   }
   if (rows == 0) return SF_OK;
+  if (dtype == SF_BF16 && c == 128 && heads <= 16) {
+    const int64_t M = rows * n;
+    k_pair_logits_bf16<<<(unsigned)((M + 127) / 128), 128, 0, stream>>>((const bf16*)z, ln_w, ln_b, (const bf16*)w,
+                                                                        (bf16*)logits, M, (int)heads);
+    count_launch();
+    return check_launch("pair_logits");
+  }
   SF_DISPATCH(dtype, {
     T* x = (T*)ws_p;
     const int64_t M = rows * n;

@@ -168,21 +168,25 @@ struct EpiLinear {  // y = post(v + bias + residual)
 };
 
 // ---------------------------------------------------------------------------
-// Strided attention, one thread per query, keys streamed through shared memory
-// in tiles; exact online softmax in fp32.  Masked logits are -FLT_MAX (not
-// -inf), which reproduces the reference's uniform average for a query whose
-// keys are all masked (sdpa.py:61-80).
+// Strided attention, one warp per query: the 32 lanes split the keys of each
+// shared-memory key tile, keep their own exact online-softmax state (fp32),
+// and merge the states by butterfly shuffles at the end.  Masked logits are
+// -FLT_MAX (not -inf), which reproduces the reference's uniform average for a
+// query whose keys are all masked (sdpa.py:61-80); keys beyond k_len take no
+// part at all.
 // ---------------------------------------------------------------------------
-constexpr int ATT_Q = 128, ATT_K = 32, ATT_DMAX = 64;
+constexpr int ATT_WARPS = 8, ATT_KT = 128, ATT_DMAX = 64;
 
-template <typename T, typename TB>
-__global__ void __launch_bounds__(ATT_Q) k_attention(sf_attention_args a) {
-  __shared__ float ks[ATT_K][ATT_DMAX + 1];
-  __shared__ float vs[ATT_K][ATT_DMAX + 1];
-  __shared__ uint8_t kvalid[ATT_K];
-  const int D = (int)a.head_dim;
+template <typename T, typename TB, int DM>
+__global__ void __launch_bounds__(ATT_WARPS * 32) k_attention(sf_attention_args a) {
+  extern __shared__ float att_smem[];
+  float* ks = att_smem;                              // [ATT_KT][D + 1]
+  const int D = (int)a.head_dim, DP = D + 1;
+  float* vs = ks + ATT_KT * DP;                      // [ATT_KT][D + 1]
+  uint8_t* kvalid = reinterpret_cast<uint8_t*>(vs + ATT_KT * DP);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t b = blockIdx.z, h = blockIdx.y;
-  const int64_t qi = (int64_t)blockIdx.x * ATT_Q + threadIdx.x;
+  const int64_t qi = (int64_t)blockIdx.x * ATT_WARPS + warp;
   const bool qin = qi < a.q_len;
   const T* qp = static_cast<const T*>(a.q) + b * a.q_sb + h * a.q_sh + (qin ? qi : 0) * a.q_sq;
   const T* kp = static_cast<const T*>(a.k) + b * a.k_sb + h * a.k_sh;
@@ -192,60 +196,77 @@ __global__ void __launch_bounds__(ATT_Q) k_attention(sf_attention_args a) {
   if (a.mask_row) row_ok = a.mask_row[b] != 0;
   if (a.mask_q && qin) row_ok = row_ok && a.mask_q[b * a.mq_sb + qi] != 0;
 
-  float q[ATT_DMAX], acc[ATT_DMAX];
+  float q[DM], acc[DM];
 #pragma unroll
-  for (int d = 0; d < ATT_DMAX; ++d) {
-    q[d] = (d < D) ? ld(qp + d) * a.scale : 0.f;
+  for (int d = 0; d < DM; ++d) {
+    q[d] = (d < D && qin) ? ld(qp + d) * a.scale : 0.f;
     acc[d] = 0.f;
   }
   float mrun = -INFINITY, lrun = 0.f;
-  for (int64_t k0 = 0; k0 < a.k_len; k0 += ATT_K) {
-    for (int e = threadIdx.x; e < ATT_K * D; e += ATT_Q) {
-      int r = e / D, c = e % D;
-      int64_t kk = k0 + r;
-      ks[r][c] = kk < a.k_len ? ld(kp + kk * a.k_sk + c) : 0.f;
-      vs[r][c] = kk < a.k_len ? ld(vp + kk * a.v_sk + c) : 0.f;
+  for (int64_t k0 = 0; k0 < a.k_len; k0 += ATT_KT) {
+    const int kn = (a.k_len - k0) < ATT_KT ? (int)(a.k_len - k0) : ATT_KT;
+    for (int e = threadIdx.x; e < kn * D; e += blockDim.x) {
+      const int r = e / D, c = e % D;
+      ks[r * DP + c] = ld(kp + (k0 + r) * a.k_sk + c);
+      vs[r * DP + c] = ld(vp + (k0 + r) * a.v_sk + c);
     }
-    if (threadIdx.x < ATT_K) {
-      int64_t kk = k0 + threadIdx.x;
-      kvalid[threadIdx.x] = kk < a.k_len && (!a.mask_k || a.mask_k[b * a.mk_sb + kk] != 0);
-    }
+    for (int r = threadIdx.x; r < kn; r += blockDim.x)
+      kvalid[r] = !a.mask_k || a.mask_k[b * a.mk_sb + k0 + r] != 0;
     __syncthreads();
-    const int kn = (a.k_len - k0) < ATT_K ? (int)(a.k_len - k0) : ATT_K;
-    for (int r = 0; r < kn; ++r) {
+    for (int r = lane; r < kn; r += 32) {
       float s;
       if (row_ok && kvalid[r]) {
         s = 0.f;
 #pragma unroll
-        for (int d = 0; d < ATT_DMAX; ++d)
-          if (d < D) s = fmaf(q[d], ks[r][d], s);
+        for (int d = 0; d < DM; ++d)
+          if (d < D) s = fmaf(q[d], ks[r * DP + d], s);
         if (bp) s += ld(bp + k0 + r);
       } else {
         s = -FLT_MAX;
       }
-      float mnew = fmaxf(mrun, s);
-      float corr = expf(mrun - mnew);
-      float p = expf(s - mnew);
-      lrun = lrun * corr + p;
+      const float mnew = fmaxf(mrun, s);
+      const float corr = expf(mrun - mnew);
+      const float pr = expf(s - mnew);
+      lrun = lrun * corr + pr;
 #pragma unroll
-      for (int d = 0; d < ATT_DMAX; ++d)
-        if (d < D) acc[d] = fmaf(acc[d], corr, p * vs[r][d]);
+      for (int d = 0; d < DM; ++d)
+        if (d < D) acc[d] = fmaf(acc[d], corr, pr * vs[r * DP + d]);
       mrun = mnew;
     }
     __syncthreads();
   }
+  // merge the 32 lane states (lanes that saw no key have m = -inf, l = 0)
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, mrun, off);
+    const float lo = __shfl_xor_sync(0xffffffffu, lrun, off);
+    const float mnew = fmaxf(mrun, mo);
+    const float ca = (mrun == -INFINITY) ? 0.f : expf(mrun - mnew);
+    const float cb = (mo == -INFINITY) ? 0.f : expf(mo - mnew);
+    lrun = lrun * ca + lo * cb;
+#pragma unroll
+    for (int d = 0; d < DM; ++d) {
+      const float ao = __shfl_xor_sync(0xffffffffu, acc[d], off);
+      acc[d] = acc[d] * ca + ao * cb;
+    }
+    mrun = mnew;
+  }
   if (!qin) return;
   T* op = static_cast<T*>(a.out) + b * a.o_sb + h * a.o_sh + qi * a.o_sq;
   const T* gp = a.gate ? static_cast<const T*>(a.gate) + b * a.g_sb + h * a.g_sh + qi * a.g_sq : nullptr;
-  float inv = lrun > 0.f ? 1.f / lrun : 0.f;
+  const float inv = lrun > 0.f ? 1.f / lrun : 0.f;
 #pragma unroll
-  for (int d = 0; d < ATT_DMAX; ++d) {
-    if (d < D) {
+  for (int d = 0; d < DM; ++d) {
+    if (d < D && (d & 31) == lane) {
       float o = acc[d] * inv;
       if (gp) o *= sigmoid_f(ld(gp + d));
       st(op + d, o);
     }
   }
+}
+
+inline size_t attention_smem_bytes(int D) {
+  return (size_t)2 * ATT_KT * (D + 1) * sizeof(float) + ATT_KT;
 }
 
 }  // namespace sf
