@@ -178,6 +178,45 @@ int sf_pair_logits(int dtype, const void* z, const float* ln_w, const float* ln_
                    void* ws, size_t ws_bytes, sf_stream_t stream);
 size_t sf_pair_logits_workspace(int dtype, int64_t rows, int64_t n, int64_t c);
 
+/* ---- diffusion-transformer and MSA helpers ----------------------------- */
+/* y = scale * LN(x) + bias (norm without affine): AdaptiveLayerNorm with
+ * single_cond (model/diffusion/transformer.py:80-93); x, scale, bias, y [rows][cols]. */
+int sf_adaln(int dtype, const void* x, const void* scale, const void* bias, void* y, int64_t rows,
+             int64_t cols, sf_stream_t stream);
+/* out = base + u * gate, elementwise (base may be null): AdaptiveZeroInit gating and
+ * residual (transformer.py:138-154, :345, :585), MSAAttention gate (trunk/blocks.py:182-183). */
+int sf_gated_residual(int dtype, const void* base, const void* u, const void* gate, void* out, int64_t n,
+                      sf_stream_t stream);
+/* out[b][i][:] = mask[i] ? src[b][idx[i]][:] : 0 — atom_layout.convert
+ * (schema/atom_layout.py:52-83) for the atom key windows (transformer.py:671-673). */
+int sf_gather_rows(int dtype, const void* src, int64_t batch, int64_t src_rows, const int32_t* idx,
+                   const uint8_t* mask, int64_t n_out, int64_t cols, void* out, sf_stream_t stream);
+/* x[r][:] = 0 where !mask[r] (masked_fill of the OPM projections, trunk/blocks.py:645-647). */
+int sf_mask_rows(int dtype, void* x, const uint8_t* mask, int64_t rows, int64_t cols, sf_stream_t stream);
+/* y = softmax(x + key_bias) over the last axis (MSAAttention weights, trunk/blocks.py:163-170). */
+int sf_softmax_rows(int dtype, const void* x, const float* key_bias, void* y, int64_t rows, int64_t k,
+                    int64_t ldy, sf_stream_t stream);
+/* out[r][i] = swish(h[r][i]) * h[r][I + i]: the GLU of the diffusion transitions
+ * (layers/primitives.py:624-631, diffusion/transformer.py:218-228). */
+int sf_swiglu(int dtype, const void* h, void* out, int64_t rows, int64_t inter, sf_stream_t stream);
+/* Batched strided transpose out[ob(b)+c*os_c+r] = in[ib(b)+r*is_r+c], b = (b1 < nb1, b2 < nb2),
+ * ib = b1*ib1 + b2*ib2, ob = b1*ob1 + b2*ob2 (layout changes of the einsums at
+ * trunk/blocks.py:179 and :667). */
+int sf_transpose(int dtype, const void* in, void* out, int64_t nb1, int64_t nb2, int64_t rows, int64_t cols,
+                 int64_t ib1, int64_t ib2, int64_t is_r, int64_t ob1, int64_t ob2, int64_t os_c,
+                 sf_stream_t stream);
+/* OuterProductMean normaliser norm[i][j] = 1/(1e-3 + sum_m mask[m,i] mask[m,j])
+ * (trunk/blocks.py:683-688); mask [n_seq][n_res] uint8, norm [n_res][n_res] fp32. */
+int sf_opm_norm(int dtype, const uint8_t* mask, int64_t n_seq, int64_t n_res, float* norm, void* ws,
+                size_t ws_bytes, sf_stream_t stream);
+size_t sf_opm_norm_workspace(int64_t n_seq, int64_t n_res);
+/* out[(i*n+j)][a*d+b] = O[i*d+a][j*d+b]: the outer-product blocks as rows for the
+ * output projection (trunk/blocks.py:667-669); O row pitch `pitch`. */
+int sf_opm_repack(int dtype, const void* o, int64_t pitch, int64_t n_res, int64_t d, void* out,
+                  sf_stream_t stream);
+/* x[r][:] *= s[r] (the OPM normaliser, trunk/blocks.py:689). */
+int sf_scale_rows(int dtype, void* x, const float* s, int64_t rows, int64_t cols, sf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,16 +42,30 @@ def replacement_map():
   for name, cls in list(orig.items()):
     if issubclass(cls, _m.B200Module):   # already applied: recover the reference base
       orig[name] = next(b for b in cls.__mro__[1:] if not issubclass(b, _m.B200Module))
-  sa = transformer.SelfAttention
-  if issubclass(sa, _m.B200Module):
-    sa = next(b for b in sa.__mro__[1:] if not issubclass(b, _m.B200Module))
+  for name in ("MSAAttention", "OuterProductMean"):
+    orig[name] = _reference_base(getattr(blocks, name))
+  diff = {name: _reference_base(getattr(transformer, name))
+          for name in ("SelfAttention", "TransitionBlock", "CrossAttention", "Transformer", "CrossAttTransformer")}
   return [
       (blocks, "GridSelfAttention", _native_class(orig["GridSelfAttention"], _m.GridSelfAttentionB200)),
       (blocks, "TriangleMultiplication", _native_class(orig["TriangleMultiplication"], _m.TriangleMultiplicationB200)),
       (blocks, "TransitionBlock", _native_class(orig["TransitionBlock"], _m.TransitionBlockB200)),
       (blocks, "SingleActUpdate", _native_class(orig["SingleActUpdate"], _m.SingleActUpdateB200)),
-      (transformer, "SelfAttention", _native_class(sa, _m.SelfAttentionB200)),
+      (blocks, "MSAAttention", _native_class(orig["MSAAttention"], _m.MSAAttentionB200)),
+      (blocks, "OuterProductMean", _native_class(orig["OuterProductMean"], _m.OuterProductMeanB200)),
+      (transformer, "SelfAttention", _native_class(diff["SelfAttention"], _m.SelfAttentionB200)),
+      (transformer, "TransitionBlock", _native_class(diff["TransitionBlock"], _m.DiffusionTransitionBlockB200)),
+      (transformer, "CrossAttention", _native_class(diff["CrossAttention"], _m.CrossAttentionB200)),
+      (transformer, "Transformer", _native_class(diff["Transformer"], _m.DiffusionTransformerB200)),
+      (transformer, "CrossAttTransformer", _native_class(diff["CrossAttTransformer"], _m.CrossAttTransformerB200)),
   ]
+
+
+def _reference_base(cls: type) -> type:
+  """The reference class behind an already applied B200 class (apply() is idempotent)."""
+  if issubclass(cls, _m.B200Module):
+    return next(b for b in cls.__mro__[1:] if not issubclass(b, _m.B200Module))
+  return cls
 
 
 def apply() -> None:

@@ -24,6 +24,12 @@ __device__ __forceinline__ float ld(const bf16* p) { return __bfloat162float(*p)
 __device__ __forceinline__ void st(float* p, float v) { *p = v; }
 __device__ __forceinline__ void st(bf16* p, float v) { *p = __float2bfloat16_rn(v); }
 
+// Round a value to the precision of storage type T (identity for fp32).
+template <typename T>
+__device__ __forceinline__ float ld_round(float v) { return v; }
+template <>
+__device__ __forceinline__ float ld_round<bf16>(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float swish_f(float x) { return x * sigmoid_f(x); }
 

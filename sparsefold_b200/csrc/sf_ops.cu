@@ -227,6 +227,14 @@ __global__ void __launch_bounds__(128) k_pair_logits_bf16(const bf16* __restrict
   }
 }
 
+__global__ void k_swiglu_bf16(const bf16* __restrict__ h, bf16* __restrict__ out, int64_t rows, int64_t I) {
+  int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= rows * I) return;
+  int64_t r = e / I, i = e % I;
+  const bf16* hr = h + r * 2 * I;
+  out[e] = __float2bfloat16_rn(swish_f(__bfloat162float(hr[i])) * __bfloat162float(hr[I + i]));
+}
+
 template <typename T>
 __global__ void k_swiglu(const float* __restrict__ h, T* __restrict__ out, int64_t rows, int64_t I) {
   int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -505,6 +513,22 @@ int sf_transition(int dtype, const void* x, const float* ln_w, const float* ln_b
   if (rows == 0) return SF_OK;
   if (dtype == SF_BF16 && c == 128 && inter == 512)   // the pair transition runs on tcgen05
     return transition_tc((const bf16*)x, ln_w, ln_b, (const bf16*)w1, (const bf16*)w2, (bf16*)y, rows, stream);
+  if (dtype == SF_BF16 && c % 8 == 0 && inter % 8 == 0 &&
+      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(w1) |
+        reinterpret_cast<uintptr_t>(w2) | reinterpret_cast<uintptr_t>(ws_p)) & 15) == 0) {
+    // other widths (the single transition): LN -> tcgen05 GEMM -> SwiGLU -> tcgen05 GEMM + residual
+    Workspace ws(ws_p, ws_bytes);
+    bf16* xn = ws.take<bf16>(rows * inter);
+    bf16* h1 = ws.take<bf16>(rows * 2 * inter);
+    bf16* h = ws.take<bf16>(rows * inter);
+    SF_TRY(launch_layernorm((const bf16*)x, xn, ln_w, ln_b, rows, (int)c, 1e-5f, stream));
+    SF_TRY(linear_tc(xn, (const bf16*)w1, nullptr, nullptr, h1, rows, c, 2 * inter, SF_POST_NONE, stream));
+    const int64_t tot = rows * inter;
+    k_swiglu_bf16<<<(unsigned)((tot + 255) / 256), 256, 0, stream>>>(h1, h, rows, inter);
+    count_launch();
+    SF_TRY(check_launch("transition.swiglu"));
+    return linear_tc(h, (const bf16*)w2, nullptr, (const bf16*)x, (bf16*)y, rows, inter, c, SF_POST_NONE, stream);
+  }
   SF_DISPATCH(dtype, {
     Workspace ws(ws_p, ws_bytes);
     T* xn = ws.take<T>(rows * inter);

@@ -170,18 +170,57 @@ class TransitionBlockB200(B200Module):
                           self._packed("w1", dt), self._packed("w2", dt))
 
 
-class SelfAttentionB200(B200Module):
-  """Diffusion ``SelfAttention`` without ``single_cond`` (transformer.py:234-345).
+def _pack_adaln(mod: "B200Module", ln, tag: str) -> None:
+  """Weights of an AdaptiveLayerNorm (diffusion/transformer.py:27-96) under prefix `tag`."""
+  if getattr(ln, "single_cond", False):
+    mod._keep(f"{tag}_sc_w", ln.single_cond_layer_norm.weight)
+    mod._pack(f"{tag}_scale_w", ln.single_cond_scale.weight.detach().float().T)
+    mod._keep(f"{tag}_scale_b", ln.single_cond_scale.bias)
+    mod._pack(f"{tag}_bias_w", ln.single_cond_bias.weight.detach().float().T)
+  else:
+    mod._keep(f"{tag}_ln_w", ln.layer_norm.weight)
+    mod._keep(f"{tag}_ln_b", ln.layer_norm.bias)
 
-  This is the Pairformer single attention (blocks.py:724-730).  q, k, v and the
-  gate come from one GEMM whose bias is q's bias (zeros elsewhere); the
-  attention kernel applies sigmoid(gate); ``zero_init.transition2`` adds the
-  residual in its epilogue.
+
+def _apply_adaln(mod: "B200Module", ln, tag: str, x: torch.Tensor, single_cond) -> torch.Tensor:
+  """AdaptiveLayerNorm.forward (transformer.py:80-96) on the C ABI."""
+  if not getattr(ln, "single_cond", False):
+    return ops.layer_norm(x, mod._kept(f"{tag}_ln_w"), mod._kept(f"{tag}_ln_b"))
+  dt = x.dtype
+  sc = ops.layer_norm(single_cond.to(dt), mod._kept(f"{tag}_sc_w"), None)
+  scale = ops.linear(sc, mod._packed(f"{tag}_scale_w", dt), bias=mod._kept(f"{tag}_scale_b"), post_op="sigmoid")
+  bias = ops.linear(sc, mod._packed(f"{tag}_bias_w", dt))
+  return ops.adaln(x, scale, bias)
+
+
+def _pack_zero_init(mod: "B200Module", zi) -> None:
+  """AdaptiveZeroInit (transformer.py:99-154): transition2 and, with single_cond, the sigmoid gate."""
+  mod._pack("zi_t2", zi.transition2.weight.detach().float().T)
+  if getattr(zi, "single_cond", False):
+    mod._pack("zi_cond_w", zi.adaptive_zero_cond.weight.detach().float().T)
+    mod._keep("zi_cond_b", zi.adaptive_zero_cond.bias)
+
+
+def _apply_zero_init(mod: "B200Module", zi, u: torch.Tensor, single_cond, residual: torch.Tensor) -> torch.Tensor:
+  """residual + AdaptiveZeroInit(u, single_cond)."""
+  dt = u.dtype
+  if not getattr(zi, "single_cond", False):
+    return ops.linear(u, mod._packed("zi_t2", dt), residual=residual)
+  v = ops.linear(u, mod._packed("zi_t2", dt))
+  cond = ops.linear(single_cond.to(dt), mod._packed("zi_cond_w", dt), bias=mod._kept("zi_cond_b"), post_op="sigmoid")
+  return ops.gated_residual(residual, v, cond)
+
+
+class SelfAttentionB200(B200Module):
+  """Diffusion ``SelfAttention`` (transformer.py:234-345), with or without ``single_cond``.
+
+  Used as the Pairformer single attention (blocks.py:724-730, no single_cond)
+  and as the diffusion token attention (AdaLN + adaptive-zero output).  q, k,
+  v and the gate come from one GEMM whose bias is q's bias; the attention
+  kernel applies sigmoid(gate) to its output.
   """
 
   def prepare_native(self):
-    if getattr(self.layer_norm, "single_cond", False):
-      raise NotImplementedError("B200 SelfAttention with single_cond is not implemented yet")
     c = self.q_projection.input_shape[0]
     h, d = self.q_projection.output_shape
     wq = self.q_projection.weight.detach().float().reshape(c, h * d).T
@@ -192,25 +231,21 @@ class SelfAttentionB200(B200Module):
     bias = torch.zeros(4 * h * d, device=self.q_projection.weight.device)
     bias[: h * d] = self.q_projection.bias.detach().float().reshape(-1)
     self._keep("qkvg_bias", bias)
-    self._pack("out", self.zero_init.transition2.weight.detach().float().T)
-    self._keep("ln_w", self.layer_norm.layer_norm.weight)
-    self._keep("ln_b", self.layer_norm.layer_norm.bias)
+    _pack_adaln(self, self.layer_norm, "ln")
+    _pack_zero_init(self, self.zero_init)
     self._hd = (h, d)
     self._native_prepared = True
 
   @_require_prepared
   def forward(self, x: torch.Tensor, mask: torch.Tensor, *, pair_logits=None, single_cond=None):
-    if single_cond is not None:
-      raise NotImplementedError("B200 SelfAttention with single_cond is not implemented yet")
     dt = x.dtype
     h, d = self._hd
-    n = x.shape[-2]
-    xn = ops.layer_norm(x, self._kept("ln_w"), self._kept("ln_b"))
+    xn = _apply_adaln(self, self.layer_norm, "ln", x, single_cond)
     y = ops.linear(xn, self._packed("qkvg", dt), bias=self._kept("qkvg_bias"))   # [..., N, 4*H*D]
     y = y.view(*x.shape[:-1], 4, h, d)
     q, k, v, g = (y[..., i, :, :] for i in range(4))
     o = ops.attention(q, k, v, mask_k=mask, bias=pair_logits, gate=g)
-    return ops.linear(o.reshape(*x.shape[:-1], h * d), self._packed("out", dt), residual=x)
+    return _apply_zero_init(self, self.zero_init, o.reshape(*x.shape[:-1], h * d), single_cond, x)
 
 
 class SingleActUpdateB200(B200Module):
@@ -230,6 +265,212 @@ class SingleActUpdateB200(B200Module):
                              self._packed("logits", dt), heads)
     single_act = self.single_attention(single_act, seq_mask, pair_logits=logits)
     return self.single_transition(single_act, broadcast_dim=None)
+
+
+class DiffusionTransitionBlockB200(B200Module):
+  """Diffusion ``TransitionBlock`` (transformer.py:157-231): AdaLN -> SwiGLU -> adaptive-zero output + residual."""
+
+  def prepare_native(self):
+    _pack_adaln(self, self.layer_norm, "ln")
+    self._pack("w1", self.transition.weight.detach().float().T)    # [2I, C]; first I rows = swish half
+    _pack_zero_init(self, self.zero_init)
+    self._native_prepared = True
+
+  @_require_prepared
+  def forward(self, x: torch.Tensor, *, single_cond=None):
+    xn = _apply_adaln(self, self.layer_norm, "ln", x, single_cond)
+    hidden = ops.swiglu(ops.linear(xn, self._packed("w1", x.dtype)))
+    return _apply_zero_init(self, self.zero_init, hidden, single_cond, x)
+
+
+class CrossAttentionB200(B200Module):
+  """Diffusion ``CrossAttention`` (transformer.py:480-585): local-window atom attention."""
+
+  def prepare_native(self):
+    c = self.q_projection.input_shape[0]
+    h, d = self.q_projection.output_shape
+    wq = self.q_projection.weight.detach().float().reshape(c, h * d).T
+    wg = self.gating_query.weight.detach().float().T
+    self._pack("qg", torch.cat([wq, wg], 0))
+    bias = torch.zeros(2 * h * d, device=self.q_projection.weight.device)
+    bias[: h * d] = self.q_projection.bias.detach().float().reshape(-1)
+    self._keep("qg_bias", bias)
+    wk = self.k_projection.weight.detach().float().reshape(c, h * d).T
+    wv = self.v_projection.weight.detach().float().reshape(c, h * d).T
+    self._pack("kv", torch.cat([wk, wv], 0))
+    _pack_adaln(self, self.q_layernorm, "lnq")
+    _pack_adaln(self, self.k_layernorm, "lnk")
+    _pack_zero_init(self, self.zero_init)
+    self._hd = (h, d)
+    self._native_prepared = True
+
+  @_require_prepared
+  def forward(self, x_q, x_k, mask_q, mask_k, pair_logits=None, single_cond_q=None, single_cond_k=None):
+    dt = x_q.dtype
+    h, d = self._hd
+    xq = _apply_adaln(self, self.q_layernorm, "lnq", x_q, single_cond_q)
+    xk = _apply_adaln(self, self.k_layernorm, "lnk", x_k.to(dt), single_cond_k)
+    qg = ops.linear(xq, self._packed("qg", dt), bias=self._kept("qg_bias")).view(*x_q.shape[:-1], 2, h, d)
+    kv = ops.linear(xk, self._packed("kv", dt)).view(*x_k.shape[:-1], 2, h, d)
+    o = ops.attention(qg[..., 0, :, :], kv[..., 0, :, :], kv[..., 1, :, :], mask_q=mask_q, mask_k=mask_k,
+                      bias=pair_logits, gate=qg[..., 1, :, :])
+    return _apply_zero_init(self, self.zero_init, o.reshape(*x_q.shape[:-1], h * d), single_cond_q, x_q)
+
+
+class DiffusionTransformerB200(B200Module):
+  """Diffusion ``Transformer`` (transformer.py:348-477): 24 blocks in super-blocks of 4 with the
+  pair-logit pack of every super-block computed once from LN(pair_cond) (transformer.py:429-447)."""
+
+  def prepare_native(self):
+    ws = [lin.weight.detach().float() for lin in self.pair_logits_projection]     # each [P, sbs, H]
+    p = ws[0].shape[0]
+    self._pack("pack_w", torch.cat([w.reshape(p, -1) for w in ws], 1).T)          # [nsb*sbs*H, P]
+    self._keep("pair_ln_w", self.pair_input_layer_norm.weight)
+    self._shape = (len(ws), ws[0].shape[1], ws[0].shape[2])
+    self._native_prepared = True
+
+  def pair_logits_pack(self, pair_cond: torch.Tensor, dtype) -> torch.Tensor:
+    nsb, sbs, h = self._shape
+    n = pair_cond.shape[0]
+    x = ops.layer_norm(pair_cond.to(dtype), self._kept("pair_ln_w"), None)
+    lg = ops.linear(x, self._packed("pack_w", dtype)).reshape(n * n, nsb * sbs * h)
+    out = torch.empty(nsb * sbs * h, n * n, dtype=dtype, device=lg.device)
+    ops.transpose_(lg, out, 1, 1, n * n, nsb * sbs * h, 0, 0, nsb * sbs * h, 0, 0, n * n)
+    return out.view(nsb, sbs, h, n, n)
+
+  @_require_prepared
+  def forward(self, act, mask, single_cond, pair_cond=None):
+    nsb, sbs, _ = self._shape
+    pack = self.pair_logits_pack(pair_cond, act.dtype) if pair_cond is not None else None
+    for sb in range(nsb):
+      for s in range(sbs):
+        act = self.self_attention[sb][s](act, mask, pair_logits=None if pack is None else pack[sb, s],
+                                         single_cond=single_cond)
+        act = self.transition_block[sb][s](act, single_cond=single_cond)
+    return act
+
+
+class CrossAttTransformerB200(B200Module):
+  """Diffusion ``CrossAttTransformer`` (transformer.py:588-693): atom-window cross attention blocks."""
+
+  def prepare_native(self):
+    w = self.pair_logits_projection.weight.detach().float()                        # [P, blocks, H]
+    self._pack("pl_w", w.reshape(w.shape[0], -1).T)
+    self._keep("pair_ln_w", self.pair_input_layer_norm.weight)
+    self._bh = (w.shape[1], w.shape[2])
+    self._native_prepared = True
+
+  @_require_prepared
+  def forward(self, queries_act, queries_mask, queries_to_keys, keys_mask, queries_single_cond, keys_single_cond,
+              pair_cond):
+    nb, h = self._bh
+    dt = queries_act.dtype
+    s_, q_, k_, _ = pair_cond.shape
+    x = ops.layer_norm(pair_cond.to(dt), self._kept("pair_ln_w"), None)
+    lg = ops.linear(x, self._packed("pl_w", dt)).reshape(s_ * q_ * k_, nb * h)
+    # "s q k b h -> b s h q k" (transformer.py:661)
+    pl = torch.empty(nb, s_, h, q_, k_, dtype=dt, device=lg.device)
+    qk = q_ * k_
+    ops.transpose_(lg, pl, s_, nb, qk, h, qk * nb * h, h, nb * h, h * qk, s_ * h * qk, qk)
+    idx = queries_to_keys.gather_idxs
+    gmask = queries_to_keys.gather_mask
+    lead = queries_act.shape[:-3]
+    for blk in range(nb):
+      src = queries_act.reshape(-1, s_ * q_, queries_act.shape[-1])
+      keys = ops.gather_rows(src, idx, gmask).view(*lead, *idx.shape, queries_act.shape[-1])
+      queries_act = self.cross_attention[blk](x_q=queries_act, x_k=keys, mask_q=queries_mask, mask_k=keys_mask,
+                                              pair_logits=pl[blk], single_cond_q=queries_single_cond,
+                                              single_cond_k=keys_single_cond)
+      queries_act = self.transition_block[blk](queries_act, single_cond=queries_single_cond)
+    return queries_act
+
+
+class MSAAttentionB200(B200Module):
+  """``MSAAttention`` pair-weighted averaging (trunk/blocks.py:99-185).
+
+  weights[h,q,k] = softmax_k(LN(pair) W_h + 1e9 (max_m mask[m,k] - 1));
+  v_avg[m,q,h,:] = sum_k weights[h,q,k] v[m,k,h,:] runs as one batched tensor-core
+  contraction per head over (m, d) rows; gated by sigmoid(LN(msa) W_g); output projection.
+  """
+
+  def prepare_native(self):
+    c = self.num_channels
+    h, d = self.v_projection.output_shape
+    self._pack("logits", self.pair_logits.weight.detach().float().T)                # [H, C2]
+    self._pack("v", self.v_projection.weight.detach().float().reshape(c, h * d).T)  # [H*D, C]
+    self._pack("gate", self.gating_query.weight.detach().float().T)
+    self._pack("out", self.output_projection.weight.detach().float().T)
+    self._keep("act_w", self.act_norm.weight)
+    self._keep("act_b", self.act_norm.bias)
+    self._keep("pair_w", self.pair_norm.weight)
+    self._keep("pair_b", self.pair_norm.bias)
+    self._hd = (h, d)
+    self._native_prepared = True
+
+  @_require_prepared
+  def forward(self, act: torch.Tensor, mask: torch.Tensor, pair_act: torch.Tensor):
+    dt = act.dtype
+    h, d = self._hd
+    m_, n_, _ = act.shape
+    nq = pair_act.shape[0]
+    x = ops.layer_norm(act, self._kept("act_w"), self._kept("act_b"))
+    logits = ops.pair_logits(pair_act.to(dt).contiguous(), self._kept("pair_w"), self._kept("pair_b"),
+                             self._packed("logits", dt), h)                              # [H, q, k]
+    # the reference forms the key bias in bf16 (blocks.py:166-167)
+    kbias = (1e9 * (mask.to(torch.bfloat16).amax(0) - 1.0)).float()
+    kp = ops.pitch(n_)
+    w = torch.zeros(h, nq, kp, dtype=dt, device=act.device)
+    ops.softmax_rows(logits.reshape(h * nq, n_), kbias, out=w, ldy=kp)
+    v = ops.linear(x, self._packed("v", dt))                                         # [M, N, H*D]
+    vt = torch.zeros(h, m_ * d, kp, dtype=dt, device=act.device)
+    # v[m][k][h][d] -> vt[h][m][d][k]
+    ops.transpose_(v, vt, m_, h, n_, d, n_ * h * d, d, h * d, d * kp, m_ * d * kp, kp)
+    pavg = ops.contract(vt, w, h, m_ * d, nq, n_)                                    # [H][M*D][pitch(q)]
+    qp = pavg.shape[-1]
+    avg = torch.empty(m_, nq, h * d, dtype=dt, device=act.device)
+    # pavg[h][m][d][q] -> avg[m][q][h][d]
+    ops.transpose_(pavg, avg, h, m_, d, nq, m_ * d * qp, d * qp, qp, d, nq * h * d, h * d)
+    gate = ops.linear(x, self._packed("gate", dt), post_op="sigmoid")
+    return ops.linear(ops.gated_residual(None, avg, gate), self._packed("out", dt))
+
+
+class OuterProductMeanB200(B200Module):
+  """``OuterProductMean`` (trunk/blocks.py:569-689).
+
+  O[(i,a),(j,b)] = sum_m L[m,i,a] R[m,j,b] is one tensor-core GEMM over the MSA
+  axis; the 32x32 blocks are regrouped per pair position and projected to the pair
+  channels with the bias, then scaled by 1/(1e-3 + sum_m mask[m,i] mask[m,j]).
+  """
+
+  def prepare_native(self):
+    self._pack("left", self.left_projection.weight.detach().float().T)     # [32, C]
+    self._pack("right", self.right_projection.weight.detach().float().T)
+    w = self.output_w.detach().float()                                       # [32, 32, C2]
+    self._pack("out", w.reshape(-1, w.shape[-1]).T)                          # [C2, 1024]
+    self._keep("out_b", self.output_b)
+    self._keep("ln_w", self.layer_norm_input.weight)
+    self._keep("ln_b", self.layer_norm_input.bias)
+    self._d = w.shape[0]
+    self._native_prepared = True
+
+  @_require_prepared
+  def forward(self, act: torch.Tensor, mask: torch.Tensor):
+    dt = act.dtype
+    d = self._d
+    m_, n_, _ = act.shape
+    x = ops.layer_norm(act, self._kept("ln_w"), self._kept("ln_b"))
+    left = ops.mask_rows_(ops.linear(x, self._packed("left", dt)), mask)     # [M, N, 32]
+    right = ops.mask_rows_(ops.linear(x, self._packed("right", dt)), mask)
+    mp = ops.pitch(m_)
+    lt = torch.zeros(n_ * d, mp, dtype=dt, device=act.device)
+    rt = torch.zeros(n_ * d, mp, dtype=dt, device=act.device)
+    ops.transpose_(left, lt, 1, 1, m_, n_ * d, 0, 0, n_ * d, 0, 0, mp)        # [M][(i,a)] -> [(i,a)][M]
+    ops.transpose_(right, rt, 1, 1, m_, n_ * d, 0, 0, n_ * d, 0, 0, mp)
+    o = ops.contract(lt, rt, 1, n_ * d, n_ * d, m_)                           # [1][(i,a)][pitch((j,b))]
+    blocks = ops.opm_repack(o.reshape(n_ * d, -1), n_, d)                    # [(i,j)][(a,b)]
+    out = ops.linear(blocks, self._packed("out", dt), bias=self._kept("out_b")).view(n_, n_, -1)
+    norm = ops.opm_norm(mask, dt)
+    return ops.scale_rows_(out, norm.reshape(-1))
 
 
 # ---------------------------------------------------------------------------
@@ -287,36 +528,44 @@ class TransitionBlock(TransitionBlockB200, torch.nn.Module):
 
 
 class _AdaptiveLayerNorm(torch.nn.Module):
-  """Parameter tree of transformer.AdaptiveLayerNorm with single_cond=None (transformer.py:70-75)."""
+  """Parameter tree of transformer.AdaptiveLayerNorm (transformer.py:33-75)."""
 
-  def __init__(self, c: int):
+  def __init__(self, c: int, single_cond_size: int | None = None):
     super().__init__()
-    self.single_cond = False
-    self.layer_norm = LayerNorm(c, name="layer_norm")
+    self.single_cond = single_cond_size is not None
+    if self.single_cond:
+      self.layer_norm = LayerNorm(c, elementwise_affine=False, name="layer_norm")
+      self.single_cond_layer_norm = LayerNorm(single_cond_size, bias=False, name="single_cond_layer_norm")
+      self.single_cond_scale = Linear(single_cond_size, c, bias=True, name="single_cond_scale")
+      self.single_cond_bias = Linear(single_cond_size, c, name="single_cond_bias")
+    else:
+      self.layer_norm = LayerNorm(c, name="layer_norm")
 
 
 class _AdaptiveZeroInit(torch.nn.Module):
-  """Parameter tree of transformer.AdaptiveZeroInit with single_cond=None (transformer.py:128-133)."""
+  """Parameter tree of transformer.AdaptiveZeroInit (transformer.py:102-133)."""
 
-  def __init__(self, hidden: int, c: int):
+  def __init__(self, hidden: int, c: int, single_cond_size: int | None = None):
     super().__init__()
-    self.single_cond = False
+    self.single_cond = single_cond_size is not None
     self.transition2 = Linear(hidden, c, name="transition2")
+    if self.single_cond:
+      self.adaptive_zero_cond = Linear(single_cond_size, c, bias=True, name="adaptive_zero_cond")
 
 
 class SelfAttention(SelfAttentionB200, torch.nn.Module):
-  def __init__(self, num_channels: int = 384, num_head: int = 16, name: str = ""):
+  def __init__(self, num_channels: int = 384, num_head: int = 16, name: str = "", single_cond_size: int | None = None):
     torch.nn.Module.__init__(self)
     self.name = name
     c = num_channels
     d = c // num_head
     self.key_dim = self.value_dim = d
-    self.layer_norm = _AdaptiveLayerNorm(c)
+    self.layer_norm = _AdaptiveLayerNorm(c, single_cond_size)
     self.q_projection = Linear(c, (num_head, d), bias=True, name="q_projection")
     self.k_projection = Linear(c, (num_head, d), name="k_projection")
     self.v_projection = Linear(c, (num_head, d), name="v_projection")
     self.gating_query = Linear(c, num_head * d, name="gating_query")
-    self.zero_init = _AdaptiveZeroInit(c, c)
+    self.zero_init = _AdaptiveZeroInit(c, c, single_cond_size)
 
 
 class SingleActUpdate(SingleActUpdateB200, torch.nn.Module):
@@ -360,6 +609,81 @@ class PairFormerIteration(torch.nn.Module):
     act = self.pair_transition(act)
     single_act = self.single_act_update(act, single_act, seq_mask)
     return act, single_act
+
+
+class DiffusionTransitionBlock(DiffusionTransitionBlockB200, torch.nn.Module):
+  def __init__(self, num_channels: int, num_intermediate_factor: int = 2, single_cond_size: int | None = None):
+    torch.nn.Module.__init__(self)
+    c = num_channels
+    i = c * num_intermediate_factor
+    self.layer_norm = _AdaptiveLayerNorm(c, single_cond_size)
+    self.transition = Linear(c, 2 * i, name="ffw_transition1")
+    self.zero_init = _AdaptiveZeroInit(i, c, single_cond_size)
+
+
+class CrossAttention(CrossAttentionB200, torch.nn.Module):
+  def __init__(self, num_channels: int = 128, num_head: int = 4, key_dim: int = 128):
+    torch.nn.Module.__init__(self)
+    c = num_channels
+    d = key_dim // num_head
+    self.q_layernorm = _AdaptiveLayerNorm(c, c)
+    self.k_layernorm = _AdaptiveLayerNorm(c, c)
+    self.q_projection = Linear(c, (num_head, d), bias=True, name="q_projection")
+    self.k_projection = Linear(c, (num_head, d), name="k_projection")
+    self.v_projection = Linear(c, (num_head, d), name="v_projection")
+    self.gating_query = Linear(c, num_head * d, name="gating_query")
+    self.zero_init = _AdaptiveZeroInit(c, c, c)
+
+
+class DiffusionTransformer(DiffusionTransformerB200, torch.nn.Module):
+  def __init__(self, num_channels: int = 768, single_cond_size: int = 384, pair_cond_size: int = 128,
+               num_head: int = 16, num_blocks: int = 24, super_block_size: int = 4, num_intermediate_factor: int = 2):
+    torch.nn.Module.__init__(self)
+    nsb = num_blocks // super_block_size
+    mk = lambda f: torch.nn.ModuleList(torch.nn.ModuleList(f() for _ in range(super_block_size)) for _ in range(nsb))
+    self.self_attention = mk(lambda: SelfAttention(num_channels, num_head, single_cond_size=single_cond_size))
+    self.transition_block = mk(lambda: DiffusionTransitionBlock(num_channels, num_intermediate_factor, single_cond_size))
+    self.pair_logits_projection = torch.nn.ModuleList(
+        Linear(pair_cond_size, (super_block_size, num_head), name="pair_logits_projection") for _ in range(nsb))
+    self.pair_input_layer_norm = LayerNorm(pair_cond_size, bias=False, name="pair_input_layer_norm")
+
+
+class CrossAttTransformer(CrossAttTransformerB200, torch.nn.Module):
+  def __init__(self, num_channels: int = 128, pair_cond_size: int = 16, num_head: int = 4, key_dim: int = 128,
+               num_blocks: int = 3, num_intermediate_factor: int = 2):
+    torch.nn.Module.__init__(self)
+    self.pair_input_layer_norm = LayerNorm(pair_cond_size, bias=False, name="pair_input_layer_norm")
+    self.pair_logits_projection = Linear(pair_cond_size, (num_blocks, num_head), name="pair_logits_projection")
+    self.cross_attention = torch.nn.ModuleList(CrossAttention(num_channels, num_head, key_dim) for _ in range(num_blocks))
+    self.transition_block = torch.nn.ModuleList(
+        DiffusionTransitionBlock(num_channels, num_intermediate_factor, num_channels) for _ in range(num_blocks))
+
+
+class MSAAttention(MSAAttentionB200, torch.nn.Module):
+  def __init__(self, num_channels: int = 64, num_output_channel: int = 128, num_head: int = 8):
+    torch.nn.Module.__init__(self)
+    self.num_channels = c = num_channels
+    self.num_output_channel = c2 = num_output_channel
+    d = c // num_head
+    self.act_norm = LayerNorm(c, name="act_norm")
+    self.pair_norm = LayerNorm(c2, name="pair_norm")
+    self.pair_logits = Linear(c2, num_head, name="pair_logits")
+    self.v_projection = Linear(c, (num_head, d), name="v_projection")
+    self.gating_query = Linear(c, num_head * d, name="gating_query")
+    self.output_projection = Linear(num_head * d, c, name="output_projection")
+
+
+class OuterProductMean(OuterProductMeanB200, torch.nn.Module):
+  def __init__(self, num_channels: int = 64, num_output_channel: int = 128, num_outer_channel: int = 32):
+    torch.nn.Module.__init__(self)
+    self.num_channels = num_channels
+    self.num_output_channel = num_output_channel
+    self.layer_norm_input = LayerNorm(num_channels, name="layer_norm_input")
+    self.left_projection = Linear(num_channels, num_outer_channel, name="left_projection")
+    self.right_projection = Linear(num_channels, num_outer_channel, name="right_projection")
+    self.output_w = torch.nn.Parameter(torch.empty(num_outer_channel, num_outer_channel, num_output_channel),
+                                       requires_grad=False)
+    self.output_b = torch.nn.Parameter(torch.empty(num_output_channel), requires_grad=False)
 
 
 def prepare(module: torch.nn.Module) -> dict[str, int]:

@@ -200,3 +200,118 @@ def pair_logits(z: torch.Tensor, ln_w, ln_b, w, heads: int) -> torch.Tensor:
   N.call("sf_pair_logits", dt, _p(z.contiguous()), _p(ln_w), _p(ln_b), _p(w), _p(out), rows, n, c, heads,
          _p(ws), ws.numel(), _stream())
   return out
+
+
+# ---------------------------------------------------------------------------
+# diffusion-transformer and MSA helpers
+# ---------------------------------------------------------------------------
+def adaln(x: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+  """scale * LN(x) + bias, all [..., C] of x's dtype (AdaptiveLayerNorm with single_cond)."""
+  _cuda(x, scale, bias)
+  x = x.contiguous()
+  scale = scale.to(x.dtype).expand_as(x).contiguous()
+  bias = bias.to(x.dtype).expand_as(x).contiguous()
+  y = torch.empty_like(x)
+  c = x.shape[-1]
+  N.call("sf_adaln", _dt(x), _p(x), _p(scale), _p(bias), _p(y), x.numel() // c, c, _stream())
+  return y
+
+
+def gated_residual(base, u: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
+  """base + u * gate (base may be None); gate broadcast to u's shape."""
+  _cuda(u, gate, base)
+  u = u.contiguous()
+  gate = gate.to(u.dtype).expand_as(u).contiguous()
+  if base is not None:
+    base = base.to(u.dtype).expand_as(u).contiguous()
+  out = torch.empty_like(u)
+  N.call("sf_gated_residual", _dt(u), _p(base), _p(u), _p(gate), _p(out), u.numel(), _stream())
+  return out
+
+
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+  """src [B, R, C] -> out [B, n_out, C] with out[b, i] = mask[i] ? src[b, idx[i]] : 0."""
+  _cuda(src, idx, mask)
+  src = src.contiguous()
+  b, r, c = src.shape
+  idx = idx.reshape(-1).to(torch.int32).contiguous()
+  m = mask_u8(mask.reshape(-1))
+  out = torch.empty(b, idx.numel(), c, dtype=src.dtype, device=src.device)
+  N.call("sf_gather_rows", _dt(src), _p(src), b, r, _p(idx), _p(m), idx.numel(), c, _p(out), _stream())
+  return out
+
+
+def mask_rows_(x: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+  """In place: x[..., :] = 0 where !mask[...] (mask has x's leading shape)."""
+  _cuda(x, mask)
+  assert x.is_contiguous()
+  c = x.shape[-1]
+  m = mask_u8(mask.expand(x.shape[:-1]).reshape(-1))
+  N.call("sf_mask_rows", _dt(x), _p(x), _p(m), x.numel() // c, c, _stream())
+  return x
+
+
+def softmax_rows(x: torch.Tensor, key_bias=None, out=None, ldy=None) -> torch.Tensor:
+  _cuda(x, key_bias)
+  x = x.contiguous()
+  k = x.shape[-1]
+  rows = x.numel() // k
+  if out is None:
+    out = torch.empty_like(x)
+  N.call("sf_softmax_rows", _dt(x), _p(x), _p(key_bias), _p(out), rows, k, ldy or k, _stream())
+  return out
+
+
+def transpose_(src: torch.Tensor, dst: torch.Tensor, nb1, nb2, rows, cols, ib1, ib2, is_r, ob1, ob2, os_c) -> None:
+  """Batched strided transpose between two CUDA buffers (strides in elements)."""
+  _cuda(src, dst)
+  N.call("sf_transpose", _dt(src), _p(src), _p(dst), nb1, nb2, rows, cols, ib1, ib2, is_r, ob1, ob2, os_c, _stream())
+
+
+def pitch(n: int) -> int:
+  return int(N.load().sf_pair_pitch(n))
+
+
+def contract(a_op: torch.Tensor, b_op: torch.Tensor, channels: int, rows: int, cols: int, kdim: int) -> torch.Tensor:
+  """P[c][i][j] = sum_k A[c][i][k] B[c][j][k]; A [c][rows][pitch(k)], B [c][cols][pitch(k)] -> [c][rows][pitch(cols)]."""
+  _cuda(a_op, b_op)
+  p = torch.empty(channels, rows, pitch(cols), dtype=a_op.dtype, device=a_op.device)
+  N.call("sf_tri_mult_contract", _dt(a_op), _p(a_op), _p(b_op), _p(p), channels, rows, cols, kdim, _stream())
+  return p
+
+
+def opm_norm(mask: torch.Tensor, dtype) -> torch.Tensor:
+  """[n_res, n_res] fp32 = 1/(1e-3 + sum_m mask[m,i] mask[m,j]) (count rounded to dtype)."""
+  _cuda(mask)
+  m = mask_u8(mask)
+  n_seq, n_res = m.shape
+  ws = _ws(N.load().sf_opm_norm_workspace(n_seq, n_res), m.device)
+  norm = torch.empty(n_res, n_res, dtype=torch.float32, device=m.device)
+  dt = N.SF_F32 if dtype == torch.float32 else N.SF_BF16
+  N.call("sf_opm_norm", dt, _p(m), n_seq, n_res, _p(norm), _p(ws), ws.numel(), _stream())
+  return norm
+
+
+def opm_repack(o: torch.Tensor, n_res: int, d: int) -> torch.Tensor:
+  _cuda(o)
+  out = torch.empty(n_res * n_res, d * d, dtype=o.dtype, device=o.device)
+  N.call("sf_opm_repack", _dt(o), _p(o), o.shape[-1], n_res, d, _p(out), _stream())
+  return out
+
+
+def scale_rows_(x: torch.Tensor, s: torch.Tensor) -> torch.Tensor:
+  _cuda(x, s)
+  assert x.is_contiguous() and s.dtype == torch.float32
+  c = x.shape[-1]
+  N.call("sf_scale_rows", _dt(x), _p(x), _p(s.contiguous()), x.numel() // c, c, _stream())
+  return x
+
+
+def swiglu(h: torch.Tensor) -> torch.Tensor:
+  """[..., 2I] -> swish(h[..., :I]) * h[..., I:]."""
+  _cuda(h)
+  h = h.contiguous()
+  i2 = h.shape[-1]
+  out = torch.empty(*h.shape[:-1], i2 // 2, dtype=h.dtype, device=h.device)
+  N.call("sf_swiglu", _dt(h), _p(h), _p(out), h.numel() // i2, i2 // 2, _stream())
+  return out

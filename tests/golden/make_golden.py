@@ -55,6 +55,10 @@ def _spec(module) -> list:
         kind, fan = ("ln_weight" if pname == "weight" else "ln_bias"), 1
       elif synth._is_linear(mod):
         kind, fan = ("weight" if pname == "weight" else "bias"), int(math.prod(mod.input_shape))
+      elif pname == "output_w":
+        kind, fan = "weight", int(p.shape[0] * p.shape[1])
+      elif pname == "output_b":
+        kind, fan = "bias", 1
       else:
         raise ValueError(full)
       out.append([full, list(p.shape), kind, fan])
@@ -137,5 +141,92 @@ def main(src: str):
   _save("pairformer_n24", _spec(blk), seed, z=z, s=s, mask=mask, z_out=zo, s_out=so)
 
 
+def diffusion_and_msa():
+  """Fixtures of the diffusion-transformer and MSA modules (small AF3-like shapes)."""
+  from sparsefold.model.diffusion import transformer as T
+  from sparsefold.model.trunk import blocks
+  from sparsefold.model import config as mc
+  from sparsefold.schema.atom_layout import GatherInfo
+  gc = mc.GlobalConfig()
+  seed = 0
+  g = torch.Generator().manual_seed(11)
+  rn = lambda *s: torch.randn(*s, generator=g)
+
+  # token self-attention with AdaLN (2 samples, 24 tokens, 21 real, c=128, 4 heads, single cond 64)
+  n, c, sc_c = 24, 128, 64
+  x, sc, pl = rn(2, n, c), rn(n, sc_c), rn(4, n, n)
+  mask = torch.arange(n) < 21
+  mod = T.SelfAttention(T.SelfAttention.Config(num_head=4), gc, num_channels=c, single_cond_size=sc_c, name="x")
+  synth.init_params(mod, seed)
+  with torch.no_grad():
+    out = mod(x, mask, pair_logits=pl, single_cond=sc)
+  _save("diff_self_attention", _spec(mod), seed, x=x, single_cond=sc, pair_logits=pl, mask=mask, out=out)
+
+  mod = T.TransitionBlock(gc, num_channels=c, num_intermediate_factor=2, single_cond_size=sc_c, name="x")
+  synth.init_params(mod, seed)
+  with torch.no_grad():
+    out = mod(x, single_cond=sc)
+  _save("diff_transition", _spec(mod), seed, x=x, single_cond=sc, out=out)
+
+  # transformer: 4 blocks in super-blocks of 2, pair_cond 16 channels
+  pc = rn(n, n, 16)
+  mod = T.Transformer(T.Transformer.Config(attention=T.SelfAttention.Config(num_head=4), num_blocks=4,
+                                           super_block_size=2), gc, num_channels=c, single_cond_size=sc_c,
+                      pair_cond_size=16)
+  synth.init_params(mod, seed)
+  with torch.no_grad():
+    out = mod(x, mask, sc, pc)
+  _save("diff_transformer", _spec(mod), seed, x=x, single_cond=sc, pair_cond=pc, mask=mask, out=out)
+
+  # atom cross attention: 4 subsets x 32 queries over 128 atoms, 128-key windows, c_atom=64, 4 heads x 16
+  s_, q_, k_, ca = 4, 32, 128, 64
+  xq = rn(2, s_, q_, ca)
+  qsc, ksc = rn(s_, q_, ca), rn(s_, k_, ca)
+  qmask = torch.rand(s_, q_, generator=g) > 0.1
+  starts = torch.clamp(32 * torch.arange(s_) + 16 - 64, 0, s_ * q_ - k_)
+  idx = (starts[:, None] + torch.arange(k_)[None, :]).to(torch.int32)
+  gmask = torch.rand(s_, k_, generator=g) > 0.05
+  kmask = gmask & (torch.rand(s_, k_, generator=g) > 0.1)
+  pcq = rn(s_, q_, k_, 8)
+  cfg = T.CrossAttention.Config(num_head=4, key_dim=64, value_dim=64)
+  mod = T.CrossAttention(cfg, gc, num_channels=ca, name="x")
+  synth.init_params(mod, seed)
+  xk = rn(2, s_, k_, ca)
+  plq = rn(s_, 4, q_, k_)
+  with torch.no_grad():
+    out = mod(xq, xk, qmask, kmask, pair_logits=plq, single_cond_q=qsc, single_cond_k=ksc)
+  _save("diff_cross_attention", _spec(mod), seed, x_q=xq, x_k=xk, mask_q=qmask, mask_k=kmask, pair_logits=plq,
+        single_cond_q=qsc, single_cond_k=ksc, out=out)
+
+  mod = T.CrossAttTransformer(T.CrossAttTransformer.Config(num_intermediate_factor=2, num_blocks=2, attention=cfg), gc,
+                              pair_cond_size=8, num_channels=ca, super_name="a")
+  synth.init_params(mod, seed)
+  info = GatherInfo(gather_idxs=idx, gather_mask=gmask, input_shape=torch.tensor([s_, q_], dtype=torch.int32))
+  with torch.no_grad():
+    out = mod(xq, qmask, info, kmask, qsc, ksc, pcq)
+  _save("diff_cross_att_transformer", _spec(mod), seed, queries_act=xq, queries_mask=qmask, gather_idxs=idx,
+        gather_mask=gmask, keys_mask=kmask, queries_single_cond=qsc, keys_single_cond=ksc, pair_cond=pcq, out=out)
+
+  # MSA pair-weighted averaging and outer-product mean: 6 MSA rows x 16 tokens, c_m=64, c_z=128
+  m_, nn_ = 6, 16
+  act, pair = rn(m_, nn_, 64), rn(nn_, nn_, 128)
+  msa_mask = torch.rand(m_, nn_, generator=g) > 0.15
+  msa_mask[:, 3] = False                        # a key masked in every row
+  mod = blocks.MSAAttention(blocks.MSAAttention.Config(), gc, num_channels=64, num_output_channel=128, name="x")
+  synth.init_params(mod, seed)
+  with torch.no_grad():
+    out = mod(act, msa_mask, pair_act=pair)
+  _save("msa_attention", _spec(mod), seed, act=act, mask=msa_mask, pair_act=pair, out=out)
+
+  mod = blocks.OuterProductMean(blocks.OuterProductMean.Config(), gc, num_channels=64, num_output_channel=128, name="x")
+  mod.output_w = torch.nn.Parameter(torch.empty(32, 32, 128), requires_grad=False)
+  mod.output_b = torch.nn.Parameter(torch.empty(128), requires_grad=False)
+  synth.init_params(mod, seed)
+  with torch.no_grad():
+    out = mod(act, msa_mask)
+  _save("outer_product_mean", _spec(mod), seed, act=act, mask=msa_mask, out=out)
+
+
 if __name__ == "__main__":
   main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+  diffusion_and_msa()

@@ -62,3 +62,49 @@ def test_fully_masked_row_averages_values():
   mk = torch.zeros(6, dtype=torch.bool)
   out = orc.dot_product_attention(q, k, v, mask_k=mk)
   torch.testing.assert_close(out, v.mean(0, keepdim=True).expand(4, 1, 8), rtol=1e-6, atol=1e-6)
+
+
+# ---- diffusion transformer and MSA ------------------------------------------
+from oracle import diffusion as dif  # noqa: E402
+
+
+def test_diffusion_self_attention_golden():
+  a, p = load("diff_self_attention")
+  out = dif.self_attention(a["x"], a["mask"], p, pair_logits=a["pair_logits"], single_cond=a["single_cond"])
+  assert max_rel_err(out, a["out"]) < 2e-6
+
+
+def test_diffusion_transition_golden():
+  a, p = load("diff_transition")
+  assert max_rel_err(dif.transition(a["x"], p, a["single_cond"]), a["out"]) < 2e-6
+
+
+def test_diffusion_transformer_golden():
+  a, p = load("diff_transformer")
+  out = dif.transformer(a["x"], a["mask"], a["single_cond"], a["pair_cond"], p, n_super=2, super_block=2)
+  assert max_rel_err(out, a["out"]) < 5e-6
+
+
+def test_cross_attention_golden():
+  a, p = load("diff_cross_attention")
+  out = dif.cross_attention(a["x_q"], a["x_k"], a["mask_q"], a["mask_k"], p, pair_logits=a["pair_logits"],
+                            single_cond_q=a["single_cond_q"], single_cond_k=a["single_cond_k"])
+  assert max_rel_err(out, a["out"]) < 2e-6
+
+
+def test_cross_att_transformer_golden():
+  a, p = load("diff_cross_att_transformer")
+  out = dif.cross_att_transformer(a["queries_act"], a["queries_mask"], a["gather_idxs"], a["gather_mask"],
+                                  a["keys_mask"], a["queries_single_cond"], a["keys_single_cond"], a["pair_cond"], p,
+                                  num_blocks=2)
+  assert max_rel_err(out, a["out"]) < 5e-6
+
+
+def test_msa_attention_golden():
+  a, p = load("msa_attention")
+  assert max_rel_err(dif.msa_attention(a["act"], a["mask"], a["pair_act"], p), a["out"]) < 1e-5
+
+
+def test_outer_product_mean_golden():
+  a, p = load("outer_product_mean")
+  assert max_rel_err(dif.outer_product_mean(a["act"], a["mask"], p), a["out"]) < 2e-6
