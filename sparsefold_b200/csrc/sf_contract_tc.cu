@@ -1,7 +1,9 @@
 // Triangle-multiplication contraction on tcgen05 (blocks.py:558):
-//   P[c][i][j] = sum_k A[c][i][k] * B[c][j][k]   (bf16 in, fp32 accumulate, bf16 out)
-// for each of the 128 channels c.  Both operands are K-major, which is how the
-// projection phase writes them for either equation.
+//   P[i][c][j] = sum_k A[i][c][k] * B[j][c][k]   (bf16 in, fp32 accumulate, bf16 out)
+// for each of the 128 channels c.  Both operands are K-major ([row][channel][k]),
+// which is how the projection phase writes them for either equation; after a
+// collective an operand may arrive as [rank][row][channel][k-chunk], which the
+// 4-D tensor maps read in place.
 //
 // Persistent, warp-specialised: warp 4 streams 128x64 A and 256x64 B tiles by
 // TMA through a 4-stage shared-memory ring; one thread of warp 5 issues
@@ -22,6 +24,7 @@ constexpr int SMEM_CONTRACT = STAGES * STAGE_BYTES + 1024 + 1024;
 struct ContractParams {
   bf16* P;
   int64_t channels, rows, cols, kdim;
+  int64_t kl_a, kl_b;       // K chunk length of each operand (kdim when unchunked)
   const float* bias;        // [cols] or null
   const bf16* residual;     // laid out like P, or null
   int post_op;              // SF_POST_*
@@ -85,8 +88,10 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
         tc::mbar_wait(&empty[s], ((q / STAGES) & 1) ^ 1, p.status, aborted);
         uint8_t* st = smem + s * STAGE_BYTES;
         tc::mbar_expect_tx(&full[s], STAGE_BYTES);
-        tc::tma_load_3d(st, &tmA, &full[s], kb * BK, i0, (int)c);
-        tc::tma_load_3d(st + SA_BYTES, &tmB, &full[s], kb * BK, j0, (int)c);
+        // K index -> (chunk, offset in chunk); chunks hold whole 64-wide K blocks
+        const int64_t k = (int64_t)kb * BK;
+        tc::tma_load_4d(st, &tmA, &full[s], (int)(k % p.kl_a), (int)c, i0, (int)(k / p.kl_a));
+        tc::tma_load_4d(st + SA_BYTES, &tmB, &full[s], (int)(k % p.kl_b), (int)c, j0, (int)(k / p.kl_b));
       }
     }
   } else if (warp == 5 && lane == 0) {
@@ -124,7 +129,7 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
       const int64_t i = (rem / nt) * BM + tid, j0 = (rem % nt) * BN;
       tc::mbar_wait(&accf[acc], (u >> 1) & 1, p.status, aborted);
       tc::tc_fence_after();
-      bf16* prow = p.P + (c * p.rows + i) * cp;
+      bf16* prow = p.P + (i * p.channels + c) * cp;
 #pragma unroll 1
       for (int ch = 0; ch < BN / 16; ++ch) {
         float v[16];
@@ -135,7 +140,7 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
             const int64_t j = j0 + ch * 16 + g * 8;
             if (j + 8 <= cp) {
               if (p.bias || p.residual || p.post_op) {
-                const bf16* res = p.residual ? p.residual + (c * p.rows + i) * cp + j : nullptr;
+                const bf16* res = p.residual ? p.residual + (i * p.channels + c) * cp + j : nullptr;
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                   float x = v[g * 8 + e];
@@ -165,26 +170,27 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
   }
 }
 
-// Tensor map over a channel-major operand [channels][rows][pitch(kdim)] bf16, box 64 (k) x box_rows.
-int make_operand_tmap(CUtensorMap* map, const void* base, int64_t channels, int64_t rows, int64_t kdim,
-                      uint32_t box_rows) {
+// Tensor map over an operand [chunks][rows][channels][pitch(kl)] bf16 (K split into
+// `chunks` pieces of kl, one per source rank after a collective), box 64 (k) x box_rows.
+int make_operand_tmap(CUtensorMap* map, const void* base, int64_t chunks, int64_t rows, int64_t channels,
+                      int64_t kl, uint32_t box_rows) {
   auto encode = tensor_map_encoder();
   if (!encode) return SF_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) {
     set_error("contraction operand %p is not 16-byte aligned", base);
     return SF_ERR_ARG;
   }
-  const int64_t kp = pair_pitch(kdim);
-  cuuint64_t dims[3] = {(cuuint64_t)kp, (cuuint64_t)rows, (cuuint64_t)channels};
-  cuuint64_t strides[2] = {(cuuint64_t)kp * 2, (cuuint64_t)(rows * kp * 2)};
-  cuuint32_t box[3] = {(cuuint32_t)BK, box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+  const int64_t kp = pair_pitch(kl);
+  cuuint64_t dims[4] = {(cuuint64_t)kp, (cuuint64_t)channels, (cuuint64_t)rows, (cuuint64_t)chunks};
+  cuuint64_t strides[3] = {(cuuint64_t)kp * 2, (cuuint64_t)(channels * kp * 2), (cuuint64_t)(rows * channels * kp * 2)};
+  cuuint32_t box[4] = {(cuuint32_t)BK, 1, box_rows, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    set_error("cuTensorMapEncodeTiled failed (%d) for operand [%lld][%lld][%lld]", (int)r, (long long)channels,
-              (long long)rows, (long long)kp);
+    set_error("cuTensorMapEncodeTiled failed (%d) for operand [%lld][%lld][%lld][%lld]", (int)r, (long long)chunks,
+              (long long)rows, (long long)channels, (long long)kp);
     return SF_ERR_CUDA;
   }
   return SF_OK;
@@ -193,27 +199,43 @@ int make_operand_tmap(CUtensorMap* map, const void* base, int64_t channels, int6
 }  // namespace
 
 static int gemm_tc_impl(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
-                        int64_t kdim, const float* bias, const bf16* residual, int post_op, cudaStream_t stream);
+                        int64_t chunks_a, int64_t kl_a, int64_t chunks_b, int64_t kl_b, const float* bias,
+                        const bf16* residual, int post_op, cudaStream_t stream);
 
 int contract_tc(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
                 int64_t kdim, cudaStream_t stream) {
-  return gemm_tc_impl(a_op, b_op, P, channels, rows, cols, kdim, nullptr, nullptr, SF_POST_NONE, stream);
+  return gemm_tc_impl(a_op, b_op, P, channels, rows, cols, 1, kdim, 1, kdim, nullptr, nullptr, SF_POST_NONE, stream);
+}
+
+int contract_chunked_tc(const bf16* a_op, int64_t chunks_a, const bf16* b_op, int64_t chunks_b, bf16* P,
+                        int64_t channels, int64_t rows, int64_t cols, int64_t kdim, cudaStream_t stream) {
+  SF_REQUIRE(chunks_a > 0 && chunks_b > 0 && kdim % chunks_a == 0 && kdim % chunks_b == 0,
+             "contract: K=%lld does not split into %lld / %lld chunks", (long long)kdim, (long long)chunks_a,
+             (long long)chunks_b);
+  const int64_t kl_a = kdim / chunks_a, kl_b = kdim / chunks_b;
+  SF_REQUIRE((chunks_a == 1 || kl_a % BK == 0) && (chunks_b == 1 || kl_b % BK == 0),
+             "contract: chunked K needs chunk lengths that are multiples of %d (got %lld / %lld)", BK,
+             (long long)kl_a, (long long)kl_b);
+  return gemm_tc_impl(a_op, b_op, P, channels, rows, cols, chunks_a, kl_a, chunks_b, kl_b, nullptr, nullptr,
+                      SF_POST_NONE, stream);
 }
 
 // y[M][N] = post(x[M][K] . wt[N][K]^T + bias + residual); K and N multiples of 8.
 int linear_tc(const bf16* x, const bf16* wt, const float* bias, const bf16* residual, bf16* y, int64_t M, int64_t K,
               int64_t N, int post_op, cudaStream_t stream) {
-  return gemm_tc_impl(x, wt, y, 1, M, N, K, bias, residual, post_op, stream);
+  return gemm_tc_impl(x, wt, y, 1, M, N, 1, K, 1, K, bias, residual, post_op, stream);
 }
 
 static int gemm_tc_impl(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
-                        int64_t kdim, const float* bias, const bf16* residual, int post_op, cudaStream_t stream) {
+                        int64_t chunks_a, int64_t kl_a, int64_t chunks_b, int64_t kl_b, const float* bias,
+                        const bf16* residual, int post_op, cudaStream_t stream) {
+  const int64_t kdim = chunks_a * kl_a;
   if (channels == 0 || rows == 0 || cols == 0) return SF_OK;
   SF_REQUIRE(rows < (1 << 30) && cols < (1 << 30) && kdim < (1 << 30) && channels < (1 << 30),
              "contract_tc: size too large");
   CUtensorMap ma, mb;
-  SF_TRY(make_operand_tmap(&ma, a_op, channels, rows, kdim, BM));
-  SF_TRY(make_operand_tmap(&mb, b_op, channels, cols, kdim, BN));
+  SF_TRY(make_operand_tmap(&ma, a_op, chunks_a, rows, channels, kl_a, BM));
+  SF_TRY(make_operand_tmap(&mb, b_op, chunks_b, cols, channels, kl_b, BN));
   uint32_t* status = device_status_ptr();
   if (!status) return SF_ERR_CUDA;
   static bool attr_set[64] = {false};
@@ -227,7 +249,7 @@ static int gemm_tc_impl(const bf16* a_op, const bf16* b_op, bf16* P, int64_t cha
     }
     attr_set[dev & 63] = true;
   }
-  ContractParams p{P, channels, rows, cols, kdim, bias, residual, post_op, status};
+  ContractParams p{P, channels, rows, cols, kdim, kl_a, kl_b, bias, residual, post_op, status};
   const int64_t ntiles = channels * ((rows + BM - 1) / BM) * ((cols + BN - 1) / BN);
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
   k_contract_tc<<<grid, 192, SMEM_CONTRACT, stream>>>(ma, mb, p);

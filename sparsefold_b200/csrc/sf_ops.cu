@@ -58,7 +58,7 @@ __global__ void k_tri_glu_scatter(const float* __restrict__ y, const uint8_t* __
                                   int64_t n, int64_t pitch, int C, int incoming, T* __restrict__ a_op,
                                   T* __restrict__ b_op) {
   __shared__ float ta[32][33], tb[32][33];
-  const int64_t M = n * n, plane = n * pitch;
+  const int64_t M = n * n;
   const int64_t m0 = (int64_t)blockIdx.x * 32;
   const int c0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
@@ -86,13 +86,13 @@ __global__ void k_tri_glu_scatter(const float* __restrict__ y, const uint8_t* __
     int64_t i = m / n, k = m % n;
     float va = ta[tx][r], vb = tb[tx][r];
     if (!incoming) {
-      int64_t t = i * pitch + k;
-      st(a_op + (int64_t)c * plane + t, va);   // A[c][i][k] = a[c,i,k]
-      st(b_op + (int64_t)c * plane + t, vb);   // B[c][j][k] = b[c,j,k]
+      int64_t t = (i * C + c) * pitch + k;
+      st(a_op + t, va);   // A[i][c][k] = a[c,i,k]
+      st(b_op + t, vb);   // B[j][c][k] = b[c,j,k]
     } else {
-      int64_t t = k * pitch + i;               // transpose of position (i, k)
-      st(a_op + (int64_t)c * plane + t, vb);   // A[c][i][k] = b[c,k,i]
-      st(b_op + (int64_t)c * plane + t, va);   // B[c][j][k] = a[c,k,j]
+      int64_t t = (k * C + c) * pitch + i;     // transpose of position (i, k)
+      st(a_op + t, vb);   // A[i][c][k] = b[c,k,i]
+      st(b_op + t, va);   // B[j][c][k] = a[c,k,j]
     }
   }
 }
@@ -104,19 +104,20 @@ __global__ void __launch_bounds__(256) k_contract(const T* __restrict__ A, const
                                                   int64_t K) {
   __shared__ float As[GK][GM + 4];
   __shared__ float Bs[GK][GN + 4];
-  const int64_t c = blockIdx.z;
+  const int64_t c = blockIdx.z, C = gridDim.z;
   const int64_t kp = pair_pitch(K), cp = pair_pitch(cols);
-  const T* Ab = A + c * rows * kp;
-  const T* Bb = B + c * cols * kp;
-  T* Pb = P + c * rows * cp;
+  // operands [row][channel][pitch]: row r of channel c starts at (r * C + c) * pitch
+  const T* Ab = A + c * kp;
+  const T* Bb = B + c * kp;
+  T* Pb = P + c * cp;
   const int tid = threadIdx.x, tm = tid / 16, tn = tid % 16;
   const int64_t m0 = (int64_t)blockIdx.y * GM, n0 = (int64_t)blockIdx.x * GN;
   float acc[4][4] = {};
   for (int64_t k0 = 0; k0 < K; k0 += GK) {
     for (int e = tid; e < GM * GK; e += 256) {
       int r = e / GK, kk = e % GK;
-      As[kk][r] = (m0 + r < rows && k0 + kk < K) ? ld(Ab + (m0 + r) * kp + k0 + kk) : 0.f;
-      Bs[kk][r] = (n0 + r < cols && k0 + kk < K) ? ld(Bb + (n0 + r) * kp + k0 + kk) : 0.f;
+      As[kk][r] = (m0 + r < rows && k0 + kk < K) ? ld(Ab + (m0 + r) * C * kp + k0 + kk) : 0.f;
+      Bs[kk][r] = (n0 + r < cols && k0 + kk < K) ? ld(Bb + (n0 + r) * C * kp + k0 + kk) : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -140,7 +141,7 @@ __global__ void __launch_bounds__(256) k_contract(const T* __restrict__ A, const
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       int64_t nn = n0 + tn * 4 + j;
-      if (nn < cols) st(Pb + m * cp + nn, acc[i][j]);
+      if (nn < cols) st(Pb + m * C * cp + nn, acc[i][j]);
     }
   }
 }
@@ -155,11 +156,11 @@ __global__ void __launch_bounds__(256) k_center_ln(const T* __restrict__ p, T* _
   extern __shared__ float tile[];  // [C][33]
   __shared__ float mean_s[32], rstd_s[32];
   const int64_t m0 = (int64_t)blockIdx.x * 32;
-  const int64_t pitch = pair_pitch(n), plane = (M / n) * pitch;
+  const int64_t pitch = pair_pitch(n);
   for (int e = threadIdx.x; e < C * 32; e += blockDim.x) {
     int c = e / 32, r = e % 32;
     const int64_t m = m0 + r;
-    tile[c * 33 + r] = (m < M) ? ld(p + (int64_t)c * plane + (m / n) * pitch + m % n) : 0.f;
+    tile[c * 33 + r] = (m < M) ? ld(p + ((m / n) * C + c) * pitch + m % n) : 0.f;
   }
   __syncthreads();
   if (threadIdx.x < 32) {

@@ -3,7 +3,7 @@
 //
 // Persistent, one CTA (4 warps) per SM, one 128-position tile (pair row r,
 // columns s0..s0+127) per iteration.  TMA brings the raw z tile (128B swizzle)
-// and the channel-major P tile ([128 channels][128 positions], no swizzle).
+// and the P tile ([128 channels][128 positions] of one pair row, no swizzle).
 // Each thread layer-norms its z row in place (A1) and normalises its
 // position's 128 channels of P across the channel axis (center_norm, dim=-3)
 // into the K-major A2 tile.  Two tcgen05 GEMMs against the resident gating and
@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(128, 1) k_trimul_output_tc(const __grid_consta
       tc::mbar_expect_tx(ldbar, 2 * A_BYTES);
       tc::tma_load_3d(smem + OFF_A1, &tmZ, ldbar, 0, (int)s0, (int)r);
       tc::tma_load_3d(smem + OFF_A1 + ATOM, &tmZ, ldbar, 64, (int)s0, (int)r);
-      tc::tma_load_3d(smem + OFF_P, &tmP, ldbar, (int)s0, (int)r, 0);
+      tc::tma_load_3d(smem + OFF_P, &tmP, ldbar, (int)s0, 0, (int)r);
     }
     tc::mbar_wait(ldbar, it & 1, p.status, aborted);
     ln_row_inplace(smem + OFF_A1, tid, p.ln_w, p.ln_b, 1e-5f);
@@ -168,9 +168,10 @@ int trimul_output_tc(const bf16* z, const bf16* P, int64_t rows, int64_t n, cons
     auto encode = tensor_map_encoder();
     if (!encode) return SF_ERR_CUDA;
     const int64_t pitch = pair_pitch(n);
-    cuuint64_t dims[3] = {(cuuint64_t)pitch, (cuuint64_t)rows, (cuuint64_t)C};
-    cuuint64_t strides[2] = {(cuuint64_t)pitch * 2, (cuuint64_t)(rows * pitch * 2)};
-    cuuint32_t box[3] = {(cuuint32_t)TILE, 1, (cuuint32_t)C};
+    // P is [rows][C][pitch]: box = 128 positions x all 128 channels of one pair row
+    cuuint64_t dims[3] = {(cuuint64_t)pitch, (cuuint64_t)C, (cuuint64_t)rows};
+    cuuint64_t strides[2] = {(cuuint64_t)pitch * 2, (cuuint64_t)(C * pitch * 2)};
+    cuuint32_t box[3] = {(cuuint32_t)TILE, (cuuint32_t)C, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = encode(&mp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16*>(P), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -6,7 +6,7 @@
 // issues 16 tcgen05.mma (M=128, N=2x256, K=128) against the GLU weight kept
 // resident in shared memory, and the epilogue reads the 512 fp32 TMEM columns
 // per row, applies sigmoid(gate) * value * mask and writes the contraction
-// operands channel-major.  The next tile's TMA is issued before the current
+// operands as [row][channel][pitch].  The next tile's TMA is issued before the current
 // tile is processed (two A stages).
 #include "sf_pair_tc.cuh"
 
@@ -76,9 +76,9 @@ __global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_const
 
   constexpr uint32_t IDESC = tc::idesc_bf16(128, 256);
   const uint32_t a_base = tc::smem_u32(A), w_base = tc::smem_u32(W);
-  // operand planes: outgoing [rows][pitch(n)], incoming (transposed) [n][pitch(rows)]
+  // operands are [row][channel][pitch]: outgoing rows = pair rows r, columns s;
+  // incoming (transposed) rows = pair columns s, columns = local pair rows r
   const int64_t pitch = pair_pitch(p.incoming ? p.rows : p.n);
-  const int64_t plane = (p.incoming ? p.n : p.rows) * pitch;
 
   int64_t tile = blockIdx.x;
   if (tid == 0 && tile < ntiles) issue(tile, 0);
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_const
     const int64_t r = p.incoming ? minor : major;     // local pair row
     const int64_t s = p.incoming ? major : minor;     // pair column
     const bool keep = valid && p.mask[p.row_offset + r] && p.mask[s];
-    const int64_t pos = p.incoming ? s * pitch + r : r * pitch + s;
+    const int64_t base = p.incoming ? s * C * pitch + r : r * C * pitch + s;
     bf16* ao = p.incoming ? p.b_op : p.a_op;          // incoming: A <- b, B <- a (transposed)
     bf16* bo = p.incoming ? p.a_op : p.b_op;
     const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_const
       if (valid) {
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const int64_t off = (int64_t)(16 * j + e) * plane + pos;
+          const int64_t off = base + (int64_t)(16 * j + e) * pitch;
           ao[off] = __float2bfloat16_rn(keep ? fast_sigmoid(ga[e]) * va[e] : 0.f);
           bo[off] = __float2bfloat16_rn(keep ? fast_sigmoid(gb[e]) * vb[e] : 0.f);
         }

@@ -419,17 +419,20 @@ class MSAAttentionB200(B200Module):
     # the reference forms the key bias in bf16 (blocks.py:166-167)
     kbias = (1e9 * (mask.to(torch.bfloat16).amax(0) - 1.0)).float()
     kp = ops.pitch(n_)
-    w = torch.zeros(h, nq, kp, dtype=dt, device=act.device)
-    ops.softmax_rows(logits.reshape(h * nq, n_), kbias, out=w, ldy=kp)
+    # contraction operands are [row][channel = head][k]: w [q][h][k], vt [(m,d)][h][k]
+    wsm = torch.empty(h, nq, n_, dtype=dt, device=act.device)
+    ops.softmax_rows(logits.reshape(h * nq, n_), kbias, out=wsm)
+    w = torch.zeros(nq, h, kp, dtype=dt, device=act.device)
+    ops.transpose_(wsm, w, h, nq, 1, n_, nq * n_, n_, n_, kp, h * kp, 1)           # [h][q][k] -> [q][h][k]
     v = ops.linear(x, self._packed("v", dt))                                         # [M, N, H*D]
-    vt = torch.zeros(h, m_ * d, kp, dtype=dt, device=act.device)
-    # v[m][k][h][d] -> vt[h][m][d][k]
-    ops.transpose_(v, vt, m_, h, n_, d, n_ * h * d, d, h * d, d * kp, m_ * d * kp, kp)
-    pavg = ops.contract(vt, w, h, m_ * d, nq, n_)                                    # [H][M*D][pitch(q)]
+    vt = torch.zeros(m_ * d, h, kp, dtype=dt, device=act.device)
+    # v[m][k][h][d] -> vt[(m, d)][h][k]
+    ops.transpose_(v, vt, m_, h, n_, d, n_ * h * d, d, h * d, d * h * kp, kp, h * kp)
+    pavg = ops.contract(vt, w, h, m_ * d, nq, n_)                                    # [(m,d)][h][pitch(q)]
     qp = pavg.shape[-1]
     avg = torch.empty(m_, nq, h * d, dtype=dt, device=act.device)
-    # pavg[h][m][d][q] -> avg[m][q][h][d]
-    ops.transpose_(pavg, avg, h, m_, d, nq, m_ * d * qp, d * qp, qp, d, nq * h * d, h * d)
+    # pavg[m][d][h][q] -> avg[m][q][h][d]
+    ops.transpose_(pavg, avg, m_, h, d, nq, d * h * qp, qp, h * qp, nq * h * d, d, h * d)
     gate = ops.linear(x, self._packed("gate", dt), post_op="sigmoid")
     return ops.linear(ops.gated_residual(None, avg, gate), self._packed("out", dt))
 
@@ -462,7 +465,7 @@ class OuterProductMeanB200(B200Module):
     left = ops.mask_rows_(ops.linear(x, self._packed("left", dt)), mask)     # [M, N, 32]
     right = ops.mask_rows_(ops.linear(x, self._packed("right", dt)), mask)
     mp = ops.pitch(m_)
-    lt = torch.zeros(n_ * d, mp, dtype=dt, device=act.device)
+    lt = torch.zeros(n_ * d, mp, dtype=dt, device=act.device)     # [(i,a)][1 channel][m]
     rt = torch.zeros(n_ * d, mp, dtype=dt, device=act.device)
     ops.transpose_(left, lt, 1, 1, m_, n_ * d, 0, 0, n_ * d, 0, 0, mp)        # [M][(i,a)] -> [(i,a)][M]
     ops.transpose_(right, rt, 1, 1, m_, n_ * d, 0, 0, n_ * d, 0, 0, mp)

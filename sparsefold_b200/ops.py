@@ -147,7 +147,7 @@ def tri_mult(z: torch.Tensor, mask_u8_: torch.Tensor, w: N.TriMultWeights, incom
   dt = _dt(z)
   lib = N.load()
   pitch = lib.sf_pair_pitch(n)
-  a_op = torch.empty(c, n, pitch, dtype=z.dtype, device=z.device)
+  a_op = torch.empty(n, c, pitch, dtype=z.dtype, device=z.device)     # [row][channel][pitch]
   b_op = torch.empty_like(a_op)
   p = torch.empty_like(a_op)
   ws = _ws(max(lib.sf_tri_mult_project_workspace(dt, n), lib.sf_tri_mult_output_workspace(dt, n, n)), z.device)
@@ -273,9 +273,9 @@ def pitch(n: int) -> int:
 
 
 def contract(a_op: torch.Tensor, b_op: torch.Tensor, channels: int, rows: int, cols: int, kdim: int) -> torch.Tensor:
-  """P[c][i][j] = sum_k A[c][i][k] B[c][j][k]; A [c][rows][pitch(k)], B [c][cols][pitch(k)] -> [c][rows][pitch(cols)]."""
+  """P[i][c][j] = sum_k A[i][c][k] B[j][c][k]; A [rows][c][pitch(k)], B [cols][c][pitch(k)] -> [rows][c][pitch(cols)]."""
   _cuda(a_op, b_op)
-  p = torch.empty(channels, rows, pitch(cols), dtype=a_op.dtype, device=a_op.device)
+  p = torch.empty(rows, channels, pitch(cols), dtype=a_op.dtype, device=a_op.device)
   N.call("sf_tri_mult_contract", _dt(a_op), _p(a_op), _p(b_op), _p(p), channels, rows, cols, kdim, _stream())
   return p
 
