@@ -151,6 +151,42 @@ int sf_tri_attention(int dtype, const void* z, const uint8_t* mask, int64_t n, i
                      void* ws, size_t ws_bytes, sf_stream_t stream);
 size_t sf_tri_attention_workspace(int dtype, int64_t n, int64_t heads);
 
+/* ---- phases of the row-sharded pair track (bf16) --------------------------
+ * The pair tensor is split by rows over P ranks (runtime/dist.py:173-235); each
+ * rank owns `rows` pair rows starting at global row `row_offset`, all n columns.
+ * The collectives between phases mirror the reference's choreography
+ * (blocks.py:541-555, :320-346) and run in NCCL through the host.            */
+/* Tri-mult projection of a row shard.  Outgoing: A, B are [rows][C][pitch(n)].
+ * Incoming: A = b^T, B = a^T are [n][C][pitch(rows)] (send buffers of the
+ * all-to-all / all-gather that assemble the K axis across ranks). */
+int sf_tri_mult_project_rows(int dtype, const void* z, const uint8_t* mask, int64_t rows, int64_t n,
+                             int64_t row_offset, int incoming, const sf_tri_mult_weights* w,
+                             void* a_op, void* b_op, sf_stream_t stream);
+/* P[i][c][j] = sum_k A[i][c][k] B[j][c][k] where each operand may hold K in
+ * `chunks` equal pieces laid out [chunk][row][C][pitch(kdim/chunks)] (one per
+ * source rank); chunk lengths must be multiples of 64 when chunks > 1. */
+int sf_tri_mult_contract_chunked(int dtype, const void* a_op, int64_t chunks_a, const void* b_op,
+                                 int64_t chunks_b, void* p, int64_t channels, int64_t rows, int64_t cols,
+                                 int64_t kdim, sf_stream_t stream);
+/* Query pitch qp of the attention buffers: Q, K, Vt [nb][4][qp][32],
+ * G [nb][qp][128], bias [qp][4][qp] (bias[q][h][k], rows gathered across ranks). */
+int64_t sf_tri_attention_query_pitch(int64_t nq);
+/* Pair bias of the local rows: bias[(r*4 + h)*ldb + s] = LN(z[r,s]) . W_b[h] (blocks.py:317-320). */
+int sf_tri_attention_bias(int dtype, const void* z, int64_t rows, int64_t n, const sf_tri_attention_weights* w,
+                          void* bias, int64_t ldb, sf_stream_t stream);
+/* LN + q/k/v/gate projections of a z block [rows][cols]; transpose = attention
+ * along columns (ending node).  With compute_bias the block's own positions
+ * write the bias rows. */
+int sf_tri_attention_project(int dtype, const void* z, int64_t rows, int64_t cols, int transpose,
+                             int compute_bias, const sf_tri_attention_weights* w, void* q, void* k,
+                             void* vt, void* g, void* bias, sf_stream_t stream);
+/* Attention + gate + output projection + residual on the z block; batch_offset
+ * is the global token index of the block's first attention row (row mask). */
+int sf_tri_attention_core(int dtype, const void* q, const void* k, const void* vt, const void* g,
+                          const void* bias, const uint8_t* mask, const void* z, void* z_out, int64_t rows,
+                          int64_t cols, int transpose, int64_t batch_offset,
+                          const sf_tri_attention_weights* w, sf_stream_t stream);
+
 /* ---- TransitionBlock (blocks.py:79-96): y = x + swish(LN(x) W1a) * (LN(x) W1b) W2
  * w1: [2I][C] (first I rows = swish half), w2: [C][I]; y may alias x.        */
 int sf_transition(int dtype, const void* x, const float* ln_w, const float* ln_b,

@@ -84,6 +84,15 @@ _SIGNATURES = {
     "sf_opm_norm_workspace": (C.c_size_t, [_i64, _i64]),
     "sf_opm_repack": (C.c_int, [C.c_int, _vp, _i64, _i64, _i64, _vp, _vp]),
     "sf_scale_rows": (C.c_int, [C.c_int, _vp, _vp, _i64, _i64, _vp]),
+    "sf_tri_mult_project_rows": (C.c_int, [C.c_int, _vp, _vp, _i64, _i64, _i64, C.c_int, C.POINTER(TriMultWeights),
+                                           _vp, _vp, _vp]),
+    "sf_tri_mult_contract_chunked": (C.c_int, [C.c_int, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),
+    "sf_tri_attention_query_pitch": (C.c_int64, [_i64]),
+    "sf_tri_attention_bias": (C.c_int, [C.c_int, _vp, _i64, _i64, C.POINTER(TriAttentionWeights), _vp, _i64, _vp]),
+    "sf_tri_attention_project": (C.c_int, [C.c_int, _vp, _i64, _i64, C.c_int, C.c_int, C.POINTER(TriAttentionWeights),
+                                           _vp, _vp, _vp, _vp, _vp, _vp]),
+    "sf_tri_attention_core": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, C.c_int, _i64,
+                                        C.POINTER(TriAttentionWeights), _vp]),
 }
 
 _lib = None

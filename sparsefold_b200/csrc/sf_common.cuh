@@ -60,6 +60,17 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 EncodeTiledFn tensor_map_encoder();
 int make_pair_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t n, bool column_tile);
 size_t triatt_tc_workspace(int64_t n);
+int64_t triatt_query_pitch(int64_t nq);
+int triatt_bias_tc(const bf16* z, int64_t rows, int64_t n, const float* ln_w, const bf16* w_bias, bf16* bias,
+                   int64_t ldb, cudaStream_t stream);
+int triatt_project_tc(const bf16* z, int64_t rows, int64_t cols, int transpose, int compute_bias, const float* ln_w,
+                      const bf16* w_qkvg, const bf16* w_bias, bf16* q, bf16* k, bf16* vt, bf16* g, bf16* bias,
+                      cudaStream_t stream);
+int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, const bf16* bias, const bf16* w_out,
+                   const uint8_t* mask, const bf16* z, bf16* z_out, int64_t rows, int64_t cols, int transpose,
+                   int64_t batch_offset, cudaStream_t stream);
+int contract_chunked_tc(const bf16* a_op, int64_t chunks_a, const bf16* b_op, int64_t chunks_b, bf16* P,
+                        int64_t channels, int64_t rows, int64_t cols, int64_t kdim, cudaStream_t stream);
 int triatt_tc(const bf16* z, const uint8_t* mask, int64_t n, int transpose, const float* ln_w, const bf16* w_qkvg,
               const bf16* w_bias, const bf16* w_out, bf16* z_out, void* ws_p, size_t ws_bytes, cudaStream_t stream);
 int make_2d_tmap(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, uint32_t box_inner,

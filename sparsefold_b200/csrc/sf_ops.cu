@@ -275,6 +275,64 @@ extern "C" {
 
 int64_t sf_pair_pitch(int64_t n) { return pair_pitch(n); }
 
+// ---- phases of the row-sharded path (bf16 only) ---------------------------------
+#define SF_REQUIRE_BF16(dtype, what) SF_REQUIRE((dtype) == SF_BF16, what ": the sharded path is bf16 only")
+
+int sf_tri_mult_project_rows(int dtype, const void* z, const uint8_t* mask, int64_t rows, int64_t n,
+                             int64_t row_offset, int incoming, const sf_tri_mult_weights* w, void* a_op, void* b_op,
+                             sf_stream_t stream) {
+  SF_REQUIRE_BF16(dtype, "sf_tri_mult_project_rows");
+  SF_REQUIRE(z && mask && w && a_op && b_op && rows >= 0 && n > 0 && row_offset >= 0,
+             "sf_tri_mult_project_rows: bad arguments");
+  const int64_t pitch = pair_pitch(incoming ? rows : n), nrow = incoming ? n : rows;
+  if (pitch != (incoming ? rows : n)) {
+    const size_t bytes = (size_t)nrow * 128 * pitch * 2;
+    if (cudaMemsetAsync(a_op, 0, bytes, stream) != cudaSuccess || cudaMemsetAsync(b_op, 0, bytes, stream) != cudaSuccess)
+      return check_launch("sf_tri_mult_project_rows.memset");
+  }
+  return trimul_project_tc((const bf16*)z, mask, rows, n, row_offset, incoming, w->ln_w, w->ln_b,
+                           (const bf16*)w->w_glu, (bf16*)a_op, (bf16*)b_op, stream);
+}
+
+int sf_tri_mult_contract_chunked(int dtype, const void* a_op, int64_t chunks_a, const void* b_op, int64_t chunks_b,
+                                 void* p, int64_t channels, int64_t rows, int64_t cols, int64_t kdim,
+                                 sf_stream_t stream) {
+  SF_REQUIRE_BF16(dtype, "sf_tri_mult_contract_chunked");
+  SF_REQUIRE(a_op && b_op && p && channels > 0 && rows >= 0 && cols >= 0 && kdim > 0,
+             "sf_tri_mult_contract_chunked: bad arguments");
+  return contract_chunked_tc((const bf16*)a_op, chunks_a, (const bf16*)b_op, chunks_b, (bf16*)p, channels, rows, cols,
+                             kdim, stream);
+}
+
+int64_t sf_tri_attention_query_pitch(int64_t nq) { return triatt_query_pitch(nq); }
+
+int sf_tri_attention_bias(int dtype, const void* z, int64_t rows, int64_t n, const sf_tri_attention_weights* w,
+                          void* bias, int64_t ldb, sf_stream_t stream) {
+  SF_REQUIRE_BF16(dtype, "sf_tri_attention_bias");
+  SF_REQUIRE(z && w && bias && w->heads == 4, "sf_tri_attention_bias: bad arguments");
+  return triatt_bias_tc((const bf16*)z, rows, n, w->ln_w, (const bf16*)w->w_bias, (bf16*)bias, ldb, stream);
+}
+
+int sf_tri_attention_project(int dtype, const void* z, int64_t rows, int64_t cols, int transpose, int compute_bias,
+                             const sf_tri_attention_weights* w, void* q, void* k, void* vt, void* g, void* bias,
+                             sf_stream_t stream) {
+  SF_REQUIRE_BF16(dtype, "sf_tri_attention_project");
+  SF_REQUIRE(z && w && q && k && vt && g && (bias || !compute_bias) && w->heads == 4,
+             "sf_tri_attention_project: bad arguments");
+  return triatt_project_tc((const bf16*)z, rows, cols, transpose, compute_bias, w->ln_w, (const bf16*)w->w_qkvg,
+                           (const bf16*)w->w_bias, (bf16*)q, (bf16*)k, (bf16*)vt, (bf16*)g, (bf16*)bias, stream);
+}
+
+int sf_tri_attention_core(int dtype, const void* q, const void* k, const void* vt, const void* g, const void* bias,
+                          const uint8_t* mask, const void* z, void* z_out, int64_t rows, int64_t cols, int transpose,
+                          int64_t batch_offset, const sf_tri_attention_weights* w, sf_stream_t stream) {
+  SF_REQUIRE_BF16(dtype, "sf_tri_attention_core");
+  SF_REQUIRE(q && k && vt && g && bias && mask && z && z_out && w && w->heads == 4, "sf_tri_attention_core: bad arguments");
+  return triatt_core_tc((const bf16*)q, (const bf16*)k, (const bf16*)vt, (const bf16*)g, (const bf16*)bias,
+                        (const bf16*)w->w_out, mask, (const bf16*)z, (bf16*)z_out, rows, cols, transpose, batch_offset,
+                        stream);
+}
+
 // ---------------------------------------------------------------------------
 int sf_layernorm(int dtype, const void* x, void* y, const float* weight, const float* bias,
                  int64_t rows, int64_t cols, float eps, sf_stream_t stream) {
@@ -405,14 +463,14 @@ int sf_tri_mult_output(int dtype, const void* z, const void* p, int64_t rows, in
   SF_REQUIRE(z && p && w && z_out && rows >= 0 && n > 0, "sf_tri_mult_output: bad arguments");
   SF_REQUIRE(w->center_w && w->center_b && w->w_out && w->w_gate && w->ln_w && w->ln_b,
              "sf_tri_mult_output: missing weights");
+  if (rows == 0) return SF_OK;
+  if (dtype == SF_BF16)   // the tcgen05 path needs no workspace
+    return trimul_output_tc((const bf16*)z, (const bf16*)p, rows, n, w->ln_w, w->ln_b, w->center_w, w->center_b,
+                            (const bf16*)w->w_gate, (const bf16*)w->w_out, (bf16*)z_out, stream);
   if (ws_bytes < sf_tri_mult_output_workspace(dtype, rows, n)) {
     set_error("sf_tri_mult_output: workspace too small");
     return SF_ERR_WORKSPACE;
   }
-  if (rows == 0) return SF_OK;
-  if (dtype == SF_BF16)
-    return trimul_output_tc((const bf16*)z, (const bf16*)p, rows, n, w->ln_w, w->ln_b, w->center_w, w->center_b,
-                            (const bf16*)w->w_gate, (const bf16*)w->w_out, (bf16*)z_out, stream);
   SF_DISPATCH(dtype, {
     Workspace ws(ws_p, ws_bytes);
     const int64_t M = rows * n;

@@ -18,7 +18,8 @@
 //
 // Intermediate layouts (qp = n rounded up to 128; padded query rows are zero):
 //   Q, K  [b][h][qp][32]    Vt [b][h][32][qp]    G = sigmoid(gate) [b][qp][128]
-//   bias  [h][qp][qp] (bias[h][q][k] = LN(z)[q,k] . W_b[h], untransposed)
+//   bias  [q][h][qp] (bias[q][h][k] = LN(z)[q,k] . W_b[h], untransposed; rows q all-gathered
+//         from the row shards when the pair tensor is distributed)
 #include <cfloat>
 
 #include "sf_pair_tc.cuh"
@@ -35,8 +36,10 @@ struct AttProjParams {
   const bf16* w_qkvg;     // [512][128]
   const bf16* w_bias;     // [4][128]
   bf16 *q, *k, *vt, *g, *bias;
-  int64_t n, qp;
-  int transpose;
+  int64_t rows, cols;     // the z block [rows][cols][128]
+  int64_t nb, nq, qp;     // attention rows (batches), queries = keys, query pitch
+  int transpose;          // attention along columns: batch = column, query = row
+  int compute_bias;       // write bias[(r*H + h)*qp + s] for the block's positions (r, s)
   uint32_t* status;
 };
 
@@ -115,7 +118,7 @@ __global__ void __launch_bounds__(128, 1) k_triatt_project_tc(const __grid_const
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
   const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t nqb = p.qp / TILE;
-  const int64_t ntiles = p.n * nqb;
+  const int64_t ntiles = p.nb * nqb;
 
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
@@ -158,13 +161,13 @@ __global__ void __launch_bounds__(128, 1) k_triatt_project_tc(const __grid_const
     }
     tc::mbar_wait(&bars[stage], (it >> 1) & 1, p.status, aborted);
     const int64_t b = tile / nqb, qi = (tile % nqb) * TILE + tid;
-    const bool valid = qi < p.n;
+    const bool valid = qi < p.nq;
     float bias[H];
     ln_row_bias(A + stage * A_BYTES, tid, p.ln_w, p.w_bias, bias);
-    if (valid) {
+    if (valid && p.compute_bias) {
       const int64_t r = p.transpose ? qi : b, s = p.transpose ? b : qi;
 #pragma unroll
-      for (int h = 0; h < H; ++h) p.bias[(h * p.qp + r) * p.qp + s] = __float2bfloat16_rn(bias[h]);
+      for (int h = 0; h < H; ++h) p.bias[(r * H + h) * p.qp + s] = __float2bfloat16_rn(bias[h]);
     }
     tc::fence_proxy_async();
     tc::tc_fence_before();
@@ -231,10 +234,12 @@ __global__ void __launch_bounds__(128, 1) k_triatt_project_tc(const __grid_const
 struct AttCoreParams {
   const bf16 *q, *k, *vt, *g, *bias;
   const bf16* w_out;      // output_projection^T [128 out][128 in]
-  const uint8_t* mask;    // [n]
-  const bf16* z;
+  const uint8_t* mask;    // [N] token mask (keys/queries are all N tokens)
+  const bf16* z;          // the z block [rows][cols][128] (residual)
   bf16* z_out;
-  int64_t n, qp;
+  int64_t cols;           // columns of the z block
+  int64_t nq, qp;         // queries = keys, pitch
+  int64_t batch_offset;   // global token index of attention row 0 (row mask)
   int transpose;
   float scale_log2;       // (1/sqrt(D)) * log2(e)
   uint32_t* status;
@@ -301,12 +306,12 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
   // key k is attended iff mask[b] && mask[k] (pair mask, blocks.py:314)
   uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
   {
-    const bool rok = p.mask[b] != 0;
+    const bool rok = p.mask[b + p.batch_offset] != 0;
     for (int w = tid; w < (int)(p.qp / 32); w += 256) {
       uint32_t bits = 0;
       for (int e = 0; e < 32; ++e) {
         const int64_t key = (int64_t)w * 32 + e;
-        if (rok && key < p.n && p.mask[key]) bits |= 1u << e;
+        if (rok && key < p.nq && p.mask[key]) bits |= 1u << e;
       }
       kbits[w] = bits;
     }
@@ -362,7 +367,7 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
       tc::mma_commit(&sdone[g]);
     }
     // bias row of this key block, fetched while the S MMA runs
-    const uint4* brow = reinterpret_cast<const uint4*>(p.bias + ((int64_t)h * p.qp + q) * p.qp + (int64_t)kb * KB);
+    const uint4* brow = reinterpret_cast<const uint4*>(p.bias + (q * H + h) * p.qp + (int64_t)kb * KB);
     uint4 bias_raw[KB / 8];
 #pragma unroll
     for (int c = 0; c < KB / 8; ++c) bias_raw[c] = __ldg(brow + c);
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
         const int64_t key = (int64_t)kb * KB + kidx;
         const float bv = (e & 1) ? bf_hi(bu[e >> 1]) : bf_lo(bu[e >> 1]);
         float x = sv[kidx] * p.scale_log2 + bv * kLog2e;
-        if (key >= p.n) x = -INFINITY;                 // padding beyond the N keys: excluded
+        if (key >= p.nq) x = -INFINITY;                // padding beyond the N keys: excluded
         else if (!((vbits >> kidx) & 1)) x = -FLT_MAX;   // masked key: the reference's -finfo.max bias
         sv[kidx] = x;
         mx = fmaxf(mx, x);
@@ -481,8 +486,8 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
   tc::mbar_wait(outdone, 0, p.status, aborted);
   tc::tc_fence_after();
   {
-    const bool live = q < p.n;
-    const int64_t pos = live ? (p.transpose ? q * p.n + b : b * p.n + q) : 0;
+    const bool live = q < p.nq;
+    const int64_t pos = live ? (p.transpose ? q * p.cols + b : b * p.cols + q) : 0;
     const uint4* zin = reinterpret_cast<const uint4*>(p.z + pos * C + g * 64);
     uint4* zo = reinterpret_cast<uint4*>(p.z_out + pos * C + g * 64);
 #pragma unroll
@@ -525,54 +530,123 @@ int set_smem(K kernel, int bytes, bool* done) {
   return SF_OK;
 }
 
+// Pair bias of the local pair rows only: bias[(r*H + h)*ldb + s] = LN(z[r,s]) . W_b[h]
+// (blocks.py:317-320), one warp per position.  Used when the attention runs on a
+// transposed block whose own positions are not the rows the bias needs.
+__global__ void k_triatt_bias(const bf16* __restrict__ z, const float* __restrict__ ln_w, const bf16* __restrict__ wb,
+                              bf16* __restrict__ bias, int64_t rows, int64_t n, int64_t ldb) {
+  const int64_t pos = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (pos >= rows * n) return;
+  const bf16* zr = z + pos * C;
+  float x[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) x[e] = __bfloat162float(zr[lane * 4 + e]);
+  const float mean = warp_sum(x[0] + x[1] + x[2] + x[3]) * (1.0f / C);
+  float v = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) v += (x[e] - mean) * (x[e] - mean);
+  const float rstd = rsqrtf(warp_sum(v) * (1.0f / C) + 1e-5f);
+  float acc[H] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int c = lane * 4 + e;
+    const float y = __bfloat162float(__float2bfloat16_rn((x[e] - mean) * rstd * ln_w[c]));
+#pragma unroll
+    for (int h = 0; h < H; ++h) acc[h] += y * __bfloat162float(wb[h * C + c]);
+  }
+#pragma unroll
+  for (int h = 0; h < H; ++h) acc[h] = warp_sum(acc[h]);
+  if (lane == 0) {
+    const int64_t r = pos / n, sc = pos % n;
+#pragma unroll
+    for (int h = 0; h < H; ++h) bias[(r * H + h) * ldb + sc] = __float2bfloat16_rn(acc[h]);
+  }
+}
+
 }  // namespace
 
+int64_t triatt_query_pitch(int64_t nq) { return (nq + 127) / 128 * 128; }
+
+int triatt_bias_tc(const bf16* z, int64_t rows, int64_t n, const float* ln_w, const bf16* w_bias, bf16* bias,
+                   int64_t ldb, cudaStream_t stream) {
+  if (rows == 0 || n == 0) return SF_OK;
+  SF_REQUIRE(ldb >= n, "triatt_bias: ldb %lld < n %lld", (long long)ldb, (long long)n);
+  const int64_t total = rows * n;
+  k_triatt_bias<<<(unsigned)((total + 7) / 8), 256, 0, stream>>>(z, ln_w, w_bias, bias, rows, n, ldb);
+  count_launch();
+  return check_launch("triatt_bias");
+}
+
+int triatt_project_tc(const bf16* z, int64_t rows, int64_t cols, int transpose, int compute_bias, const float* ln_w,
+                      const bf16* w_qkvg, const bf16* w_bias, bf16* q, bf16* k, bf16* vt, bf16* g, bf16* bias,
+                      cudaStream_t stream) {
+  if (rows == 0 || cols == 0) return SF_OK;
+  const int64_t nb = transpose ? cols : rows, nq = transpose ? rows : cols;
+  SF_REQUIRE(nb <= 65535 && nq <= 65535, "triatt_project: block [%lld][%lld] too large", (long long)rows,
+             (long long)cols);
+  uint32_t* status = device_status_ptr();
+  if (!status) return SF_ERR_CUDA;
+  static bool attr[64] = {false};
+  SF_TRY(set_smem(k_triatt_project_tc, SMEM_PROJ, attr));
+  CUtensorMap map;
+  SF_TRY(make_pair_tmap(&map, z, rows, cols, transpose != 0));
+  const int64_t qp = triatt_query_pitch(nq);
+  AttProjParams pp{ln_w, w_qkvg, w_bias, q, k, vt, g, bias, rows, cols, nb, nq, qp, transpose, compute_bias, status};
+  const int64_t ntiles = nb * (qp / TILE);
+  const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
+  k_triatt_project_tc<<<grid, 128, SMEM_PROJ, stream>>>(map, pp);
+  count_launch();
+  return check_launch("triatt_project_tc");
+}
+
+int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, const bf16* bias, const bf16* w_out,
+                   const uint8_t* mask, const bf16* z, bf16* z_out, int64_t rows, int64_t cols, int transpose,
+                   int64_t batch_offset, cudaStream_t stream) {
+  if (rows == 0 || cols == 0) return SF_OK;
+  const int64_t nb = transpose ? cols : rows, nq = transpose ? rows : cols;
+  SF_REQUIRE(nb <= 65535 && nq <= 65535, "triatt_core: block too large");
+  uint32_t* status = device_status_ptr();
+  if (!status) return SF_ERR_CUDA;
+  static bool attr[64] = {false};
+  SF_TRY(set_smem(k_triatt_core_tc, SMEM_CORE, attr));
+  const int64_t qp = triatt_query_pitch(nq);
+  AttCoreParams cp{q, k, vt, g, bias, w_out, mask, z, z_out, cols, nq, qp, batch_offset, transpose,
+                   (1.0f / sqrtf((float)D)) * kLog2e, status};
+  dim3 cgrid((unsigned)(qp / TILE), (unsigned)nb);
+  k_triatt_core_tc<<<cgrid, 256, SMEM_CORE, stream>>>(cp);
+  count_launch();
+  return check_launch("triatt_core_tc");
+}
+
+// Buffer sizes of one attention call: Q, K, Vt [nb][H][qp][32], G [nb][qp][128], bias [qp][H][qp].
 size_t triatt_tc_workspace(int64_t n) {
-  const int64_t qp = (n + 127) / 128 * 128;
-  const size_t per = (size_t)n * H * qp * D * 2;   // Q, K, Vt
+  const int64_t qp = triatt_query_pitch(n);
+  const size_t per = (size_t)n * H * qp * D * 2;
   size_t used = 0;
   for (int i = 0; i < 3; ++i) used = align_up(used, 256) + per;
-  used = align_up(used, 256) + (size_t)n * qp * C * 2;        // G
-  used = align_up(used, 256) + (size_t)H * qp * qp * 2;       // bias
+  used = align_up(used, 256) + (size_t)n * qp * C * 2;
+  used = align_up(used, 256) + (size_t)qp * H * qp * 2;
   return used;
 }
 
+// The whole op on one device (the z block is the full [n][n] pair tensor).
 int triatt_tc(const bf16* z, const uint8_t* mask, int64_t n, int transpose, const float* ln_w, const bf16* w_qkvg,
               const bf16* w_bias, const bf16* w_out, bf16* z_out, void* ws_p, size_t ws_bytes, cudaStream_t stream) {
   if (n == 0) return SF_OK;
-  SF_REQUIRE(n <= 65535, "triatt_tc: n=%lld too large", (long long)n);
   if (ws_bytes < triatt_tc_workspace(n)) {
     set_error("sf_tri_attention: workspace %zu < %zu", ws_bytes, triatt_tc_workspace(n));
     return SF_ERR_WORKSPACE;
   }
-  const int64_t qp = (n + 127) / 128 * 128;
+  const int64_t qp = triatt_query_pitch(n);
   Workspace ws(ws_p, ws_bytes);
   bf16* q = ws.take<bf16>((size_t)n * H * qp * D);
   bf16* k = ws.take<bf16>((size_t)n * H * qp * D);
   bf16* vt = ws.take<bf16>((size_t)n * H * qp * D);
   bf16* g = ws.take<bf16>((size_t)n * qp * C);
-  bf16* bias = ws.take<bf16>((size_t)H * qp * qp);
-  uint32_t* status = device_status_ptr();
-  if (!status) return SF_ERR_CUDA;
-  static bool proj_attr[64] = {false}, core_attr[64] = {false};
-  SF_TRY(set_smem(k_triatt_project_tc, SMEM_PROJ, proj_attr));
-  SF_TRY(set_smem(k_triatt_core_tc, SMEM_CORE, core_attr));
-
-  CUtensorMap map;
-  SF_TRY(make_pair_tmap(&map, z, n, n, transpose != 0));
-  AttProjParams pp{ln_w, w_qkvg, w_bias, q, k, vt, g, bias, n, qp, transpose, status};
-  const int64_t ntiles = n * (qp / TILE);
-  const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  k_triatt_project_tc<<<grid, 128, SMEM_PROJ, stream>>>(map, pp);
-  count_launch();
-  SF_TRY(check_launch("triatt_project_tc"));
-
-  AttCoreParams cp{q, k, vt, g, bias, w_out, mask, z, z_out, n, qp, transpose, (1.0f / sqrtf((float)D)) * kLog2e,
-                   status};
-  dim3 cgrid((unsigned)(qp / TILE), (unsigned)n);
-  k_triatt_core_tc<<<cgrid, 256, SMEM_CORE, stream>>>(cp);
-  count_launch();
-  return check_launch("triatt_core_tc");
+  bf16* bias = ws.take<bf16>((size_t)qp * H * qp);
+  SF_TRY(triatt_project_tc(z, n, n, transpose, 1, ln_w, w_qkvg, w_bias, q, k, vt, g, bias, stream));
+  return triatt_core_tc(q, k, vt, g, bias, w_out, mask, z, z_out, n, n, transpose, 0, stream);
 }
 
 }  // namespace sf

@@ -1,0 +1,233 @@
+"""Row sharding of the pair tensor across the GPUs of one node.
+
+The pair tensor z [N, N, 128] is split by rows over P ranks (one process per
+GPU, torch.distributed over NCCL): rank r owns rows [offset_r, offset_r + rows_r)
+and all N columns, and the single representation rows with the same indices.
+The exchanges are the reference's (runtime/dist.py:173-577, trunk/blocks.py):
+
+* triangle multiplication, outgoing: all-gather of b (blocks.py:542-546);
+* incoming: all-gather of a and an all-to-all of b (blocks.py:547-555), which
+  here arrive as K-chunks that the contraction reads in place;
+* triangle attention: all-gather of the pair bias (blocks.py:321-325); the
+  ending node also transposes the pair tensor with an all-to-all there and back
+  (blocks.py:335-346, :363-364);
+* single attention: all-gather of k and v (diffusion/transformer.py:322-330).
+
+Every kernel runs on the rank's own shard through the phase entry points of
+``libsparsefold_b200.so``; the collectives are NCCL calls on the current stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from sparsefold_b200 import _native as N
+from sparsefold_b200 import ops
+
+
+class Shard:
+  """Row partition of a length-N axis over P ranks (runtime/dist.py:173-235).
+
+  even=True requires N % P == 0; otherwise the sizes are the rounded cumulative
+  split with the largest share moved to rank 0.
+  """
+
+  def __init__(self, length: int, num_shards: int, rank: int, even: bool = True):
+    if even and length % num_shards:
+      raise ValueError(f"even partition needs length {length} divisible by {num_shards}")
+    self.length, self.num_shards, self.rank, self.is_even = length, num_shards, rank, even
+    if even:
+      sizes = [length // num_shards] * num_shards
+    elif length <= num_shards:
+      sizes = [1] * length + [0] * (num_shards - length)
+    else:
+      sizes, off = [], 0
+      step = length / num_shards
+      for i in range(num_shards):
+        end = int(round((i + 1) * step))
+        sizes.append(end - off)
+        off = end
+      mx = int(np.argmax(sizes))
+      sizes[0], sizes[mx] = sizes[mx], sizes[0]
+    self._sizes = sizes
+    self._offsets = [0] + [int(x) for x in np.cumsum(sizes)[:-1]]
+
+  def sizes(self) -> list[int]:
+    return list(self._sizes)
+
+  def offsets(self) -> list[int]:
+    return list(self._offsets)
+
+  def size(self, rank: int | None = None) -> int:
+    return self._sizes[self.rank if rank is None else rank]
+
+  def offset(self, rank: int | None = None) -> int:
+    return self._offsets[self.rank if rank is None else rank]
+
+  def shard(self, x: torch.Tensor, dim: int = 0) -> torch.Tensor:
+    return x.narrow(dim, self.offset(), self.size())
+
+
+def world_size(group=None) -> int:
+  return dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+
+
+def all_gather_rows(x: torch.Tensor, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
+  """Concatenate every rank's x along dim 0 (equal shards)."""
+  world = world_size(group)
+  x = x.contiguous()
+  if out is None:
+    out = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+  if world == 1:
+    out.copy_(x)
+  else:
+    dist.all_gather_into_tensor(out, x, group=group)
+  return out
+
+
+def all_to_all_rows(send: torch.Tensor, group=None) -> torch.Tensor:
+  """send [P * m, ...] -> recv [P * m, ...]: block p of send goes to rank p, block p of recv came from rank p."""
+  send = send.contiguous()
+  recv = torch.empty_like(send)
+  dist.all_to_all_single(recv, send, group=group)
+  return recv
+
+
+def pair_transpose_to_columns(z_loc: torch.Tensor, shard: Shard, group=None) -> torch.Tensor:
+  """[rows_loc, N, C] (row shard) -> [N, cols_loc, C] (column shard)."""
+  p = shard.num_shards
+  r, n, c = z_loc.shape
+  send = z_loc.view(r, p, n // p, c).transpose(0, 1)             # block q: my rows x columns of rank q
+  return all_to_all_rows(send.reshape(p * r, n // p, c), group).view(n, n // p, c)
+
+
+def pair_transpose_to_rows(z_col: torch.Tensor, shard: Shard, group=None) -> torch.Tensor:
+  """[N, cols_loc, C] (column shard) -> [rows_loc, N, C] (row shard)."""
+  p = shard.num_shards
+  n, cl, c = z_col.shape
+  recv = all_to_all_rows(z_col, group).view(p, n // p, cl, c)   # block q: my rows x columns of rank q
+  return recv.transpose(0, 1).reshape(n // p, n, c)
+
+
+def _stream() -> int:
+  return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t):
+  return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# sharded ops (bf16)
+# ---------------------------------------------------------------------------
+def tri_mult(mod, z_loc: torch.Tensor, mask_u8: torch.Tensor, shard: Shard, group=None) -> torch.Tensor:
+  """TriangleMultiplication (blocks.py:484-566) on a row shard."""
+  rows, n, c = z_loc.shape
+  p = shard.num_shards
+  w = mod.native_weights(z_loc.dtype)
+  dt = N.SF_BF16
+  if not mod.incoming:
+    pitch = ops.pitch(n)
+    a_op = torch.empty(rows, c, pitch, dtype=z_loc.dtype, device=z_loc.device)
+    b_op = torch.empty_like(a_op)
+    N.call("sf_tri_mult_project_rows", dt, _p(z_loc), _p(mask_u8), rows, n, shard.offset(), 0, C.byref(w), _p(a_op),
+           _p(b_op), _stream())
+    b_full = all_gather_rows(b_op, group)                                   # [N][C][pitch]
+    chunks_a = chunks_b = 1
+  else:
+    if p > 1 and (rows % 64 or ops.pitch(rows) != rows):
+      raise ValueError(f"incoming triangle multiplication needs shard rows ({rows}) that are multiples of 64")
+    pitch = ops.pitch(rows)
+    a_send = torch.empty(n, c, pitch, dtype=z_loc.dtype, device=z_loc.device)   # b^T: [i][C][k_loc]
+    b_send = torch.empty_like(a_send)                                           # a^T: [j][C][k_loc]
+    N.call("sf_tri_mult_project_rows", dt, _p(z_loc), _p(mask_u8), rows, n, shard.offset(), 1, C.byref(w),
+           _p(a_send), _p(b_send), _stream())
+    a_op = all_to_all_rows(a_send, group) if p > 1 else a_send              # [P][i_loc][C][k_loc]
+    b_full = all_gather_rows(b_send, group) if p > 1 else b_send            # [P][N][C][k_loc]
+    chunks_a = chunks_b = p
+  prod = torch.empty(rows, c, ops.pitch(n), dtype=z_loc.dtype, device=z_loc.device)
+  N.call("sf_tri_mult_contract_chunked", dt, _p(a_op), chunks_a, _p(b_full), chunks_b, _p(prod), c, rows, n, n,
+         _stream())
+  out = torch.empty_like(z_loc)
+  N.call("sf_tri_mult_output", dt, _p(z_loc), _p(prod), rows, n, C.byref(w), _p(out), None, 0, _stream())
+  return out
+
+
+def _att_buffers(nb: int, nq: int, dtype, device):
+  qp = int(N.load().sf_tri_attention_query_pitch(nq))
+  q = torch.empty(nb, 4, qp, 32, dtype=dtype, device=device)
+  return qp, q, torch.empty_like(q), torch.empty_like(q), torch.empty(nb, qp, 128, dtype=dtype, device=device)
+
+
+def tri_attention(mod, z_loc: torch.Tensor, mask_u8: torch.Tensor, shard: Shard, group=None) -> torch.Tensor:
+  """GridSelfAttention (blocks.py:293-366) on a row shard."""
+  rows, n, c = z_loc.shape
+  w = mod.native_weights(z_loc.dtype)
+  dt = N.SF_BF16
+  qp = int(N.load().sf_tri_attention_query_pitch(n))
+  bias_full = torch.empty(qp, 4, qp, dtype=z_loc.dtype, device=z_loc.device)
+  bias_loc = torch.empty(rows, 4, qp, dtype=z_loc.dtype, device=z_loc.device)
+  if not mod.transpose:
+    _, q, k, vt, g = _att_buffers(rows, n, z_loc.dtype, z_loc.device)
+    N.call("sf_tri_attention_project", dt, _p(z_loc), rows, n, 0, 1, C.byref(w), _p(q), _p(k), _p(vt), _p(g),
+           _p(bias_loc), _stream())
+    all_gather_rows(bias_loc, group, out=bias_full[:n])
+    out = torch.empty_like(z_loc)
+    N.call("sf_tri_attention_core", dt, _p(q), _p(k), _p(vt), _p(g), _p(bias_full), _p(mask_u8), _p(z_loc), _p(out),
+           rows, n, 0, shard.offset(), C.byref(w), _stream())
+    return out
+  # ending node: the bias comes from the untransposed local rows, the attention runs on columns
+  N.call("sf_tri_attention_bias", dt, _p(z_loc), rows, n, C.byref(w), _p(bias_loc), qp, _stream())
+  all_gather_rows(bias_loc, group, out=bias_full[:n])
+  z_col = pair_transpose_to_columns(z_loc, shard, group) if shard.num_shards > 1 else z_loc
+  cols = z_col.shape[1]
+  _, q, k, vt, g = _att_buffers(cols, n, z_loc.dtype, z_loc.device)
+  N.call("sf_tri_attention_project", dt, _p(z_col), n, cols, 1, 0, C.byref(w), _p(q), _p(k), _p(vt), _p(g), None,
+         _stream())
+  out_col = torch.empty_like(z_col)
+  N.call("sf_tri_attention_core", dt, _p(q), _p(k), _p(vt), _p(g), _p(bias_full), _p(mask_u8), _p(z_col),
+         _p(out_col), n, cols, 1, shard.offset(), C.byref(w), _stream())
+  return pair_transpose_to_rows(out_col, shard, group) if shard.num_shards > 1 else out_col
+
+
+def single_update(mod, z_loc: torch.Tensor, s_loc: torch.Tensor, mask: torch.Tensor, shard: Shard,
+                  group=None) -> torch.Tensor:
+  """SingleActUpdate (blocks.py:739-763) on a row shard: k and v are all-gathered (transformer.py:322-330)."""
+  dt = z_loc.dtype
+  heads = mod.single_pair_logits_projection.output_shape[0]
+  logits = ops.pair_logits(z_loc.contiguous(), mod._kept("ln_w"), mod._kept("ln_b"), mod._packed("logits", dt), heads)
+  att = mod.single_attention
+  h, d = att._hd
+  xn = ops.layer_norm(s_loc, att._kept("ln_ln_w"), att._kept("ln_ln_b"))
+  y = ops.linear(xn, att._packed("qkvg", dt), bias=att._kept("qkvg_bias"))     # [rows, 4*H*D]
+  y_full = all_gather_rows(y, group) if shard.num_shards > 1 else y
+  rows = s_loc.shape[0]
+  yl = y.view(rows, 4, h, d)
+  yf = y_full.view(-1, 4, h, d)
+  o = ops.attention(yl[:, 0], yf[:, 1], yf[:, 2], mask_k=mask, bias=logits, gate=yl[:, 3])
+  s_loc = ops.linear(o.reshape(rows, h * d), att._packed("zi_t2", dt), residual=s_loc)
+  return mod.single_transition(s_loc, broadcast_dim=None)
+
+
+def pairformer_block(block, z_loc: torch.Tensor, s_loc: torch.Tensor, mask: torch.Tensor, shard: Shard,
+                     group=None):
+  """PairFormerIteration.forward (blocks.py:862-910) on a row shard of the pair tensor."""
+  if z_loc.dtype != torch.bfloat16:
+    raise TypeError("the sharded pair track runs in bf16")
+  m8 = ops.mask_u8(mask)
+  z_loc = tri_mult(block.triangle_multiplication_outgoing, z_loc, m8, shard, group)
+  z_loc = tri_mult(block.triangle_multiplication_incoming, z_loc, m8, shard, group)
+  z_loc = tri_attention(block.pair_attention1, z_loc, m8, shard, group)
+  z_loc = tri_attention(block.pair_attention2, z_loc, m8, shard, group)
+  z_loc = block.pair_transition(z_loc)
+  s_loc = single_update(block.single_act_update, z_loc, s_loc, mask, shard, group)
+  return z_loc, s_loc
+
+
+def pairformer_trunk(trunk, z_loc, s_loc, mask, shard: Shard, group=None):
+  for blk in trunk.blocks:
+    z_loc, s_loc = pairformer_block(blk, z_loc, s_loc, mask, shard, group)
+  return z_loc, s_loc
