@@ -7,8 +7,9 @@ N_token = 512 (475 real tokens, token mask zeroes the rest), c_z = 128,
 c_s = 384, bf16 activations with fp32 accumulation, random-init weights
 (seed 0), z ~ N(0,1), s ~ N(0,1) — synthetic data of the reference's shapes.
 ``value`` is ms per Pairformer block (trunk time / 48), max over ranks.
-With --gpus N > 1 each rank runs an independent replica of the trunk
-(weak scaling); the row-sharded N = 2048 path is measured separately.
+With --gpus N > 1 the pair rows are sharded over the N ranks (NCCL
+all-gathers / all-to-alls as in the reference's distributed blocks) on the same
+workload (strong scaling); --n-token 2048 selects configs[4] (1931 real tokens).
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle
 restatement in oracle/pairformer.py of the reference Torch CPU math path) on
@@ -191,19 +192,32 @@ def run_b200(args) -> None:
   if not torch.cuda.is_available():
     raise SystemExit("bench.py --impl b200 needs a CUDA device")
   _native.check(_native.load().sf_device_check(), "sf_device_check")
+  from sparsefold_b200 import sharding
   dev = torch.device("cuda", local)
   dt = torch.bfloat16
+  n_tok = args.n_token
+  n_real = {512: N_REAL, 2048: 1931}.get(n_tok, n_tok)
   trunk = build_trunk(dev)
-  z_h, s_h, m_h = synth.pair_inputs(N_TOKEN, C_Z, C_S, n_real=N_REAL, seed=rank)
+  shard = sharding.Shard(n_tok, world, rank)
+  # identical inputs on every rank (seed 0); each rank keeps its row shard
+  z_h, s_h, m_h = synth.pair_inputs(n_tok, C_Z, C_S, n_real=n_real, seed=0)
+  if world > 1:
+    z_h = shard.shard(z_h).contiguous()
+    s_h = shard.shard(s_h).contiguous()
   z0 = z_h.to(dev, dt)
   s0 = s_h.to(dev, dt)
   mask = m_h.to(dev)
   l2_flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # 2x the 126 MB L2
   st = torch.cuda.current_stream()
 
+  def run_trunk(z, s, m):
+    if world == 1:
+      return trunk(z, s, m)
+    return sharding.pairformer_trunk(trunk, z, s, m, shard)
+
   with torch.no_grad():
     for _ in range(args.warmup):
-      trunk(z0, s0, mask)
+      run_trunk(z0, s0, mask)
     torch.cuda.synchronize()
 
     # ---- device-resident timing: K trunk passes, L2 flushed between them ----
@@ -215,7 +229,7 @@ def run_b200(args) -> None:
       for a, b in evs:
         flush_l2(l2_flush)
         a.record(st)
-        trunk(z0, s0, mask)
+        run_trunk(z0, s0, mask)
         b.record(st)
       torch.cuda.synchronize()
     launches = _native.launch_count() - launches0
@@ -241,7 +255,7 @@ def run_b200(args) -> None:
       zd = zp.to(dev, non_blocking=True)
       sd = sp.to(dev, non_blocking=True)
       md = mp.to(dev, non_blocking=True)
-      zr, sr = trunk(zd, sd, md)
+      zr, sr = run_trunk(zd, sd, md)
       zo.copy_(zr, non_blocking=True)
       so.copy_(sr, non_blocking=True)
       b.record(st)
@@ -251,7 +265,7 @@ def run_b200(args) -> None:
     d2h = zo.numel() * zo.element_size() + so.numel() * so.element_size()
 
     # ---- dominant-kernel roofline: triangle attention core ----
-    probe_ms = time_kernel_probe(N_TOKEN, dt)
+    probe_ms = time_kernel_probe(N_TOKEN, dt) if rank == 0 else 0.0
 
   peaks = load_peaks()
   flops = tri_attention_op_flops(N_TOKEN)
@@ -261,14 +275,15 @@ def run_b200(args) -> None:
     line = {
         "metric": METRIC, "value": round(ms_block, 4), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) pair/single, random-init AF3-shaped weights)",
-        "config": {"workload": "configs[1]: 48-block Pairformer trunk, N_token=512 (475 real), c_z=128, c_s=384",
-                   "n_token": N_TOKEN, "n_real": N_REAL, "blocks": N_BLOCKS,
-                   "block_gflop": round(block_flops(N_TOKEN) / 1e9, 1),
-                   "trunk_tflop_per_s": round(block_flops(N_TOKEN) / (ms_block * 1e-3) / 1e12, 2),
+        "config": {"workload": (f"{'configs[1]' if n_tok == 512 else 'configs[4]' if n_tok == 2048 else 'custom'}: "
+                                f"48-block Pairformer trunk, N_token={n_tok} ({n_real} real), c_z=128, c_s=384"),
+                   "n_token": n_tok, "n_real": n_real, "blocks": N_BLOCKS,
+                   "block_gflop": round(block_flops(n_tok) / 1e9, 1),
+                   "trunk_tflop_per_s": round(block_flops(n_tok) / (ms_block * 1e-3) / 1e12, 2),
                    "l2": "flushed (256 MiB write) before every timed step",
-                   "parallelism": "replicas" if world > 1 else "single"},
+                   "parallelism": f"pair rows sharded over {world} GPUs (NCCL)" if world > 1 else "single"},
         "e2e": {"value": round(e2e_ms / N_BLOCKS, 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
@@ -421,6 +436,7 @@ def main():
   ap.add_argument("--no-cpu-baseline", action="store_true")
   ap.add_argument("--op", choices=OPS, default=None, help="time one op alone instead of the trunk")
   ap.add_argument("--n", type=int, default=N_TOKEN, help="N_token for --op")
+  ap.add_argument("--n-token", type=int, default=N_TOKEN, help="N_token of the trunk (512 = configs[1], 2048 = configs[4])")
   args = ap.parse_args()
   if args.op:
     run_op(args)
