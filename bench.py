@@ -269,7 +269,7 @@ def run_b200(args) -> None:
 
   peaks = load_peaks()
   flops = tri_attention_op_flops(N_TOKEN)
-  achieved = flops / (probe_ms * 1e-3) / 1e12
+  achieved = flops / (probe_ms * 1e-3) / 1e12 if probe_ms > 0 else 0.0
   cpu = cpu_baseline_sample() if rank == 0 and world == 1 and not args.no_cpu_baseline else None
   if rank == 0:
     line = {

@@ -30,6 +30,7 @@ namespace {
 using namespace pt;
 
 constexpr int H = 4, D = 32;
+constexpr float kLog2e = 1.4426950408889634f;   // the bias is stored pre-scaled by log2(e)
 
 struct AttProjParams {
   const float* ln_w;      // act_norm scale [128]
@@ -45,7 +46,8 @@ struct AttProjParams {
 
 constexpr int NOUT = 512;
 constexpr int W_BYTES = NOUT * C * 2;
-constexpr int SMEM_PROJ = 2 * A_BYTES + W_BYTES + 1024 + 1024;
+constexpr int VT_STAGE = D * TILE * 2;     // one head's V^T tile [32][128] bf16 (8 KB)
+constexpr int SMEM_PROJ = 2 * A_BYTES + W_BYTES + VT_STAGE + 1024 + 1024;
 
 // LayerNorm (scale only) of row r in place, returning the 4 pair-bias logits of
 // the normalised (bf16-rounded) row.
@@ -114,7 +116,8 @@ __global__ void __launch_bounds__(128, 1) k_triatt_project_tc(const __grid_const
   uint8_t* smem = align1024(smem_raw);
   uint8_t* A = smem;
   uint8_t* W = smem + 2 * A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(W + W_BYTES);
+  bf16* vst = reinterpret_cast<bf16*>(W + W_BYTES);                 // [32][128] staging of V^T
+  uint64_t* bars = reinterpret_cast<uint64_t*>(W + W_BYTES + VT_STAGE);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
   const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t nqb = p.qp / TILE;
@@ -167,7 +170,7 @@ __global__ void __launch_bounds__(128, 1) k_triatt_project_tc(const __grid_const
     if (valid && p.compute_bias) {
       const int64_t r = p.transpose ? qi : b, s = p.transpose ? b : qi;
 #pragma unroll
-      for (int h = 0; h < H; ++h) p.bias[(r * H + h) * p.qp + s] = __float2bfloat16_rn(bias[h]);
+      for (int h = 0; h < H; ++h) p.bias[(r * H + h) * p.qp + s] = __float2bfloat16_rn(bias[h] * kLog2e);
     }
     tc::fence_proxy_async();
     tc::tc_fence_before();
@@ -206,12 +209,23 @@ __global__ void __launch_bounds__(128, 1) k_triatt_project_tc(const __grid_const
       store_row32(p.k + ((b * H + h) * p.qp + qi) * D, row, !valid);
       tc::tmem_ld16(lane_addr + 256 + h * D, v0);           // v, stored transposed (keys contiguous)
       tc::tmem_ld16(lane_addr + 256 + h * D + 16, v1);
-      bf16* vt = p.vt + ((b * H + h) * D) * p.qp + qi;
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
-        vt[(int64_t)e * p.qp] = __float2bfloat16_rn(valid ? v0[e] : 0.f);
-        vt[(int64_t)(16 + e) * p.qp] = __float2bfloat16_rn(valid ? v1[e] : 0.f);
+        vst[e * TILE + tid] = __float2bfloat16_rn(valid ? v0[e] : 0.f);
+        vst[(16 + e) * TILE + tid] = __float2bfloat16_rn(valid ? v1[e] : 0.f);
       }
+      __syncthreads();
+      {
+        // 32 rows (d) x 256 bytes: V^T[b][h][d][q0 .. q0+127]
+        bf16* vt = p.vt + ((b * H + h) * D) * p.qp + (tile % nqb) * TILE;
+#pragma unroll
+        for (int i = 0; i < (D * 16) / 128; ++i) {
+          const int e = tid + 128 * i, d = e >> 4, part = e & 15;
+          *reinterpret_cast<uint4*>(vt + (int64_t)d * p.qp + part * 8) =
+              *reinterpret_cast<const uint4*>(vst + d * TILE + part * 8);
+        }
+      }
+      __syncthreads();
       tc::tmem_ld16(lane_addr + 384 + h * D, v0);           // gate -> sigmoid
       tc::tmem_ld16(lane_addr + 384 + h * D + 16, v1);
 #pragma unroll
@@ -254,7 +268,6 @@ constexpr int OFF_W = 128 * 1024;          // 128 x 256 B output projection
 constexpr int OFF_BAR = 160 * 1024;
 constexpr int OFF_KBITS = OFF_BAR + 1024;       // key-valid bits, qp/32 words (qp <= 65536)
 constexpr int SMEM_CORE = OFF_KBITS + 8192 + 1024;
-constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_u32(dst)), "l"(src) : "memory");
@@ -344,6 +357,15 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
   constexpr uint32_t IDESC_S = tc::idesc_bf16(128, KB), IDESC_O = tc::idesc_bf16(128, D);
   float m = -INFINITY, l = 0.f, o[D];
   const int nsteps = 2 * nkb;
+  // bias row (query q, head h) of the key block of a step; prefetched one step ahead
+  uint4 bias_raw[KB / 8];
+  auto load_bias = [&](int step) {
+    const int hh_ = step / nkb, kb_ = step % nkb, h_ = g + 2 * hh_;
+    const uint4* brow = reinterpret_cast<const uint4*>(p.bias + (q * H + h_) * p.qp + (int64_t)kb_ * KB);
+#pragma unroll
+    for (int c = 0; c < KB / 8; ++c) bias_raw[c] = __ldg(brow + c);
+  };
+  load_bias(0);
   for (int j = 0; j < nsteps; ++j) {
     const int hh = j / nkb, kb = j % nkb, h = g + 2 * hh, s = j & 1;
     if (j + 1 < nsteps) {
@@ -366,11 +388,6 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
                      tc::smem_desc(kvs + kk * 32, 512, tc::kSW64), IDESC_S, kk > 0);
       tc::mma_commit(&sdone[g]);
     }
-    // bias row of this key block, fetched while the S MMA runs
-    const uint4* brow = reinterpret_cast<const uint4*>(p.bias + (q * H + h) * p.qp + (int64_t)kb * KB);
-    uint4 bias_raw[KB / 8];
-#pragma unroll
-    for (int c = 0; c < KB / 8; ++c) bias_raw[c] = __ldg(brow + c);
     const uint64_t vbits = (uint64_t)kbits[kb * 2] | ((uint64_t)kbits[kb * 2 + 1] << 32);
     tc::mbar_wait(&sdone[g], j & 1, p.status, aborted);
     tc::tc_fence_after();
@@ -390,17 +407,20 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
       for (int e = 0; e < 16; ++e) sv[16 * i + e] = v[e];
     }
     float mx = -INFINITY;
+    const bool full = (vbits == ~0ull) && ((int64_t)kb * KB + KB <= p.nq);
 #pragma unroll
     for (int c = 0; c < KB / 8; ++c) {
       const uint32_t* bu = reinterpret_cast<const uint32_t*>(&bias_raw[c]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         const int kidx = c * 8 + e;
-        const int64_t key = (int64_t)kb * KB + kidx;
         const float bv = (e & 1) ? bf_hi(bu[e >> 1]) : bf_lo(bu[e >> 1]);
-        float x = sv[kidx] * p.scale_log2 + bv * kLog2e;
-        if (key >= p.nq) x = -INFINITY;                // padding beyond the N keys: excluded
-        else if (!((vbits >> kidx) & 1)) x = -FLT_MAX;   // masked key: the reference's -finfo.max bias
+        float x = fmaf(sv[kidx], p.scale_log2, bv);      // log2 domain (bias pre-scaled by log2 e)
+        if (!full) {
+          const int64_t key = (int64_t)kb * KB + kidx;
+          if (key >= p.nq) x = -INFINITY;                 // padding beyond the N keys: excluded
+          else if (!((vbits >> kidx) & 1)) x = -FLT_MAX;  // masked key: the reference's -finfo.max bias
+        }
         sv[kidx] = x;
         mx = fmaxf(mx, x);
       }
@@ -426,6 +446,7 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
     }
     l = l * corr + psum;
     m = m_new;
+    if (j + 1 < nsteps) load_bias(j + 1);   // in flight during the P.V MMA and the next S MMA
     tc::fence_proxy_async();
     tc::tc_fence_before();
     wg_sync(g);
@@ -560,7 +581,7 @@ __global__ void k_triatt_bias(const bf16* __restrict__ z, const float* __restric
   if (lane == 0) {
     const int64_t r = pos / n, sc = pos % n;
 #pragma unroll
-    for (int h = 0; h < H; ++h) bias[(r * H + h) * ldb + sc] = __float2bfloat16_rn(acc[h]);
+    for (int h = 0; h < H; ++h) bias[(r * H + h) * ldb + sc] = __float2bfloat16_rn(acc[h] * kLog2e);
   }
 }
 

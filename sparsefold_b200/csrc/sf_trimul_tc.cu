@@ -29,7 +29,9 @@ struct ProjParams {
 
 constexpr int NOUT = 512;
 constexpr int W_BYTES = NOUT * C * 2;                       // 128 KB
-constexpr int SMEM_PROJ = 2 * A_BYTES + W_BYTES + 1024 + 1024;
+constexpr int CH_CHUNK = 32;                                // channels staged per epilogue step
+constexpr int STAGE_OUT = CH_CHUNK * TILE * 2;              // one [32][128] bf16 staging tile (8 KB)
+constexpr int SMEM_PROJ = 2 * A_BYTES + W_BYTES + 2 * STAGE_OUT + 1024 + 1024;
 
 __global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_constant__ CUtensorMap tmap,
                                                               ProjParams p) {
@@ -37,7 +39,9 @@ __global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_const
   uint8_t* smem = align1024(smem_raw);
   uint8_t* A = smem;
   uint8_t* W = smem + 2 * A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(W + W_BYTES);   // [0,1] tma stages, [2] mma
+  bf16* stA = reinterpret_cast<bf16*>(W + W_BYTES);             // [32 channels][128 positions]
+  bf16* stB = stA + CH_CHUNK * TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(W + W_BYTES + 2 * STAGE_OUT);   // [0,1] tma stages, [2] mma
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
   const int tid = threadIdx.x, warp = tid >> 5;
 
@@ -111,31 +115,46 @@ __global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_const
     tc::mbar_wait(&bars[2], it & 1, p.status, aborted);
     tc::tc_fence_after();
 
-    // ---- epilogue: row tid of the tile ----
-    const int64_t major = tile / nb, minor = (tile % nb) * TILE + tid;
+    // ---- epilogue: position tid of the tile; 32 channels at a time are staged as
+    // [channel][position] and written as contiguous 256-byte rows of the operands ----
+    const int64_t major = tile / nb, minor0 = (tile % nb) * TILE, minor = minor0 + tid;
     const bool valid = minor < span;
     const int64_t r = p.incoming ? minor : major;     // local pair row
     const int64_t s = p.incoming ? major : minor;     // pair column
     const bool keep = valid && p.mask[p.row_offset + r] && p.mask[s];
-    const int64_t base = p.incoming ? s * C * pitch + r : r * C * pitch + s;
     bf16* ao = p.incoming ? p.b_op : p.a_op;          // incoming: A <- b, B <- a (transposed)
     bf16* bo = p.incoming ? p.a_op : p.b_op;
     const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    const int64_t row_base = major * C * pitch + minor0;   // operand row `major`, first position of the tile
 #pragma unroll 1
-    for (int j = 0; j < 8; ++j) {
-      float ga[16], va[16], gb[16], vb[16];
-      tc::tmem_ld16(lane_addr + 16 * j, ga);
-      tc::tmem_ld16(lane_addr + 128 + 16 * j, va);
-      tc::tmem_ld16(lane_addr + 256 + 16 * j, gb);
-      tc::tmem_ld16(lane_addr + 384 + 16 * j, vb);
-      if (valid) {
+    for (int cc = 0; cc < C / CH_CHUNK; ++cc) {
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int c0 = cc * CH_CHUNK + hf * 16;
+        float ga[16], va[16], gb[16], vb[16];
+        tc::tmem_ld16(lane_addr + c0, ga);
+        tc::tmem_ld16(lane_addr + 128 + c0, va);
+        tc::tmem_ld16(lane_addr + 256 + c0, gb);
+        tc::tmem_ld16(lane_addr + 384 + c0, vb);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const int64_t off = base + (int64_t)(16 * j + e) * pitch;
-          ao[off] = __float2bfloat16_rn(keep ? fast_sigmoid(ga[e]) * va[e] : 0.f);
-          bo[off] = __float2bfloat16_rn(keep ? fast_sigmoid(gb[e]) * vb[e] : 0.f);
+          stA[(hf * 16 + e) * TILE + tid] = __float2bfloat16_rn(keep ? fast_sigmoid(ga[e]) * va[e] : 0.f);
+          stB[(hf * 16 + e) * TILE + tid] = __float2bfloat16_rn(keep ? fast_sigmoid(gb[e]) * vb[e] : 0.f);
         }
       }
+      __syncthreads();
+      // 32 channel rows x 16 chunks of 16 bytes per operand
+#pragma unroll
+      for (int i = 0; i < (CH_CHUNK * 16) / 128; ++i) {
+        const int e = tid + 128 * i;
+        const int c = e >> 4, part = e & 15;
+        if (minor0 + part * 8 + 8 <= pitch) {
+          const int64_t off = row_base + (int64_t)(cc * CH_CHUNK + c) * pitch + part * 8;
+          *reinterpret_cast<uint4*>(ao + off) = *reinterpret_cast<const uint4*>(stA + c * TILE + part * 8);
+          *reinterpret_cast<uint4*>(bo + off) = *reinterpret_cast<const uint4*>(stB + c * TILE + part * 8);
+        }
+      }
+      __syncthreads();
     }
     tc::tc_fence_before();
     __syncthreads();
