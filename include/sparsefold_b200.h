@@ -171,7 +171,9 @@ int sf_tri_mult_contract_chunked(int dtype, const void* a_op, int64_t chunks_a, 
 /* Query pitch qp of the attention buffers: Q, K, Vt [nb][4][qp][32],
  * G [nb][qp][128], bias [qp][4][qp] (bias[q][h][k], rows gathered across ranks). */
 int64_t sf_tri_attention_query_pitch(int64_t nq);
-/* Pair bias of the local rows: bias[(r*4 + h)*ldb + s] = LN(z[r,s]) . W_b[h] (blocks.py:317-320). */
+/* Pair bias of the local rows: bias[(r*4 + h)*ldb + s] = sqrt(32) * LN(z[r,s]) . W_b[h] in bf16
+ * (blocks.py:317-320; stored times the inverse softmax scale, the form the attention core adds
+ * Q K^T to). */
 int sf_tri_attention_bias(int dtype, const void* z, int64_t rows, int64_t n, const sf_tri_attention_weights* w,
                           void* bias, int64_t ldb, sf_stream_t stream);
 /* LN + q/k/v/gate projections of a z block [rows][cols]; transpose = attention

@@ -199,21 +199,26 @@ __global__ void __launch_bounds__(288, 1) k_transition_tc(const __grid_constant_
 
 }  // namespace
 
-// 2-D bf16 tensor map [outer][inner] (inner contiguous), 128B swizzle.
+// 2-D bf16 tensor map [outer][inner] (inner contiguous), 128B (default) or 64B swizzle.
 int make_2d_tmap(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, uint32_t box_inner,
-                 uint32_t box_outer) {
+                 uint32_t box_outer, int swizzle_bytes) {
   auto encode = tensor_map_encoder();
   if (!encode) return SF_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (inner * 2) % 16 != 0) {
     set_error("2-d tensor map: base %p / row bytes %lld not 16-byte aligned", base, (long long)(inner * 2));
     return SF_ERR_ARG;
   }
+  if (swizzle_bytes != 128 && swizzle_bytes != 64) {
+    set_error("2-d tensor map: unsupported swizzle %d", swizzle_bytes);
+    return SF_ERR_ARG;
+  }
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d) for [%lld][%lld]", (int)r, (long long)outer, (long long)inner);

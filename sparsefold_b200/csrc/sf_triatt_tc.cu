@@ -8,18 +8,20 @@
 //                       tile for the starting node, a column tile for the ending
 //                       node (transpose=True), so every store is contiguous.
 //  k_triatt_core_tc     flash attention + gate + output projection + residual for
-//                       one (attention row b, 128-query block): two softmax
-//                       warpgroups each own two heads; S = Q K^T (M128 N64 K32)
-//                       and O_blk = P V (M128 N32 K64) run on tcgen05 with TMEM
-//                       accumulators, the online softmax runs in exp2 with the
-//                       reference's -FLT_MAX masking, and the gated outputs of all
-//                       four heads feed one more tcgen05 GEMM with the resident
-//                       output projection, whose epilogue adds the residual.
+//                       one (attention row b, 128-query block): four softmax
+//                       warpgroups, one per head.  S' = sqrt(D) bias + Q K^T
+//                       (M128 N64 K32, accumulated onto the bias the warpgroup
+//                       stored in TMEM) and O += P V (M128 N32 K64) run on
+//                       tcgen05 with TMEM accumulators; K/V^T blocks arrive by
+//                       TMA; the softmax runs in exp2 with the reference's
+//                       -FLT_MAX masking; the gated outputs of all four heads
+//                       feed one more tcgen05 GEMM with the output projection,
+//                       whose epilogue adds the residual.
 //
 // Intermediate layouts (qp = n rounded up to 128; padded query rows are zero):
 //   Q, K  [b][h][qp][32]    Vt [b][h][32][qp]    G = sigmoid(gate) [b][qp][128]
-//   bias  [q][h][qp] (bias[q][h][k] = LN(z)[q,k] . W_b[h], untransposed; rows q all-gathered
-//         from the row shards when the pair tensor is distributed)
+//   bias  [q][h][qp] (bias[q][h][k] = sqrt(32) LN(z)[q,k] . W_b[h] in bf16, untransposed;
+//         rows q all-gathered from the row shards when the pair tensor is distributed)
 #include <cfloat>
 
 #include "sf_pair_tc.cuh"
@@ -30,7 +32,10 @@ namespace {
 using namespace pt;
 
 constexpr int H = 4, D = 32;
-constexpr float kLog2e = 1.4426950408889634f;   // the bias is stored pre-scaled by log2(e)
+constexpr float kLog2e = 1.4426950408889634f;
+// The pair bias is stored multiplied by sqrt(D), the inverse softmax scale, so that the
+// core can accumulate Q K^T onto it: S' = q.k + sqrt(D) b = sqrt(D) (q.k / sqrt(D) + b).
+constexpr float kBiasScale = 5.656854249492380f;
 
 struct AttProjParams {
   const float* ln_w;      // act_norm scale [128]
@@ -170,7 +175,7 @@ __global__ void __launch_bounds__(128, 1) k_triatt_project_tc(const __grid_const
     if (valid && p.compute_bias) {
       const int64_t r = p.transpose ? qi : b, s = p.transpose ? b : qi;
 #pragma unroll
-      for (int h = 0; h < H; ++h) p.bias[(r * H + h) * p.qp + s] = __float2bfloat16_rn(bias[h] * kLog2e);
+      for (int h = 0; h < H; ++h) p.bias[(r * H + h) * p.qp + s] = __float2bfloat16_rn(bias[h] * kBiasScale);
     }
     tc::fence_proxy_async();
     tc::tc_fence_before();
@@ -246,7 +251,7 @@ __global__ void __launch_bounds__(128, 1) k_triatt_project_tc(const __grid_const
 // attention core
 // ---------------------------------------------------------------------------
 struct AttCoreParams {
-  const bf16 *q, *k, *vt, *g, *bias;
+  const bf16 *g, *bias;
   const bf16* w_out;      // output_projection^T [128 out][128 in]
   const uint8_t* mask;    // [N] token mask (keys/queries are all N tokens)
   const bf16* z;          // the z block [rows][cols][128] (residual)
@@ -255,26 +260,28 @@ struct AttCoreParams {
   int64_t nq, qp;         // queries = keys, pitch
   int64_t batch_offset;   // global token index of attention row 0 (row mask)
   int transpose;
-  float scale_log2;       // (1/sqrt(D)) * log2(e)
+  float scale_log2;       // (1/sqrt(D)) * log2(e): S' = q.k + sqrt(D) b  ->  logit * log2(e) = S' * scale_log2
   uint32_t* status;
 };
 
-constexpr int KB = 64;                     // keys per block
-constexpr int OFF_Q = 0;                   // 4 heads x 128 x 64 B (64B swizzle)
-constexpr int OFF_KV = 32 * 1024;          // [wg][stage] x (K 4 KB | Vt 4 KB)
-constexpr int OFF_P = 64 * 1024;           // [wg] x 128 x 128 B (128B swizzle)
-constexpr int OFF_O = 96 * 1024;           // 128 x 256 B gated outputs of all heads
-constexpr int OFF_W = 128 * 1024;          // 128 x 256 B output projection
-constexpr int OFF_BAR = 160 * 1024;
-constexpr int OFF_KBITS = OFF_BAR + 1024;       // key-valid bits, qp/32 words (qp <= 65536)
-constexpr int SMEM_CORE = OFF_KBITS + 8192 + 1024;
+constexpr int KB = 64;                 // keys per block
+constexpr int KV_STAGES = 3;
+constexpr int KV_BYTES = 8 * 1024;     // K block 64 x 64 B (64B swizzle) | V^T block 32 x 128 B (128B swizzle)
+constexpr int P_BYTES = TILE * KB * 2; // P tile 128 x 128 B (128B swizzle)
+constexpr int MAX_QP = 32768;
+constexpr int OFF_Q = 0;                                      // [h] Q tile 128 x 64 B; W_o columns of head h after the loop
+constexpr int OFF_KV = H * 8 * 1024;                          // [h][stage]
+constexpr int OFF_P = OFF_KV + H * KV_STAGES * KV_BYTES;      // [h] P tile; gated O_h (128 x 64 B) after the loop
+constexpr int OFF_KBITS = OFF_P + H * P_BYTES;                // key-valid bits, qp/32 words
+constexpr int OFF_BAR = OFF_KBITS + MAX_QP / 8;
+constexpr int SMEM_CORE = OFF_BAR + 256 + 1024;
+constexpr float kRescale = 8.0f;       // the running max moves only when a block exceeds it by 2^8
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void wg_sync(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -282,214 +289,259 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// K block (64 keys x 32) into 64B-swizzled K-major rows and Vt block (32 x 64 keys)
-// into 128B-swizzled K-major rows, by the 128 threads of one warpgroup.
-__device__ __forceinline__ void load_kv(uint8_t* dst, const AttCoreParams& p, int64_t b, int h, int kb, int t) {
-  const bf16* ksrc = p.k + ((b * H + h) * p.qp + (int64_t)kb * KB) * D;
-  const bf16* vsrc = p.vt + ((b * H + h) * D) * p.qp + (int64_t)kb * KB;
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int e = t + 128 * i;
-    const int key = e >> 2, c = e & 3;
-    cp_async16(dst + tc::sw64_off(key, c), ksrc + key * D + c * 8);
-    const int d = e >> 3, c8 = e & 7;
-    cp_async16(dst + 4096 + tc::sw128_off(d, c8), vsrc + (int64_t)d * p.qp + c8 * 8);
-  }
-}
-
-__global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
+// One CTA = one (attention row b, 128-query tile); warpgroup h owns head h.
+// Per key block j of 64 keys a warpgroup:
+//   waits for S'_j = sqrt(D) bias_j + Q K_j^T in TMEM (the bias was stored there
+//   by the warpgroup before the MMA, with -inf for masked and padding keys),
+//   reads S'_j twice (block max; then P = 2^(S' scale - m) into shared memory),
+//   rescales its O accumulator in TMEM when the running max moved, stores the
+//   bias of block j+1 into the S' columns, and its leader issues P_j V_j (into O)
+//   and Q K_{j+1}^T (onto that bias).  K and V^T blocks arrive by TMA three
+//   blocks deep.  A row whose token is masked attends uniformly to all N keys
+//   (every logit of the reference is -FLT_MAX there).  After the last block the
+//   gated, normalised O_h and the W_o columns of head h are staged and one more
+//   tcgen05 GEMM (K = 4 heads x 32) forms the output projection; its epilogue
+//   adds the residual.
+// TMEM columns: S'_h at 64h, O_h at 256 + 32h, output projection at 384.
+__global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant__ CUtensorMap tmQ,
+                                                           const __grid_constant__ CUtensorMap tmK,
+                                                           const __grid_constant__ CUtensorMap tmV, AttCoreParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* sdone = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [2]
-  uint64_t* odone = sdone + 2;                                     // [2]
-  uint64_t* outdone = sdone + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sdone + 6);
-  const int tid = threadIdx.x, warp = tid >> 5, g = tid >> 7, t = tid & 127;
+  uint64_t* qbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [H] Q tile landed
+  uint64_t* sbar = qbar + H;                                       // [H] S'_j (and P_{j-1} V_{j-1}) done
+  uint64_t* obar = sbar + H;                                       // [H] last P V done
+  uint64_t* kvbar = obar + H;                                      // [H][KV_STAGES] K/V block landed
+  uint64_t* outbar = kvbar + H * KV_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(outbar + 1);
+  uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = tid >> 7, t = tid & 127;
   const int64_t q0 = (int64_t)blockIdx.x * TILE, b = blockIdx.y;
   const int nkb = (int)(p.qp / KB);
+  const int64_t bh = b * H + g;
 
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 5; ++i) tc::mbar_init(&sdone[i], 1);
+    for (int i = 0; i < 3 * H + H * KV_STAGES + 1; ++i) tc::mbar_init(&qbar[i], 1);
     tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmQ);
+    tc::prefetch_tmap(&tmK);
+    tc::prefetch_tmap(&tmV);
   }
-  // key k is attended iff mask[b] && mask[k] (pair mask, blocks.py:314)
-  uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
-  {
-    const bool rok = p.mask[b + p.batch_offset] != 0;
-    for (int w = tid; w < (int)(p.qp / 32); w += 256) {
-      uint32_t bits = 0;
-      for (int e = 0; e < 32; ++e) {
-        const int64_t key = (int64_t)w * 32 + e;
-        if (rok && key < p.nq && p.mask[key]) bits |= 1u << e;
-      }
-      kbits[w] = bits;
-    }
+  // key k is attended iff mask[row] && mask[k] (pair mask, blocks.py:314); bits hold mask[k] && k < N
+  for (int w = warp; w < (int)(p.qp / 32); w += 16) {
+    const int64_t key = (int64_t)w * 32 + lane;
+    const uint32_t bits = __ballot_sync(0xffffffffu, key < p.nq && p.mask[key] != 0);
+    if (lane == 0) kbits[w] = bits;
   }
-  // Q of all four heads and the output projection, by all 256 threads.
-  for (int e = tid; e < H * TILE * 4; e += 256) {
-    const int h = e >> 9, q = (e >> 2) & 127, c = e & 3;
-    cp_async16(smem + OFF_Q + h * 8192 + tc::sw64_off(q, c), p.q + ((b * H + h) * p.qp + q0 + q) * D + c * 8);
-  }
-  for (int e = tid; e < C * 16; e += 256) {
-    const int r = e >> 4, kc = e & 15;
-    cp_async16(smem + OFF_W + (kc >> 3) * 16384 + tc::sw128_off(r, kc & 7), p.w_out + r * C + kc * 8);
-  }
-  cp_async_commit();
-  uint8_t* kv = smem + OFF_KV + g * 16384;
-  load_kv(kv, p, b, g, 0, t);   // first step of this warpgroup: head g, key block 0
-  cp_async_commit();
-  cp_async_wait<1>();           // Q and W_o landed (loaded by both warpgroups)
-  tc::fence_proxy_async();
+  const bool uniform = p.mask[b + p.batch_offset] == 0;
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
-  const uint32_t s_col = g * KB, o_col = 128 + g * D;
+  const uint32_t s_col = (uint32_t)g * KB, o_col = 256u + (uint32_t)g * D;
+  const uint32_t sb = tc::smem_u32(smem);
+  const uint32_t q_s = sb + OFF_Q + g * 8192, p_s = sb + OFF_P + g * P_BYTES;
+  uint8_t* kv = smem + OFF_KV + g * KV_STAGES * KV_BYTES;
   bool aborted = false;
+  constexpr uint32_t IDESC_S = tc::idesc_bf16(128, KB), IDESC_O = tc::idesc_bf16(128, D);
+
+  auto issue_kv = [&](int jj) {
+    const int st = jj % KV_STAGES;
+    tc::mbar_expect_tx(&kvbar[g * KV_STAGES + st], KV_BYTES);
+    tc::tma_load_2d(kv + st * KV_BYTES, &tmK, &kvbar[g * KV_STAGES + st], 0, (int)(bh * p.qp + (int64_t)jj * KB));
+    tc::tma_load_2d(kv + st * KV_BYTES + 4096, &tmV, &kvbar[g * KV_STAGES + st], jj * KB, (int)(bh * D));
+  };
+  auto issue_s = [&](int jj) {   // S' (+)= Q K_jj^T
+    const uint32_t ks = sb + OFF_KV + (g * KV_STAGES + jj % KV_STAGES) * KV_BYTES;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk)
+      tc::mma_bf16(tbase + s_col, tc::smem_desc(q_s + kk * 32, 512, tc::kSW64), tc::smem_desc(ks + kk * 32, 512, tc::kSW64),
+                   IDESC_S, !uniform || kk > 0);
+  };
 
   const int64_t q = q0 + t;
-  const uint32_t sb = tc::smem_u32(smem);
-  constexpr uint32_t IDESC_S = tc::idesc_bf16(128, KB), IDESC_O = tc::idesc_bf16(128, D);
-  float m = -INFINITY, l = 0.f, o[D];
-  const int nsteps = 2 * nkb;
-  // bias row (query q, head h) of the key block of a step; prefetched one step ahead
-  uint4 bias_raw[KB / 8];
-  auto load_bias = [&](int step) {
-    const int hh_ = step / nkb, kb_ = step % nkb, h_ = g + 2 * hh_;
-    const uint4* brow = reinterpret_cast<const uint4*>(p.bias + (q * H + h_) * p.qp + (int64_t)kb_ * KB);
+  const uint4* brow = reinterpret_cast<const uint4*>(p.bias + (q * H + g) * p.qp);
+  uint4 braw[KB / 8];
+  auto load_bias = [&](int jj) {
 #pragma unroll
-    for (int c = 0; c < KB / 8; ++c) bias_raw[c] = __ldg(brow + c);
+    for (int c = 0; c < KB / 8; ++c) braw[c] = __ldg(brow + jj * (KB / 8) + c);
   };
-  load_bias(0);
-  for (int j = 0; j < nsteps; ++j) {
-    const int hh = j / nkb, kb = j % nkb, h = g + 2 * hh, s = j & 1;
-    if (j + 1 < nsteps) {
-      const int j1 = j + 1;
-      load_kv(kv + (s ^ 1) * 8192, p, b, g + 2 * (j1 / nkb), j1 % nkb, t);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    tc::fence_proxy_async();
-    tc::tc_fence_before();
-    wg_sync(g);
-    const uint32_t kvs = sb + OFF_KV + g * 16384 + s * 8192;
-    if (t == 0) {
-      tc::tc_fence_after();
+  // bias of block jj (bf16, already x sqrt(D)) into the S' columns; -inf where the key is masked or padding
+  auto store_bias = [&](int jj) {
+    const uint64_t vb = (uint64_t)kbits[2 * jj] | ((uint64_t)kbits[2 * jj + 1] << 32);
+    const bool full = vb == ~0ull;
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
-        tc::mma_bf16(tbase + s_col, tc::smem_desc(sb + OFF_Q + h * 8192 + kk * 32, 512, tc::kSW64),
-                     tc::smem_desc(kvs + kk * 32, 512, tc::kSW64), IDESC_S, kk > 0);
-      tc::mma_commit(&sdone[g]);
+    for (int c = 0; c < KB / 16; ++c) {
+      uint32_t r[16];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t u = reinterpret_cast<const uint32_t*>(&braw[2 * c + (e >> 2)])[e & 3];
+        r[2 * e] = u << 16;
+        r[2 * e + 1] = u & 0xFFFF0000u;
+      }
+      if (!full) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (!((vb >> (16 * c + e)) & 1)) r[e] = 0xFF800000u;
+      }
+      tc::tmem_st16(lane_addr + s_col + 16 * c, r);
     }
-    const uint64_t vbits = (uint64_t)kbits[kb * 2] | ((uint64_t)kbits[kb * 2 + 1] << 32);
-    tc::mbar_wait(&sdone[g], j & 1, p.status, aborted);
+    tc::tmem_wait_st();
+  };
+
+  // ---- prologue: Q, K/V blocks 0 and 1, bias of block 0, S'_0 ----
+  if (t == 0) {
+    tc::mbar_expect_tx(&qbar[g], 8192);
+    tc::tma_load_2d(smem + OFF_Q + g * 8192, &tmQ, &qbar[g], 0, (int)(bh * p.qp + q0));
+    issue_kv(0);
+    issue_kv(1);   // qp >= 128: at least two key blocks
+  }
+  if (!uniform) {
+    load_bias(0);
+    store_bias(0);
+    load_bias(1);
+  }
+  tc::tc_fence_before();
+  wg_sync(g);
+  if (t == 0) {
     tc::tc_fence_after();
-    if (kb == 0) {
-      m = -INFINITY;
-      l = 0.f;
+    tc::mbar_wait(&qbar[g], 0, p.status, aborted);
+    tc::mbar_wait(&kvbar[g * KV_STAGES], 0, p.status, aborted);
+    issue_s(0);
+    tc::mma_commit(&sbar[g]);
+  }
+
+  float m_run = -INFINITY, l = 0.f;
+  for (int j = 0; j < nkb; ++j) {
+    tc::mbar_wait(&sbar[g], j & 1, p.status, aborted);
+    tc::tc_fence_after();
+    if (t == 0 && j + 2 < nkb) issue_kv(j + 2);   // its stage held block j-1, whose P V is done
+    if (j == nkb - 1) {
+      // no bias is pending in the last block: its registers take the gate of this head
+      const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
 #pragma unroll
-      for (int d = 0; d < D; ++d) o[d] = 0.f;
+      for (int c = 0; c < D / 8; ++c) braw[c] = __ldg(grow + c);
     }
-    // ---- online softmax over this key block (log2 domain) ----
-    float sv[KB];
+    // ---- block max (log2 domain) and the running max ----
+    float corr = 1.f, m_use = 0.f;
+    if (!uniform) {
+      float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < KB / 16; ++i) {
-      float v[16];
-      tc::tmem_ld16(lane_addr + s_col + 16 * i, v);
+      for (int c = 0; c < KB / 16; ++c) {
+        float v[16];
+        tc::tmem_ld16(lane_addr + s_col + 16 * c, v);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) sv[16 * i + e] = v[e];
-    }
-    float mx = -INFINITY;
-    const bool full = (vbits == ~0ull) && ((int64_t)kb * KB + KB <= p.nq);
-#pragma unroll
-    for (int c = 0; c < KB / 8; ++c) {
-      const uint32_t* bu = reinterpret_cast<const uint32_t*>(&bias_raw[c]);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int kidx = c * 8 + e;
-        const float bv = (e & 1) ? bf_hi(bu[e >> 1]) : bf_lo(bu[e >> 1]);
-        float x = fmaf(sv[kidx], p.scale_log2, bv);      // log2 domain (bias pre-scaled by log2 e)
-        if (!full) {
-          const int64_t key = (int64_t)kb * KB + kidx;
-          if (key >= p.nq) x = -INFINITY;                 // padding beyond the N keys: excluded
-          else if (!((vbits >> kidx) & 1)) x = -FLT_MAX;  // masked key: the reference's -finfo.max bias
-        }
-        sv[kidx] = x;
-        mx = fmaxf(mx, x);
+        for (int e = 0; e < 16; e += 2) mx = tc::fmax3(mx, v[e], v[e + 1]);
       }
+      mx *= p.scale_log2;
+      if (mx > m_run + kRescale) {   // m_run = -inf: any finite block max
+        corr = ex2(m_run - mx);
+        m_run = mx;
+      }
+      m_use = m_run == -INFINITY ? 0.f : m_run;
     }
-    const float m_new = fmaxf(m, mx);
-    const float corr = ex2(m - m_new);
+    if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+      // O (blocks < j, complete) *= corr
+#pragma unroll
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        float v[16];
+        uint32_t r[16];
+        tc::tmem_ld16(lane_addr + o_col + 16 * hlf, v);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(v[e] * corr);
+        tc::tmem_st16(lane_addr + o_col + 16 * hlf, r);
+      }
+      tc::tmem_wait_st();
+    }
+    // ---- P = 2^(S' scale - m) into the 128B-swizzled P tile (row t) ----
     float psum = 0.f;
-    uint8_t* prow = smem + OFF_P + g * 16384;
+    uint8_t* prow = smem + OFF_P + g * P_BYTES;
+    const float nm = -m_use;
 #pragma unroll
-    for (int c = 0; c < KB / 8; ++c) {
-      float pv[8];
+    for (int c = 0; c < KB / 16; ++c) {
+      float v[16];
+      if (!uniform) {
+        tc::tmem_ld16(lane_addr + s_col + 16 * c, v);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        pv[e] = ex2(sv[c * 8 + e] - m_new);
-        psum += pv[e];
+        for (int e = 0; e < 16; ++e) v[e] = ex2(fmaf(v[e], p.scale_log2, nm));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = ((int64_t)j * KB + 16 * c + e < p.nq) ? 1.f : 0.f;
       }
-      uint4 pk;
-      pk.x = pack_bf2(pv[0], pv[1]);
-      pk.y = pack_bf2(pv[2], pv[3]);
-      pk.z = pack_bf2(pv[4], pv[5]);
-      pk.w = pack_bf2(pv[6], pv[7]);
-      *reinterpret_cast<uint4*>(prow + tc::sw128_off(t, c)) = pk;
+#pragma unroll
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint4 pk;
+        pk.x = pack_bf2(v[8 * hlf + 0], v[8 * hlf + 1]);
+        pk.y = pack_bf2(v[8 * hlf + 2], v[8 * hlf + 3]);
+        pk.z = pack_bf2(v[8 * hlf + 4], v[8 * hlf + 5]);
+        pk.w = pack_bf2(v[8 * hlf + 6], v[8 * hlf + 7]);
+        *reinterpret_cast<uint4*>(prow + tc::sw128_off(t, 2 * c + hlf)) = pk;
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) psum += v[e];
     }
     l = l * corr + psum;
-    m = m_new;
-    if (j + 1 < nsteps) load_bias(j + 1);   // in flight during the P.V MMA and the next S MMA
+    if (!uniform && j + 1 < nkb) {
+      store_bias(j + 1);               // S'_j has been read
+      if (j + 2 < nkb) load_bias(j + 2);
+    }
     tc::fence_proxy_async();
     tc::tc_fence_before();
     wg_sync(g);
     if (t == 0) {
       tc::tc_fence_after();
+      const uint32_t vs = sb + OFF_KV + (g * KV_STAGES + j % KV_STAGES) * KV_BYTES + 4096;
 #pragma unroll
       for (int kk = 0; kk < KB / 16; ++kk)
-        tc::mma_bf16(tbase + o_col, tc::smem_desc(sb + OFF_P + g * 16384 + kk * 32, 1024, tc::kSW128),
-                     tc::smem_desc(kvs + 4096 + kk * 32, 1024, tc::kSW128), IDESC_O, kk > 0);
-      tc::mma_commit(&odone[g]);
-    }
-    tc::mbar_wait(&odone[g], j & 1, p.status, aborted);
-    tc::tc_fence_after();
-    {
-      float v0[16], v1[16];
-      tc::tmem_ld16(lane_addr + o_col, v0);
-      tc::tmem_ld16(lane_addr + o_col + 16, v1);
-#pragma unroll
-      for (int d = 0; d < 16; ++d) {
-        o[d] = o[d] * corr + v0[d];
-        o[16 + d] = o[16 + d] * corr + v1[d];
-      }
-    }
-    if (kb == nkb - 1) {
-      // normalise, gate with sigmoid(gate), stage as the A operand of the output projection
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
-      const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + h * D);
-      uint8_t* orow = smem + OFF_O + (h >> 1) * 16384;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const uint4 gg = __ldg(grow + cc);
-        const uint32_t* gu = reinterpret_cast<const uint32_t*>(&gg);
-        uint4 ok;
-        uint32_t* ou = reinterpret_cast<uint32_t*>(&ok);
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          ou[e] = pack_bf2(o[cc * 8 + 2 * e] * inv * bf_lo(gu[e]), o[cc * 8 + 2 * e + 1] * inv * bf_hi(gu[e]));
-        *reinterpret_cast<uint4*>(orow + tc::sw128_off(t, (h & 1) * 4 + cc)) = ok;
+        tc::mma_bf16(tbase + o_col, tc::smem_desc(p_s + kk * 32, 1024, tc::kSW128),
+                     tc::smem_desc(vs + kk * 32, 1024, tc::kSW128), IDESC_O, j > 0 || kk > 0);
+      if (j + 1 < nkb) {
+        tc::mbar_wait(&kvbar[g * KV_STAGES + (j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, p.status, aborted);
+        issue_s(j + 1);
+        tc::mma_commit(&sbar[g]);
+      } else {
+        tc::mma_commit(&obar[g]);
       }
     }
   }
 
-  // ---- output projection of the gated heads + residual ----
+  // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) over this head's P tile ----
+  tc::mbar_wait(&obar[g], 0, p.status, aborted);
+  tc::tc_fence_after();
+  {
+    const float inv = l > 0.f ? 1.0f / l : 0.f;
+    float v0[16], v1[16];
+    tc::tmem_ld16(lane_addr + o_col, v0);
+    tc::tmem_ld16(lane_addr + o_col + 16, v1);
+    uint8_t* ost = smem + OFF_P + g * P_BYTES;
+#pragma unroll
+    for (int cc = 0; cc < D / 8; ++cc) {
+      const uint32_t* gu = reinterpret_cast<const uint32_t*>(&braw[cc]);
+      uint4 ok;
+      uint32_t* ou = reinterpret_cast<uint32_t*>(&ok);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = cc * 8 + 2 * e;
+        const float a0 = d < 16 ? v0[d] : v1[d - 16], a1 = d + 1 < 16 ? v0[d + 1] : v1[d - 15];
+        ou[e] = pack_bf2(a0 * inv * bf_lo(gu[e]), a1 * inv * bf_hi(gu[e]));
+      }
+      *reinterpret_cast<uint4*>(ost + tc::sw64_off(t, cc)) = ok;
+    }
+    // W_o[:, 32h .. 32h+31] as K-major 128 x 32 (64B swizzle) over this head's Q tile (its S' MMAs are done)
+    uint8_t* wst = smem + OFF_Q + g * 8192;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = t + 128 * i, n = e >> 2, c = e & 3;
+      cp_async16(wst + tc::sw64_off(n, c), p.w_out + n * C + g * D + c * 8);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+  }
   tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();
@@ -497,34 +549,38 @@ __global__ void __launch_bounds__(256, 1) k_triatt_core_tc(AttCoreParams p) {
     tc::tc_fence_after();
     constexpr uint32_t IDESC = tc::idesc_bf16(128, 128);
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int ka = k >> 2, kk = k & 3;
-      tc::mma_bf16(tbase + 256, tc::smem_desc(sb + OFF_O + ka * 16384 + kk * 32, 1024, tc::kSW128),
-                   tc::smem_desc(sb + OFF_W + ka * 16384 + kk * 32, 1024, tc::kSW128), IDESC, k > 0);
+    for (int k = 0; k < 2 * H; ++k) {
+      const int h = k >> 1, kk = k & 1;
+      tc::mma_bf16(tbase + 384, tc::smem_desc(sb + OFF_P + h * P_BYTES + kk * 32, 512, tc::kSW64),
+                   tc::smem_desc(sb + OFF_Q + h * 8192 + kk * 32, 512, tc::kSW64), IDESC, k > 0);
     }
-    tc::mma_commit(outdone);
+    tc::mma_commit(outbar);
   }
-  tc::mbar_wait(outdone, 0, p.status, aborted);
+  tc::mbar_wait(outbar, 0, p.status, aborted);
   tc::tc_fence_after();
   {
+    // query q, output channels 32g .. 32g+31
     const bool live = q < p.nq;
     const int64_t pos = live ? (p.transpose ? q * p.cols + b : b * p.cols + q) : 0;
-    const uint4* zin = reinterpret_cast<const uint4*>(p.z + pos * C + g * 64);
-    uint4* zo = reinterpret_cast<uint4*>(p.z_out + pos * C + g * 64);
+    const uint4* zin = reinterpret_cast<const uint4*>(p.z + pos * C + g * D);
+    uint4* zo = reinterpret_cast<uint4*>(p.z_out + pos * C + g * D);
+    float v0[16], v1[16];
+    tc::tmem_ld16(lane_addr + 384 + g * D, v0);   // warp-collective: every lane loads
+    tc::tmem_ld16(lane_addr + 384 + g * D + 16, v1);
+    if (live) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float v[16];
-      tc::tmem_ld16(lane_addr + 256 + g * 64 + 16 * i, v);   // warp-collective: every lane loads
-#pragma unroll
-      for (int hlf = 0; hlf < 2 && live; ++hlf) {
-        const uint4 zz = zin[2 * i + hlf];
+      for (int cc = 0; cc < D / 8; ++cc) {
+        const uint4 zz = zin[cc];
         const uint32_t* zu = reinterpret_cast<const uint32_t*>(&zz);
         uint4 r;
         uint32_t* ru = reinterpret_cast<uint32_t*>(&r);
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          ru[e] = pack_bf2(bf_lo(zu[e]) + v[hlf * 8 + 2 * e], bf_hi(zu[e]) + v[hlf * 8 + 2 * e + 1]);
-        zo[2 * i + hlf] = r;
+        for (int e = 0; e < 4; ++e) {
+          const int d = cc * 8 + 2 * e;
+          const float a0 = d < 16 ? v0[d] : v1[d - 16], a1 = d + 1 < 16 ? v0[d + 1] : v1[d - 15];
+          ru[e] = pack_bf2(bf_lo(zu[e]) + a0, bf_hi(zu[e]) + a1);
+        }
+        zo[cc] = r;
       }
     }
   }
@@ -581,7 +637,7 @@ __global__ void k_triatt_bias(const bf16* __restrict__ z, const float* __restric
   if (lane == 0) {
     const int64_t r = pos / n, sc = pos % n;
 #pragma unroll
-    for (int h = 0; h < H; ++h) bias[(r * H + h) * ldb + sc] = __float2bfloat16_rn(acc[h] * kLog2e);
+    for (int h = 0; h < H; ++h) bias[(r * H + h) * ldb + sc] = __float2bfloat16_rn(acc[h] * kBiasScale);
   }
 }
 
@@ -626,16 +682,24 @@ int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, 
                    int64_t batch_offset, cudaStream_t stream) {
   if (rows == 0 || cols == 0) return SF_OK;
   const int64_t nb = transpose ? cols : rows, nq = transpose ? rows : cols;
-  SF_REQUIRE(nb <= 65535 && nq <= 65535, "triatt_core: block too large");
+  const int64_t qp = triatt_query_pitch(nq);
+  SF_REQUIRE(nb <= 65535 && qp <= MAX_QP, "triatt_core: block [%lld][%lld] too large", (long long)rows,
+             (long long)cols);
+  SF_REQUIRE(nb * H * qp < (int64_t(1) << 31), "triatt_core: %lld attention rows x %lld keys exceed the TMA range",
+             (long long)nb, (long long)qp);
   uint32_t* status = device_status_ptr();
   if (!status) return SF_ERR_CUDA;
   static bool attr[64] = {false};
   SF_TRY(set_smem(k_triatt_core_tc, SMEM_CORE, attr));
-  const int64_t qp = triatt_query_pitch(nq);
-  AttCoreParams cp{q, k, vt, g, bias, w_out, mask, z, z_out, cols, nq, qp, batch_offset, transpose,
+  // Q, K [nb*H*qp][32] (64B swizzle, 128- and 64-row boxes); V^T [nb*H*32][qp] (128B swizzle, 64 keys x 32)
+  CUtensorMap mq, mk, mv;
+  SF_TRY(make_2d_tmap(&mq, q, D, nb * H * qp, D, TILE, 64));
+  SF_TRY(make_2d_tmap(&mk, k, D, nb * H * qp, D, KB, 64));
+  SF_TRY(make_2d_tmap(&mv, vt, qp, nb * H * D, KB, D, 128));
+  AttCoreParams cp{g, bias, w_out, mask, z, z_out, cols, nq, qp, batch_offset, transpose,
                    (1.0f / sqrtf((float)D)) * kLog2e, status};
   dim3 cgrid((unsigned)(qp / TILE), (unsigned)nb);
-  k_triatt_core_tc<<<cgrid, 256, SMEM_CORE, stream>>>(cp);
+  k_triatt_core_tc<<<cgrid, 512, SMEM_CORE, stream>>>(mq, mk, mv, cp);
   count_launch();
   return check_launch("triatt_core_tc");
 }
