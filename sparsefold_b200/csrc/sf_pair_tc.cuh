@@ -20,6 +20,13 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 __device__ __forceinline__ float fast_sigmoid(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+// sigmoid(x) = (1 + tanh(x/2)) / 2 with the single-instruction tanh approximation
+// (absolute error ~1e-3 of the hardware tanh, below bf16 resolution of the results).
+__device__ __forceinline__ float sigmoid_tanh(float x) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * x));
+  return fmaf(0.5f, t, 0.5f);
+}
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -75,6 +82,58 @@ __device__ __forceinline__ void ln_row_inplace(uint8_t* tile, int r, const float
 #pragma unroll
     for (int c = 0; c < 8; ++c)
       *reinterpret_cast<uint4*>(tile + ka * ATOM + tc::sw128_off(r, c)) = v[ka * 8 + c];
+}
+
+// Same LayerNorm with few registers (for kernels with many warps), from row r
+// of tile `src` into row r of tile `dst` (both 128B-swizzled K-major, may be
+// the same tile): the row is re-read from shared memory for each statistic
+// pass and normalised one 16-byte chunk at a time.  w and b (b may be null)
+// must be 16-byte aligned.
+__device__ __forceinline__ void ln_row_lr(const uint8_t* src, uint8_t* dst, int r, const float* __restrict__ w,
+                                          const float* __restrict__ b, float eps) {
+  auto off = [&](int i) -> uint32_t { return (uint32_t)(i >> 3) * ATOM + tc::sw128_off(r, i & 7); };
+  float s = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src + off(i));
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s += bf_lo(u[j]) + bf_hi(u[j]);
+  }
+  const float mean = s * (1.0f / C);
+  float q = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src + off(i));
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d0 = bf_lo(u[j]) - mean, d1 = bf_hi(u[j]) - mean;
+      q += d0 * d0 + d1 * d1;
+    }
+  }
+  const float rstd = rsqrtf(q * (1.0f / C) + eps);
+#pragma unroll 2
+  for (int i = 0; i < 16; ++i) {
+    uint4 v = *reinterpret_cast<const uint4*>(src + off(i));
+    uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + 8 * i));
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + 8 * i + 4));
+    float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+    if (b) {
+      b0 = __ldg(reinterpret_cast<const float4*>(b + 8 * i));
+      b1 = __ldg(reinterpret_cast<const float4*>(b + 8 * i + 4));
+    }
+    u[0] = pack_bf2((bf_lo(u[0]) - mean) * rstd * w0.x + b0.x, (bf_hi(u[0]) - mean) * rstd * w0.y + b0.y);
+    u[1] = pack_bf2((bf_lo(u[1]) - mean) * rstd * w0.z + b0.z, (bf_hi(u[1]) - mean) * rstd * w0.w + b0.w);
+    u[2] = pack_bf2((bf_lo(u[2]) - mean) * rstd * w1.x + b1.x, (bf_hi(u[2]) - mean) * rstd * w1.y + b1.y);
+    u[3] = pack_bf2((bf_lo(u[3]) - mean) * rstd * w1.z + b1.z, (bf_hi(u[3]) - mean) * rstd * w1.w + b1.w);
+    *reinterpret_cast<uint4*>(dst + off(i)) = v;
+  }
+}
+__device__ __forceinline__ void ln_row_inplace_lr(uint8_t* tile, int r, const float* __restrict__ w,
+                                                  const float* __restrict__ b, float eps) {
+  ln_row_lr(tile, tile, r, w, b, eps);
 }
 
 // Copies a weight matrix Wt[rows][128] (bf16, k contiguous) into shared memory

@@ -1,13 +1,14 @@
 // Triangle multiplication, bf16 track, on tcgen05 (blocks.py:484-566).
 //
-// k_trimul_project_tc: persistent, one CTA (4 warps) per SM.  Per 128-position
-// tile: TMA brings the raw z tile into shared memory (128B swizzle, the UMMA
-// K-major layout), every thread layer-norms its row in place, one thread
-// issues 16 tcgen05.mma (M=128, N=2x256, K=128) against the GLU weight kept
-// resident in shared memory, and the epilogue reads the 512 fp32 TMEM columns
-// per row, applies sigmoid(gate) * value * mask and writes the contraction
-// operands as [row][channel][pitch].  The next tile's TMA is issued before the current
-// tile is processed (two A stages).
+// k_trimul_project_tc: persistent, one warp-specialised CTA per SM.  Per
+// 128-position tile: TMA brings the raw z tile into shared memory (128B
+// swizzle, the UMMA K-major layout, two stages), four warps layer-norm its
+// rows in place, one thread issues the GLU GEMMs transposed,
+// D[out channel][position] = W . LN(z)^T (M=128, N=128, K=128, four weight
+// matrices kept resident), into two TMEM halves so the epilogue of one operand
+// overlaps the GEMM of the other, and eight epilogue warps apply
+// sigmoid(gate) * value * mask and TMA-store the contraction operands as
+// [row][channel][pitch] (each TMEM lane is one channel row of the output).
 #include "sf_pair_tc.cuh"
 
 namespace sf {
@@ -19,31 +20,43 @@ struct ProjParams {
   const uint8_t* mask;      // [n] token mask
   const float* ln_w;
   const float* ln_b;
-  const bf16* w_glu;        // [512][128]
-  bf16* a_op;
-  bf16* b_op;
-  int64_t rows, n, row_offset;
+  int64_t rows, n, row_offset, pitch;
   int incoming;
   uint32_t* status;
 };
 
+// Warp roles (448 threads):
+//   warps 0-7   epilogue: warp w reads TMEM lanes 32(w%4).. (output channels) and
+//               positions 64(w/4)..+63 of the tile; stages sigmoid(gate) * value *
+//               mask as [32 channels][64 positions] (128B swizzle) and TMA-stores it
+//   warps 8-11  layer norm of the tile rows in place (thread = position)
+//   warp 12     TMA producer of z tiles (two stages)
+//   warp 13     MMA issuer: D[out channel][position] = W_x . LN(z)^T for the four
+//               GLU matrices, two at a time (TMEM halves a = cols 0-255, b = 256-511)
 constexpr int NOUT = 512;
-constexpr int W_BYTES = NOUT * C * 2;                       // 128 KB
-constexpr int CH_CHUNK = 32;                                // channels staged per epilogue step
-constexpr int STAGE_OUT = CH_CHUNK * TILE * 2;              // one [32][128] bf16 staging tile (8 KB)
-constexpr int SMEM_PROJ = 2 * A_BYTES + W_BYTES + 2 * STAGE_OUT + 1024 + 1024;
+constexpr int W_BYTES = NOUT * C * 2;                       // 128 KB, rows = gate_a, val_a, gate_b, val_b
+constexpr int EPI_WARPS = 8;
+constexpr int PROJ_THREADS = (EPI_WARPS + 4 + 2) * 32;
+constexpr int ST_BYTES = 32 * 128;                          // one epilogue warp's staging: 32 channels x 64 positions
+constexpr int OFF_PW = 0;
+constexpr int OFF_PZ = W_BYTES;                             // two z stages
+constexpr int OFF_PST = OFF_PZ + 2 * A_BYTES;               // 8 staging tiles
+constexpr int OFF_PBAR = OFF_PST + EPI_WARPS * ST_BYTES;
+constexpr int SMEM_PROJ = OFF_PBAR + 256 + 1024;
 
-__global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_constant__ CUtensorMap tmap,
-                                                              ProjParams p) {
+__global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __grid_constant__ CUtensorMap tmZ,
+                                                                       const __grid_constant__ CUtensorMap tmA,
+                                                                       const __grid_constant__ CUtensorMap tmB,
+                                                                       const bf16* __restrict__ w_glu, ProjParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* A = smem;
-  uint8_t* W = smem + 2 * A_BYTES;
-  bf16* stA = reinterpret_cast<bf16*>(W + W_BYTES);             // [32 channels][128 positions]
-  bf16* stB = stA + CH_CHUNK * TILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(W + W_BYTES + 2 * STAGE_OUT);   // [0,1] tma stages, [2] mma
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_PBAR);   // [2] z tile landed
+  uint64_t* normed = full + 2;                                      // [2] z tile normalised (128 arrivals)
+  uint64_t* zfree = normed + 2;                                     // [2] MMAs of the stage done
+  uint64_t* tfull = zfree + 2;                                      // [2] TMEM half written
+  uint64_t* tfree = tfull + 2;                                      // [2] TMEM half read (8 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   const int64_t span = p.incoming ? p.rows : p.n;              // positions along a tile's axis
   const int64_t nb = (span + TILE - 1) / TILE;
@@ -54,111 +67,147 @@ __global__ void __launch_bounds__(128, 1) k_trimul_project_tc(const __grid_const
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    tc::mbar_init(&bars[0], 1);
-    tc::mbar_init(&bars[1], 1);
-    tc::mbar_init(&bars[2], 1);
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&normed[s], 128);
+      tc::mbar_init(&zfree[s], 1);
+      tc::mbar_init(&tfull[s], 1);
+      tc::mbar_init(&tfree[s], EPI_WARPS);
+    }
     tc::fence_mbar_init();
-    tc::prefetch_tmap(&tmap);
+    tc::prefetch_tmap(&tmZ);
+    tc::prefetch_tmap(&tmA);
+    tc::prefetch_tmap(&tmB);
   }
-  load_weight_sw128(W, p.w_glu, NOUT, tid, 128);
+  load_weight_sw128(smem + OFF_PW, w_glu, NOUT, tid, PROJ_THREADS);
   tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
 
-  auto issue = [&](int64_t tile, int stage) {
-    const int64_t major = tile / nb, minor = (tile % nb) * TILE;
-    // tensor coordinates (channel, column, row)
-    const int c1 = (int)(p.incoming ? major : minor);
-    const int c2 = (int)(p.incoming ? minor : major);
-    tc::mbar_expect_tx(&bars[stage], A_BYTES);
-    tc::tma_load_3d(A + stage * A_BYTES, &tmap, &bars[stage], 0, c1, c2);
-    tc::tma_load_3d(A + stage * A_BYTES + ATOM, &tmap, &bars[stage], 64, c1, c2);
-  };
-
-  constexpr uint32_t IDESC = tc::idesc_bf16(128, 256);
-  const uint32_t a_base = tc::smem_u32(A), w_base = tc::smem_u32(W);
-  // operands are [row][channel][pitch]: outgoing rows = pair rows r, columns s;
-  // incoming (transposed) rows = pair columns s, columns = local pair rows r
-  const int64_t pitch = pair_pitch(p.incoming ? p.rows : p.n);
-
-  int64_t tile = blockIdx.x;
-  if (tid == 0 && tile < ntiles) issue(tile, 0);
-  for (uint32_t it = 0; tile < ntiles; tile += gridDim.x, ++it) {
-    const int stage = it & 1;
-    if (tid == 0 && tile + gridDim.x < ntiles) {
+  if (warp == 12) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+        const int st = it & 1;
+        if (it >= 2) tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
+        const int64_t major = tile / nb, minor = (tile % nb) * TILE;
+        const int c1 = (int)(p.incoming ? major : minor);    // tensor coordinates (channel, column, row)
+        const int c2 = (int)(p.incoming ? minor : major);
+        uint8_t* dst = smem + OFF_PZ + st * A_BYTES;
+        tc::mbar_expect_tx(&full[st], A_BYTES);
+        tc::tma_load_3d(dst, &tmZ, &full[st], 0, c1, c2);
+        tc::tma_load_3d(dst + ATOM, &tmZ, &full[st], 64, c1, c2);
+      }
+    }
+  } else if (warp == 13) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t IDESC = tc::idesc_bf16(128, 128);
+      uint32_t it = 0;
+      for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+        const int st = it & 1;
+        tc::mbar_wait(&normed[st], (it >> 1) & 1, p.status, aborted);
+        tc::tc_fence_after();
+        const uint32_t zb = sb + OFF_PZ + st * A_BYTES;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          if (it >= 1) tc::mbar_wait(&tfree[hh], (it - 1) & 1, p.status, aborted);
+          tc::tc_fence_after();
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {          // gate, value of operand hh
+            const int mtx = 2 * hh + mt;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int ka = k >> 2, kk = k & 3;
+              tc::mma_bf16(tbase + hh * 256 + mt * 128,
+                           tc::smem_desc(sb + OFF_PW + ka * (NOUT * 128) + mtx * (128 * 128) + kk * 32, 1024, tc::kSW128),
+                           tc::smem_desc(zb + ka * ATOM + kk * 32, 1024, tc::kSW128), IDESC, k > 0);
+            }
+          }
+          tc::mma_commit(&tfull[hh]);
+        }
+        tc::mma_commit(&zfree[st]);
+      }
+    }
+  } else if (warp >= EPI_WARPS) {
+    // ---- layer norm (thread = tile row) ----
+    const int r = tid - EPI_WARPS * 32;
+    uint32_t it = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int st = it & 1;
+      tc::mbar_wait(&full[st], (it >> 1) & 1, p.status, aborted);
+      ln_row_inplace_lr(smem + OFF_PZ + st * A_BYTES, r, p.ln_w, p.ln_b, 1e-5f);
       tc::fence_proxy_async();
-      issue(tile + gridDim.x, stage ^ 1);
+      tc::mbar_arrive(&normed[st]);
     }
-    tc::mbar_wait(&bars[stage], (it >> 1) & 1, p.status, aborted);
-    uint8_t* At = A + stage * A_BYTES;
-    ln_row_inplace(At, tid, p.ln_w, p.ln_b, 1e-5f);
-    tc::fence_proxy_async();
-    tc::tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc::tc_fence_after();
+  } else {
+    // ---- epilogue ----
+    const int quad = warp & 3, hf = warp >> 2;
+    const uint32_t lane_addr = tbase + ((uint32_t)(32 * quad) << 16);
+    uint8_t* stg = smem + OFF_PST + warp * ST_BYTES;
+    uint32_t it = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int64_t major = tile / nb, minor0 = (tile % nb) * TILE + hf * 64;
+      // keep[pos] = valid && mask[row] && mask[col] for the warp's 64 positions
+      uint64_t keep;
+      {
+        uint32_t kw[2];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int ka = k >> 2, kk = k & 3;
-        const uint64_t ad = tc::smem_desc(a_base + stage * A_BYTES + ka * ATOM + kk * 32, 1024, tc::kSW128);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint64_t bd = tc::smem_desc(w_base + ka * (NOUT * 128) + h * (256 * 128) + kk * 32, 1024, tc::kSW128);
-          tc::mma_bf16(tbase + h * 256, ad, bd, IDESC, k > 0);
+        for (int i = 0; i < 2; ++i) {
+          const int64_t minor = minor0 + 32 * i + lane;
+          bool k = minor < span;
+          if (k) {
+            const int64_t rr = p.incoming ? minor : major, ss = p.incoming ? major : minor;
+            k = p.mask[p.row_offset + rr] != 0 && p.mask[ss] != 0;
+          }
+          kw[i] = __ballot_sync(0xffffffffu, k);
         }
+        keep = (uint64_t)kw[0] | ((uint64_t)kw[1] << 32);
       }
-      tc::mma_commit(&bars[2]);
-    }
-    tc::mbar_wait(&bars[2], it & 1, p.status, aborted);
-    tc::tc_fence_after();
-
-    // ---- epilogue: position tid of the tile; 32 channels at a time are staged as
-    // [channel][position] and written as contiguous 256-byte rows of the operands ----
-    const int64_t major = tile / nb, minor0 = (tile % nb) * TILE, minor = minor0 + tid;
-    const bool valid = minor < span;
-    const int64_t r = p.incoming ? minor : major;     // local pair row
-    const int64_t s = p.incoming ? major : minor;     // pair column
-    const bool keep = valid && p.mask[p.row_offset + r] && p.mask[s];
-    bf16* ao = p.incoming ? p.b_op : p.a_op;          // incoming: A <- b, B <- a (transposed)
-    bf16* bo = p.incoming ? p.a_op : p.b_op;
-    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
-    const int64_t row_base = major * C * pitch + minor0;   // operand row `major`, first position of the tile
 #pragma unroll 1
-    for (int cc = 0; cc < C / CH_CHUNK; ++cc) {
+      for (int hh = 0; hh < 2; ++hh) {
+        tc::mbar_wait(&tfull[hh], it & 1, p.status, aborted);
+        tc::tc_fence_after();
+        if (lane == 0) tc::bulk_wait_read0();   // previous store from this staging tile has read it
+        __syncwarp();
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int c0 = cc * CH_CHUNK + hf * 16;
-        float ga[16], va[16], gb[16], vb[16];
-        tc::tmem_ld16(lane_addr + c0, ga);
-        tc::tmem_ld16(lane_addr + 128 + c0, va);
-        tc::tmem_ld16(lane_addr + 256 + c0, gb);
-        tc::tmem_ld16(lane_addr + 384 + c0, vb);
+        for (int k = 0; k < 4; ++k) {
+          float gt[16], vl[16];
+          tc::tmem_ld16(lane_addr + hh * 256 + hf * 64 + 16 * k, gt);
+          tc::tmem_ld16(lane_addr + hh * 256 + 128 + hf * 64 + 16 * k, vl);
+          uint32_t pk[8];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          stA[(hf * 16 + e) * TILE + tid] = __float2bfloat16_rn(keep ? fast_sigmoid(ga[e]) * va[e] : 0.f);
-          stB[(hf * 16 + e) * TILE + tid] = __float2bfloat16_rn(keep ? fast_sigmoid(gb[e]) * vb[e] : 0.f);
+          for (int e = 0; e < 8; ++e) {
+            const int i0 = 16 * k + 2 * e;
+            const float o0 = ((keep >> i0) & 1) ? sigmoid_tanh(gt[2 * e]) * vl[2 * e] : 0.f;
+            const float o1 = ((keep >> (i0 + 1)) & 1) ? sigmoid_tanh(gt[2 * e + 1]) * vl[2 * e + 1] : 0.f;
+            pk[e] = pack_bf2(o0, o1);
+          }
+          *reinterpret_cast<uint4*>(stg + tc::sw128_off(lane, 2 * k)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(stg + tc::sw128_off(lane, 2 * k + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        }
+        tc::tc_fence_before();
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&tfree[hh]);
+          // tmA receives the gate_a/val_a product, tmB the gate_b/val_b one (the host swaps
+          // the operands for the incoming direction)
+          if (minor0 < p.pitch) {
+            tc::tma_store_3d(hh == 0 ? &tmA : &tmB, stg, (int)minor0, 32 * quad, (int)major);
+            tc::bulk_commit();
+          }
         }
       }
-      __syncthreads();
-      // 32 channel rows x 16 chunks of 16 bytes per operand
-#pragma unroll
-      for (int i = 0; i < (CH_CHUNK * 16) / 128; ++i) {
-        const int e = tid + 128 * i;
-        const int c = e >> 4, part = e & 15;
-        if (minor0 + part * 8 + 8 <= pitch) {
-          const int64_t off = row_base + (int64_t)(cc * CH_CHUNK + c) * pitch + part * 8;
-          *reinterpret_cast<uint4*>(ao + off) = *reinterpret_cast<const uint4*>(stA + c * TILE + part * 8);
-          *reinterpret_cast<uint4*>(bo + off) = *reinterpret_cast<const uint4*>(stB + c * TILE + part * 8);
-        }
-      }
-      __syncthreads();
     }
-    tc::tc_fence_before();
-    __syncthreads();
+    if (lane == 0) tc::bulk_wait0();
   }
+  tc::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc::tc_fence_after();
@@ -230,8 +279,38 @@ int trimul_project_tc(const bf16* z, const uint8_t* mask, int64_t rows, int64_t 
                       cudaStream_t stream) {
   if (rows == 0 || n == 0) return SF_OK;
   SF_REQUIRE(n <= (1 << 24) && rows <= (1 << 24), "trimul_project_tc: size too large");
-  CUtensorMap map;
-  SF_TRY(make_pair_tmap(&map, z, rows, n, incoming != 0));
+  SF_REQUIRE((reinterpret_cast<uintptr_t>(ln_w) & 15) == 0 && (reinterpret_cast<uintptr_t>(ln_b) & 15) == 0,
+             "trimul_project_tc: layer-norm parameters must be 16-byte aligned");
+  CUtensorMap mz, ma, mb;
+  SF_TRY(make_pair_tmap(&mz, z, rows, n, incoming != 0));
+  // operands [majors][C][pitch]: outgoing majors = local rows (positions = columns),
+  // incoming majors = columns (positions = local rows) with A <- b and B <- a
+  const int64_t majors = incoming ? n : rows;
+  const int64_t pitch = pair_pitch(incoming ? rows : n);
+  {
+    auto encode = tensor_map_encoder();
+    if (!encode) return SF_ERR_CUDA;
+    bf16* dst[2] = {incoming ? b_op : a_op, incoming ? a_op : b_op};
+    CUtensorMap* maps[2] = {&ma, &mb};
+    for (int i = 0; i < 2; ++i) {
+      if ((reinterpret_cast<uintptr_t>(dst[i]) & 15) != 0) {
+        set_error("trimul_project_tc: operand %p is not 16-byte aligned", (void*)dst[i]);
+        return SF_ERR_ARG;
+      }
+      cuuint64_t dims[3] = {(cuuint64_t)pitch, (cuuint64_t)pt::C, (cuuint64_t)majors};
+      cuuint64_t strides[2] = {(cuuint64_t)pitch * 2, (cuuint64_t)(pt::C * pitch * 2)};
+      cuuint32_t box[3] = {64, 32, 1};
+      cuuint32_t estr[3] = {1, 1, 1};
+      CUresult r = encode(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dst[i], dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d) for operand [%lld][128][%lld]", (int)r, (long long)majors,
+                  (long long)pitch);
+        return SF_ERR_CUDA;
+      }
+    }
+  }
   uint32_t* status = device_status_ptr();
   if (!status) return SF_ERR_CUDA;
   static bool attr_set[64] = {false};
@@ -245,11 +324,11 @@ int trimul_project_tc(const bf16* z, const uint8_t* mask, int64_t rows, int64_t 
     }
     attr_set[dev & 63] = true;
   }
-  ProjParams p{mask, ln_w, ln_b, w_glu, a_op, b_op, rows, n, row_offset, incoming, status};
+  ProjParams p{mask, ln_w, ln_b, rows, n, row_offset, pitch, incoming, status};
   const int64_t span = incoming ? rows : n;
-  const int64_t ntiles = (incoming ? n : rows) * ((span + pt::TILE - 1) / pt::TILE);
+  const int64_t ntiles = majors * ((span + pt::TILE - 1) / pt::TILE);
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  k_trimul_project_tc<<<grid, 128, SMEM_PROJ, stream>>>(map, p);
+  k_trimul_project_tc<<<grid, PROJ_THREADS, SMEM_PROJ, stream>>>(mz, ma, mb, w_glu, p);
   count_launch();
   return check_launch("trimul_project_tc");
 }
