@@ -1,14 +1,18 @@
 // Pair transition (TransitionBlock, blocks.py:79-96) on tcgen05, bf16 track:
 //   y = x + (swish(LN(x) W1a) * (LN(x) W1b)) W2,   C = 128, I = 512.
 //
-// One CTA (8 epilogue warps + 1 weight-producer warp) handles 256 positions per
-// iteration as two 128-row tiles that share every weight chunk.  The hidden
-// layer is walked in 8 chunks of 64 units: GEMM1 (M128 N128 K128 per tile,
-// a- and b-halves of the chunk side by side) lands in TMEM columns [0,256);
-// the epilogue warps turn it into swish(a)*b (bf16) in shared memory; GEMM2
-// (M128 N128 K64 per tile) accumulates the down projection in TMEM columns
-// [256,512).  W1/W2 chunks (32 + 16 KB) stream through a 2-stage TMA ring, so
-// the full 384 KB of weights is read once per 256 positions from L2.
+// Persistent, one warp-specialised CTA per SM; 256 positions (two 128-row
+// tiles sharing every weight chunk) per pass.  The hidden layer is walked in 16
+// chunks of 32 units:
+//   warp 8      TMA producer: the x tiles of a pass, and per chunk the 64 rows of
+//               W1 (32 a + 32 b, 16 KB) and the 32 columns of W2 (8 KB), each in a
+//               4-stage ring
+//   warp 9      MMA issuer: GEMM1 of chunk c (M128 N64 K128 per tile) into one of
+//               two TMEM buffers, then GEMM2 of chunk c-1 (M128 N128 K32 per tile)
+//               accumulating the down projection in TMEM columns [256,512)
+//   warps 0-7   thread = position (warps 0-3 tile 0, 4-7 tile 1): LayerNorm of
+//               the pass in place, then per chunk swish(a) * b from TMEM into the
+//               64B-swizzled hidden tile, and finally y = x + acc.
 #include "sf_pair_tc.cuh"
 
 namespace sf {
@@ -16,14 +20,19 @@ namespace {
 
 using namespace pt;
 
-constexpr int I = 512, HC = 64, NCHUNK = I / HC;
+constexpr int I = 512, HC = 32, NCHUNK = I / HC;
+constexpr int TR_STAGES = 4;
 constexpr int X_BYTES = 2 * A_BYTES;           // two 128x128 input tiles
-constexpr int H_BYTES = 2 * TILE * 128;        // two 128x64 hidden tiles (one 128B atom each)
-constexpr int W1C_BYTES = 128 * 256;           // 128 rows (64 a + 64 b) x 128 k
-constexpr int W2C_BYTES = 128 * 128;           // 128 out rows x 64 k
-constexpr int WST_BYTES = W1C_BYTES + W2C_BYTES;
-constexpr int OFF_X = 0, OFF_H = X_BYTES, OFF_W = OFF_H + H_BYTES, OFF_BAR = OFF_W + 2 * WST_BYTES;
-constexpr int SMEM_TR = OFF_BAR + 1024 + 1024;
+constexpr int H_BYTES = TILE * HC * 2;         // one 128 x 32 hidden tile (8 KB)
+constexpr int W1C_BYTES = 2 * 64 * 128;        // 64 rows (32 a + 32 b) x 128 k, two 64-channel atoms
+constexpr int W2C_BYTES = C * HC * 2;          // 128 out rows x 32 k (64B swizzle)
+constexpr int OFF_X = 0;
+constexpr int OFF_H = OFF_X + X_BYTES;                       // [2 buffers][2 tiles]
+constexpr int OFF_W1 = OFF_H + 4 * H_BYTES;                  // [stage]
+constexpr int OFF_W2 = OFF_W1 + TR_STAGES * W1C_BYTES;       // [stage]
+constexpr int OFF_BAR = OFF_W2 + TR_STAGES * W2C_BYTES;
+constexpr int SMEM_TR = OFF_BAR + 512 + 1024;
+constexpr int TR_THREADS = 10 * 32;
 
 struct TrParams {
   const bf16* x;
@@ -34,26 +43,51 @@ struct TrParams {
   uint32_t* status;
 };
 
-__global__ void __launch_bounds__(288, 1) k_transition_tc(const __grid_constant__ CUtensorMap tmX,
-                                                          const __grid_constant__ CUtensorMap tmW1,
-                                                          const __grid_constant__ CUtensorMap tmW2, TrParams p) {
+__global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_constant__ CUtensorMap tmX,
+                                                                 const __grid_constant__ CUtensorMap tmW1,
+                                                                 const __grid_constant__ CUtensorMap tmW2, TrParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [2]
-  uint64_t* wempty = wfull + 2;                                     // [2]
-  uint64_t* xbar = wfull + 4;
-  uint64_t* g1bar = wfull + 5;
-  uint64_t* g2bar = wfull + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wfull + 8);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* xfull = bars;                        // x tiles landed
+  uint64_t* xready = bars + 1;                   // LN done (256)
+  uint64_t* xfree = bars + 2;                    // last GEMM1 of the pass done
+  uint64_t* accfull = bars + 3;                  // last GEMM2 of the pass done
+  uint64_t* accfree = bars + 4;                  // accumulators read (8 warps)
+  uint64_t* w1full = bars + 5;                   // [TR_STAGES]
+  uint64_t* w1free = w1full + TR_STAGES;
+  uint64_t* w2full = w1free + TR_STAGES;
+  uint64_t* w2free = w2full + TR_STAGES;
+  uint64_t* s1full = w2free + TR_STAGES;         // [2]
+  uint64_t* s1free = s1full + 2;                 // [2] (8 warps)
+  uint64_t* hfull = s1free + 2;                  // [2] (8 warps)
+  uint64_t* hfree = hfull + 2;                   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hfree + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t npairs = (p.M + 2 * TILE - 1) / (2 * TILE);
+  const int64_t npasses = (p.M + 2 * TILE - 1) / (2 * TILE);
 
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 7; ++i) tc::mbar_init(&wfull[i], 1);
+    tc::mbar_init(xfull, 1);
+    tc::mbar_init(xready, 256);
+    tc::mbar_init(xfree, 1);
+    tc::mbar_init(accfull, 1);
+    tc::mbar_init(accfree, 8);
+    for (int s = 0; s < TR_STAGES; ++s) {
+      tc::mbar_init(&w1full[s], 1);
+      tc::mbar_init(&w1free[s], 1);
+      tc::mbar_init(&w2full[s], 1);
+      tc::mbar_init(&w2free[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(&s1full[s], 1);
+      tc::mbar_init(&s1free[s], 8);
+      tc::mbar_init(&hfull[s], 8);
+      tc::mbar_init(&hfree[s], 1);
+    }
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmX);
     tc::prefetch_tmap(&tmW1);
@@ -63,133 +97,150 @@ __global__ void __launch_bounds__(288, 1) k_transition_tc(const __grid_constant_
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
 
   if (warp == 8) {
-    // ---- weight producer: W1/W2 chunks for every (pair, chunk), 2-stage ring ----
+    // ---- TMA producer ----
     if (lane == 0) {
-      uint32_t q = 0;
-      for (int64_t pr = blockIdx.x; pr < npairs; pr += gridDim.x) {
+      uint32_t q = 0, pi = 0;
+      for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
+        const int64_t m0 = ps * 2 * TILE;
+        if (pi >= 1) tc::mbar_wait(xfree, (pi - 1) & 1, p.status, aborted);
+        tc::mbar_expect_tx(xfull, X_BYTES);
+        for (int t2 = 0; t2 < 2; ++t2)
+          for (int ka = 0; ka < 2; ++ka)
+            tc::tma_load_2d(smem + OFF_X + t2 * A_BYTES + ka * ATOM, &tmX, xfull, ka * 64, (int)(m0 + t2 * TILE));
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
-          const int s = q & 1;
-          tc::mbar_wait(&wempty[s], ((q >> 1) & 1) ^ 1, p.status, aborted);
-          uint8_t* w = smem + OFF_W + s * WST_BYTES;
-          tc::mbar_expect_tx(&wfull[s], WST_BYTES);
+          const int st = q % TR_STAGES;
+          const uint32_t ph = ((q / TR_STAGES) + 1) & 1;
+          if (q >= TR_STAGES) tc::mbar_wait(&w1free[st], ph, p.status, aborted);
+          uint8_t* w1 = smem + OFF_W1 + st * W1C_BYTES;
+          tc::mbar_expect_tx(&w1full[st], W1C_BYTES);
           for (int ka = 0; ka < 2; ++ka) {
-            tc::tma_load_2d(w + ka * (128 * 128), &tmW1, &wfull[s], ka * 64, hc * HC);             // a rows
-            tc::tma_load_2d(w + ka * (128 * 128) + 64 * 128, &tmW1, &wfull[s], ka * 64, I + hc * HC);  // b rows
+            tc::tma_load_2d(w1 + ka * 8192, &tmW1, &w1full[st], ka * 64, hc * HC);              // a rows
+            tc::tma_load_2d(w1 + ka * 8192 + 4096, &tmW1, &w1full[st], ka * 64, I + hc * HC);   // b rows
           }
-          tc::tma_load_2d(w + W1C_BYTES, &tmW2, &wfull[s], hc * HC, 0);
+          if (q >= TR_STAGES) tc::mbar_wait(&w2free[st], ph, p.status, aborted);
+          tc::mbar_expect_tx(&w2full[st], W2C_BYTES);
+          tc::tma_load_2d(smem + OFF_W2 + st * W2C_BYTES, &tmW2, &w2full[st], hc * HC, 0);
         }
       }
     }
-  } else {
-    // ---- 8 epilogue warps: warps 0-3 own tile 0, warps 4-7 tile 1; thread = row ----
-    const int tt = warp >> 2, r = tid & 127;
-    const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
-    const uint32_t sb = tc::smem_u32(smem);
-    uint32_t q = 0, it = 0;
-    for (int64_t pr = blockIdx.x; pr < npairs; pr += gridDim.x, ++it) {
-      const int64_t m0 = pr * 2 * TILE;
-      if (tid == 0) {
-        tc::mbar_expect_tx(xbar, X_BYTES);
+  } else if (warp == 9) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t ID1 = tc::idesc_bf16(128, 2 * HC), ID2 = tc::idesc_bf16(128, 128);
+      uint32_t q = 0, pi = 0;
+      auto gemm2 = [&](uint32_t qq, int first) {   // chunk qq: acc[t2] += H[t2] . W2 chunk^T
+        const int st = qq % TR_STAGES, hb = qq & 1;
+        tc::mbar_wait(&hfull[hb], (qq >> 1) & 1, p.status, aborted);
+        tc::mbar_wait(&w2full[st], (qq / TR_STAGES) & 1, p.status, aborted);
+        tc::tc_fence_after();
+        const uint32_t w2 = sb + OFF_W2 + st * W2C_BYTES;
         for (int t2 = 0; t2 < 2; ++t2)
-          for (int ka = 0; ka < 2; ++ka)
-            tc::tma_load_2d(smem + OFF_X + t2 * A_BYTES + ka * ATOM, &tmX, xbar, ka * 64, (int)(m0 + t2 * TILE));
-      }
-      tc::mbar_wait(xbar, it & 1, p.status, aborted);
-      ln_row_inplace(smem + OFF_X + tt * A_BYTES, r, p.ln_w, p.ln_b, 1e-5f);
-      tc::fence_proxy_async();
-      tc::tc_fence_before();
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
-        const int s = q & 1;
-        if (tid == 0) {
-          // GEMM1 for both tiles: acc1[t2] = LN(x)[t2] (128 x 128) . W1 chunk (128 x 128)
-          tc::mbar_wait(&wfull[s], (q >> 1) & 1, p.status, aborted);
+#pragma unroll
+          for (int kk = 0; kk < HC / 16; ++kk)
+            tc::mma_bf16(tbase + 256 + t2 * 128,
+                         tc::smem_desc(sb + OFF_H + (hb * 2 + t2) * H_BYTES + kk * 32, 512, tc::kSW64),
+                         tc::smem_desc(w2 + kk * 32, 512, tc::kSW64), ID2, !(first && kk == 0));
+        tc::mma_commit(&hfree[hb]);
+        tc::mma_commit(&w2free[st]);
+      };
+      for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
+        tc::mbar_wait(xready, pi & 1, p.status, aborted);
+        for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
+          const int st = q % TR_STAGES, sbuf = q & 1;
+          tc::mbar_wait(&w1full[st], (q / TR_STAGES) & 1, p.status, aborted);
+          if (q >= 2) tc::mbar_wait(&s1free[sbuf], ((q >> 1) + 1) & 1, p.status, aborted);
           tc::tc_fence_after();
-          constexpr uint32_t ID1 = tc::idesc_bf16(128, 128);
-          const uint32_t wb = sb + OFF_W + s * WST_BYTES;
+          const uint32_t w1 = sb + OFF_W1 + st * W1C_BYTES;
           for (int t2 = 0; t2 < 2; ++t2)
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
               const int ka = k >> 2, kk = k & 3;
-              tc::mma_bf16(tbase + t2 * 128,
+              tc::mma_bf16(tbase + sbuf * 128 + t2 * 64,
                            tc::smem_desc(sb + OFF_X + t2 * A_BYTES + ka * ATOM + kk * 32, 1024, tc::kSW128),
-                           tc::smem_desc(wb + ka * (128 * 128) + kk * 32, 1024, tc::kSW128), ID1, k > 0);
+                           tc::smem_desc(w1 + ka * 8192 + kk * 32, 1024, tc::kSW128), ID1, k > 0);
             }
-          tc::mma_commit(g1bar);
-        }
-        // the hidden tile H is reused: GEMM2 of the previous chunk must have finished with it
-        if (q > 0) tc::mbar_wait(g2bar, (q - 1) & 1, p.status, aborted);
-        tc::mbar_wait(g1bar, q & 1, p.status, aborted);
-        tc::tc_fence_after();
-        uint8_t* hrow = smem + OFF_H + tt * (TILE * 128);
-#pragma unroll 1
-        for (int cg = 0; cg < 4; ++cg) {   // 16 hidden units at a time
-          float a[16], bv[16];
-          tc::tmem_ld16(lane_addr + tt * 128 + cg * 16, a);
-          tc::tmem_ld16(lane_addr + tt * 128 + 64 + cg * 16, bv);
-          uint4 o0, o1;
-          uint32_t* u0 = reinterpret_cast<uint32_t*>(&o0);
-          uint32_t* u1 = reinterpret_cast<uint32_t*>(&o1);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            u0[e] = pack_bf2(a[2 * e] * fast_sigmoid(a[2 * e]) * bv[2 * e],
-                             a[2 * e + 1] * fast_sigmoid(a[2 * e + 1]) * bv[2 * e + 1]);
-            u1[e] = pack_bf2(a[8 + 2 * e] * fast_sigmoid(a[8 + 2 * e]) * bv[8 + 2 * e],
-                             a[9 + 2 * e] * fast_sigmoid(a[9 + 2 * e]) * bv[9 + 2 * e]);
+          tc::mma_commit(&s1full[sbuf]);
+          tc::mma_commit(&w1free[st]);
+          if (hc == NCHUNK - 1) tc::mma_commit(xfree);
+          if (hc >= 1) {
+            if (hc == 1 && pi >= 1) tc::mbar_wait(accfree, (pi - 1) & 1, p.status, aborted);
+            gemm2(q - 1, hc == 1);
           }
-          *reinterpret_cast<uint4*>(hrow + tc::sw128_off(r, 2 * cg)) = o0;
-          *reinterpret_cast<uint4*>(hrow + tc::sw128_off(r, 2 * cg + 1)) = o1;
         }
-        tc::fence_proxy_async();
-        tc::tc_fence_before();
-        asm volatile("bar.sync 1, 256;" ::: "memory");
-        if (tid == 0) {
-          // GEMM2 for both tiles: acc2[t2] += H[t2] (128 x 64) . W2 chunk (128 x 64)
-          tc::tc_fence_after();
-          constexpr uint32_t ID2 = tc::idesc_bf16(128, 128);
-          const uint32_t wb = sb + OFF_W + s * WST_BYTES + W1C_BYTES;
-          for (int t2 = 0; t2 < 2; ++t2)
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc::mma_bf16(tbase + 256 + t2 * 128,
-                           tc::smem_desc(sb + OFF_H + t2 * (TILE * 128) + kk * 32, 1024, tc::kSW128),
-                           tc::smem_desc(wb + kk * 32, 1024, tc::kSW128), ID2, (hc | kk) != 0);
-          tc::mma_commit(&wempty[s]);   // weight stage free once both GEMMs of this chunk are done
-          tc::mma_commit(g2bar);
-        }
+        gemm2(q - 1, 0);
+        tc::mma_commit(accfull);
       }
-      // ---- residual epilogue: y = x + acc2 ----
-      tc::mbar_wait(g2bar, (q - 1) & 1, p.status, aborted);
+    }
+  } else {
+    // ---- 8 warps, thread = position: warps 0-3 tile 0, 4-7 tile 1 ----
+    const int t2 = warp >> 2, r = tid & 127;
+    const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
+    uint32_t q = 0, pi = 0;
+    for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
+      const int64_t m0 = ps * 2 * TILE;
+      tc::mbar_wait(xfull, pi & 1, p.status, aborted);
+      ln_row_inplace_lr(smem + OFF_X + t2 * A_BYTES, r, p.ln_w, p.ln_b, 1e-5f);
+      tc::fence_proxy_async();
+      tc::mbar_arrive(xready);
+      for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
+        const int sbuf = q & 1;
+        tc::mbar_wait(&s1full[sbuf], (q >> 1) & 1, p.status, aborted);
+        tc::tc_fence_after();
+        float a[HC], bv[HC];
+        tc::tmem_ld32(lane_addr + sbuf * 128 + t2 * 64, a);
+        tc::tmem_ld32(lane_addr + sbuf * 128 + t2 * 64 + HC, bv);
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&s1free[sbuf]);
+        uint32_t hv[HC / 2];
+#pragma unroll
+        for (int e = 0; e < HC / 2; ++e)
+          hv[e] = pack_bf2(a[2 * e] * sigmoid_tanh(a[2 * e]) * bv[2 * e],
+                           a[2 * e + 1] * sigmoid_tanh(a[2 * e + 1]) * bv[2 * e + 1]);
+        if (q >= 2) tc::mbar_wait(&hfree[sbuf], ((q >> 1) + 1) & 1, p.status, aborted);
+        uint8_t* hrow = smem + OFF_H + (sbuf * 2 + t2) * H_BYTES;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4*>(hrow + tc::sw64_off(r, c)) =
+              make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&hfull[sbuf]);
+      }
+      // ---- residual epilogue: y = x + acc ----
+      tc::mbar_wait(accfull, pi & 1, p.status, aborted);
       tc::tc_fence_after();
-      const int64_t m = m0 + tt * TILE + r;
+      const int64_t m = m0 + t2 * TILE + r;
       const bool live = m < p.M;
       const uint4* xr = reinterpret_cast<const uint4*>(p.x + (live ? m : 0) * C);
       uint4* yr = reinterpret_cast<uint4*>(p.y + (live ? m : 0) * C);
 #pragma unroll 1
-      for (int i = 0; i < 8; ++i) {
-        float v[16];
-        tc::tmem_ld16(lane_addr + 256 + tt * 128 + 16 * i, v);
+      for (int i = 0; i < 4; ++i) {
+        float v[32];
+        tc::tmem_ld32(lane_addr + 256 + t2 * 128 + 32 * i, v);
         if (live) {
 #pragma unroll
-          for (int hlf = 0; hlf < 2; ++hlf) {
-            const uint4 xx = xr[2 * i + hlf];
-            const uint32_t* xu = reinterpret_cast<const uint32_t*>(&xx);
-            uint4 o;
-            uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
+          for (int c = 0; c < 4; ++c) {
+            const uint4 xx = xr[4 * i + c];
+            const uint32_t xu[4] = {xx.x, xx.y, xx.z, xx.w};
+            uint32_t o[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-              ou[e] = pack_bf2(bf_lo(xu[e]) + v[hlf * 8 + 2 * e], bf_hi(xu[e]) + v[hlf * 8 + 2 * e + 1]);
-            yr[2 * i + hlf] = o;
+              o[e] = pack_bf2(bf_lo(xu[e]) + v[8 * c + 2 * e], bf_hi(xu[e]) + v[8 * c + 2 * e + 1]);
+            yr[4 * i + c] = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
       }
       tc::tc_fence_before();
-      asm volatile("bar.sync 1, 256;" ::: "memory");   // x tile and TMEM free for the next pair
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(accfree);
     }
   }
+  tc::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc::tc_fence_after();
@@ -232,10 +283,12 @@ int transition_tc(const bf16* x, const float* ln_w, const float* ln_b, const bf1
                   int64_t M, cudaStream_t stream) {
   if (M == 0) return SF_OK;
   SF_REQUIRE(M < (int64_t(1) << 31), "transition_tc: too many rows");
+  SF_REQUIRE((reinterpret_cast<uintptr_t>(ln_w) & 15) == 0 && (reinterpret_cast<uintptr_t>(ln_b) & 15) == 0,
+             "transition_tc: layer-norm parameters must be 16-byte aligned");
   CUtensorMap mx, mw1, mw2;
   SF_TRY(make_2d_tmap(&mx, x, C, M, 64, TILE));
-  SF_TRY(make_2d_tmap(&mw1, w1, C, 2 * I, 64, HC));
-  SF_TRY(make_2d_tmap(&mw2, w2, I, C, 64, C));
+  SF_TRY(make_2d_tmap(&mw1, w1, C, 2 * I, 64, HC));         // W1 [1024][128]: 64 k x 32 rows
+  SF_TRY(make_2d_tmap(&mw2, w2, I, C, HC, C, 64));          // W2 [128][512]: 32 k x 128 rows, 64B swizzle
   uint32_t* status = device_status_ptr();
   if (!status) return SF_ERR_CUDA;
   static bool attr[64] = {false};
@@ -252,7 +305,7 @@ int transition_tc(const bf16* x, const float* ln_w, const float* ln_b, const bf1
   TrParams p{x, y, ln_w, ln_b, M, status};
   const int64_t npairs = (M + 2 * TILE - 1) / (2 * TILE);
   const int grid = (int)(npairs < num_sms() ? npairs : num_sms());
-  k_transition_tc<<<grid, 288, SMEM_TR, stream>>>(mx, mw1, mw2, p);
+  k_transition_tc<<<grid, TR_THREADS, SMEM_TR, stream>>>(mx, mw1, mw2, p);
   count_launch();
   return check_launch("transition_tc");
 }
