@@ -267,12 +267,12 @@ struct AttCoreParams {
 constexpr int KB = 64;                 // keys per block
 constexpr int KV_STAGES = 3;
 constexpr int KV_BYTES = 8 * 1024;     // K block 64 x 64 B (64B swizzle) | V^T block 32 x 128 B (128B swizzle)
-constexpr int P_BYTES = TILE * KB * 2; // P tile 128 x 128 B (128B swizzle)
+constexpr int BS_BYTES = TILE * KB * 2;  // bias staging of one warpgroup: 128 rows x 128 B (16-byte chunks swizzled)
 constexpr int MAX_QP = 32768;
 constexpr int OFF_Q = 0;                                      // [h] Q tile 128 x 64 B; W_o columns of head h after the loop
 constexpr int OFF_KV = H * 8 * 1024;                          // [h][stage]
-constexpr int OFF_P = OFF_KV + H * KV_STAGES * KV_BYTES;      // [h] P tile; gated O_h (128 x 64 B) after the loop
-constexpr int OFF_KBITS = OFF_P + H * P_BYTES;                // key-valid bits, qp/32 words
+constexpr int OFF_BS = OFF_KV + H * KV_STAGES * KV_BYTES;     // [h] bias rows of the next block; gated O_h after the loop
+constexpr int OFF_KBITS = OFF_BS + H * BS_BYTES;              // key-valid bits, qp/32 words
 constexpr int OFF_BAR = OFF_KBITS + MAX_QP / 8;
 constexpr int SMEM_CORE = OFF_BAR + 256 + 1024;
 constexpr float kRescale = 8.0f;       // the running max moves only when a block exceeds it by 2^8
@@ -289,20 +289,21 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// One CTA = one (attention row b, 128-query tile); warpgroup h owns head h.
+// One CTA = one (attention row b, 128-query tile); warpgroup h owns head h and
+// TMEM columns [128h, 128h+128): S' (64), O (32), P (32 columns of bf16 pairs).
 // Per key block j of 64 keys a warpgroup:
-//   waits for S'_j = sqrt(D) bias_j + Q K_j^T in TMEM (the bias was stored there
-//   by the warpgroup before the MMA, with -inf for masked and padding keys),
-//   reads S'_j twice (block max; then P = 2^(S' scale - m) into shared memory),
-//   rescales its O accumulator in TMEM when the running max moved, stores the
-//   bias of block j+1 into the S' columns, and its leader issues P_j V_j (into O)
-//   and Q K_{j+1}^T (onto that bias).  K and V^T blocks arrive by TMA three
-//   blocks deep.  A row whose token is masked attends uniformly to all N keys
-//   (every logit of the reference is -FLT_MAX there).  After the last block the
-//   gated, normalised O_h and the W_o columns of head h are staged and one more
-//   tcgen05 GEMM (K = 4 heads x 32) forms the output projection; its epilogue
-//   adds the residual.
-// TMEM columns: S'_h at 64h, O_h at 256 + 32h, output projection at 384.
+//   waits for S'_j = sqrt(D) bias_j + Q K_j^T (the bias was stored into S' by the
+//   warpgroup before the MMA, -inf where the key is masked or padding), reads it
+//   once, moves the running max when the block exceeds it by 2^8 (rescaling O in
+//   TMEM), writes P = 2^(S' scale - m) as bf16 into TMEM, stores the bias of
+//   block j+1 (staged in shared memory by cp.async one block ahead, thread t
+//   owning row t) into S', and its leader issues O += P_j V_j (P from TMEM) and
+//   S'_{j+1} += Q K_{j+1}^T.  K and V^T blocks arrive by TMA three blocks deep.
+//   A row whose token is masked attends uniformly to all N keys (every logit of
+//   the reference is -FLT_MAX there).  After the last block the gated,
+//   normalised O_h and the W_o columns of head h are staged in shared memory and
+//   one more tcgen05 GEMM (K = 4 heads x 32) forms the output projection in
+//   columns [0,128); its epilogue adds the residual.
 __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant__ CUtensorMap tmQ,
                                                            const __grid_constant__ CUtensorMap tmK,
                                                            const __grid_constant__ CUtensorMap tmV, AttCoreParams p) {
@@ -343,10 +344,11 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
-  const uint32_t s_col = (uint32_t)g * KB, o_col = 256u + (uint32_t)g * D;
+  const uint32_t s_col = (uint32_t)g * 128, o_col = s_col + 64, p_col = s_col + 96;
   const uint32_t sb = tc::smem_u32(smem);
-  const uint32_t q_s = sb + OFF_Q + g * 8192, p_s = sb + OFF_P + g * P_BYTES;
+  const uint32_t q_s = sb + OFF_Q + g * 8192;
   uint8_t* kv = smem + OFF_KV + g * KV_STAGES * KV_BYTES;
+  uint8_t* brow_s = smem + OFF_BS + g * BS_BYTES + t * 128;   // this thread's staged bias row
   bool aborted = false;
   constexpr uint32_t IDESC_S = tc::idesc_bf16(128, KB), IDESC_O = tc::idesc_bf16(128, D);
 
@@ -365,33 +367,39 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
   };
 
   const int64_t q = q0 + t;
-  const uint4* brow = reinterpret_cast<const uint4*>(p.bias + (q * H + g) * p.qp);
-  uint4 braw[KB / 8];
-  auto load_bias = [&](int jj) {
+  const bf16* bias_row = p.bias + (q * H + g) * p.qp;
+  // bias row of block jj -> this thread's staging row (chunk c at c ^ (t & 7): conflict-free reads)
+  auto stage_bias = [&](int jj) {
 #pragma unroll
-    for (int c = 0; c < KB / 8; ++c) braw[c] = __ldg(brow + jj * (KB / 8) + c);
+    for (int c = 0; c < KB / 8; ++c) cp_async16(brow_s + ((c ^ (t & 7)) << 4), bias_row + (int64_t)jj * KB + c * 8);
+    cp_async_commit();
   };
-  // bias of block jj (bf16, already x sqrt(D)) into the S' columns; -inf where the key is masked or padding
+  // staged bias of block jj (bf16, already x sqrt(D)) into the S' columns; -inf where the key is masked or padding
   auto store_bias = [&](int jj) {
+    cp_async_wait_all();
     const uint64_t vb = (uint64_t)kbits[2 * jj] | ((uint64_t)kbits[2 * jj + 1] << 32);
     const bool full = vb == ~0ull;
 #pragma unroll
-    for (int c = 0; c < KB / 16; ++c) {
+    for (int c2 = 0; c2 < KB / 16; ++c2) {
       uint32_t r[16];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const uint32_t u = reinterpret_cast<const uint32_t*>(&braw[2 * c + (e >> 2)])[e & 3];
-        r[2 * e] = u << 16;
-        r[2 * e + 1] = u & 0xFFFF0000u;
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int c = 2 * c2 + h2;
+        const uint4 raw = *reinterpret_cast<const uint4*>(brow_s + ((c ^ (t & 7)) << 4));
+        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          r[8 * h2 + 2 * e] = u[e] << 16;
+          r[8 * h2 + 2 * e + 1] = u[e] & 0xFFFF0000u;
+        }
       }
       if (!full) {
 #pragma unroll
         for (int e = 0; e < 16; ++e)
-          if (!((vb >> (16 * c + e)) & 1)) r[e] = 0xFF800000u;
+          if (!((vb >> (16 * c2 + e)) & 1)) r[e] = 0xFF800000u;
       }
-      tc::tmem_st16(lane_addr + s_col + 16 * c, r);
+      tc::tmem_st16(lane_addr + s_col + 16 * c2, r);
     }
-    tc::tmem_wait_st();
   };
 
   // ---- prologue: Q, K/V blocks 0 and 1, bias of block 0, S'_0 ----
@@ -402,9 +410,10 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     issue_kv(1);   // qp >= 128: at least two key blocks
   }
   if (!uniform) {
-    load_bias(0);
+    stage_bias(0);
     store_bias(0);
-    load_bias(1);
+    tc::tmem_wait_st();
+    stage_bias(1);
   }
   tc::tc_fence_before();
   wg_sync(g);
@@ -421,76 +430,60 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     tc::mbar_wait(&sbar[g], j & 1, p.status, aborted);
     tc::tc_fence_after();
     if (t == 0 && j + 2 < nkb) issue_kv(j + 2);   // its stage held block j-1, whose P V is done
-    if (j == nkb - 1) {
-      // no bias is pending in the last block: its registers take the gate of this head
-      const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
-#pragma unroll
-      for (int c = 0; c < D / 8; ++c) braw[c] = __ldg(grow + c);
-    }
-    // ---- block max (log2 domain) and the running max ----
+    float sv[KB];
     float corr = 1.f, m_use = 0.f;
     if (!uniform) {
-      float mx = -INFINITY;
+      tc::tmem_ld64(lane_addr + s_col, sv);
+      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < KB / 16; ++c) {
-        float v[16];
-        tc::tmem_ld16(lane_addr + s_col + 16 * c, v);
-#pragma unroll
-        for (int e = 0; e < 16; e += 2) mx = tc::fmax3(mx, v[e], v[e + 1]);
+      for (int e = 0; e < KB; e += 8) {
+        m4[0] = tc::fmax3(m4[0], sv[e], sv[e + 1]);
+        m4[1] = tc::fmax3(m4[1], sv[e + 2], sv[e + 3]);
+        m4[2] = tc::fmax3(m4[2], sv[e + 4], sv[e + 5]);
+        m4[3] = tc::fmax3(m4[3], sv[e + 6], sv[e + 7]);
       }
-      mx *= p.scale_log2;
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
       if (mx > m_run + kRescale) {   // m_run = -inf: any finite block max
         corr = ex2(m_run - mx);
         m_run = mx;
       }
       m_use = m_run == -INFINITY ? 0.f : m_run;
+    } else {
+#pragma unroll
+      for (int e = 0; e < KB; ++e) sv[e] = ((int64_t)j * KB + e < p.nq) ? 1.f : 0.f;
     }
     if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
       // O (blocks < j, complete) *= corr
+      float ov[D];
+      uint32_t r[D];
+      tc::tmem_ld32(lane_addr + o_col, ov);
 #pragma unroll
-      for (int hlf = 0; hlf < 2; ++hlf) {
-        float v[16];
-        uint32_t r[16];
-        tc::tmem_ld16(lane_addr + o_col + 16 * hlf, v);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(v[e] * corr);
-        tc::tmem_st16(lane_addr + o_col + 16 * hlf, r);
-      }
-      tc::tmem_wait_st();
+      for (int e = 0; e < D; ++e) r[e] = __float_as_uint(ov[e] * corr);
+      tc::tmem_st32(lane_addr + o_col, r);
     }
-    // ---- P = 2^(S' scale - m) into the 128B-swizzled P tile (row t) ----
-    float psum = 0.f;
-    uint8_t* prow = smem + OFF_P + g * P_BYTES;
-    const float nm = -m_use;
+    // ---- P = 2^(S' scale - m) as bf16 pairs into TMEM ----
+    {
+      const float nm = -m_use;
+      uint32_t pk[KB / 2];
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int c = 0; c < KB / 16; ++c) {
-      float v[16];
-      if (!uniform) {
-        tc::tmem_ld16(lane_addr + s_col + 16 * c, v);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = ex2(fmaf(v[e], p.scale_log2, nm));
-      } else {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) v[e] = ((int64_t)j * KB + 16 * c + e < p.nq) ? 1.f : 0.f;
+      for (int e = 0; e < KB; e += 2) {
+        float p0 = sv[e], p1 = sv[e + 1];
+        if (!uniform) {
+          p0 = ex2(fmaf(p0, p.scale_log2, nm));
+          p1 = ex2(fmaf(p1, p.scale_log2, nm));
+        }
+        ps[(e >> 1) & 3] += p0 + p1;
+        pk[e >> 1] = pack_bf2(p0, p1);
       }
-#pragma unroll
-      for (int hlf = 0; hlf < 2; ++hlf) {
-        uint4 pk;
-        pk.x = pack_bf2(v[8 * hlf + 0], v[8 * hlf + 1]);
-        pk.y = pack_bf2(v[8 * hlf + 2], v[8 * hlf + 3]);
-        pk.z = pack_bf2(v[8 * hlf + 4], v[8 * hlf + 5]);
-        pk.w = pack_bf2(v[8 * hlf + 6], v[8 * hlf + 7]);
-        *reinterpret_cast<uint4*>(prow + tc::sw128_off(t, 2 * c + hlf)) = pk;
-      }
-#pragma unroll
-      for (int e = 0; e < 16; ++e) psum += v[e];
+      tc::tmem_st32(lane_addr + p_col, pk);
+      l = l * corr + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
     }
-    l = l * corr + psum;
     if (!uniform && j + 1 < nkb) {
       store_bias(j + 1);               // S'_j has been read
-      if (j + 2 < nkb) load_bias(j + 2);
+      if (j + 2 < nkb) stage_bias(j + 2);
     }
-    tc::fence_proxy_async();
+    tc::tmem_wait_st();
     tc::tc_fence_before();
     wg_sync(g);
     if (t == 0) {
@@ -498,8 +491,8 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
       const uint32_t vs = sb + OFF_KV + (g * KV_STAGES + j % KV_STAGES) * KV_BYTES + 4096;
 #pragma unroll
       for (int kk = 0; kk < KB / 16; ++kk)
-        tc::mma_bf16(tbase + o_col, tc::smem_desc(p_s + kk * 32, 1024, tc::kSW128),
-                     tc::smem_desc(vs + kk * 32, 1024, tc::kSW128), IDESC_O, j > 0 || kk > 0);
+        tc::mma_bf16_ts(tbase + o_col, tbase + p_col + kk * 8, tc::smem_desc(vs + kk * 32, 1024, tc::kSW128), IDESC_O,
+                        j > 0 || kk > 0);
       if (j + 1 < nkb) {
         tc::mbar_wait(&kvbar[g * KV_STAGES + (j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, p.status, aborted);
         issue_s(j + 1);
@@ -510,25 +503,27 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     }
   }
 
-  // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) over this head's P tile ----
+  // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) over this head's bias staging ----
+  const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
+  uint4 graw[D / 8];
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) graw[c] = __ldg(grow + c);
   tc::mbar_wait(&obar[g], 0, p.status, aborted);
   tc::tc_fence_after();
   {
     const float inv = l > 0.f ? 1.0f / l : 0.f;
-    float v0[16], v1[16];
-    tc::tmem_ld16(lane_addr + o_col, v0);
-    tc::tmem_ld16(lane_addr + o_col + 16, v1);
-    uint8_t* ost = smem + OFF_P + g * P_BYTES;
+    float ov[D];
+    tc::tmem_ld32(lane_addr + o_col, ov);
+    uint8_t* ost = smem + OFF_BS + g * BS_BYTES;
 #pragma unroll
     for (int cc = 0; cc < D / 8; ++cc) {
-      const uint32_t* gu = reinterpret_cast<const uint32_t*>(&braw[cc]);
+      const uint32_t* gu = reinterpret_cast<const uint32_t*>(&graw[cc]);
       uint4 ok;
       uint32_t* ou = reinterpret_cast<uint32_t*>(&ok);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int d = cc * 8 + 2 * e;
-        const float a0 = d < 16 ? v0[d] : v1[d - 16], a1 = d + 1 < 16 ? v0[d + 1] : v1[d - 15];
-        ou[e] = pack_bf2(a0 * inv * bf_lo(gu[e]), a1 * inv * bf_hi(gu[e]));
+        ou[e] = pack_bf2(ov[d] * inv * bf_lo(gu[e]), ov[d + 1] * inv * bf_hi(gu[e]));
       }
       *reinterpret_cast<uint4*>(ost + tc::sw64_off(t, cc)) = ok;
     }
@@ -551,7 +546,7 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
 #pragma unroll
     for (int k = 0; k < 2 * H; ++k) {
       const int h = k >> 1, kk = k & 1;
-      tc::mma_bf16(tbase + 384, tc::smem_desc(sb + OFF_P + h * P_BYTES + kk * 32, 512, tc::kSW64),
+      tc::mma_bf16(tbase, tc::smem_desc(sb + OFF_BS + h * BS_BYTES + kk * 32, 512, tc::kSW64),
                    tc::smem_desc(sb + OFF_Q + h * 8192 + kk * 32, 512, tc::kSW64), IDESC, k > 0);
     }
     tc::mma_commit(outbar);
@@ -564,9 +559,8 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     const int64_t pos = live ? (p.transpose ? q * p.cols + b : b * p.cols + q) : 0;
     const uint4* zin = reinterpret_cast<const uint4*>(p.z + pos * C + g * D);
     uint4* zo = reinterpret_cast<uint4*>(p.z_out + pos * C + g * D);
-    float v0[16], v1[16];
-    tc::tmem_ld16(lane_addr + 384 + g * D, v0);   // warp-collective: every lane loads
-    tc::tmem_ld16(lane_addr + 384 + g * D + 16, v1);
+    float ov[D];
+    tc::tmem_ld32(lane_addr + g * D, ov);   // warp-collective: every lane loads
     if (live) {
 #pragma unroll
       for (int cc = 0; cc < D / 8; ++cc) {
@@ -577,8 +571,7 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int d = cc * 8 + 2 * e;
-          const float a0 = d < 16 ? v0[d] : v1[d - 16], a1 = d + 1 < 16 ? v0[d + 1] : v1[d - 15];
-          ru[e] = pack_bf2(bf_lo(zu[e]) + a0, bf_hi(zu[e]) + a1);
+          ru[e] = pack_bf2(bf_lo(zu[e]) + ov[d], bf_hi(zu[e]) + ov[d + 1]);
         }
         zo[cc] = r;
       }
