@@ -182,52 +182,6 @@ __global__ void __launch_bounds__(256) k_center_ln(const T* __restrict__ p, T* _
   }
 }
 
-// Pair logits of SingleActUpdate (blocks.py:745-749), bf16: logits[h][m] = LN(z[m]) . W[h].
-// 128 positions per block, staged by coalesced 16-byte loads into padded rows.
-constexpr int PL_ROW = 128 + 8;   // bf16 elements per staged row (16-byte pad, no bank conflicts)
-
-__global__ void __launch_bounds__(128) k_pair_logits_bf16(const bf16* __restrict__ z, const float* __restrict__ ln_w,
-                                                          const float* __restrict__ ln_b, const bf16* __restrict__ w,
-                                                          bf16* __restrict__ logits, int64_t M, int heads) {
-  __shared__ __align__(16) bf16 rows_s[128 * PL_ROW];
-  __shared__ float w_s[16 * 128];
-  const int tid = threadIdx.x;
-  const int64_t m0 = (int64_t)blockIdx.x * 128;
-  for (int e = tid; e < heads * 128; e += 128) w_s[e] = __bfloat162float(w[e]);
-  for (int e = tid; e < 128 * 16; e += 128) {
-    const int r = e >> 4, c = e & 15;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (m0 + r < M) v = __ldg(reinterpret_cast<const uint4*>(z + (m0 + r) * 128) + c);
-    *reinterpret_cast<uint4*>(rows_s + r * PL_ROW + c * 8) = v;
-  }
-  __syncthreads();
-  const bf16* row = rows_s + tid * PL_ROW;
-  float s = 0.f;
-  for (int c = 0; c < 128; ++c) s += __bfloat162float(row[c]);
-  const float mean = s * (1.0f / 128);
-  float q = 0.f;
-  for (int c = 0; c < 128; ++c) {
-    const float d = __bfloat162float(row[c]) - mean;
-    q += d * d;
-  }
-  const float rstd = rsqrtf(q * (1.0f / 128) + 1e-5f);
-  float acc[16];
-#pragma unroll
-  for (int h = 0; h < 16; ++h) acc[h] = 0.f;
-  for (int c = 0; c < 128; ++c) {
-    // the reference rounds LN(z) to the activation dtype before the projection
-    const float y = __bfloat162float(__float2bfloat16_rn((__bfloat162float(row[c]) - mean) * rstd * ln_w[c] + ln_b[c]));
-#pragma unroll
-    for (int h = 0; h < 16; ++h)
-      if (h < heads) acc[h] = fmaf(y, w_s[h * 128 + c], acc[h]);
-  }
-  if (m0 + tid < M) {
-#pragma unroll
-    for (int h = 0; h < 16; ++h)
-      if (h < heads) logits[(int64_t)h * M + m0 + tid] = __float2bfloat16_rn(acc[h]);
-  }
-}
-
 __global__ void k_swiglu_bf16(const bf16* __restrict__ h, bf16* __restrict__ out, int64_t rows, int64_t I) {
   int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= rows * I) return;
@@ -621,11 +575,7 @@ int sf_pair_logits(int dtype, const void* z, const float* ln_w, const float* ln_
   }
   if (rows == 0) return SF_OK;
   if (dtype == SF_BF16 && c == 128 && heads <= 16) {
-    const int64_t M = rows * n;
-    k_pair_logits_bf16<<<(unsigned)((M + 127) / 128), 128, 0, stream>>>((const bf16*)z, ln_w, ln_b, (const bf16*)w,
-                                                                        (bf16*)logits, M, (int)heads);
-    count_launch();
-    return check_launch("pair_logits");
+    return pair_logits_tc((const bf16*)z, ln_w, ln_b, (const bf16*)w, (bf16*)logits, rows * n, (int)heads, stream);
   }
   SF_DISPATCH(dtype, {
     T* x = (T*)ws_p;

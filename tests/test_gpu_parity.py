@@ -120,18 +120,19 @@ def test_edge_sizes(op, n, n_real, dtype):
   assert max_rel_err(got.float().cpu(), ref) < TOL[dtype]
 
 
-@pytest.mark.parametrize("op", PAIR_OPS)
+@pytest.mark.parametrize("op", PAIR_OPS + ["single_update"])
 def test_many_tiles_bf16(op):
   """Several tiles per SM (persistent pipelines wrap their stages many times), ragged N."""
   n, n_real = 320, 301
-  z, _, mask = synth.pair_inputs(n, n_real=n_real, seed=3)
+  z, s, mask = synth.pair_inputs(n, n_real=n_real, seed=3)
   m = _make(op)
   p = synth.init_params(m, seed=9)
   modules.prepare(m)
   m = m.cuda()
   dt = torch.bfloat16
-  got = _run(m, op, z.to(dt).cuda(), mask.cuda())
-  ref = _oracle(op, _round(p, dt), z.to(dt).float(), mask)
+  s_in = s.to(dt) if op == "single_update" else None
+  got = _run(m, op, z.to(dt).cuda(), mask.cuda(), None if s_in is None else s_in.cuda())
+  ref = _oracle(op, _round(p, dt), z.to(dt).float(), mask, None if s_in is None else s_in.float())
   assert max_rel_err(got.float().cpu(), ref) < TOL[dt]
   assert _native.device_status() == 0
 
