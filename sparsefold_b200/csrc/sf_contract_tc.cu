@@ -15,11 +15,15 @@
 namespace sf {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BK = 64, STAGES = 4;
 constexpr int SA_BYTES = BM * BK * 2;              // 16 KB
-constexpr int SB_BYTES = BN * BK * 2;              // 32 KB
-constexpr int STAGE_BYTES = SA_BYTES + SB_BYTES;   // 48 KB
-constexpr int SMEM_CONTRACT = STAGES * STAGE_BYTES + 1024 + 1024;
+template <int BN>
+struct Tile {
+  static constexpr int SB_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = SA_BYTES + SB_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024;
+  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+};
 
 struct ContractParams {
   bf16* P;
@@ -38,9 +42,11 @@ __device__ __forceinline__ float post(float v, int op) {
   return v;
 }
 
+template <int BN>
 __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ CUtensorMap tmA,
                                                         const __grid_constant__ CUtensorMap tmB,
                                                         ContractParams p) {
+  constexpr int STAGE_BYTES = Tile<BN>::STAGE_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = pt::align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
@@ -55,7 +61,7 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
   const int nk = (int)((p.kdim + BK - 1) / BK);
 
   if (warp == 0) {
-    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_alloc(tmem_slot, Tile<BN>::TMEM_COLS);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
@@ -140,13 +146,27 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
             const int64_t j = j0 + ch * 16 + g * 8;
             if (j + 8 <= cp) {
               if (p.bias || p.residual || p.post_op) {
-                const bf16* res = p.residual ? p.residual + (i * p.channels + c) * cp + j : nullptr;
+                float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                if (p.bias) {
+                  if (j + 8 <= p.cols) {   // bias is [cols] fp32, 16-byte aligned (checked on the host)
+                    const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + j));
+                    const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + j + 4));
+                    bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
+                    bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+                  } else {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) bv[e] = j + e < p.cols ? __ldg(p.bias + j + e) : 0.f;
+                  }
+                }
+                uint32_t ru[4] = {0u, 0u, 0u, 0u};
+                if (p.residual) {
+                  const uint4 rr = *reinterpret_cast<const uint4*>(p.residual + (i * p.channels + c) * cp + j);
+                  ru[0] = rr.x; ru[1] = rr.y; ru[2] = rr.z; ru[3] = rr.w;
+                }
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                  float x = v[g * 8 + e];
-                  if (p.bias && j + e < p.cols) x += __ldg(p.bias + j + e);
-                  if (res) x += __bfloat162float(res[e]);
-                  v[g * 8 + e] = post(x, p.post_op);
+                  const float r = (e & 1) ? pt::bf_hi(ru[e >> 1]) : pt::bf_lo(ru[e >> 1]);
+                  v[g * 8 + e] = post(v[g * 8 + e] + bv[e] + r, p.post_op);
                 }
               }
               uint4 o;
@@ -166,7 +186,7 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
   __syncthreads();
   if (warp == 0) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tbase, 512);
+    tc::tmem_dealloc(tbase, Tile<BN>::TMEM_COLS);
   }
 }
 
@@ -226,6 +246,28 @@ int linear_tc(const bf16* x, const bf16* wt, const float* bias, const bf16* resi
   return gemm_tc_impl(x, wt, y, 1, M, N, 1, K, 1, K, bias, residual, post_op, stream);
 }
 
+template <int BN>
+static int launch_gemm_tc(const CUtensorMap& ma, const bf16* b_op, int64_t chunks_b, int64_t kl_b, int64_t channels,
+                          int64_t cols, const ContractParams& p, int64_t ntiles, cudaStream_t stream) {
+  CUtensorMap mb;
+  SF_TRY(make_operand_tmap(&mb, b_op, chunks_b, cols, channels, kl_b, BN));
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(k_contract_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Tile<BN>::SMEM);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(contract): %s", cudaGetErrorString(e));
+      return SF_ERR_CUDA;
+    }
+    attr_set[dev & 63] = true;
+  }
+  const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
+  k_contract_tc<BN><<<grid, 192, Tile<BN>::SMEM, stream>>>(ma, mb, p);
+  count_launch();
+  return check_launch("contract_tc");
+}
+
 static int gemm_tc_impl(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
                         int64_t chunks_a, int64_t kl_a, int64_t chunks_b, int64_t kl_b, const float* bias,
                         const bf16* residual, int post_op, cudaStream_t stream) {
@@ -233,28 +275,19 @@ static int gemm_tc_impl(const bf16* a_op, const bf16* b_op, bf16* P, int64_t cha
   if (channels == 0 || rows == 0 || cols == 0) return SF_OK;
   SF_REQUIRE(rows < (1 << 30) && cols < (1 << 30) && kdim < (1 << 30) && channels < (1 << 30),
              "contract_tc: size too large");
-  CUtensorMap ma, mb;
+  SF_REQUIRE((reinterpret_cast<uintptr_t>(bias) & 15) == 0 && (reinterpret_cast<uintptr_t>(residual) & 15) == 0,
+             "contract_tc: bias and residual must be 16-byte aligned");
+  CUtensorMap ma;
   SF_TRY(make_operand_tmap(&ma, a_op, chunks_a, rows, channels, kl_a, BM));
-  SF_TRY(make_operand_tmap(&mb, b_op, chunks_b, cols, channels, kl_b, BN));
   uint32_t* status = device_status_ptr();
   if (!status) return SF_ERR_CUDA;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(k_contract_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_CONTRACT);
-    if (e != cudaSuccess) {
-      set_error("cudaFuncSetAttribute(contract): %s", cudaGetErrorString(e));
-      return SF_ERR_CUDA;
-    }
-    attr_set[dev & 63] = true;
-  }
   ContractParams p{P, channels, rows, cols, kdim, kl_a, kl_b, bias, residual, post_op, status};
-  const int64_t ntiles = channels * ((rows + BM - 1) / BM) * ((cols + BN - 1) / BN);
-  const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  k_contract_tc<<<grid, 192, SMEM_CONTRACT, stream>>>(ma, mb, p);
-  count_launch();
-  return check_launch("contract_tc");
+  const int64_t mt = (rows + BM - 1) / BM;
+  auto tiles = [&](int64_t bn) { return channels * mt * ((cols + bn - 1) / bn); };
+  // the widest N tile that still gives every SM a tile (or that covers N exactly)
+  if (cols > 128 && tiles(256) >= num_sms()) return launch_gemm_tc<256>(ma, b_op, chunks_b, kl_b, channels, cols, p, tiles(256), stream);
+  if (cols > 64 && tiles(128) >= num_sms() / 2) return launch_gemm_tc<128>(ma, b_op, chunks_b, kl_b, channels, cols, p, tiles(128), stream);
+  return launch_gemm_tc<64>(ma, b_op, chunks_b, kl_b, channels, cols, p, tiles(64), stream);
 }
 
 }  // namespace sf
