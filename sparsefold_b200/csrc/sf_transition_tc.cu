@@ -7,9 +7,10 @@
 //   warp 8      TMA producer: the x tiles of a pass, and per chunk the 64 rows of
 //               W1 (32 a + 32 b, 16 KB) and the 32 columns of W2 (8 KB), each in a
 //               4-stage ring
-//   warp 9      MMA issuer: GEMM1 of chunk c (M128 N64 K128 per tile) into one of
-//               two TMEM buffers, then GEMM2 of chunk c-1 (M128 N128 K32 per tile)
-//               accumulating the down projection in TMEM columns [256,512)
+//   warp 9      GEMM1 issuer: chunk c (M128 N64 K128 per tile) into one of two
+//               TMEM buffers as soon as the buffer and the weight chunk are free
+//   warp 10     GEMM2 issuer: chunk c (M128 N128 K32 per tile) from the hidden
+//               tile, accumulating the down projection in TMEM columns [256,512)
 //   warps 0-7   thread = position (warps 0-3 tile 0, 4-7 tile 1): LayerNorm of
 //               the pass in place, then per chunk swish(a) * b from TMEM into the
 //               64B-swizzled hidden tile, and finally y = x + acc.
@@ -32,7 +33,7 @@ constexpr int OFF_W1 = OFF_H + 4 * H_BYTES;                  // [stage]
 constexpr int OFF_W2 = OFF_W1 + TR_STAGES * W1C_BYTES;       // [stage]
 constexpr int OFF_BAR = OFF_W2 + TR_STAGES * W2C_BYTES;
 constexpr int SMEM_TR = OFF_BAR + 512 + 1024;
-constexpr int TR_THREADS = 10 * 32;
+constexpr int TR_THREADS = 11 * 32;
 
 struct TrParams {
   const bf16* x;
@@ -128,25 +129,10 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       }
     }
   } else if (warp == 9) {
-    // ---- MMA issuer ----
+    // ---- GEMM1 issuer ----
     if (lane == 0) {
-      constexpr uint32_t ID1 = tc::idesc_bf16(128, 2 * HC), ID2 = tc::idesc_bf16(128, 128);
+      constexpr uint32_t ID1 = tc::idesc_bf16(128, 2 * HC);
       uint32_t q = 0, pi = 0;
-      auto gemm2 = [&](uint32_t qq, int first) {   // chunk qq: acc[t2] += H[t2] . W2 chunk^T
-        const int st = qq % TR_STAGES, hb = qq & 1;
-        tc::mbar_wait(&hfull[hb], (qq >> 1) & 1, p.status, aborted);
-        tc::mbar_wait(&w2full[st], (qq / TR_STAGES) & 1, p.status, aborted);
-        tc::tc_fence_after();
-        const uint32_t w2 = sb + OFF_W2 + st * W2C_BYTES;
-        for (int t2 = 0; t2 < 2; ++t2)
-#pragma unroll
-          for (int kk = 0; kk < HC / 16; ++kk)
-            tc::mma_bf16(tbase + 256 + t2 * 128,
-                         tc::smem_desc(sb + OFF_H + (hb * 2 + t2) * H_BYTES + kk * 32, 512, tc::kSW64),
-                         tc::smem_desc(w2 + kk * 32, 512, tc::kSW64), ID2, !(first && kk == 0));
-        tc::mma_commit(&hfree[hb]);
-        tc::mma_commit(&w2free[st]);
-      };
       for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
         tc::mbar_wait(xready, pi & 1, p.status, aborted);
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
@@ -166,12 +152,31 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
           tc::mma_commit(&s1full[sbuf]);
           tc::mma_commit(&w1free[st]);
           if (hc == NCHUNK - 1) tc::mma_commit(xfree);
-          if (hc >= 1) {
-            if (hc == 1 && pi >= 1) tc::mbar_wait(accfree, (pi - 1) & 1, p.status, aborted);
-            gemm2(q - 1, hc == 1);
-          }
         }
-        gemm2(q - 1, 0);
+      }
+    }
+  } else if (warp == 10) {
+    // ---- GEMM2 issuer: acc[t2] += H[t2] . W2 chunk^T ----
+    if (lane == 0) {
+      constexpr uint32_t ID2 = tc::idesc_bf16(128, 128);
+      uint32_t q = 0, pi = 0;
+      for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
+        for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
+          const int st = q % TR_STAGES, hb = q & 1;
+          if (hc == 0 && pi >= 1) tc::mbar_wait(accfree, (pi - 1) & 1, p.status, aborted);
+          tc::mbar_wait(&hfull[hb], (q >> 1) & 1, p.status, aborted);
+          tc::mbar_wait(&w2full[st], (q / TR_STAGES) & 1, p.status, aborted);
+          tc::tc_fence_after();
+          const uint32_t w2 = sb + OFF_W2 + st * W2C_BYTES;
+          for (int t2 = 0; t2 < 2; ++t2)
+#pragma unroll
+            for (int kk = 0; kk < HC / 16; ++kk)
+              tc::mma_bf16(tbase + 256 + t2 * 128,
+                           tc::smem_desc(sb + OFF_H + (hb * 2 + t2) * H_BYTES + kk * 32, 512, tc::kSW64),
+                           tc::smem_desc(w2 + kk * 32, 512, tc::kSW64), ID2, !(hc == 0 && kk == 0));
+          tc::mma_commit(&hfree[hb]);
+          tc::mma_commit(&w2free[st]);
+        }
         tc::mma_commit(accfull);
       }
     }
@@ -186,8 +191,17 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       ln_row_inplace_lr(smem + OFF_X + t2 * A_BYTES, r, p.ln_w, p.ln_b, 1e-5f);
       tc::fence_proxy_async();
       tc::mbar_arrive(xready);
+      const int64_t m = m0 + t2 * TILE + r;
+      const bool live = m < p.M;
+      const uint4* xr = reinterpret_cast<const uint4*>(p.x + (live ? m : 0) * C);
+      uint4* yr = reinterpret_cast<uint4*>(p.y + (live ? m : 0) * C);
+      uint4 xpre[16];
       for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
         const int sbuf = q & 1;
+        if (hc == NCHUNK - 4) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) xpre[c] = xr[c];   // raw x row for the residual (the tile in smem is normalised)
+        }
         tc::mbar_wait(&s1full[sbuf], (q >> 1) & 1, p.status, aborted);
         tc::tc_fence_after();
         float a[HC], bv[HC];
@@ -211,21 +225,17 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&hfull[sbuf]);
       }
-      // ---- residual epilogue: y = x + acc ----
+      // ---- residual epilogue: y = x + acc (the x row was prefetched during the last chunks) ----
       tc::mbar_wait(accfull, pi & 1, p.status, aborted);
       tc::tc_fence_after();
-      const int64_t m = m0 + t2 * TILE + r;
-      const bool live = m < p.M;
-      const uint4* xr = reinterpret_cast<const uint4*>(p.x + (live ? m : 0) * C);
-      uint4* yr = reinterpret_cast<uint4*>(p.y + (live ? m : 0) * C);
-#pragma unroll 1
+#pragma unroll
       for (int i = 0; i < 4; ++i) {
         float v[32];
         tc::tmem_ld32(lane_addr + 256 + t2 * 128 + 32 * i, v);
         if (live) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            const uint4 xx = xr[4 * i + c];
+            const uint4 xx = xpre[4 * i + c];
             const uint32_t xu[4] = {xx.x, xx.y, xx.z, xx.w};
             uint32_t o[4];
 #pragma unroll
