@@ -320,22 +320,29 @@ int sf_attention(const sf_attention_args* a, sf_stream_t stream) {
   if (a->batch == 0 || a->q_len == 0) return SF_OK;
   SF_REQUIRE(a->k_len > 0, "sf_attention: k_len must be positive");
   SF_REQUIRE(!a->bias || a->bias_dtype == SF_F32 || a->bias_dtype == a->dtype, "sf_attention: bias dtype");
-  dim3 grid((unsigned)((a->q_len + ATT_WARPS - 1) / ATT_WARPS), (unsigned)a->heads, (unsigned)a->batch);
+  SF_REQUIRE((a->q_len + ATT_QB - 1) / ATT_QB <= 0x7fffffff, "sf_attention: q_len too large");
+  dim3 grid((unsigned)((a->q_len + ATT_QB - 1) / ATT_QB), (unsigned)a->heads, (unsigned)a->batch);
   const size_t smem = attention_smem_bytes((int)a->head_dim);
   SF_DISPATCH(a->dtype, {
     const bool f32bias = a->bias && a->bias_dtype == SF_F32;
-    const bool small = a->head_dim <= 32;
-    auto kern = small ? (f32bias ? k_attention<T, float, 32> : k_attention<T, T, 32>)
-                      : (f32bias ? k_attention<T, float, 64> : k_attention<T, T, 64>);
-    static bool attr_done[64][4] = {};
+    using K = void (*)(sf_attention_args);
+    // compile-time head dims for the common sizes; the generic kernel takes any D <= 64
+    const int hd = (int)a->head_dim;
+    const int di = hd == 16 ? 0 : hd == 24 ? 1 : hd == 32 ? 2 : hd == 48 ? 3 : hd == 64 ? 4 : 5;
+    static const K kerns[2][6] = {
+        {k_attention<T, T, 16, 16>, k_attention<T, T, 24, 24>, k_attention<T, T, 32, 32>,
+         k_attention<T, T, 48, 48>, k_attention<T, T, 64, 64>, k_attention<T, T, 0, 64>},
+        {k_attention<T, float, 16, 16>, k_attention<T, float, 24, 24>, k_attention<T, float, 32, 32>,
+         k_attention<T, float, 48, 48>, k_attention<T, float, 64, 64>, k_attention<T, float, 0, 64>}};
+    K kern = kerns[f32bias ? 1 : 0][di];
+    static bool attr_done[64][2][6] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    const int slot = (small ? 2 : 0) + (f32bias ? 1 : 0);
-    if (!attr_done[dev & 63][slot]) {
+    if (!attr_done[dev & 63][f32bias ? 1 : 0][di]) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem_bytes(64));
-      attr_done[dev & 63][slot] = true;
+      attr_done[dev & 63][f32bias ? 1 : 0][di] = true;
     }
-    kern<<<grid, ATT_WARPS * 32, smem, stream>>>(*a);
+    kern<<<grid, ATT_NS * 32, smem, stream>>>(*a);
     count_launch();
     return check_launch("sf_attention");
   });

@@ -168,30 +168,39 @@ struct EpiLinear {  // y = post(v + bias + residual)
 };
 
 // ---------------------------------------------------------------------------
-// Strided attention, one warp per query: the 32 lanes split the keys of each
-// shared-memory key tile, keep their own exact online-softmax state (fp32),
-// and merge the states by butterfly shuffles at the end.  Masked logits are
-// -FLT_MAX (not -inf), which reproduces the reference's uniform average for a
-// query whose keys are all masked (sdpa.py:61-80); keys beyond k_len take no
-// part at all.
+// Strided attention (fp32 online softmax).  Masked logits are -FLT_MAX (not
+// -inf), which reproduces the reference's uniform average for a query whose
+// keys are all masked (sdpa.py:61-80); keys beyond k_len take no part at all.
 // ---------------------------------------------------------------------------
-constexpr int ATT_WARPS = 8, ATT_KT = 128, ATT_DMAX = 64;
+constexpr int ATT_QB = 32, ATT_NS = 8, ATT_KT = 128, ATT_DMAX = 64;
+constexpr int ATT_KPS = ATT_KT / ATT_NS;            // keys of a tile handled by one split (warp)
 
-template <typename T, typename TB, int DM>
-__global__ void __launch_bounds__(ATT_WARPS * 32) k_attention(sf_attention_args a) {
-  extern __shared__ float att_smem[];
-  float* ks = att_smem;                              // [ATT_KT][D + 1]
-  const int D = (int)a.head_dim, DP = D + 1;
-  float* vs = ks + ATT_KT * DP;                      // [ATT_KT][D + 1]
-  uint8_t* kvalid = reinterpret_cast<uint8_t*>(vs + ATT_KT * DP);
+// Block = (batch b, head h, 32 queries); warp w = key split, lane = query.  Each
+// 128-key tile of K and V (fp32 rows) and the block's 32 x 128 bias tile are
+// staged in shared memory once per block (coalesced), so the eight warps read
+// K/V rows as broadcasts (16-byte vectors when the head dim DK is a compile-time
+// multiple of 4; DK = 0 is the generic runtime head dim).  Each thread scores its
+// split's 16 keys, takes their max, rescales its running state once per tile and
+// spends one exp per key; the eight split states of a query are merged through
+// shared memory at the end.
+template <typename T, typename TB, int DK, int DM>
+__global__ void __launch_bounds__(ATT_NS * 32) k_attention(sf_attention_args a) {
+  extern __shared__ float4 att_smem4[];
+  float* att_smem = reinterpret_cast<float*>(att_smem4);
+  const int D = DK > 0 ? DK : (int)a.head_dim;
+  constexpr bool VEC = DK > 0 && DK % 4 == 0;
+  float* ks = att_smem;                               // [KT][D]
+  float* vs = ks + ATT_KT * D;                        // [KT][D]
+  float* bs = vs + ATT_KT * D;                        // [QB][KT + 1]
+  uint8_t* kvalid = reinterpret_cast<uint8_t*>(bs + ATT_QB * (ATT_KT + 1));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t b = blockIdx.z, h = blockIdx.y;
-  const int64_t qi = (int64_t)blockIdx.x * ATT_WARPS + warp;
+  const int64_t q0 = (int64_t)blockIdx.x * ATT_QB, qi = q0 + lane;
   const bool qin = qi < a.q_len;
   const T* qp = static_cast<const T*>(a.q) + b * a.q_sb + h * a.q_sh + (qin ? qi : 0) * a.q_sq;
   const T* kp = static_cast<const T*>(a.k) + b * a.k_sb + h * a.k_sh;
   const T* vp = static_cast<const T*>(a.v) + b * a.v_sb + h * a.v_sh;
-  const TB* bp = a.bias ? static_cast<const TB*>(a.bias) + b * a.b_sb + h * a.b_sh + (qin ? qi : 0) * a.b_sq : nullptr;
+  const TB* bbase = a.bias ? static_cast<const TB*>(a.bias) + b * a.b_sb + h * a.b_sh : nullptr;
   bool row_ok = true;
   if (a.mask_row) row_ok = a.mask_row[b] != 0;
   if (a.mask_q && qin) row_ok = row_ok && a.mask_q[b * a.mq_sb + qi] != 0;
@@ -202,71 +211,137 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) k_attention(sf_attention_args 
     q[d] = (d < D && qin) ? ld(qp + d) * a.scale : 0.f;
     acc[d] = 0.f;
   }
+  auto dot = [&](const float* kr) {
+    float s = 0.f;
+    if constexpr (VEC) {
+#pragma unroll
+      for (int d = 0; d < DK; d += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
+        s = fmaf(q[d], k4.x, s);
+        s = fmaf(q[d + 1], k4.y, s);
+        s = fmaf(q[d + 2], k4.z, s);
+        s = fmaf(q[d + 3], k4.w, s);
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < DM; ++d)
+        if (d < D) s = fmaf(q[d], kr[d], s);
+    }
+    return s;
+  };
+  auto axpy = [&](float pr, const float* vr) {
+    if constexpr (VEC) {
+#pragma unroll
+      for (int d = 0; d < DK; d += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(vr + d);
+        acc[d] = fmaf(pr, v4.x, acc[d]);
+        acc[d + 1] = fmaf(pr, v4.y, acc[d + 1]);
+        acc[d + 2] = fmaf(pr, v4.z, acc[d + 2]);
+        acc[d + 3] = fmaf(pr, v4.w, acc[d + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < DM; ++d)
+        if (d < D) acc[d] = fmaf(pr, vr[d], acc[d]);
+    }
+  };
   float mrun = -INFINITY, lrun = 0.f;
   for (int64_t k0 = 0; k0 < a.k_len; k0 += ATT_KT) {
     const int kn = (a.k_len - k0) < ATT_KT ? (int)(a.k_len - k0) : ATT_KT;
-    for (int e = threadIdx.x; e < kn * D; e += blockDim.x) {
-      const int r = e / D, c = e % D;
-      ks[r * DP + c] = ld(kp + (k0 + r) * a.k_sk + c);
-      vs[r * DP + c] = ld(vp + (k0 + r) * a.v_sk + c);
+    for (int r = warp; r < kn; r += ATT_NS) {         // one key row per warp, lanes along d
+      const T* kr = kp + (k0 + r) * a.k_sk;
+      const T* vr = vp + (k0 + r) * a.v_sk;
+      for (int c = lane; c < D; c += 32) {
+        ks[r * D + c] = ld(kr + c);
+        vs[r * D + c] = ld(vr + c);
+      }
+    }
+    if (bbase) {
+      for (int qq = warp; qq < ATT_QB; qq += ATT_NS) {
+        if (q0 + qq >= a.q_len) continue;
+        const TB* br = bbase + (q0 + qq) * a.b_sq + k0;
+        for (int k = lane; k < kn; k += 32) bs[qq * (ATT_KT + 1) + k] = ld(br + k);
+      }
     }
     for (int r = threadIdx.x; r < kn; r += blockDim.x)
       kvalid[r] = !a.mask_k || a.mask_k[b * a.mk_sb + k0 + r] != 0;
     __syncthreads();
-    for (int r = lane; r < kn; r += 32) {
-      float s;
-      if (row_ok && kvalid[r]) {
-        s = 0.f;
+    float sc[ATT_KPS];
+    float mt = -INFINITY;
 #pragma unroll
-        for (int d = 0; d < DM; ++d)
-          if (d < D) s = fmaf(q[d], ks[r * DP + d], s);
-        if (bp) s += ld(bp + k0 + r);
-      } else {
-        s = -FLT_MAX;
+    for (int j = 0; j < ATT_KPS; ++j) {
+      const int kk = warp * ATT_KPS + j;
+      float s = -INFINITY;                            // beyond the last key: excluded
+      if (kk < kn) {
+        if (row_ok && kvalid[kk]) {
+          s = dot(ks + kk * D);
+          if (bbase) s += bs[lane * (ATT_KT + 1) + kk];
+        } else {
+          s = -FLT_MAX;                               // masked: the reference's -finfo.max bias
+        }
       }
-      const float mnew = fmaxf(mrun, s);
-      const float corr = expf(mrun - mnew);
-      const float pr = expf(s - mnew);
-      lrun = lrun * corr + pr;
+      sc[j] = s;
+      mt = fmaxf(mt, s);
+    }
+    const float mnew = fmaxf(mrun, mt);
+    if (mnew != -INFINITY) {
+      const float corr = (mrun == -INFINITY) ? 0.f : expf(mrun - mnew);
+      lrun *= corr;
 #pragma unroll
-      for (int d = 0; d < DM; ++d)
-        if (d < D) acc[d] = fmaf(acc[d], corr, pr * vs[r * DP + d]);
+      for (int d = 0; d < DM; ++d) acc[d] *= corr;
+#pragma unroll
+      for (int j = 0; j < ATT_KPS; ++j) {
+        const int kk = warp * ATT_KPS + j;
+        if (kk < kn) {
+          const float pr = expf(sc[j] - mnew);
+          lrun += pr;
+          axpy(pr, vs + kk * D);
+        }
+      }
       mrun = mnew;
     }
     __syncthreads();
   }
-  // merge the 32 lane states (lanes that saw no key have m = -inf, l = 0)
+  // merge the key splits of each query (the K/V area is free now)
+  float* ms = att_smem;                               // [NS][QB]
+  float* ls = ms + ATT_NS * ATT_QB;                   // [NS][QB]
+  float* as = ls + ATT_NS * ATT_QB;                   // [NS][QB][D]
+  ms[warp * ATT_QB + lane] = mrun;
+  ls[warp * ATT_QB + lane] = lrun;
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    const float mo = __shfl_xor_sync(0xffffffffu, mrun, off);
-    const float lo = __shfl_xor_sync(0xffffffffu, lrun, off);
-    const float mnew = fmaxf(mrun, mo);
-    const float ca = (mrun == -INFINITY) ? 0.f : expf(mrun - mnew);
-    const float cb = (mo == -INFINITY) ? 0.f : expf(mo - mnew);
-    lrun = lrun * ca + lo * cb;
+  for (int d = 0; d < DM; ++d)
+    if (d < D) as[(warp * ATT_QB + lane) * D + d] = acc[d];
+  __syncthreads();
+  const int qq = threadIdx.x % ATT_QB, d0 = threadIdx.x / ATT_QB;
+  const int64_t qo = q0 + qq;
+  if (qo >= a.q_len) return;
+  float m = -INFINITY;
 #pragma unroll
-    for (int d = 0; d < DM; ++d) {
-      const float ao = __shfl_xor_sync(0xffffffffu, acc[d], off);
-      acc[d] = acc[d] * ca + ao * cb;
-    }
-    mrun = mnew;
+  for (int sp = 0; sp < ATT_NS; ++sp) m = fmaxf(m, ms[sp * ATT_QB + qq]);
+  float wgt[ATT_NS], l = 0.f;
+#pragma unroll
+  for (int sp = 0; sp < ATT_NS; ++sp) {
+    const float ms_ = ms[sp * ATT_QB + qq];
+    wgt[sp] = (ms_ == -INFINITY) ? 0.f : expf(ms_ - m);
+    l += ls[sp * ATT_QB + qq] * wgt[sp];
   }
-  if (!qin) return;
-  T* op = static_cast<T*>(a.out) + b * a.o_sb + h * a.o_sh + qi * a.o_sq;
-  const T* gp = a.gate ? static_cast<const T*>(a.gate) + b * a.g_sb + h * a.g_sh + qi * a.g_sq : nullptr;
-  const float inv = lrun > 0.f ? 1.f / lrun : 0.f;
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  T* op = static_cast<T*>(a.out) + b * a.o_sb + h * a.o_sh + qo * a.o_sq;
+  const T* gp = a.gate ? static_cast<const T*>(a.gate) + b * a.g_sb + h * a.g_sh + qo * a.g_sq : nullptr;
+  for (int d = d0; d < D; d += ATT_NS) {
+    float o = 0.f;
 #pragma unroll
-  for (int d = 0; d < DM; ++d) {
-    if (d < D && (d & 31) == lane) {
-      float o = acc[d] * inv;
-      if (gp) o *= sigmoid_f(ld(gp + d));
-      st(op + d, o);
-    }
+    for (int sp = 0; sp < ATT_NS; ++sp) o += as[(sp * ATT_QB + qq) * D + d] * wgt[sp];
+    o *= inv;
+    if (gp) o *= sigmoid_f(ld(gp + d));
+    st(op + d, o);
   }
 }
 
 inline size_t attention_smem_bytes(int D) {
-  return (size_t)2 * ATT_KT * (D + 1) * sizeof(float) + ATT_KT;
+  const size_t main = (size_t)(2 * ATT_KT * D + ATT_QB * (ATT_KT + 1)) * sizeof(float) + ATT_KT;
+  const size_t merge = (size_t)ATT_NS * ATT_QB * (D + 2) * sizeof(float);
+  return main > merge ? main : merge;
 }
 
 }  // namespace sf
