@@ -267,12 +267,13 @@ struct AttCoreParams {
 constexpr int KB = 64;                 // keys per block
 constexpr int KV_STAGES = 3;
 constexpr int KV_BYTES = 8 * 1024;     // K block 64 x 64 B (64B swizzle) | V^T block 32 x 128 B (128B swizzle)
-constexpr int BS_BYTES = TILE * KB * 2;  // bias staging of one warpgroup: 128 rows x 128 B (16-byte chunks swizzled)
+constexpr int BT_BYTES = TILE * KB * 2;  // bias tile of one head: 128 queries x 64 keys (128B swizzle, K-major)
 constexpr int MAX_QP = 32768;
 constexpr int OFF_Q = 0;                                      // [h] Q tile 128 x 64 B; W_o columns of head h after the loop
 constexpr int OFF_KV = H * 8 * 1024;                          // [h][stage]
-constexpr int OFF_BS = OFF_KV + H * KV_STAGES * KV_BYTES;     // [h] bias rows of the next block; gated O_h after the loop
-constexpr int OFF_KBITS = OFF_BS + H * BS_BYTES;              // key-valid bits, qp/32 words
+constexpr int OFF_BT = OFF_KV + H * KV_STAGES * KV_BYTES;     // [h] bias tile of the next block; gated O_h after the loop
+constexpr int OFF_ID = OFF_BT + H * BT_BYTES;                 // 64 x 64 identity (128B swizzle, K-major)
+constexpr int OFF_KBITS = OFF_ID + KB * 128;                  // key-valid bits, qp/32 words
 constexpr int OFF_BAR = OFF_KBITS + MAX_QP / 8;
 constexpr int SMEM_CORE = OFF_BAR + 256 + 1024;
 constexpr float kRescale = 8.0f;       // the running max moves only when a block exceeds it by 2^8
@@ -292,27 +293,32 @@ __device__ __forceinline__ float ex2(float x) {
 // One CTA = one (attention row b, 128-query tile); warpgroup h owns head h and
 // TMEM columns [128h, 128h+128): S' (64), O (32), P (32 columns of bf16 pairs).
 // Per key block j of 64 keys a warpgroup:
-//   waits for S'_j = sqrt(D) bias_j + Q K_j^T (the bias was stored into S' by the
-//   warpgroup before the MMA, -inf where the key is masked or padding), reads it
-//   once, moves the running max when the block exceeds it by 2^8 (rescaling O in
-//   TMEM), writes P = 2^(S' scale - m) as bf16 into TMEM, stores the bias of
-//   block j+1 (staged in shared memory by cp.async one block ahead, thread t
-//   owning row t) into S', and its leader issues O += P_j V_j (P from TMEM) and
-//   S'_{j+1} += Q K_{j+1}^T.  K and V^T blocks arrive by TMA three blocks deep.
-//   A row whose token is masked attends uniformly to all N keys (every logit of
-//   the reference is -FLT_MAX there).  After the last block the gated,
-//   normalised O_h and the W_o columns of head h are staged in shared memory and
-//   one more tcgen05 GEMM (K = 4 heads x 32) forms the output projection in
-//   columns [0,128); its epilogue adds the residual.
+//   waits for S'_j = sqrt(D) bias_j + Q K_j^T, formed entirely on the tensor core:
+//   the bias tile [128 queries][64 keys] arrives by TMA (keys beyond N read as 0)
+//   and is multiplied by a 64 x 64 identity into S', then Q K_j^T accumulates
+//   onto it.  The warpgroup reads S' once, sets masked and padding keys to -inf
+//   (only in blocks that have any), moves the running max when the block exceeds
+//   it by 2^8 (rescaling O in TMEM), and writes P = 2^(S' scale - m) as bf16 into
+//   TMEM.  Then one thread issues S'_{j+1} (the next thing the warpgroup waits
+//   for) while a thread of another warp issues O += P_j V_j (P from TMEM), whose
+//   completion is awaited only before P or O are touched again.  K and V^T
+//   blocks arrive by TMA three blocks deep, the bias tile one block ahead.  A row
+//   whose token is masked attends uniformly to all N keys (every logit of the
+//   reference is -FLT_MAX there).  After the last block the gated, normalised
+//   O_h and the W_o columns of head h are staged in shared memory and one more
+//   tcgen05 GEMM (K = 4 heads x 32) forms the output projection in columns
+//   [0,128); its epilogue adds the residual.
 __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant__ CUtensorMap tmQ,
                                                            const __grid_constant__ CUtensorMap tmK,
-                                                           const __grid_constant__ CUtensorMap tmV, AttCoreParams p) {
+                                                           const __grid_constant__ CUtensorMap tmV,
+                                                           const __grid_constant__ CUtensorMap tmB, AttCoreParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* qbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [H] Q tile landed
-  uint64_t* sbar = qbar + H;                                       // [H] S'_j (and P_{j-1} V_{j-1}) done
-  uint64_t* obar = sbar + H;                                       // [H] last P V done
-  uint64_t* kvbar = obar + H;                                      // [H][KV_STAGES] K/V block landed
+  uint64_t* sbar = qbar + H;                                       // [H] S'_j done
+  uint64_t* pvbar = sbar + H;                                      // [H] P_j V_j done (one phase per block)
+  uint64_t* bbar = pvbar + H;                                      // [H] bias tile landed (one phase per block)
+  uint64_t* kvbar = bbar + H;                                      // [H][KV_STAGES] K/V block landed
   uint64_t* outbar = kvbar + H * KV_STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(outbar + 1);
   uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
@@ -326,11 +332,12 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 3 * H + H * KV_STAGES + 1; ++i) tc::mbar_init(&qbar[i], 1);
+    for (int i = 0; i < 4 * H + H * KV_STAGES + 1; ++i) tc::mbar_init(&qbar[i], 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmQ);
     tc::prefetch_tmap(&tmK);
     tc::prefetch_tmap(&tmV);
+    tc::prefetch_tmap(&tmB);
   }
   // key k is attended iff mask[row] && mask[k] (pair mask, blocks.py:314); bits hold mask[k] && k < N
   for (int w = warp; w < (int)(p.qp / 32); w += 16) {
@@ -338,7 +345,15 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     const uint32_t bits = __ballot_sync(0xffffffffu, key < p.nq && p.mask[key] != 0);
     if (lane == 0) kbits[w] = bits;
   }
+  // 64 x 64 identity, K-major rows of 128 B: row k holds 1.0 in column k
+  for (int e = tid; e < KB * 8; e += 512) {
+    const int r = e >> 3, c = e & 7;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if ((r >> 3) == c) reinterpret_cast<uint16_t*>(&v)[r & 7] = 0x3F80u;
+    *reinterpret_cast<uint4*>(smem + OFF_ID + tc::sw128_off(r, c)) = v;
+  }
   const bool uniform = p.mask[b + p.batch_offset] == 0;
+  tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -346,9 +361,8 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
   const uint32_t s_col = (uint32_t)g * 128, o_col = s_col + 64, p_col = s_col + 96;
   const uint32_t sb = tc::smem_u32(smem);
-  const uint32_t q_s = sb + OFF_Q + g * 8192;
+  const uint32_t q_s = sb + OFF_Q + g * 8192, bt_s = sb + OFF_BT + g * BT_BYTES;
   uint8_t* kv = smem + OFF_KV + g * KV_STAGES * KV_BYTES;
-  uint8_t* brow_s = smem + OFF_BS + g * BS_BYTES + t * 128;   // this thread's staged bias row
   bool aborted = false;
   constexpr uint32_t IDESC_S = tc::idesc_bf16(128, KB), IDESC_O = tc::idesc_bf16(128, D);
 
@@ -358,82 +372,55 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     tc::tma_load_2d(kv + st * KV_BYTES, &tmK, &kvbar[g * KV_STAGES + st], 0, (int)(bh * p.qp + (int64_t)jj * KB));
     tc::tma_load_2d(kv + st * KV_BYTES + 4096, &tmV, &kvbar[g * KV_STAGES + st], jj * KB, (int)(bh * D));
   };
-  auto issue_s = [&](int jj) {   // S' (+)= Q K_jj^T
+  auto issue_bias = [&](int jj) {   // bias[q0..q0+127][g][64 jj .. 64 jj + 63]
+    tc::mbar_expect_tx(&bbar[g], BT_BYTES);
+    tc::tma_load_3d(smem + OFF_BT + g * BT_BYTES, &tmB, &bbar[g], jj * KB, g, (int)q0);
+  };
+  auto issue_s = [&](int jj) {   // S' = bias_jj . I + Q K_jj^T
     const uint32_t ks = sb + OFF_KV + (g * KV_STAGES + jj % KV_STAGES) * KV_BYTES;
+    if (!uniform) {
+#pragma unroll
+      for (int kk = 0; kk < KB / 16; ++kk)
+        tc::mma_bf16(tbase + s_col, tc::smem_desc(bt_s + kk * 32, 1024, tc::kSW128),
+                     tc::smem_desc(sb + OFF_ID + kk * 32, 1024, tc::kSW128), IDESC_S, kk > 0);
+    }
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk)
       tc::mma_bf16(tbase + s_col, tc::smem_desc(q_s + kk * 32, 512, tc::kSW64), tc::smem_desc(ks + kk * 32, 512, tc::kSW64),
                    IDESC_S, !uniform || kk > 0);
   };
 
-  const int64_t q = q0 + t;
-  const bf16* bias_row = p.bias + (q * H + g) * p.qp;
-  // bias row of block jj -> this thread's staging row (chunk c at c ^ (t & 7): conflict-free reads)
-  auto stage_bias = [&](int jj) {
-#pragma unroll
-    for (int c = 0; c < KB / 8; ++c) cp_async16(brow_s + ((c ^ (t & 7)) << 4), bias_row + (int64_t)jj * KB + c * 8);
-    cp_async_commit();
-  };
-  // staged bias of block jj (bf16, already x sqrt(D)) into the S' columns; -inf where the key is masked or padding
-  auto store_bias = [&](int jj) {
-    cp_async_wait_all();
-    const uint64_t vb = (uint64_t)kbits[2 * jj] | ((uint64_t)kbits[2 * jj + 1] << 32);
-    const bool full = vb == ~0ull;
-#pragma unroll
-    for (int c2 = 0; c2 < KB / 16; ++c2) {
-      uint32_t r[16];
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int c = 2 * c2 + h2;
-        const uint4 raw = *reinterpret_cast<const uint4*>(brow_s + ((c ^ (t & 7)) << 4));
-        const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          r[8 * h2 + 2 * e] = u[e] << 16;
-          r[8 * h2 + 2 * e + 1] = u[e] & 0xFFFF0000u;
-        }
-      }
-      if (!full) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          if (!((vb >> (16 * c2 + e)) & 1)) r[e] = 0xFF800000u;
-      }
-      tc::tmem_st16(lane_addr + s_col + 16 * c2, r);
-    }
-  };
-
-  // ---- prologue: Q, K/V blocks 0 and 1, bias of block 0, S'_0 ----
+  // ---- prologue: Q, K/V blocks 0 and 1, bias tile 0, S'_0 ----
   if (t == 0) {
     tc::mbar_expect_tx(&qbar[g], 8192);
     tc::tma_load_2d(smem + OFF_Q + g * 8192, &tmQ, &qbar[g], 0, (int)(bh * p.qp + q0));
     issue_kv(0);
     issue_kv(1);   // qp >= 128: at least two key blocks
-  }
-  if (!uniform) {
-    stage_bias(0);
-    store_bias(0);
-    tc::tmem_wait_st();
-    stage_bias(1);
-  }
-  tc::tc_fence_before();
-  wg_sync(g);
-  if (t == 0) {
-    tc::tc_fence_after();
+    issue_bias(0);
     tc::mbar_wait(&qbar[g], 0, p.status, aborted);
     tc::mbar_wait(&kvbar[g * KV_STAGES], 0, p.status, aborted);
+    tc::mbar_wait(&bbar[g], 0, p.status, aborted);
+    tc::tc_fence_after();
     issue_s(0);
     tc::mma_commit(&sbar[g]);
   }
 
+  const int64_t q = q0 + t;
   float m_run = -INFINITY, l = 0.f;
   for (int j = 0; j < nkb; ++j) {
     tc::mbar_wait(&sbar[g], j & 1, p.status, aborted);
     tc::tc_fence_after();
-    if (t == 0 && j + 2 < nkb) issue_kv(j + 2);   // its stage held block j-1, whose P V is done
+    if (t == 0 && j + 1 < nkb) issue_bias(j + 1);   // S'_j has consumed the bias tile
     float sv[KB];
     float corr = 1.f, m_use = 0.f;
     if (!uniform) {
       tc::tmem_ld64(lane_addr + s_col, sv);
+      const uint64_t vb = (uint64_t)kbits[2 * j] | ((uint64_t)kbits[2 * j + 1] << 32);
+      if (vb != ~0ull) {   // masked or padding keys in this block: excluded
+#pragma unroll
+        for (int e = 0; e < KB; ++e)
+          if (!((vb >> e) & 1)) sv[e] = -INFINITY;
+      }
       float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int e = 0; e < KB; e += 8) {
@@ -452,6 +439,12 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
 #pragma unroll
       for (int e = 0; e < KB; ++e) sv[e] = ((int64_t)j * KB + e < p.nq) ? 1.f : 0.f;
     }
+    // P_{j-1} V_{j-1} must be done before O is rescaled or P is overwritten
+    if (j > 0) {
+      tc::mbar_wait(&pvbar[g], (j - 1) & 1, p.status, aborted);
+      tc::tc_fence_after();
+    }
+    if (t == 0 && j + 2 < nkb) issue_kv(j + 2);   // its stage held block j-1, whose P V is done
     if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
       // O (blocks < j, complete) *= corr
       float ov[D];
@@ -479,42 +472,40 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
       tc::tmem_st32(lane_addr + p_col, pk);
       l = l * corr + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
     }
-    if (!uniform && j + 1 < nkb) {
-      store_bias(j + 1);               // S'_j has been read
-      if (j + 2 < nkb) stage_bias(j + 2);
-    }
     tc::tmem_wait_st();
     tc::tc_fence_before();
     wg_sync(g);
-    if (t == 0) {
+    if (t == 0 && j + 1 < nkb) {
+      // S'_{j+1} first: it is what this warpgroup waits for next
+      tc::tc_fence_after();
+      tc::mbar_wait(&kvbar[g * KV_STAGES + (j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, p.status, aborted);
+      tc::mbar_wait(&bbar[g], (j + 1) & 1, p.status, aborted);
+      issue_s(j + 1);
+      tc::mma_commit(&sbar[g]);
+    } else if (t == 32) {
+      // O += P_j V_j, issued from another warp in parallel with the S' MMAs
       tc::tc_fence_after();
       const uint32_t vs = sb + OFF_KV + (g * KV_STAGES + j % KV_STAGES) * KV_BYTES + 4096;
 #pragma unroll
       for (int kk = 0; kk < KB / 16; ++kk)
         tc::mma_bf16_ts(tbase + o_col, tbase + p_col + kk * 8, tc::smem_desc(vs + kk * 32, 1024, tc::kSW128), IDESC_O,
                         j > 0 || kk > 0);
-      if (j + 1 < nkb) {
-        tc::mbar_wait(&kvbar[g * KV_STAGES + (j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, p.status, aborted);
-        issue_s(j + 1);
-        tc::mma_commit(&sbar[g]);
-      } else {
-        tc::mma_commit(&obar[g]);
-      }
+      tc::mma_commit(&pvbar[g]);
     }
   }
 
-  // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) over this head's bias staging ----
+  // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) over this head's bias tile ----
   const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
   uint4 graw[D / 8];
 #pragma unroll
   for (int c = 0; c < D / 8; ++c) graw[c] = __ldg(grow + c);
-  tc::mbar_wait(&obar[g], 0, p.status, aborted);
+  tc::mbar_wait(&pvbar[g], (nkb - 1) & 1, p.status, aborted);   // the last P V (and every S' before it)
   tc::tc_fence_after();
   {
     const float inv = l > 0.f ? 1.0f / l : 0.f;
     float ov[D];
     tc::tmem_ld32(lane_addr + o_col, ov);
-    uint8_t* ost = smem + OFF_BS + g * BS_BYTES;
+    uint8_t* ost = smem + OFF_BT + g * BT_BYTES;
 #pragma unroll
     for (int cc = 0; cc < D / 8; ++cc) {
       const uint32_t* gu = reinterpret_cast<const uint32_t*>(&graw[cc]);
@@ -546,7 +537,7 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
 #pragma unroll
     for (int k = 0; k < 2 * H; ++k) {
       const int h = k >> 1, kk = k & 1;
-      tc::mma_bf16(tbase, tc::smem_desc(sb + OFF_BS + h * BS_BYTES + kk * 32, 512, tc::kSW64),
+      tc::mma_bf16(tbase, tc::smem_desc(sb + OFF_BT + h * BT_BYTES + kk * 32, 512, tc::kSW64),
                    tc::smem_desc(sb + OFF_Q + h * 8192 + kk * 32, 512, tc::kSW64), IDESC, k > 0);
     }
     tc::mma_commit(outbar);
@@ -689,10 +680,31 @@ int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, 
   SF_TRY(make_2d_tmap(&mq, q, D, nb * H * qp, D, TILE, 64));
   SF_TRY(make_2d_tmap(&mk, k, D, nb * H * qp, D, KB, 64));
   SF_TRY(make_2d_tmap(&mv, vt, qp, nb * H * D, KB, D, 128));
+  // bias [qp][H][qp]: tiles of 64 keys x 1 head x 128 queries; keys >= N read as zero
+  CUtensorMap mb;
+  {
+    auto encode = tensor_map_encoder();
+    if (!encode) return SF_ERR_CUDA;
+    if ((reinterpret_cast<uintptr_t>(bias) & 15) != 0) {
+      set_error("triatt_core: bias %p is not 16-byte aligned", (const void*)bias);
+      return SF_ERR_ARG;
+    }
+    cuuint64_t dims[3] = {(cuuint64_t)nq, (cuuint64_t)H, (cuuint64_t)qp};
+    cuuint64_t strides[2] = {(cuuint64_t)qp * 2, (cuuint64_t)(H * qp * 2)};
+    cuuint32_t box[3] = {(cuuint32_t)KB, 1, (cuuint32_t)TILE};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = encode(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16*>(bias), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled failed (%d) for the attention bias", (int)r);
+      return SF_ERR_CUDA;
+    }
+  }
   AttCoreParams cp{g, bias, w_out, mask, z, z_out, cols, nq, qp, batch_offset, transpose,
                    (1.0f / sqrtf((float)D)) * kLog2e, status};
   dim3 cgrid((unsigned)(qp / TILE), (unsigned)nb);
-  k_triatt_core_tc<<<cgrid, 512, SMEM_CORE, stream>>>(mq, mk, mv, cp);
+  k_triatt_core_tc<<<cgrid, 512, SMEM_CORE, stream>>>(mq, mk, mv, mb, cp);
   count_launch();
   return check_launch("triatt_core_tc");
 }
