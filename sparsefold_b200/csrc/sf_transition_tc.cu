@@ -269,7 +269,7 @@ int make_2d_tmap(CUtensorMap* map, const void* base, int64_t inner, int64_t oute
     set_error("2-d tensor map: base %p / row bytes %lld not 16-byte aligned", base, (long long)(inner * 2));
     return SF_ERR_ARG;
   }
-  if (swizzle_bytes != 128 && swizzle_bytes != 64) {
+  if (swizzle_bytes != 128 && swizzle_bytes != 64 && swizzle_bytes != 0) {
     set_error("2-d tensor map: unsupported swizzle %d", swizzle_bytes);
     return SF_ERR_ARG;
   }
@@ -277,7 +277,9 @@ int make_2d_tmap(CUtensorMap* map, const void* base, int64_t inner, int64_t oute
   cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapSwizzle sw = swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                      : CU_TENSOR_MAP_SWIZZLE_NONE;
   CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

@@ -1,17 +1,19 @@
 // Triangle attention (GridSelfAttention, blocks.py:270-366), bf16 track, on tcgen05.
 //
 // Two kernels per call:
-//  k_triatt_project_tc  LN(z) (scale only, blocks.py:260-264) -> [q | k | v | gate]
-//                       (one tcgen05 GEMM, N = 4 x 128) and the 4-head pair bias
-//                       (CUDA-core dot products while the row is in registers).
-//                       Tiles run along the query axis of the attention: a row
-//                       tile for the starting node, a column tile for the ending
-//                       node (transpose=True), so every store is contiguous.
+//  k_triatt_project_tc  persistent and warp-specialised: TMA brings 128-query z
+//                       tiles (row tiles for the starting node, column tiles for
+//                       the ending node, transpose=True), four warps apply the
+//                       scale-only LN (blocks.py:260-264) in place and form the
+//                       4-head pair bias on CUDA cores, one thread issues
+//                       D[channel][query] = W . LN(z)^T for q, k, v, gate into
+//                       two TMEM halves, and eight epilogue warps stage the
+//                       outputs and TMA-store them.
 //  k_triatt_core_tc     flash attention + gate + output projection + residual for
 //                       one (attention row b, 128-query block): four softmax
 //                       warpgroups, one per head.  S' = sqrt(D) bias + Q K^T
-//                       (M128 N64 K32, accumulated onto the bias the warpgroup
-//                       stored in TMEM) and O += P V (M128 N32 K64) run on
+//                       (the bias tile times an identity, then M128 N64 K32)
+//                       and O += P V (M128 N32 K64) run on
 //                       tcgen05 with TMEM accumulators; K/V^T blocks arrive by
 //                       TMA; the softmax runs in exp2 with the reference's
 //                       -FLT_MAX masking; the gated outputs of all four heads
@@ -39,42 +41,57 @@ constexpr float kBiasScale = 5.656854249492380f;
 
 struct AttProjParams {
   const float* ln_w;      // act_norm scale [128]
-  const bf16* w_qkvg;     // [512][128]
   const bf16* w_bias;     // [4][128]
-  bf16 *q, *k, *vt, *g, *bias;
-  int64_t rows, cols;     // the z block [rows][cols][128]
+  bf16* bias;             // [.][H][qp]
   int64_t nb, nq, qp;     // attention rows (batches), queries = keys, query pitch
   int transpose;          // attention along columns: batch = column, query = row
   int compute_bias;       // write bias[(r*H + h)*qp + s] for the block's positions (r, s)
   uint32_t* status;
 };
 
-constexpr int NOUT = 512;
+// Warp roles (448 threads), one 128-query tile of one attention row at a time:
+//   warps 0-7   epilogue: warp w reads TMEM lanes 32(w%4).. (output channels
+//               32(w%4).., i.e. head w%4 of q, k, v and gate channels of that
+//               head) for queries 64(w/4)..+63, stages them and TMA-stores them:
+//               q, k, gate transposed to [query][32] rows, v^T as [32][query]
+//   warps 8-11  thread = query: scale-only LayerNorm of its row in place and the
+//               four pair-bias logits LN(z) . W_b[h]
+//   warp 12     TMA producer of z tiles (row tiles, or column tiles for the
+//               ending node), two stages
+//   warp 13     MMA issuer: D[out channel][query] = W_x . LN(z)^T for x = q, k
+//               (TMEM half 0, columns 0-255) and v, gate (half 1, 256-511)
+constexpr int NOUT = 512;                   // w_qkvg rows: q, k, v, gate
 constexpr int W_BYTES = NOUT * C * 2;
-constexpr int VT_STAGE = D * TILE * 2;     // one head's V^T tile [32][128] bf16 (8 KB)
-constexpr int SMEM_PROJ = 2 * A_BYTES + W_BYTES + VT_STAGE + 1024 + 1024;
+constexpr int PJ_EPI_WARPS = 8;
+constexpr int PJ_THREADS = (PJ_EPI_WARPS + 4 + 2) * 32;
+constexpr int PJ_ST_BYTES = 64 * D * 2;     // one epilogue warp's staging tile (64 queries x 32 channels)
+constexpr int OFF_JW = 0;
+constexpr int OFF_JZ = W_BYTES;                            // [2] z tiles
+constexpr int OFF_JST = OFF_JZ + 2 * A_BYTES;              // [8] staging tiles
+constexpr int OFF_JWB = OFF_JST + PJ_EPI_WARPS * PJ_ST_BYTES;   // W_b [4][128] bf16
+constexpr int OFF_JBAR = OFF_JWB + H * C * 2;
+constexpr int SMEM_PROJ = OFF_JBAR + 256 + 1024;
+static_assert(SMEM_PROJ <= 232448, "projection shared memory");
 
-// LayerNorm (scale only) of row r in place, returning the 4 pair-bias logits of
-// the normalised (bf16-rounded) row.
-__device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* __restrict__ w,
-                                            const bf16* __restrict__ wb, float (&bias)[H]) {
-  uint4 v[16];
-#pragma unroll
-  for (int ka = 0; ka < 2; ++ka)
-#pragma unroll
-    for (int c = 0; c < 8; ++c) v[ka * 8 + c] = *reinterpret_cast<const uint4*>(tile + ka * ATOM + tc::sw128_off(r, c));
+// Scale-only LayerNorm of tile row r in place (three passes over shared memory)
+// and the four pair-bias logits of the bf16-rounded normalised row.
+__device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* __restrict__ w, const bf16* wb_s,
+                                            float (&bias)[H]) {
+  auto off = [&](int i) -> uint32_t { return (uint32_t)(i >> 3) * ATOM + tc::sw128_off(r, i & 7); };
   float s = 0.f;
-#pragma unroll
+#pragma unroll 4
   for (int i = 0; i < 16; ++i) {
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll
     for (int j = 0; j < 4; ++j) s += bf_lo(u[j]) + bf_hi(u[j]);
   }
   const float mean = s * (1.0f / C);
   float q = 0.f;
-#pragma unroll
+#pragma unroll 4
   for (int i = 0; i < 16; ++i) {
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[i]);
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float d0 = bf_lo(u[j]) - mean, d1 = bf_hi(u[j]) - mean;
@@ -84,162 +101,199 @@ __device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* _
   const float rstd = rsqrtf(q * (1.0f / C) + 1e-5f);
 #pragma unroll
   for (int h = 0; h < H; ++h) bias[h] = 0.f;
-#pragma unroll
+#pragma unroll 2
   for (int i = 0; i < 16; ++i) {
-    uint32_t* u = reinterpret_cast<uint32_t*>(&v[i]);
+    uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
+    uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + 8 * i));
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + 8 * i + 4));
+    const float wl[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    uint4 wv[H];
+#pragma unroll
+    for (int h = 0; h < H; ++h) wv[h] = *reinterpret_cast<const uint4*>(wb_s + h * C + 8 * i);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int k = i * 8 + 2 * j;
-      u[j] = pack_bf2((bf_lo(u[j]) - mean) * rstd * __ldg(w + k), (bf_hi(u[j]) - mean) * rstd * __ldg(w + k + 1));
-      const float y0 = bf_lo(u[j]), y1 = bf_hi(u[j]);
+      u[j] = pack_bf2((bf_lo(u[j]) - mean) * rstd * wl[2 * j], (bf_hi(u[j]) - mean) * rstd * wl[2 * j + 1]);
+      const float y0 = bf_lo(u[j]), y1 = bf_hi(u[j]);   // the bias uses the bf16-rounded normalised row
 #pragma unroll
-      for (int h = 0; h < H; ++h)
-        bias[h] += y0 * __bfloat162float(wb[h * C + k]) + y1 * __bfloat162float(wb[h * C + k + 1]);
+      for (int h = 0; h < H; ++h) {
+        const uint32_t wp = reinterpret_cast<const uint32_t*>(&wv[h])[j];
+        bias[h] = fmaf(y0, bf_lo(wp), fmaf(y1, bf_hi(wp), bias[h]));
+      }
     }
-  }
-#pragma unroll
-  for (int ka = 0; ka < 2; ++ka)
-#pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(tile + ka * ATOM + tc::sw128_off(r, c)) = v[ka * 8 + c];
-}
-
-__device__ __forceinline__ void store_row32(bf16* dst, const float* v, bool zero) {
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    uint4 o;
-    o.x = zero ? 0u : pack_bf2(v[8 * g + 0], v[8 * g + 1]);
-    o.y = zero ? 0u : pack_bf2(v[8 * g + 2], v[8 * g + 3]);
-    o.z = zero ? 0u : pack_bf2(v[8 * g + 4], v[8 * g + 5]);
-    o.w = zero ? 0u : pack_bf2(v[8 * g + 6], v[8 * g + 7]);
-    reinterpret_cast<uint4*>(dst)[g] = o;
+    *reinterpret_cast<uint4*>(tile + off(i)) = v;
   }
 }
 
-__global__ void __launch_bounds__(128, 1) k_triatt_project_tc(const __grid_constant__ CUtensorMap tmap,
-                                                              AttProjParams p) {
+__global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __grid_constant__ CUtensorMap tmZ,
+                                                                     const __grid_constant__ CUtensorMap tmQ,
+                                                                     const __grid_constant__ CUtensorMap tmK,
+                                                                     const __grid_constant__ CUtensorMap tmV,
+                                                                     const __grid_constant__ CUtensorMap tmG,
+                                                                     const bf16* __restrict__ w_qkvg, AttProjParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* A = smem;
-  uint8_t* W = smem + 2 * A_BYTES;
-  bf16* vst = reinterpret_cast<bf16*>(W + W_BYTES);                 // [32][128] staging of V^T
-  uint64_t* bars = reinterpret_cast<uint64_t*>(W + W_BYTES + VT_STAGE);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t nqb = p.qp / TILE;
-  const int64_t ntiles = p.nb * nqb;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_JBAR);   // [2] z tile landed
+  uint64_t* normed = full + 2;                                      // [2] z tile normalised (128 arrivals)
+  uint64_t* zfree = normed + 2;                                     // [2] MMAs of the stage done
+  uint64_t* tfull = zfree + 2;                                      // [2] TMEM half written
+  uint64_t* tfree = tfull + 2;                                      // [2] TMEM half read (8 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t nqb = p.qp / TILE, ntiles = p.nb * nqb;
 
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    tc::mbar_init(&bars[0], 1);
-    tc::mbar_init(&bars[1], 1);
-    tc::mbar_init(&bars[2], 1);
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(&full[s], 1);
+      tc::mbar_init(&normed[s], 128);
+      tc::mbar_init(&zfree[s], 1);
+      tc::mbar_init(&tfull[s], 1);
+      tc::mbar_init(&tfree[s], PJ_EPI_WARPS);
+    }
     tc::fence_mbar_init();
-    tc::prefetch_tmap(&tmap);
+    tc::prefetch_tmap(&tmZ);
+    tc::prefetch_tmap(&tmQ);
+    tc::prefetch_tmap(&tmK);
+    tc::prefetch_tmap(&tmV);
+    tc::prefetch_tmap(&tmG);
   }
-  load_weight_sw128(W, p.w_qkvg, NOUT, tid, 128);
+  for (int e = tid; e < H * C / 8; e += PJ_THREADS)
+    reinterpret_cast<uint4*>(smem + OFF_JWB)[e] = __ldg(reinterpret_cast<const uint4*>(p.w_bias) + e);
+  load_weight_sw128(smem + OFF_JW, w_qkvg, NOUT, tid, PJ_THREADS);
   tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
 
-  auto issue = [&](int64_t tile, int stage) {
-    const int b = (int)(tile / nqb), q0 = (int)((tile % nqb) * TILE);
-    const int c1 = p.transpose ? b : q0;     // column coordinate
-    const int c2 = p.transpose ? q0 : b;     // row coordinate
-    tc::mbar_expect_tx(&bars[stage], A_BYTES);
-    tc::tma_load_3d(A + stage * A_BYTES, &tmap, &bars[stage], 0, c1, c2);
-    tc::tma_load_3d(A + stage * A_BYTES + ATOM, &tmap, &bars[stage], 64, c1, c2);
-  };
-
-  constexpr uint32_t IDESC = tc::idesc_bf16(128, 256);
-  const uint32_t a_base = tc::smem_u32(A), w_base = tc::smem_u32(W);
-
-  int64_t tile = blockIdx.x;
-  if (tid == 0 && tile < ntiles) issue(tile, 0);
-  for (uint32_t it = 0; tile < ntiles; tile += gridDim.x, ++it) {
-    const int stage = it & 1;
-    if (tid == 0 && tile + gridDim.x < ntiles) {
-      tc::fence_proxy_async();
-      issue(tile + gridDim.x, stage ^ 1);
+  if (warp == 12) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+        const int st = it & 1;
+        if (it >= 2) tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
+        const int b = (int)(tile / nqb), q0 = (int)((tile % nqb) * TILE);
+        const int c1 = p.transpose ? b : q0;     // column coordinate
+        const int c2 = p.transpose ? q0 : b;     // row coordinate
+        uint8_t* dst = smem + OFF_JZ + st * A_BYTES;
+        tc::mbar_expect_tx(&full[st], A_BYTES);
+        tc::tma_load_3d(dst, &tmZ, &full[st], 0, c1, c2);
+        tc::tma_load_3d(dst + ATOM, &tmZ, &full[st], 64, c1, c2);
+      }
     }
-    tc::mbar_wait(&bars[stage], (it >> 1) & 1, p.status, aborted);
-    const int64_t b = tile / nqb, qi = (tile % nqb) * TILE + tid;
-    const bool valid = qi < p.nq;
-    float bias[H];
-    ln_row_bias(A + stage * A_BYTES, tid, p.ln_w, p.w_bias, bias);
-    if (valid && p.compute_bias) {
-      const int64_t r = p.transpose ? qi : b, s = p.transpose ? b : qi;
-#pragma unroll
-      for (int h = 0; h < H; ++h) p.bias[(r * H + h) * p.qp + s] = __float2bfloat16_rn(bias[h] * kBiasScale);
-    }
-    tc::fence_proxy_async();
-    tc::tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc::tc_fence_after();
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int ka = k >> 2, kk = k & 3;
-        const uint64_t ad = tc::smem_desc(a_base + stage * A_BYTES + ka * ATOM + kk * 32, 1024, tc::kSW128);
+  } else if (warp == 13) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      constexpr uint32_t IDESC = tc::idesc_bf16(128, 128);
+      uint32_t it = 0;
+      for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+        const int st = it & 1;
+        tc::mbar_wait(&normed[st], (it >> 1) & 1, p.status, aborted);
+        tc::tc_fence_after();
+        const uint32_t zb = sb + OFF_JZ + st * A_BYTES;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          const uint64_t bd = tc::smem_desc(w_base + ka * (NOUT * 128) + hh * (256 * 128) + kk * 32, 1024, tc::kSW128);
-          tc::mma_bf16(tbase + hh * 256, ad, bd, IDESC, k > 0);
+          if (it >= 1) tc::mbar_wait(&tfree[hh], (it - 1) & 1, p.status, aborted);
+          tc::tc_fence_after();
+#pragma unroll
+          for (int mt = 0; mt < 2; ++mt) {          // q, k | v, gate
+            const int mtx = 2 * hh + mt;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const int ka = k >> 2, kk = k & 3;
+              tc::mma_bf16(tbase + hh * 256 + mt * 128,
+                           tc::smem_desc(sb + OFF_JW + ka * (NOUT * 128) + mtx * (128 * 128) + kk * 32, 1024, tc::kSW128),
+                           tc::smem_desc(zb + ka * ATOM + kk * 32, 1024, tc::kSW128), IDESC, k > 0);
+            }
+          }
+          tc::mma_commit(&tfull[hh]);
         }
+        tc::mma_commit(&zfree[st]);
       }
-      tc::mma_commit(&bars[2]);
     }
-    tc::mbar_wait(&bars[2], it & 1, p.status, aborted);
-    tc::tc_fence_after();
-
-    // ---- epilogue: query qi of attention row b ----
-    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+  } else if (warp >= PJ_EPI_WARPS) {
+    // ---- LayerNorm in place + pair bias (thread = query of the tile) ----
+    const int r = tid - PJ_EPI_WARPS * 32;
+    const bf16* wb_s = reinterpret_cast<const bf16*>(smem + OFF_JWB);
+    uint32_t it = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int st = it & 1;
+      tc::mbar_wait(&full[st], (it >> 1) & 1, p.status, aborted);
+      float bias[H];
+      ln_row_bias(smem + OFF_JZ + st * A_BYTES, r, p.ln_w, wb_s, bias);
+      tc::fence_proxy_async();
+      tc::mbar_arrive(&normed[st]);
+      const int64_t b = tile / nqb, qi = (tile % nqb) * TILE + r;
+      if (p.compute_bias && qi < p.nq) {
+        const int64_t rr = p.transpose ? qi : b, ss = p.transpose ? b : qi;
+#pragma unroll
+        for (int h = 0; h < H; ++h) p.bias[(rr * H + h) * p.qp + ss] = __float2bfloat16_rn(bias[h] * kBiasScale);
+      }
+    }
+  } else {
+    // ---- epilogue: head `quad`, queries q0 + 64 hf .. +63 ----
+    const int quad = warp & 3, hf = warp >> 2;
+    const uint32_t lane_addr = tbase + ((uint32_t)(32 * quad) << 16);
+    uint8_t* stg = smem + OFF_JST + warp * PJ_ST_BYTES;
+    uint32_t it = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      const int b = (int)(tile / nqb), q0 = (int)((tile % nqb) * TILE) + 64 * hf;
 #pragma unroll 1
-    for (int h = 0; h < H; ++h) {
-      float v0[16], v1[16], row[32];
-      tc::tmem_ld16(lane_addr + h * D, v0);                 // q
-      tc::tmem_ld16(lane_addr + h * D + 16, v1);
+      for (int hh = 0; hh < 2; ++hh) {
+        tc::mbar_wait(&tfull[hh], it & 1, p.status, aborted);
+        tc::tc_fence_after();
+#pragma unroll 1
+        for (int mt = 0; mt < 2; ++mt) {
+          const int o = 2 * hh + mt;   // 0 q, 1 k, 2 v, 3 gate
+          float v[64];
+          tc::tmem_ld64(lane_addr + hh * 256 + mt * 128 + 64 * hf, v);   // channel 32 quad + lane, 64 queries
+          if (mt == 1) {
+            // both TMEM columns of this half are in registers
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&tfree[hh]);
+          }
+          if (o == 3) {
 #pragma unroll
-      for (int e = 0; e < 16; ++e) { row[e] = v0[e]; row[16 + e] = v1[e]; }
-      store_row32(p.q + ((b * H + h) * p.qp + qi) * D, row, !valid);
-      tc::tmem_ld16(lane_addr + 128 + h * D, v0);           // k
-      tc::tmem_ld16(lane_addr + 128 + h * D + 16, v1);
+            for (int e = 0; e < 64; ++e) v[e] = sigmoid_tanh(v[e]);
+          }
+          if (lane == 0) tc::bulk_wait_read0();   // the previous store has read the staging tile
+          __syncwarp();
+          if (o == 2) {
+            // v^T: [32 channels][64 queries], 128B swizzle; this lane's row is its channel
 #pragma unroll
-      for (int e = 0; e < 16; ++e) { row[e] = v0[e]; row[16 + e] = v1[e]; }
-      store_row32(p.k + ((b * H + h) * p.qp + qi) * D, row, !valid);
-      tc::tmem_ld16(lane_addr + 256 + h * D, v0);           // v, stored transposed (keys contiguous)
-      tc::tmem_ld16(lane_addr + 256 + h * D + 16, v1);
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(stg + tc::sw128_off(lane, c)) =
+                  make_uint4(pack_bf2(v[8 * c], v[8 * c + 1]), pack_bf2(v[8 * c + 2], v[8 * c + 3]),
+                             pack_bf2(v[8 * c + 4], v[8 * c + 5]), pack_bf2(v[8 * c + 6], v[8 * c + 7]));
+          } else {
+            // q, k, gate: [64 queries][32 channels] rows of 64 bytes; this lane is column `lane`
+            bf16* st16 = reinterpret_cast<bf16*>(stg) + lane;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        vst[e * TILE + tid] = __float2bfloat16_rn(valid ? v0[e] : 0.f);
-        vst[(16 + e) * TILE + tid] = __float2bfloat16_rn(valid ? v1[e] : 0.f);
-      }
-      __syncthreads();
-      {
-        // 32 rows (d) x 256 bytes: V^T[b][h][d][q0 .. q0+127]
-        bf16* vt = p.vt + ((b * H + h) * D) * p.qp + (tile % nqb) * TILE;
-#pragma unroll
-        for (int i = 0; i < (D * 16) / 128; ++i) {
-          const int e = tid + 128 * i, d = e >> 4, part = e & 15;
-          *reinterpret_cast<uint4*>(vt + (int64_t)d * p.qp + part * 8) =
-              *reinterpret_cast<const uint4*>(vst + d * TILE + part * 8);
+            for (int e = 0; e < 64; ++e) st16[e * D] = __float2bfloat16_rn(v[e]);
+          }
+          tc::fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            if (o == 0) tc::tma_store_2d(&tmQ, stg, 0, (int)(((int64_t)b * H + quad) * p.qp + q0));
+            else if (o == 1) tc::tma_store_2d(&tmK, stg, 0, (int)(((int64_t)b * H + quad) * p.qp + q0));
+            else if (o == 2) tc::tma_store_2d(&tmV, stg, q0, (b * H + quad) * D);
+            else tc::tma_store_2d(&tmG, stg, quad * D, (int)((int64_t)b * p.qp + q0));
+            tc::bulk_commit();
+          }
         }
       }
-      __syncthreads();
-      tc::tmem_ld16(lane_addr + 384 + h * D, v0);           // gate -> sigmoid
-      tc::tmem_ld16(lane_addr + 384 + h * D + 16, v1);
-#pragma unroll
-      for (int e = 0; e < 16; ++e) { row[e] = fast_sigmoid(v0[e]); row[16 + e] = fast_sigmoid(v1[e]); }
-      store_row32(p.g + (b * p.qp + qi) * C + h * D, row, false);
     }
-    tc::tc_fence_before();
-    __syncthreads();
+    if (lane == 0) tc::bulk_wait0();
   }
+  tc::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc::tc_fence_after();
@@ -648,15 +702,25 @@ int triatt_project_tc(const bf16* z, int64_t rows, int64_t cols, int transpose, 
              (long long)cols);
   uint32_t* status = device_status_ptr();
   if (!status) return SF_ERR_CUDA;
+  SF_REQUIRE(((reinterpret_cast<uintptr_t>(ln_w) | reinterpret_cast<uintptr_t>(w_qkvg) |
+               reinterpret_cast<uintptr_t>(w_bias)) & 15) == 0,
+             "triatt_project: weights must be 16-byte aligned");
+  const int64_t qp = triatt_query_pitch(nq);
+  SF_REQUIRE(nb * H * qp < (int64_t(1) << 31), "triatt_project: %lld attention rows x %lld queries exceed the TMA range",
+             (long long)nb, (long long)qp);
   static bool attr[64] = {false};
   SF_TRY(set_smem(k_triatt_project_tc, SMEM_PROJ, attr));
-  CUtensorMap map;
-  SF_TRY(make_pair_tmap(&map, z, rows, cols, transpose != 0));
-  const int64_t qp = triatt_query_pitch(nq);
-  AttProjParams pp{ln_w, w_qkvg, w_bias, q, k, vt, g, bias, rows, cols, nb, nq, qp, transpose, compute_bias, status};
+  CUtensorMap mz, mq, mk, mv, mg;
+  SF_TRY(make_pair_tmap(&mz, z, rows, cols, transpose != 0));
+  // stores of 64 queries per epilogue warp: Q, K [nb*H*qp][32], V^T [nb*H*32][qp], G [nb*qp][128]
+  SF_TRY(make_2d_tmap(&mq, q, D, nb * H * qp, D, 64, 0));
+  SF_TRY(make_2d_tmap(&mk, k, D, nb * H * qp, D, 64, 0));
+  SF_TRY(make_2d_tmap(&mv, vt, qp, nb * H * D, 64, D, 128));
+  SF_TRY(make_2d_tmap(&mg, g, C, nb * qp, D, 64, 0));
+  AttProjParams pp{ln_w, w_bias, bias, nb, nq, qp, transpose, compute_bias, status};
   const int64_t ntiles = nb * (qp / TILE);
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  k_triatt_project_tc<<<grid, 128, SMEM_PROJ, stream>>>(map, pp);
+  k_triatt_project_tc<<<grid, PJ_THREADS, SMEM_PROJ, stream>>>(mz, mq, mk, mv, mg, w_qkvg, pp);
   count_launch();
   return check_launch("triatt_project_tc");
 }
