@@ -329,14 +329,9 @@ constexpr int OFF_BT = OFF_KV + H * KV_STAGES * KV_BYTES;     // [h] bias tile o
 constexpr int OFF_ID = OFF_BT + H * BT_BYTES;                 // 64 x 64 identity (128B swizzle, K-major)
 constexpr int OFF_KBITS = OFF_ID + KB * 128;                  // key-valid bits, qp/32 words
 constexpr int OFF_BAR = OFF_KBITS + MAX_QP / 8;
-constexpr int SMEM_CORE = OFF_BAR + 256 + 1024;
+constexpr int SMEM_CORE = OFF_BAR + 512 + 1024;
 constexpr float kRescale = 8.0f;       // the running max moves only when a block exceeds it by 2^8
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(tc::smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void wg_sync(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -358,14 +353,20 @@ __device__ __forceinline__ float ex2(float x) {
 //   completion is awaited only before P or O are touched again.  K and V^T
 //   blocks arrive by TMA three blocks deep, the bias tile one block ahead.  A row
 //   whose token is masked attends uniformly to all N keys (every logit of the
-//   reference is -FLT_MAX there).  After the last block the gated, normalised
-//   O_h and the W_o columns of head h are staged in shared memory and one more
-//   tcgen05 GEMM (K = 4 heads x 32) forms the output projection in columns
-//   [0,128); its epilogue adds the residual.
+//   reference is -FLT_MAX there).  Two blocks before the end the residual tile
+//   z[queries][32h .. 32h+31] arrives by TMA in a K/V stage that is no longer
+//   needed, and once the last S' is done the W_o columns of head h arrive by
+//   TMA over the Q tile.  After the last block the gated, normalised O_h is
+//   staged in shared memory, one more tcgen05 GEMM (K = 4 heads x 32) forms the
+//   output projection in columns [0,128), and each warpgroup adds its 32
+//   output channels to the residual tile in place and TMA-stores it.
 __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant__ CUtensorMap tmQ,
                                                            const __grid_constant__ CUtensorMap tmK,
                                                            const __grid_constant__ CUtensorMap tmV,
-                                                           const __grid_constant__ CUtensorMap tmB, AttCoreParams p) {
+                                                           const __grid_constant__ CUtensorMap tmB,
+                                                           const __grid_constant__ CUtensorMap tmW,
+                                                           const __grid_constant__ CUtensorMap tmR,
+                                                           const __grid_constant__ CUtensorMap tmO, AttCoreParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* qbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [H] Q tile landed
@@ -373,7 +374,9 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
   uint64_t* pvbar = sbar + H;                                      // [H] P_j V_j done (one phase per block)
   uint64_t* bbar = pvbar + H;                                      // [H] bias tile landed (one phase per block)
   uint64_t* kvbar = bbar + H;                                      // [H][KV_STAGES] K/V block landed
-  uint64_t* outbar = kvbar + H * KV_STAGES;
+  uint64_t* rbar = kvbar + H * KV_STAGES;                          // [H] residual tile landed
+  uint64_t* wbar = rbar + H;                                       // [H] W_o columns landed
+  uint64_t* outbar = wbar + H;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(outbar + 1);
   uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = tid >> 7, t = tid & 127;
@@ -386,12 +389,15 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 4 * H + H * KV_STAGES + 1; ++i) tc::mbar_init(&qbar[i], 1);
+    for (int i = 0; i < 6 * H + H * KV_STAGES + 1; ++i) tc::mbar_init(&qbar[i], 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmQ);
     tc::prefetch_tmap(&tmK);
     tc::prefetch_tmap(&tmV);
     tc::prefetch_tmap(&tmB);
+    tc::prefetch_tmap(&tmW);
+    tc::prefetch_tmap(&tmR);
+    tc::prefetch_tmap(&tmO);
   }
   // key k is attended iff mask[row] && mask[k] (pair mask, blocks.py:314); bits hold mask[k] && k < N
   for (int w = warp; w < (int)(p.qp / 32); w += 16) {
@@ -430,6 +436,9 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     tc::mbar_expect_tx(&bbar[g], BT_BYTES);
     tc::tma_load_3d(smem + OFF_BT + g * BT_BYTES, &tmB, &bbar[g], jj * KB, g, (int)q0);
   };
+  // residual tile z[b][q0..q0+127][32g..] (or z[q0..][b][32g..] for the ending node): 128 rows of 64 B
+  const int rc1 = p.transpose ? (int)b : (int)q0, rc2 = p.transpose ? (int)q0 : (int)b;
+  uint8_t* resid = kv + (nkb % KV_STAGES) * KV_BYTES;   // a stage no K/V block uses after block nkb-3
   auto issue_s = [&](int jj) {   // S' = bias_jj . I + Q K_jj^T
     const uint32_t ks = sb + OFF_KV + (g * KV_STAGES + jj % KV_STAGES) * KV_BYTES;
     if (!uniform) {
@@ -465,6 +474,11 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     tc::mbar_wait(&sbar[g], j & 1, p.status, aborted);
     tc::tc_fence_after();
     if (t == 0 && j + 1 < nkb) issue_bias(j + 1);   // S'_j has consumed the bias tile
+    if (t == 0 && j + 1 == nkb) {
+      // the last S' is done: the Q tile takes W_o[:, 32g .. 32g+31] (K-major 128 x 32, 64B swizzle)
+      tc::mbar_expect_tx(&wbar[g], 8192);
+      tc::tma_load_2d(smem + OFF_Q + g * 8192, &tmW, &wbar[g], g * D, 0);
+    }
     float sv[KB];
     float corr = 1.f, m_use = 0.f;
     if (!uniform) {
@@ -499,6 +513,11 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
       tc::tc_fence_after();
     }
     if (t == 0 && j + 2 < nkb) issue_kv(j + 2);   // its stage held block j-1, whose P V is done
+    if (t == 0 && j + 2 == nkb) {
+      // stage nkb % 3 held block nkb-3 (its P V is done) or was never used (nkb = 2)
+      tc::mbar_expect_tx(&rbar[g], TILE * D * 2);
+      tc::tma_load_3d(resid, &tmR, &rbar[g], g * D, rc1, rc2);
+    }
     if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
       // O (blocks < j, complete) *= corr
       float ov[D];
@@ -572,20 +591,12 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
       }
       *reinterpret_cast<uint4*>(ost + tc::sw64_off(t, cc)) = ok;
     }
-    // W_o[:, 32h .. 32h+31] as K-major 128 x 32 (64B swizzle) over this head's Q tile (its S' MMAs are done)
-    uint8_t* wst = smem + OFF_Q + g * 8192;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = t + 128 * i, n = e >> 2, c = e & 3;
-      cp_async16(wst + tc::sw64_off(n, c), p.w_out + n * C + g * D + c * 8);
-    }
-    cp_async_commit();
-    cp_async_wait_all();
   }
   tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();
   if (tid == 0) {
+    for (int h = 0; h < H; ++h) tc::mbar_wait(&wbar[h], 0, p.status, aborted);
     tc::tc_fence_after();
     constexpr uint32_t IDESC = tc::idesc_bf16(128, 128);
 #pragma unroll
@@ -599,27 +610,26 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
   tc::mbar_wait(outbar, 0, p.status, aborted);
   tc::tc_fence_after();
   {
-    // query q, output channels 32g .. 32g+31
-    const bool live = q < p.nq;
-    const int64_t pos = live ? (p.transpose ? q * p.cols + b : b * p.cols + q) : 0;
-    const uint4* zin = reinterpret_cast<const uint4*>(p.z + pos * C + g * D);
-    uint4* zo = reinterpret_cast<uint4*>(p.z_out + pos * C + g * D);
+    // query q, output channels 32g .. 32g+31: residual + projection in place, then one TMA store
     float ov[D];
-    tc::tmem_ld32(lane_addr + g * D, ov);   // warp-collective: every lane loads
-    if (live) {
+    tc::tmem_ld32(lane_addr + g * D, ov);
+    tc::mbar_wait(&rbar[g], 0, p.status, aborted);
 #pragma unroll
-      for (int cc = 0; cc < D / 8; ++cc) {
-        const uint4 zz = zin[cc];
-        const uint32_t* zu = reinterpret_cast<const uint32_t*>(&zz);
-        uint4 r;
-        uint32_t* ru = reinterpret_cast<uint32_t*>(&r);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d = cc * 8 + 2 * e;
-          ru[e] = pack_bf2(bf_lo(zu[e]) + ov[d], bf_hi(zu[e]) + ov[d + 1]);
-        }
-        zo[cc] = r;
-      }
+    for (int cc = 0; cc < D / 8; ++cc) {
+      uint4* zp = reinterpret_cast<uint4*>(resid + tc::sw64_off(t, cc));
+      const uint4 zz = *zp;
+      const int d = cc * 8;
+      *zp = make_uint4(pack_bf2(bf_lo(zz.x) + ov[d], bf_hi(zz.x) + ov[d + 1]),
+                       pack_bf2(bf_lo(zz.y) + ov[d + 2], bf_hi(zz.y) + ov[d + 3]),
+                       pack_bf2(bf_lo(zz.z) + ov[d + 4], bf_hi(zz.z) + ov[d + 5]),
+                       pack_bf2(bf_lo(zz.w) + ov[d + 6], bf_hi(zz.w) + ov[d + 7]));
+    }
+    tc::fence_proxy_async();
+    wg_sync(g);
+    if (t == 0) {
+      tc::tma_store_3d(&tmO, resid, g * D, rc1, rc2);   // rows beyond N are clipped
+      tc::bulk_commit();
+      tc::bulk_wait0();
     }
   }
   tc::tc_fence_before();
@@ -725,6 +735,29 @@ int triatt_project_tc(const bf16* z, int64_t rows, int64_t cols, int transpose, 
   return check_launch("triatt_project_tc");
 }
 
+// z block [rows][cols][128] seen as tiles of 32 channels x 128 positions along a row
+// (starting node) or along a column (ending node), 64B swizzle.
+static int make_resid_tmap(CUtensorMap* map, const bf16* base, int64_t rows, int64_t cols, bool column_tile) {
+  auto encode = tensor_map_encoder();
+  if (!encode) return SF_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) {
+    set_error("triatt_core: z %p is not 16-byte aligned", (const void*)base);
+    return SF_ERR_ARG;
+  }
+  cuuint64_t dims[3] = {(cuuint64_t)C, (cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[2] = {(cuuint64_t)C * 2, (cuuint64_t)(cols * C * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)D, column_tile ? 1u : (cuuint32_t)TILE, column_tile ? (cuuint32_t)TILE : 1u};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for the attention residual", (int)r);
+    return SF_ERR_CUDA;
+  }
+  return SF_OK;
+}
+
 int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, const bf16* bias, const bf16* w_out,
                    const uint8_t* mask, const bf16* z, bf16* z_out, int64_t rows, int64_t cols, int transpose,
                    int64_t batch_offset, cudaStream_t stream) {
@@ -765,10 +798,16 @@ int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, 
       return SF_ERR_CUDA;
     }
   }
+  // W_o [128 out][128 in]: 32 input channels x 128 rows per head (64B swizzle)
+  CUtensorMap mw, mr, mo;
+  SF_TRY(make_2d_tmap(&mw, w_out, C, C, D, C, 64));
+  // residual in / out: 32 channels x 128 queries of the z block (64B swizzle)
+  SF_TRY(make_resid_tmap(&mr, z, rows, cols, transpose != 0));
+  SF_TRY(make_resid_tmap(&mo, z_out, rows, cols, transpose != 0));
   AttCoreParams cp{g, bias, w_out, mask, z, z_out, cols, nq, qp, batch_offset, transpose,
                    (1.0f / sqrtf((float)D)) * kLog2e, status};
   dim3 cgrid((unsigned)(qp / TILE), (unsigned)nb);
-  k_triatt_core_tc<<<cgrid, 512, SMEM_CORE, stream>>>(mq, mk, mv, mb, cp);
+  k_triatt_core_tc<<<cgrid, 512, SMEM_CORE, stream>>>(mq, mk, mv, mb, mw, mr, mo, cp);
   count_launch();
   return check_launch("triatt_core_tc");
 }
