@@ -171,8 +171,8 @@ int sf_tri_mult_contract_chunked(int dtype, const void* a_op, int64_t chunks_a, 
 /* Query pitch qp of the attention buffers: Q, K, Vt [nb][4][qp][32],
  * G [nb][qp][128], bias [qp][4][qp] (bias[q][h][k], rows gathered across ranks). */
 int64_t sf_tri_attention_query_pitch(int64_t nq);
-/* Pair bias of the local rows: bias[(r*4 + h)*ldb + s] = sqrt(32) * LN(z[r,s]) . W_b[h] in bf16
- * (blocks.py:317-320; stored times the inverse softmax scale, the form the attention core adds
+/* Pair bias of the local rows: bias[(r*4 + h)*ldb + s] = log2(e) * LN(z[r,s]) . W_b[h] in bf16
+ * (blocks.py:317-320; stored in base-2 logit units, the form the attention core adds its scaled
  * Q K^T to). */
 int sf_tri_attention_bias(int dtype, const void* z, int64_t rows, int64_t n, const sf_tri_attention_weights* w,
                           void* bias, int64_t ldb, sf_stream_t stream);

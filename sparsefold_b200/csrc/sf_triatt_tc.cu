@@ -11,18 +11,17 @@
 //                       outputs and TMA-store them.
 //  k_triatt_core_tc     flash attention + gate + output projection + residual for
 //                       one (attention row b, 128-query block): four softmax
-//                       warpgroups, one per head.  S' = sqrt(D) bias + Q K^T
-//                       (the bias tile times an identity, then M128 N64 K32)
-//                       and O += P V (M128 N32 K64) run on
-//                       tcgen05 with TMEM accumulators; K/V^T blocks arrive by
-//                       TMA; the softmax runs in exp2 with the reference's
-//                       -FLT_MAX masking; the gated outputs of all four heads
-//                       feed one more tcgen05 GEMM with the output projection,
-//                       whose epilogue adds the residual.
+//                       warpgroups, one per head.  S = Q K^T and O += P V
+//                       (M128 N32 K32, Q and P from TMEM) run on tcgen05 with
+//                       TMEM accumulators; K/V^T blocks and bias tiles arrive
+//                       by TMA; the softmax adds the bias and runs in exp2 with
+//                       the reference's -FLT_MAX masking; the gated outputs of
+//                       all four heads feed one more tcgen05 GEMM with the
+//                       output projection, whose epilogue adds the residual.
 //
 // Intermediate layouts (qp = n rounded up to 128; padded query rows are zero):
 //   Q, K  [b][h][qp][32]    Vt [b][h][32][qp]    G = sigmoid(gate) [b][qp][128]
-//   bias  [q][h][qp] (bias[q][h][k] = sqrt(32) LN(z)[q,k] . W_b[h] in bf16, untransposed;
+//   bias  [q][h][qp] (bias[q][h][k] = log2(e) LN(z)[q,k] . W_b[h] in bf16, untransposed;
 //         rows q all-gathered from the row shards when the pair tensor is distributed)
 #include <cfloat>
 
@@ -35,9 +34,9 @@ using namespace pt;
 
 constexpr int H = 4, D = 32;
 constexpr float kLog2e = 1.4426950408889634f;
-// The pair bias is stored multiplied by sqrt(D), the inverse softmax scale, so that the
-// core can accumulate Q K^T onto it: S' = q.k + sqrt(D) b = sqrt(D) (q.k / sqrt(D) + b).
-constexpr float kBiasScale = 5.656854249492380f;
+// The pair bias is stored multiplied by log2(e): the core works in base 2 and forms
+// logit * log2(e) = (q.k) (log2(e) / sqrt(D)) + log2(e) b with one FMA per key.
+constexpr float kBiasScale = kLog2e;
 
 struct AttProjParams {
   const float* ln_w;      // act_norm scale [128]
@@ -305,7 +304,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
 // attention core
 // ---------------------------------------------------------------------------
 struct AttCoreParams {
-  const bf16 *g, *bias;
+  const bf16 *q, *g, *bias;
   const bf16* w_out;      // output_projection^T [128 out][128 in]
   const uint8_t* mask;    // [N] token mask (keys/queries are all N tokens)
   const bf16* z;          // the z block [rows][cols][128] (residual)
@@ -318,19 +317,19 @@ struct AttCoreParams {
   uint32_t* status;
 };
 
-constexpr int KB = 64;                 // keys per block
-constexpr int KV_STAGES = 3;
-constexpr int KV_BYTES = 8 * 1024;     // K block 64 x 64 B (64B swizzle) | V^T block 32 x 128 B (128B swizzle)
-constexpr int BT_BYTES = TILE * KB * 2;  // bias tile of one head: 128 queries x 64 keys (128B swizzle, K-major)
+constexpr int KB = 32;                 // keys per block
+constexpr int RING = 4;                // key blocks in flight: K, V^T and bias tile of each
+constexpr int K_BYTES = KB * D * 2;    // K block 32 keys x 64 B (64B swizzle)
+constexpr int V_BYTES = D * KB * 2;    // V^T block 32 dims x 64 B (64B swizzle)
+constexpr int BT_BYTES = TILE * KB * 2;  // bias tile of one head: 128 queries x 32 keys (64B swizzle)
+constexpr int SLOT_BYTES = K_BYTES + V_BYTES + BT_BYTES;
 constexpr int MAX_QP = 32768;
-constexpr int OFF_Q = 0;                                      // [h] Q tile 128 x 64 B; W_o columns of head h after the loop
-constexpr int OFF_KV = H * 8 * 1024;                          // [h][stage]
-constexpr int OFF_BT = OFF_KV + H * KV_STAGES * KV_BYTES;     // [h] bias tile of the next block; gated O_h after the loop
-constexpr int OFF_ID = OFF_BT + H * BT_BYTES;                 // 64 x 64 identity (128B swizzle, K-major)
-constexpr int OFF_KBITS = OFF_ID + KB * 128;                  // key-valid bits, qp/32 words
+constexpr int OFF_RING = 0;                                   // [h][RING] slots: K | V^T | bias (residual, W_o, gated O at the end)
+constexpr int OFF_KBITS = OFF_RING + H * RING * SLOT_BYTES;   // key-valid bits, qp/32 words
 constexpr int OFF_BAR = OFF_KBITS + MAX_QP / 8;
-constexpr int SMEM_CORE = OFF_BAR + 512 + 1024;
+constexpr int SMEM_CORE = OFF_BAR + 1024 + 1024;
 constexpr float kRescale = 8.0f;       // the running max moves only when a block exceeds it by 2^8
+constexpr int CORE_THREADS = (16 + 4) * 32;   // four softmax warpgroups + one issue warp per head
 
 __device__ __forceinline__ void wg_sync(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
 __device__ __forceinline__ float ex2(float x) {
@@ -340,28 +339,31 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 // One CTA = one (attention row b, 128-query tile); warpgroup h owns head h and
-// TMEM columns [128h, 128h+128): S' (64), O (32), P (32 columns of bf16 pairs).
-// Per key block j of 64 keys a warpgroup:
-//   waits for S'_j = sqrt(D) bias_j + Q K_j^T, formed entirely on the tensor core:
-//   the bias tile [128 queries][64 keys] arrives by TMA (keys beyond N read as 0)
-//   and is multiplied by a 64 x 64 identity into S', then Q K_j^T accumulates
-//   onto it.  The warpgroup reads S' once, sets masked and padding keys to -inf
-//   (only in blocks that have any), moves the running max when the block exceeds
-//   it by 2^8 (rescaling O in TMEM), and writes P = 2^(S' scale - m) as bf16 into
-//   TMEM.  Then one thread issues S'_{j+1} (the next thing the warpgroup waits
-//   for) while a thread of another warp issues O += P_j V_j (P from TMEM), whose
-//   completion is awaited only before P or O are touched again.  K and V^T
-//   blocks arrive by TMA three blocks deep, the bias tile one block ahead.  A row
-//   whose token is masked attends uniformly to all N keys (every logit of the
-//   reference is -FLT_MAX there).  Two blocks before the end the residual tile
-//   z[queries][32h .. 32h+31] arrives by TMA in a K/V stage that is no longer
-//   needed, and once the last S' is done the W_o columns of head h arrive by
-//   TMA over the Q tile.  After the last block the gated, normalised O_h is
-//   staged in shared memory, one more tcgen05 GEMM (K = 4 heads x 32) forms the
-//   output projection in columns [0,128), and each warpgroup adds its 32
-//   output channels to the residual tile in place and TMA-stores it.
-__global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant__ CUtensorMap tmQ,
-                                                           const __grid_constant__ CUtensorMap tmK,
+// TMEM columns [128h, 128h+128): two S buffers (32 fp32 columns each), O (32),
+// P (16 columns of bf16 pairs) and Q (16 columns of bf16 pairs).  Keys go in
+// blocks of 32.  The tensor core only runs TMEM-operand MMAs: S_j = Q K_j^T
+// (A = Q from TMEM) and O += P_j V_j (A = P from TMEM).  The pair bias, stored
+// as log2(e) * bias, arrives by TMA as a [128 queries][32 keys] tile and each
+// thread adds its query's row on the CUDA cores: logit2 = S scale + bias'.  Per
+// block j a warpgroup reads S_j and its bias row, sets masked and padding keys
+// to -inf and forms 2^(logit2 - m) against the running max m while it tracks
+// the block max in the same pass (so exponentials and CUDA-core work
+// interleave); when the block max exceeds m by more than 2^8 the block's values
+// are rescaled (or, past 2^64, recomputed) and O is rescaled in TMEM once
+// P_{j-1} V_{j-1} is done.  It writes P_j as bf16 and signals it.  A separate issue warp per head (warps 16-19) then issues
+// O += P_j V_j and S_{j+2} (into the S buffer just read) and refills the TMA
+// rings, so neither MMA issue (about 130 cycles per instruction for the issuing
+// warp) nor loads sit on the softmax warps, and the tensor core works two
+// blocks ahead of the softmax.  The K block, V^T block and bias tile of a key
+// block arrive by TMA on one barrier, four blocks deep; the issue warp folds
+// that barrier into the S barrier, so a softmax warp waits twice per block.  A row whose token
+// is masked attends uniformly to all N keys (every logit of the reference is
+// -FLT_MAX there).  Freed bias slots receive, near the end, the residual tile
+// z[queries][32h .. 32h+31] and the W_o columns of head h; the gated,
+// normalised O_h is staged in the last one, one more tcgen05 GEMM (K = 4 heads
+// x 32) forms the output projection in columns [0,128), and each warpgroup
+// adds its 32 output channels to the residual tile in place and TMA-stores it.
+__global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid_constant__ CUtensorMap tmK,
                                                            const __grid_constant__ CUtensorMap tmV,
                                                            const __grid_constant__ CUtensorMap tmB,
                                                            const __grid_constant__ CUtensorMap tmW,
@@ -369,29 +371,31 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
                                                            const __grid_constant__ CUtensorMap tmO, AttCoreParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* qbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [H] Q tile landed
-  uint64_t* sbar = qbar + H;                                       // [H] S'_j done
-  uint64_t* pvbar = sbar + H;                                      // [H] P_j V_j done (one phase per block)
-  uint64_t* bbar = pvbar + H;                                      // [H] bias tile landed (one phase per block)
-  uint64_t* kvbar = bbar + H;                                      // [H][KV_STAGES] K/V block landed
-  uint64_t* rbar = kvbar + H * KV_STAGES;                          // [H] residual tile landed
+  uint64_t* sbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [H][2] S buffer written and its block landed (2 arrivals)
+  uint64_t* pvbar = sbar + 2 * H;                                  // [H] P V done (one phase per block)
+  uint64_t* lbar = pvbar + H;                                      // [H][RING] K, V^T and bias of a block landed
+  uint64_t* rbar = lbar + RING * H;                                // [H] residual tile landed
   uint64_t* wbar = rbar + H;                                       // [H] W_o columns landed
-  uint64_t* outbar = wbar + H;
+  uint64_t* pready = wbar + H;                                     // [H] P_j written (4 softmax warps), per block
+  uint64_t* outbar = pready + H;
+  constexpr int NBAR = (6 + RING) * H + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(outbar + 1);
   uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = tid >> 7, t = tid & 127;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool issuer = warp >= 16;
+  const int g = issuer ? warp - 16 : tid >> 7, t = tid & 127;
   const int64_t q0 = (int64_t)blockIdx.x * TILE, b = blockIdx.y;
-  const int nkb = (int)(p.qp / KB);
+  const int nkb = (int)(p.qp / KB);   // >= 4
   const int64_t bh = b * H + g;
+  const int64_t q = q0 + t;
 
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 6 * H + H * KV_STAGES + 1; ++i) tc::mbar_init(&qbar[i], 1);
+    for (int i = 0; i < NBAR; ++i) tc::mbar_init(&sbar[i], i < 2 * H ? 2 : (i >= (5 + RING) * H && i < NBAR - 1) ? 4 : 1);
     tc::fence_mbar_init();
-    tc::prefetch_tmap(&tmQ);
     tc::prefetch_tmap(&tmK);
     tc::prefetch_tmap(&tmV);
     tc::prefetch_tmap(&tmB);
@@ -400,196 +404,239 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
     tc::prefetch_tmap(&tmO);
   }
   // key k is attended iff mask[row] && mask[k] (pair mask, blocks.py:314); bits hold mask[k] && k < N
-  for (int w = warp; w < (int)(p.qp / 32); w += 16) {
+  for (int w = warp; w < (int)(p.qp / 32); w += CORE_THREADS / 32) {
     const int64_t key = (int64_t)w * 32 + lane;
     const uint32_t bits = __ballot_sync(0xffffffffu, key < p.nq && p.mask[key] != 0);
     if (lane == 0) kbits[w] = bits;
   }
-  // 64 x 64 identity, K-major rows of 128 B: row k holds 1.0 in column k
-  for (int e = tid; e < KB * 8; e += 512) {
-    const int r = e >> 3, c = e & 7;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if ((r >> 3) == c) reinterpret_cast<uint16_t*>(&v)[r & 7] = 0x3F80u;
-    *reinterpret_cast<uint4*>(smem + OFF_ID + tc::sw128_off(r, c)) = v;
+  // this thread's query row of Q (64 B), for TMEM
+  uint4 qrow[4];
+  if (!issuer) {
+    const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (bh * p.qp + q) * D);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) qrow[c] = __ldg(qsrc + c);
   }
   const bool uniform = p.mask[b + p.batch_offset] == 0;
-  tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
-  const uint32_t s_col = (uint32_t)g * 128, o_col = s_col + 64, p_col = s_col + 96;
-  const uint32_t sb = tc::smem_u32(smem);
-  const uint32_t q_s = sb + OFF_Q + g * 8192, bt_s = sb + OFF_BT + g * BT_BYTES;
-  uint8_t* kv = smem + OFF_KV + g * KV_STAGES * KV_BYTES;
+  const uint32_t s_col = (uint32_t)g * 128, o_col = s_col + 64, p_col = s_col + 96, qt_col = s_col + 112;
+  uint8_t* ring = smem + OFF_RING + g * RING * SLOT_BYTES;   // slot s: K at +0, V^T at +K_BYTES, bias at +K_BYTES+V_BYTES
+  auto k_of = [&](int jj) { return ring + (jj % RING) * SLOT_BYTES; };
+  auto v_of = [&](int jj) { return ring + (jj % RING) * SLOT_BYTES + K_BYTES; };
+  auto bt_of = [&](int jj) { return ring + (jj % RING) * SLOT_BYTES + K_BYTES + V_BYTES; };
   bool aborted = false;
-  constexpr uint32_t IDESC_S = tc::idesc_bf16(128, KB), IDESC_O = tc::idesc_bf16(128, D);
-
-  auto issue_kv = [&](int jj) {
-    const int st = jj % KV_STAGES;
-    tc::mbar_expect_tx(&kvbar[g * KV_STAGES + st], KV_BYTES);
-    tc::tma_load_2d(kv + st * KV_BYTES, &tmK, &kvbar[g * KV_STAGES + st], 0, (int)(bh * p.qp + (int64_t)jj * KB));
-    tc::tma_load_2d(kv + st * KV_BYTES + 4096, &tmV, &kvbar[g * KV_STAGES + st], jj * KB, (int)(bh * D));
-  };
-  auto issue_bias = [&](int jj) {   // bias[q0..q0+127][g][64 jj .. 64 jj + 63]
-    tc::mbar_expect_tx(&bbar[g], BT_BYTES);
-    tc::tma_load_3d(smem + OFF_BT + g * BT_BYTES, &tmB, &bbar[g], jj * KB, g, (int)q0);
-  };
-  // residual tile z[b][q0..q0+127][32g..] (or z[q0..][b][32g..] for the ending node): 128 rows of 64 B
-  const int rc1 = p.transpose ? (int)b : (int)q0, rc2 = p.transpose ? (int)q0 : (int)b;
-  uint8_t* resid = kv + (nkb % KV_STAGES) * KV_BYTES;   // a stage no K/V block uses after block nkb-3
-  auto issue_s = [&](int jj) {   // S' = bias_jj . I + Q K_jj^T
-    const uint32_t ks = sb + OFF_KV + (g * KV_STAGES + jj % KV_STAGES) * KV_BYTES;
-    if (!uniform) {
+  constexpr uint32_t IDESC = tc::idesc_bf16(128, 32);   // S (N = 32 keys) and O (N = 32 dims)
+  if (!issuer) {
+    uint32_t qw[16];
 #pragma unroll
-      for (int kk = 0; kk < KB / 16; ++kk)
-        tc::mma_bf16(tbase + s_col, tc::smem_desc(bt_s + kk * 32, 1024, tc::kSW128),
-                     tc::smem_desc(sb + OFF_ID + kk * 32, 1024, tc::kSW128), IDESC_S, kk > 0);
+    for (int c = 0; c < 4; ++c) {
+      qw[4 * c] = qrow[c].x;
+      qw[4 * c + 1] = qrow[c].y;
+      qw[4 * c + 2] = qrow[c].z;
+      qw[4 * c + 3] = qrow[c].w;
     }
+    tc::tmem_st16(lane_addr + qt_col, qw);
+    tc::tmem_wait_st();
+  }
+
+  auto issue_load = [&](int jj) {   // K, V^T and bias[q0..q0+127][g][32 jj .. 32 jj + 31] of block jj
+    uint64_t* bar = &lbar[g * RING + jj % RING];
+    tc::mbar_expect_tx(bar, K_BYTES + V_BYTES + BT_BYTES);
+    tc::tma_load_2d(k_of(jj), &tmK, bar, 0, (int)(bh * p.qp + (int64_t)jj * KB));
+    tc::tma_load_2d(v_of(jj), &tmV, bar, jj * KB, (int)(bh * D));
+    tc::tma_load_3d(bt_of(jj), &tmB, bar, jj * KB, g, (int)q0);
+  };
+  auto issue_s = [&](int jj) {   // S_jj = Q K_jj^T into S buffer jj % 2, once block jj has landed
+    tc::mbar_wait(&lbar[g * RING + jj % RING], (jj / RING) & 1, p.status, aborted);
+    tc::mbar_arrive(&sbar[g * 2 + (jj & 1)]);   // the softmax reads the bias tile once S_jj is signalled
+    tc::tc_fence_after();
+    const uint32_t ks = tc::smem_u32(k_of(jj));
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk)
-      tc::mma_bf16(tbase + s_col, tc::smem_desc(q_s + kk * 32, 512, tc::kSW64), tc::smem_desc(ks + kk * 32, 512, tc::kSW64),
-                   IDESC_S, !uniform || kk > 0);
+      tc::mma_bf16_ts(tbase + s_col + (jj & 1) * KB, tbase + qt_col + kk * 8, tc::smem_desc(ks + kk * 32, 512, tc::kSW64),
+                      IDESC, kk > 0);
+    tc::mma_commit(&sbar[g * 2 + (jj & 1)]);
   };
 
-  // ---- prologue: Q, K/V blocks 0 and 1, bias tile 0, S'_0 ----
-  if (t == 0) {
-    tc::mbar_expect_tx(&qbar[g], 8192);
-    tc::tma_load_2d(smem + OFF_Q + g * 8192, &tmQ, &qbar[g], 0, (int)(bh * p.qp + q0));
-    issue_kv(0);
-    issue_kv(1);   // qp >= 128: at least two key blocks
-    issue_bias(0);
-    tc::mbar_wait(&qbar[g], 0, p.status, aborted);
-    tc::mbar_wait(&kvbar[g * KV_STAGES], 0, p.status, aborted);
-    tc::mbar_wait(&bbar[g], 0, p.status, aborted);
-    tc::tc_fence_after();
-    issue_s(0);
-    tc::mma_commit(&sbar[g]);
-  }
+  // residual tile z[b][q0..q0+127][32g..] (or z[q0..][b][32g..] for the ending node): 128 rows of 64 B
+  const int rc1 = p.transpose ? (int)b : (int)q0, rc2 = p.transpose ? (int)q0 : (int)b;
+  uint8_t* resid = bt_of(nkb);        // bias part of the slot of block nkb-4
+  uint8_t* wstage = bt_of(nkb + 1);   // ... of block nkb-3
+  uint8_t* ostage = bt_of(nkb + 3);   // ... of block nkb-1
 
-  const int64_t q = q0 + t;
+  // ---- prologue: K, V^T, bias of blocks 0-3; S_0, S_1 (issue warp of head g) ----
+  tc::tc_fence_before();
+  __syncthreads();   // Q is in TMEM
   float m_run = -INFINITY, l = 0.f;
-  for (int j = 0; j < nkb; ++j) {
-    tc::mbar_wait(&sbar[g], j & 1, p.status, aborted);
-    tc::tc_fence_after();
-    if (t == 0 && j + 1 < nkb) issue_bias(j + 1);   // S'_j has consumed the bias tile
-    if (t == 0 && j + 1 == nkb) {
-      // the last S' is done: the Q tile takes W_o[:, 32g .. 32g+31] (K-major 128 x 32, 64B swizzle)
-      tc::mbar_expect_tx(&wbar[g], 8192);
-      tc::tma_load_2d(smem + OFF_Q + g * 8192, &tmW, &wbar[g], g * D, 0);
-    }
-    float sv[KB];
-    float corr = 1.f, m_use = 0.f;
-    if (!uniform) {
-      tc::tmem_ld64(lane_addr + s_col, sv);
-      const uint64_t vb = (uint64_t)kbits[2 * j] | ((uint64_t)kbits[2 * j + 1] << 32);
-      if (vb != ~0ull) {   // masked or padding keys in this block: excluded
-#pragma unroll
-        for (int e = 0; e < KB; ++e)
-          if (!((vb >> e) & 1)) sv[e] = -INFINITY;
-      }
-      float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int e = 0; e < KB; e += 8) {
-        m4[0] = tc::fmax3(m4[0], sv[e], sv[e + 1]);
-        m4[1] = tc::fmax3(m4[1], sv[e + 2], sv[e + 3]);
-        m4[2] = tc::fmax3(m4[2], sv[e + 4], sv[e + 5]);
-        m4[3] = tc::fmax3(m4[3], sv[e + 6], sv[e + 7]);
-      }
-      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;
-      if (mx > m_run + kRescale) {   // m_run = -inf: any finite block max
-        corr = ex2(m_run - mx);
-        m_run = mx;
-      }
-      m_use = m_run == -INFINITY ? 0.f : m_run;
-    } else {
-#pragma unroll
-      for (int e = 0; e < KB; ++e) sv[e] = ((int64_t)j * KB + e < p.nq) ? 1.f : 0.f;
-    }
-    // P_{j-1} V_{j-1} must be done before O is rescaled or P is overwritten
-    if (j > 0) {
-      tc::mbar_wait(&pvbar[g], (j - 1) & 1, p.status, aborted);
+  if (issuer) {
+    if (lane == 0) {
       tc::tc_fence_after();
-    }
-    if (t == 0 && j + 2 < nkb) issue_kv(j + 2);   // its stage held block j-1, whose P V is done
-    if (t == 0 && j + 2 == nkb) {
-      // stage nkb % 3 held block nkb-3 (its P V is done) or was never used (nkb = 2)
-      tc::mbar_expect_tx(&rbar[g], TILE * D * 2);
-      tc::tma_load_3d(resid, &tmR, &rbar[g], g * D, rc1, rc2);
-    }
-    if (j > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-      // O (blocks < j, complete) *= corr
-      float ov[D];
-      uint32_t r[D];
-      tc::tmem_ld32(lane_addr + o_col, ov);
+      for (int jj = 0; jj < RING; ++jj) issue_load(jj);   // nkb >= 4
+      issue_s(0);
+      issue_s(1);
+      for (int j = 0; j < nkb; ++j) {
+        // P_j is in TMEM: S_j and bias_j have been read, P_{j-1} V_{j-1} awaited by the softmax
+        tc::mbar_wait(&pready[g], j & 1, p.status, aborted);
+        tc::tc_fence_after();
+        // O += P_j V_j (V^T of block j landed before S_j was signalled)
+        const uint32_t vs = tc::smem_u32(v_of(j));
 #pragma unroll
-      for (int e = 0; e < D; ++e) r[e] = __float_as_uint(ov[e] * corr);
-      tc::tmem_st32(lane_addr + o_col, r);
-    }
-    // ---- P = 2^(S' scale - m) as bf16 pairs into TMEM ----
-    {
-      const float nm = -m_use;
-      uint32_t pk[KB / 2];
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int e = 0; e < KB; e += 2) {
-        float p0 = sv[e], p1 = sv[e + 1];
-        if (!uniform) {
-          p0 = ex2(fmaf(p0, p.scale_log2, nm));
-          p1 = ex2(fmaf(p1, p.scale_log2, nm));
+        for (int kk = 0; kk < KB / 16; ++kk)
+          tc::mma_bf16_ts(tbase + o_col, tbase + p_col + kk * 8, tc::smem_desc(vs + kk * 32, 512, tc::kSW64), IDESC,
+                          j > 0 || kk > 0);
+        tc::mma_commit(&pvbar[g]);
+        // S_{j+2} into the S buffer just read
+        if (j + 2 < nkb) issue_s(j + 2);
+        // the slot of block j-1 is free (S, P V and the bias read are done): block j+3, or the epilogue tiles
+        if (j >= 1) {
+          if (j + RING - 1 < nkb) {
+            issue_load(j + RING - 1);
+          } else if (j + RING - 1 == nkb) {
+            tc::mbar_expect_tx(&rbar[g], TILE * D * 2);
+            tc::tma_load_3d(resid, &tmR, &rbar[g], g * D, rc1, rc2);
+          } else if (j + RING - 1 == nkb + 1) {
+            // W_o[:, 32g .. 32g+31] (K-major 128 x 32, 64B swizzle)
+            tc::mbar_expect_tx(&wbar[g], 8192);
+            tc::tma_load_2d(wstage, &tmW, &wbar[g], g * D, 0);
+          }
         }
-        ps[(e >> 1) & 3] += p0 + p1;
-        pk[e >> 1] = pack_bf2(p0, p1);
       }
-      tc::tmem_st32(lane_addr + p_col, pk);
-      l = l * corr + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
     }
-    tc::tmem_wait_st();
-    tc::tc_fence_before();
-    wg_sync(g);
-    if (t == 0 && j + 1 < nkb) {
-      // S'_{j+1} first: it is what this warpgroup waits for next
+  } else {
+    for (int j = 0; j < nkb; ++j) {
+      // S_j is written and block j (its bias tile) has landed
+      tc::mbar_wait(&sbar[g * 2 + (j & 1)], (j >> 1) & 1, p.status, aborted);
       tc::tc_fence_after();
-      tc::mbar_wait(&kvbar[g * KV_STAGES + (j + 1) % KV_STAGES], ((j + 1) / KV_STAGES) & 1, p.status, aborted);
-      tc::mbar_wait(&bbar[g], (j + 1) & 1, p.status, aborted);
-      issue_s(j + 1);
-      tc::mma_commit(&sbar[g]);
-    } else if (t == 32) {
-      // O += P_j V_j, issued from another warp in parallel with the S' MMAs
-      tc::tc_fence_after();
-      const uint32_t vs = sb + OFF_KV + (g * KV_STAGES + j % KV_STAGES) * KV_BYTES + 4096;
+      float sv[KB];
+      float corr = 1.f;
+      const uint8_t* brow = bt_of(j);
+      const uint32_t vb = kbits[j];
+      // logit2 of key e: S scale + bias' (bias' = log2(e) bias), -inf where the key is excluded
+      auto load_logits = [&]() {
+        tc::tmem_ld32(lane_addr + s_col + (j & 1) * KB, sv);
 #pragma unroll
-      for (int kk = 0; kk < KB / 16; ++kk)
-        tc::mma_bf16_ts(tbase + o_col, tbase + p_col + kk * 8, tc::smem_desc(vs + kk * 32, 1024, tc::kSW128), IDESC_O,
-                        j > 0 || kk > 0);
-      tc::mma_commit(&pvbar[g]);
+        for (int c = 0; c < KB / 8; ++c) {
+          const uint4 bb = *reinterpret_cast<const uint4*>(brow + tc::sw64_off(t, c));
+          const uint32_t bw[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const int e = 8 * c + 2 * e2;
+            sv[e] = fmaf(sv[e], p.scale_log2, bf_lo(bw[e2]));
+            sv[e + 1] = fmaf(sv[e + 1], p.scale_log2, bf_hi(bw[e2]));
+          }
+        }
+        if (vb != ~0u) {   // masked or padding keys in this block
+#pragma unroll
+          for (int e = 0; e < KB; ++e)
+            if (!((vb >> e) & 1)) sv[e] = -INFINITY;
+        }
+      };
+      if (!uniform) {
+        load_logits();
+        // tcgen05.ld is warp-collective: every branch that reloads S below is warp-uniform
+        float ma = -INFINITY, mb = -INFINITY;
+        if (j == 0) {
+          // first block: its max first
+#pragma unroll
+          for (int e = 0; e < KB; e += 4) {
+            ma = tc::fmax3(ma, sv[e], sv[e + 1]);
+            mb = tc::fmax3(mb, sv[e + 2], sv[e + 3]);
+          }
+          const float mx = fmaxf(ma, mb);
+          const float mu = mx == -INFINITY ? 0.f : mx;
+#pragma unroll
+          for (int e = 0; e < KB; ++e) sv[e] = ex2(sv[e] - mu);
+          m_run = mx;
+        } else {
+          // exponentials against the running max (+inf while no key has counted: all 0) while the
+          // block max is tracked
+          const float m_spec = m_run == -INFINITY ? INFINITY : m_run;
+#pragma unroll
+          for (int e = 0; e < KB; e += 4) {
+            ma = tc::fmax3(ma, sv[e], sv[e + 1]);
+            mb = tc::fmax3(mb, sv[e + 2], sv[e + 3]);
+            sv[e] = ex2(sv[e] - m_spec);
+            sv[e + 1] = ex2(sv[e + 1] - m_spec);
+            sv[e + 2] = ex2(sv[e + 2] - m_spec);
+            sv[e + 3] = ex2(sv[e + 3] - m_spec);
+          }
+          const float mx = fmaxf(ma, mb);
+          const bool moves = mx > m_run + kRescale;          // also the first finite block after -inf
+          const bool redo = moves && !(mx <= m_run + 64.f);  // values up to 2^(mx - m) could overflow
+          if (__any_sync(0xffffffffu, redo)) {
+            // recompute the whole warp's values from S and the bias tile
+            load_logits();
+            const float mr = moves ? mx : (m_run == -INFINITY ? 0.f : m_run);
+#pragma unroll
+            for (int e = 0; e < KB; ++e) sv[e] = ex2(sv[e] - mr);
+            if (moves) {
+              corr = ex2(m_run - mx);
+              m_run = mx;
+            }
+          } else if (moves) {
+            corr = ex2(m_run - mx);
+#pragma unroll
+            for (int e = 0; e < KB; ++e) sv[e] *= corr;
+            m_run = mx;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < KB; ++e) sv[e] = ((int64_t)j * KB + e < p.nq) ? 1.f : 0.f;
+      }
+      // ---- P as bf16 pairs; the row sum ----
+      uint32_t pk[KB / 2];
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int e = 0; e < KB; e += 4) {
+        ps0 += sv[e] + sv[e + 1];
+        ps1 += sv[e + 2] + sv[e + 3];
+        pk[e >> 1] = pack_bf2(sv[e], sv[e + 1]);
+        pk[(e >> 1) + 1] = pack_bf2(sv[e + 2], sv[e + 3]);
+      }
+      l = l * corr + (ps0 + ps1);
+      // P_{j-1} V_{j-1} is done before P is overwritten or O rescaled
+      if (j >= 1) tc::mbar_wait(&pvbar[g], (j - 1) & 1, p.status, aborted);
+      tc::tc_fence_after();
+      if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+        float ov[D];
+        tc::tmem_ld32(lane_addr + o_col, ov);
+        uint32_t r[D];
+#pragma unroll
+        for (int e = 0; e < D; ++e) r[e] = __float_as_uint(ov[e] * corr);
+        tc::tmem_st32(lane_addr + o_col, r);
+      }
+      tc::tmem_st16(lane_addr + p_col, pk);
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&pready[g]);
     }
   }
 
-  // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) over this head's bias tile ----
-  const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
-  uint4 graw[D / 8];
+  // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) in the last bias slot ----
+  if (!issuer) {
+    const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
+    uint4 graw[D / 8];
 #pragma unroll
-  for (int c = 0; c < D / 8; ++c) graw[c] = __ldg(grow + c);
-  tc::mbar_wait(&pvbar[g], (nkb - 1) & 1, p.status, aborted);   // the last P V (and every S' before it)
-  tc::tc_fence_after();
-  {
+    for (int c = 0; c < D / 8; ++c) graw[c] = __ldg(grow + c);
+    tc::mbar_wait(&pvbar[g], (nkb - 1) & 1, p.status, aborted);   // the last P V
+    tc::tc_fence_after();
     const float inv = l > 0.f ? 1.0f / l : 0.f;
     float ov[D];
     tc::tmem_ld32(lane_addr + o_col, ov);
-    uint8_t* ost = smem + OFF_BT + g * BT_BYTES;
 #pragma unroll
     for (int cc = 0; cc < D / 8; ++cc) {
-      const uint32_t* gu = reinterpret_cast<const uint32_t*>(&graw[cc]);
-      uint4 ok;
-      uint32_t* ou = reinterpret_cast<uint32_t*>(&ok);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int d = cc * 8 + 2 * e;
-        ou[e] = pack_bf2(ov[d] * inv * bf_lo(gu[e]), ov[d + 1] * inv * bf_hi(gu[e]));
-      }
-      *reinterpret_cast<uint4*>(ost + tc::sw64_off(t, cc)) = ok;
+      const uint4 gg = graw[cc];
+      const int d = cc * 8;
+      *reinterpret_cast<uint4*>(ostage + tc::sw64_off(t, cc)) =
+          make_uint4(pack_bf2(ov[d] * inv * bf_lo(gg.x), ov[d + 1] * inv * bf_hi(gg.x)),
+                     pack_bf2(ov[d + 2] * inv * bf_lo(gg.y), ov[d + 3] * inv * bf_hi(gg.y)),
+                     pack_bf2(ov[d + 4] * inv * bf_lo(gg.z), ov[d + 5] * inv * bf_hi(gg.z)),
+                     pack_bf2(ov[d + 6] * inv * bf_lo(gg.w), ov[d + 7] * inv * bf_hi(gg.w)));
     }
   }
   tc::fence_proxy_async();
@@ -598,18 +645,19 @@ __global__ void __launch_bounds__(512, 1) k_triatt_core_tc(const __grid_constant
   if (tid == 0) {
     for (int h = 0; h < H; ++h) tc::mbar_wait(&wbar[h], 0, p.status, aborted);
     tc::tc_fence_after();
-    constexpr uint32_t IDESC = tc::idesc_bf16(128, 128);
+    constexpr uint32_t IDESC_OUT = tc::idesc_bf16(128, 128);
+    const uint32_t os = tc::smem_u32(ostage), ws = tc::smem_u32(wstage);   // head 0's slots (g = 0)
 #pragma unroll
     for (int k = 0; k < 2 * H; ++k) {
       const int h = k >> 1, kk = k & 1;
-      tc::mma_bf16(tbase, tc::smem_desc(sb + OFF_BT + h * BT_BYTES + kk * 32, 512, tc::kSW64),
-                   tc::smem_desc(sb + OFF_Q + h * 8192 + kk * 32, 512, tc::kSW64), IDESC, k > 0);
+      tc::mma_bf16(tbase, tc::smem_desc(os + h * RING * SLOT_BYTES + kk * 32, 512, tc::kSW64),
+                   tc::smem_desc(ws + h * RING * SLOT_BYTES + kk * 32, 512, tc::kSW64), IDESC_OUT, k > 0);
     }
     tc::mma_commit(outbar);
   }
   tc::mbar_wait(outbar, 0, p.status, aborted);
   tc::tc_fence_after();
-  {
+  if (!issuer) {
     // query q, output channels 32g .. 32g+31: residual + projection in place, then one TMA store
     float ov[D];
     tc::tmem_ld32(lane_addr + g * D, ov);
@@ -772,12 +820,12 @@ int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, 
   if (!status) return SF_ERR_CUDA;
   static bool attr[64] = {false};
   SF_TRY(set_smem(k_triatt_core_tc, SMEM_CORE, attr));
-  // Q, K [nb*H*qp][32] (64B swizzle, 128- and 64-row boxes); V^T [nb*H*32][qp] (128B swizzle, 64 keys x 32)
-  CUtensorMap mq, mk, mv;
-  SF_TRY(make_2d_tmap(&mq, q, D, nb * H * qp, D, TILE, 64));
+  // K [nb*H*qp][32] (32-row boxes); V^T [nb*H*32][qp] (32 keys x 32); 64B swizzle
+  SF_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0, "triatt_core: q must be 16-byte aligned");
+  CUtensorMap mk, mv;
   SF_TRY(make_2d_tmap(&mk, k, D, nb * H * qp, D, KB, 64));
-  SF_TRY(make_2d_tmap(&mv, vt, qp, nb * H * D, KB, D, 128));
-  // bias [qp][H][qp]: tiles of 64 keys x 1 head x 128 queries; keys >= N read as zero
+  SF_TRY(make_2d_tmap(&mv, vt, qp, nb * H * D, KB, D, 64));
+  // bias [qp][H][qp]: tiles of 32 keys x 1 head x 128 queries (64B swizzle); keys >= N read as zero
   CUtensorMap mb;
   {
     auto encode = tensor_map_encoder();
@@ -791,7 +839,7 @@ int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, 
     cuuint32_t box[3] = {(cuuint32_t)KB, 1, (cuuint32_t)TILE};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = encode(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16*>(bias), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       set_error("cuTensorMapEncodeTiled failed (%d) for the attention bias", (int)r);
@@ -804,10 +852,10 @@ int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, 
   // residual in / out: 32 channels x 128 queries of the z block (64B swizzle)
   SF_TRY(make_resid_tmap(&mr, z, rows, cols, transpose != 0));
   SF_TRY(make_resid_tmap(&mo, z_out, rows, cols, transpose != 0));
-  AttCoreParams cp{g, bias, w_out, mask, z, z_out, cols, nq, qp, batch_offset, transpose,
+  AttCoreParams cp{q, g, bias, w_out, mask, z, z_out, cols, nq, qp, batch_offset, transpose,
                    (1.0f / sqrtf((float)D)) * kLog2e, status};
   dim3 cgrid((unsigned)(qp / TILE), (unsigned)nb);
-  k_triatt_core_tc<<<cgrid, 512, SMEM_CORE, stream>>>(mq, mk, mv, mb, mw, mr, mo, cp);
+  k_triatt_core_tc<<<cgrid, CORE_THREADS, SMEM_CORE, stream>>>(mk, mv, mb, mw, mr, mo, cp);
   count_launch();
   return check_launch("triatt_core_tc");
 }
