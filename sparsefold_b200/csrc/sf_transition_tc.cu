@@ -7,8 +7,10 @@
 //   warp 8      TMA producer: the x tiles of a pass, and per chunk the 64 rows of
 //               W1 (32 a + 32 b, 16 KB) and the 32 columns of W2 (8 KB), each in a
 //               4-stage ring
-//   warp 9      GEMM1 issuer: chunk c (M128 N64 K128 per tile) into one of two
-//               TMEM buffers as soon as the buffer and the weight chunk are free
+//   warps 9, 11 GEMM1 issuers, one per tile (an issuing warp gets one MMA per
+//               ~126 cycles, so a single issuer of both tiles bounds the kernel):
+//               chunk c (M128 N64 K128) into one of two TMEM buffers as soon as
+//               the tile's half of the buffer and the weight chunk are free
 //   warp 10     GEMM2 issuer: chunk c (M128 N128 K32 per tile) from the hidden
 //               tile, accumulating the down projection in TMEM columns [256,512)
 //   warps 0-7   thread = position (warps 0-3 tile 0, 4-7 tile 1): LayerNorm of
@@ -33,7 +35,7 @@ constexpr int OFF_W1 = OFF_H + 4 * H_BYTES;                  // [stage]
 constexpr int OFF_W2 = OFF_W1 + TR_STAGES * W1C_BYTES;       // [stage]
 constexpr int OFF_BAR = OFF_W2 + TR_STAGES * W2C_BYTES;
 constexpr int SMEM_TR = OFF_BAR + 512 + 1024;
-constexpr int TR_THREADS = 11 * 32;
+constexpr int TR_THREADS = 12 * 32;
 
 struct TrParams {
   const bf16* x;
@@ -52,16 +54,16 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* xfull = bars;                        // x tiles landed
   uint64_t* xready = bars + 1;                   // LN done (256)
-  uint64_t* xfree = bars + 2;                    // last GEMM1 of the pass done
+  uint64_t* xfree = bars + 2;                    // last GEMM1 of the pass done (both issuers)
   uint64_t* accfull = bars + 3;                  // last GEMM2 of the pass done
   uint64_t* accfree = bars + 4;                  // accumulators read (8 warps)
   uint64_t* w1full = bars + 5;                   // [TR_STAGES]
-  uint64_t* w1free = w1full + TR_STAGES;
+  uint64_t* w1free = w1full + TR_STAGES;         // both GEMM1 issuers done with the chunk
   uint64_t* w2full = w1free + TR_STAGES;
   uint64_t* w2free = w2full + TR_STAGES;
-  uint64_t* s1full = w2free + TR_STAGES;         // [2]
-  uint64_t* s1free = s1full + 2;                 // [2] (8 warps)
-  uint64_t* hfull = s1free + 2;                  // [2] (8 warps)
+  uint64_t* s1full = w2free + TR_STAGES;         // [2 buffers][2 tiles]
+  uint64_t* s1free = s1full + 4;                 // [2 buffers][2 tiles] (4 warps)
+  uint64_t* hfull = s1free + 4;                  // [2] (8 warps)
   uint64_t* hfree = hfull + 2;                   // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hfree + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -74,18 +76,20 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   if (tid == 0) {
     tc::mbar_init(xfull, 1);
     tc::mbar_init(xready, 256);
-    tc::mbar_init(xfree, 1);
+    tc::mbar_init(xfree, 2);
     tc::mbar_init(accfull, 1);
     tc::mbar_init(accfree, 8);
     for (int s = 0; s < TR_STAGES; ++s) {
       tc::mbar_init(&w1full[s], 1);
-      tc::mbar_init(&w1free[s], 1);
+      tc::mbar_init(&w1free[s], 2);
       tc::mbar_init(&w2full[s], 1);
       tc::mbar_init(&w2free[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < 4; ++s) {
       tc::mbar_init(&s1full[s], 1);
-      tc::mbar_init(&s1free[s], 8);
+      tc::mbar_init(&s1free[s], 4);
+    }
+    for (int s = 0; s < 2; ++s) {
       tc::mbar_init(&hfull[s], 8);
       tc::mbar_init(&hfree[s], 1);
     }
@@ -128,9 +132,10 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
         }
       }
     }
-  } else if (warp == 9) {
-    // ---- GEMM1 issuer ----
+  } else if (warp == 9 || warp == 11) {
+    // ---- GEMM1 issuer of tile t2 ----
     if (lane == 0) {
+      const int t2 = warp == 9 ? 0 : 1;
       constexpr uint32_t ID1 = tc::idesc_bf16(128, 2 * HC);
       uint32_t q = 0, pi = 0;
       for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
@@ -138,18 +143,17 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
           const int st = q % TR_STAGES, sbuf = q & 1;
           tc::mbar_wait(&w1full[st], (q / TR_STAGES) & 1, p.status, aborted);
-          if (q >= 2) tc::mbar_wait(&s1free[sbuf], ((q >> 1) + 1) & 1, p.status, aborted);
+          if (q >= 2) tc::mbar_wait(&s1free[sbuf * 2 + t2], ((q >> 1) + 1) & 1, p.status, aborted);
           tc::tc_fence_after();
           const uint32_t w1 = sb + OFF_W1 + st * W1C_BYTES;
-          for (int t2 = 0; t2 < 2; ++t2)
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int ka = k >> 2, kk = k & 3;
-              tc::mma_bf16(tbase + sbuf * 128 + t2 * 64,
-                           tc::smem_desc(sb + OFF_X + t2 * A_BYTES + ka * ATOM + kk * 32, 1024, tc::kSW128),
-                           tc::smem_desc(w1 + ka * 8192 + kk * 32, 1024, tc::kSW128), ID1, k > 0);
-            }
-          tc::mma_commit(&s1full[sbuf]);
+          for (int k = 0; k < 8; ++k) {
+            const int ka = k >> 2, kk = k & 3;
+            tc::mma_bf16(tbase + sbuf * 128 + t2 * 64,
+                         tc::smem_desc(sb + OFF_X + t2 * A_BYTES + ka * ATOM + kk * 32, 1024, tc::kSW128),
+                         tc::smem_desc(w1 + ka * 8192 + kk * 32, 1024, tc::kSW128), ID1, k > 0);
+          }
+          tc::mma_commit(&s1full[sbuf * 2 + t2]);
           tc::mma_commit(&w1free[st]);
           if (hc == NCHUNK - 1) tc::mma_commit(xfree);
         }
@@ -202,14 +206,14 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
 #pragma unroll
           for (int c = 0; c < 16; ++c) xpre[c] = xr[c];   // raw x row for the residual (the tile in smem is normalised)
         }
-        tc::mbar_wait(&s1full[sbuf], (q >> 1) & 1, p.status, aborted);
+        tc::mbar_wait(&s1full[sbuf * 2 + t2], (q >> 1) & 1, p.status, aborted);
         tc::tc_fence_after();
         float a[HC], bv[HC];
         tc::tmem_ld32(lane_addr + sbuf * 128 + t2 * 64, a);
         tc::tmem_ld32(lane_addr + sbuf * 128 + t2 * 64 + HC, bv);
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&s1free[sbuf]);
+        if (lane == 0) tc::mbar_arrive(&s1free[sbuf * 2 + t2]);
         uint32_t hv[HC / 2];
 #pragma unroll
         for (int e = 0; e < HC / 2; ++e)
