@@ -151,6 +151,19 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t sbo_bytes
   return d;
 }
 
+// Descriptor of an M/N-major operand (M or N contiguous): 128-byte rows of one
+// swizzle atom hold consecutive M/N elements, 8 K-rows per atom; lbo_bytes =
+// stride between atoms along M/N, sbo_bytes = stride between 8-row K groups.
+__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes, Swizzle sw) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;  // LBO
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;  // SBO
+  d |= (uint64_t)1 << 46;                             // version
+  d |= (uint64_t)sw << 61;
+  return d;
+}
+
 // bf16 x bf16 -> fp32, both operands K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
   return (1u << 4)                       // D = f32

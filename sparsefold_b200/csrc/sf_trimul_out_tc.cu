@@ -1,18 +1,22 @@
 // Output phase of triangle multiplication on tcgen05 (blocks.py:559-566), bf16 track:
 //   z_out = z + (centerLN(P) W_out) * sigmoid(LN(z) W_gate)
 //
-// Persistent, one warp-specialised CTA per SM, one 128-position tile (pair row
-// r, columns s0..s0+127) at a time, two tiles in flight:
-//   warp 12     TMA producer: raw z tile (128B swizzle, two stages) and P tile
-//               ([128 channels][128 positions] of one pair row, no swizzle)
-//   warps 8-11  thread = position: LN(z) into the A1 tile; center LayerNorm of the
-//               position's 128 channels of P (center_norm, dim=-3) into the K-major
-//               A2 tile
-//   warp 13     MMA issuer: gate = A1 W_gate^T and update = A2 W_out^T (M=N=K=128,
-//               weights resident) into one of two TMEM buffers of 256 columns
+// Both layer norms are folded into the GEMMs, so the tensor core reads the raw
+// tiles as they arrive: with LN(x)[c] = (x[c] - mu) rho w[c] + b[c],
+//   LN(x) . W[o] = rho (x . W'[o] - mu s[o]) + b'[o],
+//   W'[o][c] = W[o][c] w[c] (bf16),  s[o] = sum_c W'[o][c],  b'[o] = sum_c b[c] W[o][c],
+// and the epilogue applies rho, mu of each position.  Persistent, one
+// warp-specialised CTA per SM, one 128-position tile (pair row r, columns
+// s0..s0+127) at a time, two tiles in flight:
+//   warp 12     TMA producer: raw z tile (K-major, 128B swizzle) and P tile
+//               ([128 channels][128 positions] as two 64-position boxes, 128B
+//               swizzle: the M-major A operand of the update GEMM), two stages each
+//   warp 13     MMA issuer: gate = z W_gate'^T and update = P^T W_out'^T (M=N=K=128,
+//               folded weights resident) into one of two TMEM buffers of 256 columns
+//   warps 8-11  thread = position: mean and rstd of its z row and of its P column
 //   warps 0-7   epilogue: warp w takes positions 32(w%4).. and channels 64(w/4)..,
-//               adds update * sigmoid(gate) to the raw z still in shared memory, in
-//               place, and TMA-stores that 32 x 64 block of z_out.
+//               applies the folded norms, adds update * sigmoid(gate) to the raw z
+//               still in shared memory, in place, and TMA-stores that 32 x 64 block.
 #include "sf_pair_tc.cuh"
 
 namespace sf {
@@ -22,21 +26,53 @@ using namespace pt;
 
 constexpr int OUT_EPI_WARPS = 8;
 constexpr int OUT_THREADS = (OUT_EPI_WARPS + 4 + 2) * 32;
-constexpr int OFF_WG = 0, OFF_WO = A_BYTES;
+constexpr int OFF_WG = 0, OFF_WO = A_BYTES;     // folded weights (K-major, 128B swizzle)
 constexpr int OFF_Z = 2 * A_BYTES;              // [2] raw z tiles, then z_out staging
-constexpr int OFF_P = OFF_Z + 2 * A_BYTES;      // P tile [channel][position]
-constexpr int OFF_A1 = OFF_P + A_BYTES;         // LN(z)
-constexpr int OFF_A2 = OFF_A1 + A_BYTES;        // centerLN(P), K-major
-constexpr int OFF_BAR = OFF_A2 + A_BYTES;
-constexpr int OFF_CW = OFF_BAR + 256;           // center-norm scale and offset, 128 floats each
-constexpr int OFF_CB = OFF_CW + C * 4;
-constexpr int SMEM_OUT = OFF_CB + C * 4 + 1024;
+constexpr int OFF_P = OFF_Z + 2 * A_BYTES;      // [2] P tiles: two 64-position boxes of [128 ch][64 pos]
+constexpr int OFF_ST = OFF_P + 2 * A_BYTES;     // [2][4][128] floats: mean z, rstd z, mean P, rstd P
+constexpr int OFF_VEC = OFF_ST + 2 * 4 * C * 4; // [4][128] floats: s_gate, b_gate, s_out, b_out
+constexpr int OFF_BAR = OFF_VEC + 4 * C * 4;
+constexpr int SMEM_OUT = OFF_BAR + 256 + 1024;
 
 struct OutParams {
   const float *ln_w, *ln_b, *center_w, *center_b;
   int64_t rows, n;
   uint32_t* status;
 };
+
+// W'[o][c] = bf16(W[o][c] w[c]) in the 128B-swizzled K-major layout (atom column ka at dst + ka * 16 KB).
+__device__ __forceinline__ void load_folded_weight(uint8_t* dst, const bf16* __restrict__ wt, const float* __restrict__ w,
+                                                   int tid, int nthreads) {
+  for (int e = tid; e < C * 16; e += nthreads) {
+    const int r = e >> 4, kc = e & 15;
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(wt + (size_t)r * C + kc * 8));
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + kc * 8));
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + kc * 8 + 4));
+    const uint4 o = make_uint4(pack_bf2(bf_lo(v.x) * w0.x, bf_hi(v.x) * w0.y), pack_bf2(bf_lo(v.y) * w0.z, bf_hi(v.y) * w0.w),
+                               pack_bf2(bf_lo(v.z) * w1.x, bf_hi(v.z) * w1.y), pack_bf2(bf_lo(v.w) * w1.z, bf_hi(v.w) * w1.w));
+    *reinterpret_cast<uint4*>(dst + (kc >> 3) * ATOM + tc::sw128_off(r, kc & 7)) = o;
+  }
+}
+
+// s[o] = sum_c bf16(W[o][c] w[c]) (the values the MMA uses), b'[o] = sum_c b[c] W[o][c].
+__device__ __forceinline__ void fold_vectors(int o, const bf16* __restrict__ wt, const float* __restrict__ w,
+                                             const float* __restrict__ b, float* s_out, float* b_out) {
+  float s = 0.f, bb = 0.f;
+  for (int kc = 0; kc < 16; ++kc) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(wt + (size_t)o * C + kc * 8));
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = kc * 8 + 2 * e;
+      const float w0 = bf_lo(u[e]), w1 = bf_hi(u[e]);
+      s += __bfloat162float(__float2bfloat16_rn(w0 * __ldg(w + c))) +
+           __bfloat162float(__float2bfloat16_rn(w1 * __ldg(w + c + 1)));
+      bb = fmaf(__ldg(b + c), w0, fmaf(__ldg(b + c + 1), w1, bb));
+    }
+  }
+  s_out[o] = s;
+  b_out[o] = bb;
+}
 
 __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __grid_constant__ CUtensorMap tmZ,
                                                                      const __grid_constant__ CUtensorMap tmP,
@@ -47,15 +83,15 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
   uint8_t* smem = align1024(smem_raw);
   uint64_t* zfull = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // [2] z tile landed
   uint64_t* zfree = zfull + 2;                                      // [2] z_out stored (8 warps)
-  uint64_t* tfull = zfree + 2;                                      // [2] TMEM buffer written
+  uint64_t* pfull = zfree + 2;                                      // [2] P tile landed
+  uint64_t* pfree = pfull + 2;                                      // [2] P read by the MMA (commit) and the stats (128)
+  uint64_t* sfull = pfree + 2;                                      // [2] stats written (128)
+  uint64_t* tfull = sfull + 2;                                      // [2] TMEM buffer written
   uint64_t* tfree = tfull + 2;                                      // [2] TMEM buffer read (8 warps)
-  uint64_t* pfull = tfree + 2;                                      // P tile landed
-  uint64_t* pfree = pfull + 1;                                      // P tile read (128)
-  uint64_t* normed = pfree + 1;                                     // A1 and A2 written (128)
-  uint64_t* afree = normed + 1;                                     // MMAs done with A1 and A2
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(afree + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t nb = (p.n + TILE - 1) / TILE, ntiles = p.rows * nb;
+  float* vec = reinterpret_cast<float*>(smem + OFF_VEC);
 
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
@@ -65,24 +101,23 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(&zfull[s], 1);
       tc::mbar_init(&zfree[s], OUT_EPI_WARPS);
+      tc::mbar_init(&pfull[s], 1);
+      tc::mbar_init(&pfree[s], 1 + 128);
+      tc::mbar_init(&sfull[s], 128);
       tc::mbar_init(&tfull[s], 1);
       tc::mbar_init(&tfree[s], OUT_EPI_WARPS);
     }
-    tc::mbar_init(pfull, 1);
-    tc::mbar_init(pfree, 128);
-    tc::mbar_init(normed, 128);
-    tc::mbar_init(afree, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmZ);
     tc::prefetch_tmap(&tmP);
     tc::prefetch_tmap(&tmO);
   }
-  if (tid < C) {
-    reinterpret_cast<float*>(smem + OFF_CW)[tid] = p.center_w[tid];
-    reinterpret_cast<float*>(smem + OFF_CB)[tid] = p.center_b[tid];
-  }
-  load_weight_sw128(smem + OFF_WG, w_gate, C, tid, OUT_THREADS);
-  load_weight_sw128(smem + OFF_WO, w_out, C, tid, OUT_THREADS);
+  load_folded_weight(smem + OFF_WG, w_gate, p.ln_w, tid, OUT_THREADS);
+  load_folded_weight(smem + OFF_WO, w_out, p.center_w, tid, OUT_THREADS);
+  if (tid < C)
+    fold_vectors(tid, w_gate, p.ln_w, p.ln_b, vec, vec + C);
+  else if (tid < 2 * C)
+    fold_vectors(tid - C, w_out, p.center_w, p.center_b, vec + 2 * C, vec + 3 * C);
   tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();
@@ -92,91 +127,120 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
   bool aborted = false;
 
   if (warp == 12) {
+    // ---- TMA producer ----
     if (lane == 0) {
       uint32_t it = 0;
       for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int st = it & 1;
-        if (it >= 2) tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
         const int64_t r = tile / nb, s0 = (tile % nb) * TILE;
+        if (it >= 2) tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
         uint8_t* zs = smem + OFF_Z + st * A_BYTES;
         tc::mbar_expect_tx(&zfull[st], A_BYTES);
         tc::tma_load_3d(zs, &tmZ, &zfull[st], 0, (int)s0, (int)r);
         tc::tma_load_3d(zs + ATOM, &tmZ, &zfull[st], 64, (int)s0, (int)r);
-        if (it >= 1) tc::mbar_wait(pfree, (it - 1) & 1, p.status, aborted);
-        tc::mbar_expect_tx(pfull, A_BYTES);
-        tc::tma_load_3d(smem + OFF_P, &tmP, pfull, (int)s0, 0, (int)r);
+        if (it >= 2) tc::mbar_wait(&pfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
+        uint8_t* ps = smem + OFF_P + st * A_BYTES;
+        tc::mbar_expect_tx(&pfull[st], A_BYTES);
+        tc::tma_load_3d(ps, &tmP, &pfull[st], (int)s0, 0, (int)r);
+        tc::tma_load_3d(ps + ATOM, &tmP, &pfull[st], (int)s0 + 64, 0, (int)r);
       }
     }
   } else if (warp == 13) {
+    // ---- MMA issuer ----
     if (lane == 0) {
-      constexpr uint32_t IDESC = tc::idesc_bf16(128, 128);
+      constexpr uint32_t IDESC_G = tc::idesc_bf16(128, 128);
+      constexpr uint32_t IDESC_U = tc::idesc_bf16(128, 128) | (1u << 15);   // A (P) M-major
       uint32_t it = 0;
       for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
-        const int buf = it & 1;
-        tc::mbar_wait(normed, it & 1, p.status, aborted);
+        const int st = it & 1, buf = it & 1;
+        tc::mbar_wait(&zfull[st], (it >> 1) & 1, p.status, aborted);
+        tc::mbar_wait(&pfull[st], (it >> 1) & 1, p.status, aborted);
         if (it >= 2) tc::mbar_wait(&tfree[buf], ((it >> 1) + 1) & 1, p.status, aborted);
         tc::tc_fence_after();
+        const uint32_t zb = sb + OFF_Z + st * A_BYTES, pb = sb + OFF_P + st * A_BYTES;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int ka = k >> 2, kk = k & 3;
-          tc::mma_bf16(tbase + buf * 256, tc::smem_desc(sb + OFF_A1 + ka * ATOM + kk * 32, 1024, tc::kSW128),
-                       tc::smem_desc(sb + OFF_WG + ka * ATOM + kk * 32, 1024, tc::kSW128), IDESC, k > 0);
-          tc::mma_bf16(tbase + buf * 256 + 128, tc::smem_desc(sb + OFF_A2 + ka * ATOM + kk * 32, 1024, tc::kSW128),
-                       tc::smem_desc(sb + OFF_WO + ka * ATOM + kk * 32, 1024, tc::kSW128), IDESC, k > 0);
+          tc::mma_bf16(tbase + buf * 256, tc::smem_desc(zb + ka * ATOM + kk * 32, 1024, tc::kSW128),
+                       tc::smem_desc(sb + OFF_WG + ka * ATOM + kk * 32, 1024, tc::kSW128), IDESC_G, k > 0);
+          // P: channels 16k .. 16k+15 are rows 16k.. of both 64-position boxes (atoms 16 KB apart)
+          tc::mma_bf16(tbase + buf * 256 + 128, tc::smem_desc_mn(pb + k * 2048, ATOM, 1024, tc::kSW128),
+                       tc::smem_desc(sb + OFF_WO + ka * ATOM + kk * 32, 1024, tc::kSW128), IDESC_U, k > 0);
         }
         tc::mma_commit(&tfull[buf]);
-        tc::mma_commit(afree);
+        tc::mma_commit(&pfree[st]);
       }
     }
   } else if (warp >= OUT_EPI_WARPS) {
-    // ---- layer norms, thread = position ----
+    // ---- per-position statistics ----
     const int pos = tid - OUT_EPI_WARPS * 32;
-    const float* cw = reinterpret_cast<const float*>(smem + OFF_CW);
-    const float* cb = reinterpret_cast<const float*>(smem + OFF_CB);
     uint32_t it = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       const int st = it & 1;
+      float* stats = reinterpret_cast<float*>(smem + OFF_ST) + st * 4 * C;
       tc::mbar_wait(&zfull[st], (it >> 1) & 1, p.status, aborted);
-      if (it >= 1) tc::mbar_wait(afree, (it - 1) & 1, p.status, aborted);
-      ln_row_lr(smem + OFF_Z + st * A_BYTES, smem + OFF_A1, pos, p.ln_w, p.ln_b, 1e-5f);
-      // center LayerNorm of this position across the 128 channels of P (column `pos`)
-      tc::mbar_wait(pfull, it & 1, p.status, aborted);
-      const bf16* pc = reinterpret_cast<const bf16*>(smem + OFF_P) + pos;
-      float s = 0.f;
-#pragma unroll 16
-      for (int c = 0; c < C; ++c) s += __bfloat162float(pc[c * TILE]);
-      const float mean = s * (1.0f / C);
-      float q = 0.f;
-#pragma unroll 16
-      for (int c = 0; c < C; ++c) {
-        const float d = __bfloat162float(pc[c * TILE]) - mean;
-        q += d * d;
-      }
-      const float rstd = rsqrtf(q * (1.0f / C) + 1e-5f);
-#pragma unroll 2
-      for (int kc = 0; kc < 16; ++kc) {
-        uint32_t o[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = 8 * kc + 2 * e;
-          o[e] = pack_bf2((__bfloat162float(pc[c * TILE]) - mean) * rstd * cw[c] + cb[c],
-                          (__bfloat162float(pc[(c + 1) * TILE]) - mean) * rstd * cw[c + 1] + cb[c + 1]);
+      {
+        // z row: mean, then the centred sum of squares (two passes over shared memory)
+        const uint8_t* zs = smem + OFF_Z + st * A_BYTES;
+        float s = 0.f;
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {
+          const uint4 v = *reinterpret_cast<const uint4*>(zs + (i >> 3) * ATOM + tc::sw128_off(pos, i & 7));
+          s += ((bf_lo(v.x) + bf_hi(v.x)) + (bf_lo(v.y) + bf_hi(v.y))) + ((bf_lo(v.z) + bf_hi(v.z)) + (bf_lo(v.w) + bf_hi(v.w)));
         }
-        *reinterpret_cast<uint4*>(smem + OFF_A2 + (kc >> 3) * ATOM + tc::sw128_off(pos, kc & 7)) =
-            make_uint4(o[0], o[1], o[2], o[3]);
+        const float mean = s * (1.0f / C);
+        float q = 0.f;
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {
+          const uint4 v = *reinterpret_cast<const uint4*>(zs + (i >> 3) * ATOM + tc::sw128_off(pos, i & 7));
+          const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float d0 = bf_lo(u[e]) - mean, d1 = bf_hi(u[e]) - mean;
+            q = fmaf(d0, d0, fmaf(d1, d1, q));
+          }
+        }
+        stats[pos] = mean;
+        stats[C + pos] = rsqrtf(q * (1.0f / C) + 1e-5f);
       }
-      tc::mbar_arrive(pfree);
-      tc::fence_proxy_async();
-      tc::mbar_arrive(normed);
+      tc::mbar_wait(&pfull[st], (it >> 1) & 1, p.status, aborted);
+      {
+        // P column: one pass of sums shifted by the first channel's value (avoids cancellation)
+        const uint8_t* pcol = smem + OFF_P + st * A_BYTES + (pos >> 6) * ATOM + (pos & 7) * 2;
+        const int chunk = (pos & 63) >> 3;
+        auto pval = [&](int c) {
+          return __bfloat162float(*reinterpret_cast<const bf16*>(pcol + c * 128 + ((chunk ^ (c & 7)) << 4)));
+        };
+        const float x0 = pval(0);
+        float s = 0.f, q = 0.f;
+#pragma unroll 16
+        for (int c = 0; c < C; ++c) {
+          const float d = pval(c) - x0;
+          s += d;
+          q = fmaf(d, d, q);
+        }
+        const float md = s * (1.0f / C);
+        stats[2 * C + pos] = x0 + md;
+        stats[3 * C + pos] = rsqrtf(fmaxf(q * (1.0f / C) - md * md, 0.f) + 1e-5f);
+      }
+      tc::mbar_arrive(&pfree[st]);
+      tc::mbar_arrive(&sfull[st]);
     }
   } else {
     // ---- epilogue: positions 32*quad.., channels 64*hf.. ----
     const int quad = warp & 3, hf = warp >> 2, pos = 32 * quad + lane;
     const uint32_t lane_addr = tbase + ((uint32_t)(32 * quad) << 16);
+    const float* sg = vec + 64 * hf;
+    const float* bg = vec + C + 64 * hf;
+    const float* so = vec + 2 * C + 64 * hf;
+    const float* bo = vec + 3 * C + 64 * hf;
     uint32_t it = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       const int st = it & 1, buf = it & 1;
       const int64_t r = tile / nb, s0 = (tile % nb) * TILE;
+      const float* stats = reinterpret_cast<const float*>(smem + OFF_ST) + st * 4 * C;
+      tc::mbar_wait(&sfull[st], (it >> 1) & 1, p.status, aborted);
+      const float mz = stats[pos], rz = stats[C + pos], mp = stats[2 * C + pos], rp = stats[3 * C + pos];
       tc::mbar_wait(&tfull[buf], (it >> 1) & 1, p.status, aborted);
       tc::tc_fence_after();
       uint8_t* zrow = smem + OFF_Z + st * A_BYTES + hf * ATOM;
@@ -188,14 +252,19 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
           uint4* zp = reinterpret_cast<uint4*>(zrow + tc::sw128_off(pos, 2 * k + h2));
-          uint4 zz = *zp;
-          uint32_t* zu = reinterpret_cast<uint32_t*>(&zz);
+          const uint4 zz = *zp;
+          const uint32_t zu[4] = {zz.x, zz.y, zz.z, zz.w};
+          uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int j = 8 * h2 + 2 * e;
-            zu[e] = pack_bf2(bf_lo(zu[e]) + u[j] * sigmoid_tanh(g[j]), bf_hi(zu[e]) + u[j + 1] * sigmoid_tanh(g[j + 1]));
+            const int j = 8 * h2 + 2 * e, c = 16 * k + j;
+            const float g0 = fmaf(rz, fmaf(-mz, sg[c], g[j]), bg[c]);
+            const float g1 = fmaf(rz, fmaf(-mz, sg[c + 1], g[j + 1]), bg[c + 1]);
+            const float u0 = fmaf(rp, fmaf(-mp, so[c], u[j]), bo[c]);
+            const float u1 = fmaf(rp, fmaf(-mp, so[c + 1], u[j + 1]), bo[c + 1]);
+            o[e] = pack_bf2(fmaf(u0, sigmoid_tanh(g0), bf_lo(zu[e])), fmaf(u1, sigmoid_tanh(g1), bf_hi(zu[e])));
           }
-          *zp = zz;
+          *zp = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
       tc::tc_fence_before();
@@ -229,8 +298,9 @@ int trimul_output_tc(const bf16* z, const bf16* P, int64_t rows, int64_t n, cons
                      cudaStream_t stream) {
   if (rows == 0 || n == 0) return SF_OK;
   SF_REQUIRE(n <= (1 << 24) && rows <= (1 << 24), "trimul_output_tc: size too large");
-  SF_REQUIRE((reinterpret_cast<uintptr_t>(ln_w) & 15) == 0 && (reinterpret_cast<uintptr_t>(ln_b) & 15) == 0,
-             "trimul_output_tc: layer-norm parameters must be 16-byte aligned");
+  SF_REQUIRE(((reinterpret_cast<uintptr_t>(ln_w) | reinterpret_cast<uintptr_t>(center_w) |
+               reinterpret_cast<uintptr_t>(w_gate) | reinterpret_cast<uintptr_t>(w_out)) & 15) == 0,
+             "trimul_output_tc: layer-norm scales and weights must be 16-byte aligned");
   CUtensorMap mz, mp, mo;
   SF_TRY(make_pair_tmap(&mz, z, rows, n, false));
   {
@@ -241,13 +311,13 @@ int trimul_output_tc(const bf16* z, const bf16* P, int64_t rows, int64_t n, cons
       return SF_ERR_ARG;
     }
     const int64_t pitch = pair_pitch(n);
-    // P is [rows][C][pitch]: box = 128 positions x all 128 channels of one pair row
+    // P is [rows][C][pitch]: box = 64 positions x all 128 channels of one pair row (128B swizzle)
     cuuint64_t dims[3] = {(cuuint64_t)pitch, (cuuint64_t)C, (cuuint64_t)rows};
     cuuint64_t strides[2] = {(cuuint64_t)pitch * 2, (cuuint64_t)(C * pitch * 2)};
-    cuuint32_t box[3] = {(cuuint32_t)TILE, (cuuint32_t)C, 1};
+    cuuint32_t box[3] = {64, (cuuint32_t)C, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = encode(&mp, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16*>(P), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       set_error("cuTensorMapEncodeTiled failed (%d) for P", (int)r);
