@@ -3,6 +3,8 @@
 // K-major layout, resident weight loading, bf16 pack/unpack.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "sf_tc.cuh"
 
 namespace sf {
@@ -136,6 +138,55 @@ __device__ __forceinline__ void ln_row_inplace_lr(uint8_t* tile, int r, const fl
   ln_row_lr(tile, tile, r, w, b, eps);
 }
 
+// The same layer norm with two threads per row: the thread with half h takes the
+// 64 channels of atom column h and adds its partner's sums (lane ^ 1, same warp)
+// by shuffle.  The halves walk their eight chunks four apart so the two threads
+// of a row never hit the same shared-memory banks.
+__device__ __forceinline__ void ln_half_row_inplace(uint8_t* tile, int r, int h, const float* __restrict__ w,
+                                                    const float* __restrict__ b, float eps) {
+  uint8_t* base = tile + h * ATOM;
+  auto off = [&](int i) -> uint32_t { return tc::sw128_off(r, (i + 4 * h) & 7); };
+  float s = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < 8; ++i) {
+    const uint4 v = *reinterpret_cast<const uint4*>(base + off(i));
+    s += ((bf_lo(v.x) + bf_hi(v.x)) + (bf_lo(v.y) + bf_hi(v.y))) + ((bf_lo(v.z) + bf_hi(v.z)) + (bf_lo(v.w) + bf_hi(v.w)));
+  }
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  const float mean = s * (1.0f / C);
+  float q = 0.f;
+#pragma unroll 4
+  for (int i = 0; i < 8; ++i) {
+    const uint4 v = *reinterpret_cast<const uint4*>(base + off(i));
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d0 = bf_lo(u[j]) - mean, d1 = bf_hi(u[j]) - mean;
+      q = fmaf(d0, d0, fmaf(d1, d1, q));
+    }
+  }
+  q += __shfl_xor_sync(0xffffffffu, q, 1);
+  const float rstd = rsqrtf(q * (1.0f / C) + eps);
+#pragma unroll 2
+  for (int i = 0; i < 8; ++i) {
+    const int c8 = 64 * h + 8 * ((i + 4 * h) & 7);   // first channel of this chunk
+    uint4 v = *reinterpret_cast<const uint4*>(base + off(i));
+    uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + c8));
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + c8 + 4));
+    float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+    if (b) {
+      b0 = __ldg(reinterpret_cast<const float4*>(b + c8));
+      b1 = __ldg(reinterpret_cast<const float4*>(b + c8 + 4));
+    }
+    u[0] = pack_bf2((bf_lo(u[0]) - mean) * rstd * w0.x + b0.x, (bf_hi(u[0]) - mean) * rstd * w0.y + b0.y);
+    u[1] = pack_bf2((bf_lo(u[1]) - mean) * rstd * w0.z + b0.z, (bf_hi(u[1]) - mean) * rstd * w0.w + b0.w);
+    u[2] = pack_bf2((bf_lo(u[2]) - mean) * rstd * w1.x + b1.x, (bf_hi(u[2]) - mean) * rstd * w1.y + b1.y);
+    u[3] = pack_bf2((bf_lo(u[3]) - mean) * rstd * w1.z + b1.z, (bf_hi(u[3]) - mean) * rstd * w1.w + b1.w);
+    *reinterpret_cast<uint4*>(base + off(i)) = v;
+  }
+}
+
 // Copies a weight matrix Wt[rows][128] (bf16, k contiguous) into shared memory
 // in the 128B-swizzled K-major layout: atom column ka (channels 64ka..) at
 // dst + ka * rows * 128.
@@ -146,6 +197,65 @@ __device__ __forceinline__ void load_weight_sw128(uint8_t* dst, const bf16* __re
     const int ka = kc >> 3, c = kc & 7;
     uint4 val = __ldg(reinterpret_cast<const uint4*>(wt + (size_t)r * C + kc * 8));
     *reinterpret_cast<uint4*>(dst + (size_t)ka * rows * 128 + tc::sw128_off(r, c)) = val;
+  }
+}
+
+// Layer norm folded into the GEMM that follows it: with
+//   LN(x)[c] = (x[c] - mu) rho w[c] + b[c],
+//   LN(x) . W[o] = rho (x . W'[o] - mu s[o]) + b'[o],
+//   W'[o][c] = bf16(W[o][c] w[c]),  s[o] = sum_c W'[o][c],  b'[o] = sum_c b[c] W[o][c],
+// so the tensor core reads the raw x tile and the epilogue applies rho and mu.
+// fold_weight writes W' (128B-swizzled K-major, atom column ka at dst + ka * rows
+// * 128) and s, b' for rows [0, rows).  w_s and b_s are the layer-norm scale and
+// bias staged in shared memory (b_s all zero for a scale-only norm).  Called by
+// every thread of the block (nthreads a multiple of 32): a 16-lane group owns a
+// row per pass and reduces s and b' with shuffles.
+__device__ __forceinline__ void fold_weight(uint8_t* dst, const bf16* __restrict__ wt, const float* w_s,
+                                            const float* b_s, int rows, float* s, float* bp, int tid, int nthreads) {
+  const int total = rows * 16;
+  for (int e0 = 0; e0 < total; e0 += nthreads) {
+    const int e = e0 + tid;
+    const bool valid = e < total;
+    const int r = e >> 4, kc = e & 15;
+    float ps = 0.f, pb = 0.f;
+    if (valid) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(wt + (size_t)r * C + kc * 8));
+      const float4 w0 = *reinterpret_cast<const float4*>(w_s + kc * 8);
+      const float4 w1 = *reinterpret_cast<const float4*>(w_s + kc * 8 + 4);
+      const float4 b0 = *reinterpret_cast<const float4*>(b_s + kc * 8);
+      const float4 b1 = *reinterpret_cast<const float4*>(b_s + kc * 8 + 4);
+      const float wl[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const float bl[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x0 = bf_lo(u[i]), x1 = bf_hi(u[i]);
+        o[i] = pack_bf2(x0 * wl[2 * i], x1 * wl[2 * i + 1]);
+        ps += bf_lo(o[i]) + bf_hi(o[i]);
+        pb = fmaf(bl[2 * i], x0, fmaf(bl[2 * i + 1], x1, pb));
+      }
+      *reinterpret_cast<uint4*>(dst + (size_t)(kc >> 3) * rows * 128 + tc::sw128_off(r, kc & 7)) =
+          make_uint4(o[0], o[1], o[2], o[3]);
+    }
+#pragma unroll
+    for (int m = 8; m >= 1; m >>= 1) {
+      ps += __shfl_xor_sync(0xffffffffu, ps, m);
+      pb += __shfl_xor_sync(0xffffffffu, pb, m);
+    }
+    if (valid && kc == 0) {
+      s[r] = ps;
+      bp[r] = pb;
+    }
+  }
+}
+
+// Stages a layer norm's scale and bias (128 floats each; bias may be null) in shared memory.
+__device__ __forceinline__ void stage_norm_params(float* w_s, float* b_s, const float* __restrict__ w,
+                                                  const float* __restrict__ b, int tid) {
+  if (tid < C) {
+    w_s[tid] = __ldg(w + tid);
+    b_s[tid] = b ? __ldg(b + tid) : 0.f;
   }
 }
 

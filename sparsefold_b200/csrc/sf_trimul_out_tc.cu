@@ -40,40 +40,6 @@ struct OutParams {
   uint32_t* status;
 };
 
-// W'[o][c] = bf16(W[o][c] w[c]) in the 128B-swizzled K-major layout (atom column ka at dst + ka * 16 KB).
-__device__ __forceinline__ void load_folded_weight(uint8_t* dst, const bf16* __restrict__ wt, const float* __restrict__ w,
-                                                   int tid, int nthreads) {
-  for (int e = tid; e < C * 16; e += nthreads) {
-    const int r = e >> 4, kc = e & 15;
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(wt + (size_t)r * C + kc * 8));
-    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + kc * 8));
-    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + kc * 8 + 4));
-    const uint4 o = make_uint4(pack_bf2(bf_lo(v.x) * w0.x, bf_hi(v.x) * w0.y), pack_bf2(bf_lo(v.y) * w0.z, bf_hi(v.y) * w0.w),
-                               pack_bf2(bf_lo(v.z) * w1.x, bf_hi(v.z) * w1.y), pack_bf2(bf_lo(v.w) * w1.z, bf_hi(v.w) * w1.w));
-    *reinterpret_cast<uint4*>(dst + (kc >> 3) * ATOM + tc::sw128_off(r, kc & 7)) = o;
-  }
-}
-
-// s[o] = sum_c bf16(W[o][c] w[c]) (the values the MMA uses), b'[o] = sum_c b[c] W[o][c].
-__device__ __forceinline__ void fold_vectors(int o, const bf16* __restrict__ wt, const float* __restrict__ w,
-                                             const float* __restrict__ b, float* s_out, float* b_out) {
-  float s = 0.f, bb = 0.f;
-  for (int kc = 0; kc < 16; ++kc) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(wt + (size_t)o * C + kc * 8));
-    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int c = kc * 8 + 2 * e;
-      const float w0 = bf_lo(u[e]), w1 = bf_hi(u[e]);
-      s += __bfloat162float(__float2bfloat16_rn(w0 * __ldg(w + c))) +
-           __bfloat162float(__float2bfloat16_rn(w1 * __ldg(w + c + 1)));
-      bb = fmaf(__ldg(b + c), w0, fmaf(__ldg(b + c + 1), w1, bb));
-    }
-  }
-  s_out[o] = s;
-  b_out[o] = bb;
-}
-
 __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __grid_constant__ CUtensorMap tmZ,
                                                                      const __grid_constant__ CUtensorMap tmP,
                                                                      const __grid_constant__ CUtensorMap tmO,
@@ -112,12 +78,15 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
     tc::prefetch_tmap(&tmP);
     tc::prefetch_tmap(&tmO);
   }
-  load_folded_weight(smem + OFF_WG, w_gate, p.ln_w, tid, OUT_THREADS);
-  load_folded_weight(smem + OFF_WO, w_out, p.center_w, tid, OUT_THREADS);
-  if (tid < C)
-    fold_vectors(tid, w_gate, p.ln_w, p.ln_b, vec, vec + C);
-  else if (tid < 2 * C)
-    fold_vectors(tid - C, w_out, p.center_w, p.center_b, vec + 2 * C, vec + 3 * C);
+  {
+    // both norms folded into their weights; their parameters go through the (still unused) stats area
+    float* prm = reinterpret_cast<float*>(smem + OFF_ST);
+    stage_norm_params(prm, prm + C, p.ln_w, p.ln_b, tid);
+    stage_norm_params(prm + 2 * C, prm + 3 * C, p.center_w, p.center_b, tid);
+    __syncthreads();
+    fold_weight(smem + OFF_WG, w_gate, prm, prm + C, C, vec, vec + C, tid, OUT_THREADS);
+    fold_weight(smem + OFF_WO, w_out, prm + 2 * C, prm + 3 * C, C, vec + 2 * C, vec + 3 * C, tid, OUT_THREADS);
+  }
   tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();

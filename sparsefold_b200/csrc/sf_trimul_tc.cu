@@ -2,8 +2,8 @@
 //
 // k_trimul_project_tc: persistent, one warp-specialised CTA per SM.  Per
 // 128-position tile: TMA brings the raw z tile into shared memory (128B
-// swizzle, the UMMA K-major layout, two stages), four warps layer-norm its
-// rows in place, one thread issues the GLU GEMMs transposed,
+// swizzle, the UMMA K-major layout, two stages), eight warps layer-norm its
+// rows in place (two threads per row), one thread issues the GLU GEMMs transposed,
 // D[out channel][position] = W . LN(z)^T (M=128, N=128, K=128, four weight
 // matrices kept resident), into two TMEM halves so the epilogue of one operand
 // overlaps the GEMM of the other, and eight epilogue warps apply
@@ -25,18 +25,19 @@ struct ProjParams {
   uint32_t* status;
 };
 
-// Warp roles (448 threads):
+// Warp roles (576 threads):
 //   warps 0-7   epilogue: warp w reads TMEM lanes 32(w%4).. (output channels) and
 //               positions 64(w/4)..+63 of the tile; stages sigmoid(gate) * value *
 //               mask as [32 channels][64 positions] (128B swizzle) and TMA-stores it
-//   warps 8-11  layer norm of the tile rows in place (thread = position)
-//   warp 12     TMA producer of z tiles (two stages)
-//   warp 13     MMA issuer: D[out channel][position] = W_x . LN(z)^T for the four
+//   warps 8-15  layer norm of the tile rows in place (two threads per position)
+//   warp 16     TMA producer of z tiles (two stages)
+//   warp 17     MMA issuer: D[out channel][position] = W_x . LN(z)^T for the four
 //               GLU matrices, two at a time (TMEM halves a = cols 0-255, b = 256-511)
 constexpr int NOUT = 512;
 constexpr int W_BYTES = NOUT * C * 2;                       // 128 KB, rows = gate_a, val_a, gate_b, val_b
 constexpr int EPI_WARPS = 8;
-constexpr int PROJ_THREADS = (EPI_WARPS + 4 + 2) * 32;
+constexpr int LN_WARPS = 8;
+constexpr int PROJ_THREADS = (EPI_WARPS + LN_WARPS + 2) * 32;
 constexpr int ST_BYTES = 32 * 128;                          // one epilogue warp's staging: 32 channels x 64 positions
 constexpr int OFF_PW = 0;
 constexpr int OFF_PZ = W_BYTES;                             // two z stages
@@ -69,7 +70,7 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
       tc::mbar_init(&full[s], 1);
-      tc::mbar_init(&normed[s], 128);
+      tc::mbar_init(&normed[s], LN_WARPS * 32);
       tc::mbar_init(&zfree[s], 1);
       tc::mbar_init(&tfull[s], 1);
       tc::mbar_init(&tfree[s], EPI_WARPS);
@@ -88,7 +89,7 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
 
-  if (warp == 12) {
+  if (warp == EPI_WARPS + LN_WARPS) {
     // ---- TMA producer ----
     if (lane == 0) {
       uint32_t it = 0;
@@ -104,7 +105,7 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
         tc::tma_load_3d(dst + ATOM, &tmZ, &full[st], 64, c1, c2);
       }
     }
-  } else if (warp == 13) {
+  } else if (warp == EPI_WARPS + LN_WARPS + 1) {
     // ---- MMA issuer ----
     if (lane == 0) {
       constexpr uint32_t IDESC = tc::idesc_bf16(128, 128);
@@ -135,13 +136,13 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
       }
     }
   } else if (warp >= EPI_WARPS) {
-    // ---- layer norm (thread = tile row) ----
-    const int r = tid - EPI_WARPS * 32;
+    // ---- layer norm (two threads per tile row) ----
+    const int u = tid - EPI_WARPS * 32, r = u >> 1, half = u & 1;
     uint32_t it = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       const int st = it & 1;
       tc::mbar_wait(&full[st], (it >> 1) & 1, p.status, aborted);
-      ln_row_inplace_lr(smem + OFF_PZ + st * A_BYTES, r, p.ln_w, p.ln_b, 1e-5f);
+      ln_half_row_inplace(smem + OFF_PZ + st * A_BYTES, r, half, p.ln_w, p.ln_b, 1e-5f);
       tc::fence_proxy_async();
       tc::mbar_arrive(&normed[st]);
     }
@@ -181,12 +182,19 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
           tc::tmem_ld16(lane_addr + hh * 256 + hf * 64 + 16 * k, gt);
           tc::tmem_ld16(lane_addr + hh * 256 + 128 + hf * 64 + 16 * k, vl);
           uint32_t pk[8];
+          // a column is one position, the same for every lane: the mask test is warp-uniform
+          const uint32_t kw = (uint32_t)(keep >> (16 * k)) & 0xFFFFu;
+          if (kw == 0xFFFFu) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int i0 = 16 * k + 2 * e;
-            const float o0 = ((keep >> i0) & 1) ? sigmoid_tanh(gt[2 * e]) * vl[2 * e] : 0.f;
-            const float o1 = ((keep >> (i0 + 1)) & 1) ? sigmoid_tanh(gt[2 * e + 1]) * vl[2 * e + 1] : 0.f;
-            pk[e] = pack_bf2(o0, o1);
+            for (int e = 0; e < 8; ++e)
+              pk[e] = pack_bf2(sigmoid_tanh(gt[2 * e]) * vl[2 * e], sigmoid_tanh(gt[2 * e + 1]) * vl[2 * e + 1]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float o0 = ((kw >> (2 * e)) & 1) ? sigmoid_tanh(gt[2 * e]) * vl[2 * e] : 0.f;
+              const float o1 = ((kw >> (2 * e + 1)) & 1) ? sigmoid_tanh(gt[2 * e + 1]) * vl[2 * e + 1] : 0.f;
+              pk[e] = pack_bf2(o0, o1);
+            }
           }
           *reinterpret_cast<uint4*>(stg + tc::sw128_off(lane, 2 * k)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
           *reinterpret_cast<uint4*>(stg + tc::sw128_off(lane, 2 * k + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
