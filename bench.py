@@ -54,7 +54,7 @@ def load_peaks() -> dict:
 
 
 class ClockSampler:
-  """nvidia-smi clocks and throttle reasons sampled every 200 ms while active."""
+  """nvidia-smi clocks and throttle reasons sampled every 50 ms while active."""
 
   FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -68,7 +68,7 @@ class ClockSampler:
     try:
       self.proc = subprocess.Popen(
           ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+           "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
     except OSError:
       self.proc = None
     return self
@@ -159,6 +159,16 @@ def tri_attention_op_flops(n: int) -> float:
   """Algorithmic FLOPs of one GridSelfAttention call: core 512 N^3 + projections
   (q, k, v, gate, bias: 2*128*(512+4) per position) + output projection (2*128*128)."""
   return tri_attention_core_flops(n) + n * n * (2.0 * 128 * 516 + 2.0 * 128 * 128)
+
+
+# DRAM bytes of one triangle attention (projection + core) at N=512, from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum; profiles/k_triatt_tc_n512.md).
+TRI_ATT_TRAFFIC_N512 = int((67.29 + 216.11 + 337.76 + 57.46) * 1e6)
+
+
+def tri_attention_exp2_count(n: int) -> float:
+  """exp2 evaluations of one attention call: one per (row, head, query, key)."""
+  return 4.0 * n * n * n
 
 
 def time_kernel_probe(n: int, dtype, iters: int = 10) -> float:
@@ -291,7 +301,11 @@ def run_b200(args) -> None:
                                "with fused output projection), N=512, 4 heads x 32",
                      "bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
-                     "peak_source": peaks["source"], "launch_ms": round(probe_ms, 4), "traffic": None},
+                     "peak_source": peaks["source"], "launch_ms": round(probe_ms, 4),
+                     "traffic": TRI_ATT_TRAFFIC_N512 if N_TOKEN == 512 else None,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of k_triatt_project_tc + "
+                                       "k_triatt_core_tc, profiles/k_triatt_tc_n512.md",
+                     "exp2_bound_ms": round(tri_attention_exp2_count(N_TOKEN) / (16 * 148 * 1.9e9) * 1e3, 4)},
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
