@@ -339,30 +339,32 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 // One CTA = one (attention row b, 128-query tile); warpgroup h owns head h and
-// TMEM columns [128h, 128h+128): two S buffers (32 fp32 columns each), O (32),
-// P (16 columns of bf16 pairs) and Q (16 columns of bf16 pairs).  Keys go in
-// blocks of 32.  The tensor core only runs TMEM-operand MMAs: S_j = Q K_j^T
-// (A = Q from TMEM) and O += P_j V_j (A = P from TMEM).  The pair bias, stored
-// as log2(e) * bias, arrives by TMA as a [128 queries][32 keys] tile and each
-// thread adds its query's row on the CUDA cores: logit2 = S scale + bias'.  Per
-// block j a warpgroup reads S_j and its bias row, sets masked and padding keys
-// to -inf and forms 2^(logit2 - m) against the running max m while it tracks
-// the block max in the same pass (so exponentials and CUDA-core work
-// interleave); when the block max exceeds m by more than 2^8 the block's values
-// are rescaled (or, past 2^64, recomputed) and O is rescaled in TMEM once
-// P_{j-1} V_{j-1} is done.  It writes P_j as bf16 and signals it.  A separate issue warp per head (warps 16-19) then issues
-// O += P_j V_j and S_{j+2} (into the S buffer just read) and refills the TMA
-// rings, so neither MMA issue (about 130 cycles per instruction for the issuing
-// warp) nor loads sit on the softmax warps, and the tensor core works two
-// blocks ahead of the softmax.  The K block, V^T block and bias tile of a key
-// block arrive by TMA on one barrier, four blocks deep; the issue warp folds
-// that barrier into the S barrier, so a softmax warp waits twice per block.  A row whose token
-// is masked attends uniformly to all N keys (every logit of the reference is
-// -FLT_MAX there).  Freed bias slots receive, near the end, the residual tile
-// z[queries][32h .. 32h+31] and the W_o columns of head h; the gated,
-// normalised O_h is staged in the last one, one more tcgen05 GEMM (K = 4 heads
-// x 32) forms the output projection in columns [0,128), and each warpgroup
-// adds its 32 output channels to the residual tile in place and TMA-stores it.
+// TMEM columns [128h, 128h+128): two S buffers (32 fp32 columns each; P_j, 16
+// columns of bf16 pairs, is written over S_j once it has been read), O (32) and
+// Q (16 columns of bf16 pairs).  Keys go in blocks of 32.  The tensor core only
+// runs TMEM-operand MMAs: S_j = Q K_j^T (A = Q) and O += P_j V_j (A = P).  The
+// pair bias, stored as log2(e) * bias, arrives by TMA as a [128 queries][32
+// keys] tile and each thread adds its query's row on the CUDA cores: logit2 =
+// S scale + bias'.  Per block j a warpgroup reads S_j and its bias row, sets
+// masked and padding keys to -inf and forms 2^(logit2 - m) against the running
+// max m while it tracks the block max in the same pass (exponentials and
+// CUDA-core work interleave); when the block max exceeds m by more than 2^8 the
+// block's values are rescaled (or, past 2^64, recomputed) and O is rescaled in
+// TMEM once P_{j-1} V_{j-1} is done.  It writes P_j as bf16 and signals it.
+// One issue warp per head (warps 16-19; an issuing warp gets one tcgen05.mma
+// per ~130 cycles, which must not sit on the softmax warps) then issues
+// O += P_j V_j, refills the TMA rings and, once P_j V_j is done, issues S_{j+2}
+// into the same buffer, so the tensor core works two blocks ahead and S_j
+// complete also means P_{j-2} V_{j-2} complete.  The K block, V^T block and
+// bias tile of a key block arrive by TMA on one barrier, four blocks deep, which
+// the issue warp folds into the S barrier: a softmax warp waits once per block.
+// A row whose token is masked attends uniformly to all N keys (every logit of
+// the reference is -FLT_MAX there).  Freed ring slots receive, near the end, the
+// residual tile z[queries][32h .. 32h+31] and the W_o columns of head h; the
+// gated, normalised O_h is staged in the last one, one more tcgen05 GEMM (K = 4
+// heads x 32) forms the output projection in columns [0,128), and each
+// warpgroup adds its 32 output channels to the residual tile in place and
+// TMA-stores it.
 __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid_constant__ CUtensorMap tmK,
                                                            const __grid_constant__ CUtensorMap tmV,
                                                            const __grid_constant__ CUtensorMap tmB,
@@ -371,14 +373,17 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
                                                            const __grid_constant__ CUtensorMap tmO, AttCoreParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
+  // Block-indexed barriers come in pairs (block j uses [j & 1], phase j >> 1): a parity
+  // wait only tells phases apart within one phase of the barrier, and the softmax warps,
+  // the issue warp and the tensor core may each run up to a block ahead of one another.
   uint64_t* sbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [H][2] S buffer written and its block landed (2 arrivals)
-  uint64_t* pvbar = sbar + 2 * H;                                  // [H] P V done (one phase per block)
-  uint64_t* lbar = pvbar + H;                                      // [H][RING] K, V^T and bias of a block landed
+  uint64_t* pvbar = sbar + 2 * H;                                  // [H][2] P_j V_j done
+  uint64_t* pready = pvbar + 2 * H;                                // [H][2] P_j written (4 softmax warps)
+  uint64_t* lbar = pready + 2 * H;                                 // [H][RING] K, V^T and bias of a block landed
   uint64_t* rbar = lbar + RING * H;                                // [H] residual tile landed
   uint64_t* wbar = rbar + H;                                       // [H] W_o columns landed
-  uint64_t* pready = wbar + H;                                     // [H] P_j written (4 softmax warps), per block
-  uint64_t* outbar = pready + H;
-  constexpr int NBAR = (6 + RING) * H + 1;
+  uint64_t* outbar = wbar + H;
+  constexpr int NBAR = (8 + RING) * H + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(outbar + 1);
   uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < NBAR; ++i) tc::mbar_init(&sbar[i], i < 2 * H ? 2 : (i >= (5 + RING) * H && i < NBAR - 1) ? 4 : 1);
+    for (int i = 0; i < NBAR; ++i) tc::mbar_init(&sbar[i], i < 2 * H ? 2 : (i >= 4 * H && i < 6 * H) ? 4 : 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmK);
     tc::prefetch_tmap(&tmV);
@@ -422,7 +427,8 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
-  const uint32_t s_col = (uint32_t)g * 128, o_col = s_col + 64, p_col = s_col + 96, qt_col = s_col + 112;
+  // S buffers [0,32) and [32,64) (P_j written over the first 16 columns of S_j), O [64,96), Q [96,112)
+  const uint32_t s_col = (uint32_t)g * 128, o_col = s_col + 64, qt_col = s_col + 96;
   uint8_t* ring = smem + OFF_RING + g * RING * SLOT_BYTES;   // slot s: K at +0, V^T at +K_BYTES, bias at +K_BYTES+V_BYTES
   auto k_of = [&](int jj) { return ring + (jj % RING) * SLOT_BYTES; };
   auto v_of = [&](int jj) { return ring + (jj % RING) * SLOT_BYTES + K_BYTES; };
@@ -479,17 +485,15 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
       issue_s(1);
       for (int j = 0; j < nkb; ++j) {
         // P_j is in TMEM: S_j and bias_j have been read, P_{j-1} V_{j-1} awaited by the softmax
-        tc::mbar_wait(&pready[g], j & 1, p.status, aborted);
+        tc::mbar_wait(&pready[g * 2 + (j & 1)], (j >> 1) & 1, p.status, aborted);
         tc::tc_fence_after();
-        // O += P_j V_j (V^T of block j landed before S_j was signalled)
+        // O += P_j V_j (P_j over S_j; V^T of block j landed before S_j was signalled)
         const uint32_t vs = tc::smem_u32(v_of(j));
 #pragma unroll
         for (int kk = 0; kk < KB / 16; ++kk)
-          tc::mma_bf16_ts(tbase + o_col, tbase + p_col + kk * 8, tc::smem_desc(vs + kk * 32, 512, tc::kSW64), IDESC,
-                          j > 0 || kk > 0);
-        tc::mma_commit(&pvbar[g]);
-        // S_{j+2} into the S buffer just read
-        if (j + 2 < nkb) issue_s(j + 2);
+          tc::mma_bf16_ts(tbase + o_col, tbase + s_col + (j & 1) * KB + kk * 8, tc::smem_desc(vs + kk * 32, 512, tc::kSW64),
+                          IDESC, j > 0 || kk > 0);
+        tc::mma_commit(&pvbar[g * 2 + (j & 1)]);
         // the slot of block j-1 is free (S, P V and the bias read are done): block j+3, or the epilogue tiles
         if (j >= 1) {
           if (j + RING - 1 < nkb) {
@@ -502,6 +506,11 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
             tc::mbar_expect_tx(&wbar[g], 8192);
             tc::tma_load_2d(wstage, &tmW, &wbar[g], g * D, 0);
           }
+        }
+        // S_{j+2} over P_j once P_j V_j has read it
+        if (j + 2 < nkb) {
+          tc::mbar_wait(&pvbar[g * 2 + (j & 1)], (j >> 1) & 1, p.status, aborted);
+          issue_s(j + 2);
         }
       }
     }
@@ -598,10 +607,11 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
         pk[(e >> 1) + 1] = pack_bf2(sv[e + 2], sv[e + 3]);
       }
       l = l * corr + (ps0 + ps1);
-      // P_{j-1} V_{j-1} is done before P is overwritten or O rescaled
-      if (j >= 1) tc::mbar_wait(&pvbar[g], (j - 1) & 1, p.status, aborted);
-      tc::tc_fence_after();
+      // P_j over S_j (S_j complete means P_{j-2} V_{j-2}, the last reader of this buffer, is done);
+      // O is rescaled only after P_{j-1} V_{j-1}
       if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+        tc::mbar_wait(&pvbar[g * 2 + ((j - 1) & 1)], ((j - 1) >> 1) & 1, p.status, aborted);
+        tc::tc_fence_after();
         float ov[D];
         tc::tmem_ld32(lane_addr + o_col, ov);
         uint32_t r[D];
@@ -609,11 +619,11 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
         for (int e = 0; e < D; ++e) r[e] = __float_as_uint(ov[e] * corr);
         tc::tmem_st32(lane_addr + o_col, r);
       }
-      tc::tmem_st16(lane_addr + p_col, pk);
+      tc::tmem_st16(lane_addr + s_col + (j & 1) * KB, pk);
       tc::tmem_wait_st();
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&pready[g]);
+      if (lane == 0) tc::mbar_arrive(&pready[g * 2 + (j & 1)]);
     }
   }
 
@@ -623,7 +633,9 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
     uint4 graw[D / 8];
 #pragma unroll
     for (int c = 0; c < D / 8; ++c) graw[c] = __ldg(grow + c);
-    tc::mbar_wait(&pvbar[g], (nkb - 1) & 1, p.status, aborted);   // the last P V
+    // the last two P V (S_{nkb-1} complete only means P V up to block nkb-3 is)
+    tc::mbar_wait(&pvbar[g * 2 + ((nkb - 2) & 1)], ((nkb - 2) >> 1) & 1, p.status, aborted);
+    tc::mbar_wait(&pvbar[g * 2 + ((nkb - 1) & 1)], ((nkb - 1) >> 1) & 1, p.status, aborted);
     tc::tc_fence_after();
     const float inv = l > 0.f ? 1.0f / l : 0.f;
     float ov[D];
