@@ -6,9 +6,11 @@
 //                       the ending node, transpose=True), four warps apply the
 //                       scale-only LN (blocks.py:260-264) in place and form the
 //                       4-head pair bias on CUDA cores, one thread issues
-//                       D[channel][query] = W . LN(z)^T for q, k, v, gate into
-//                       two TMEM halves, and eight epilogue warps stage the
-//                       outputs and TMA-store them.
+//                       D[query][channel] = LN(z) . W^T for q|k (one N=256 GEMM)
+//                       and the gate, and D[channel][query] for v (so v^T rows
+//                       come out of TMEM directly), into two TMEM halves, and
+//                       eight epilogue warps stage the outputs in shared memory
+//                       and TMA-store them.
 //  k_triatt_core_tc     flash attention + gate + output projection + residual for
 //                       one (attention row b, 128-query block): four softmax
 //                       warpgroups, one per head.  S = Q K^T and O += P V
@@ -49,16 +51,18 @@ struct AttProjParams {
 };
 
 // Warp roles (448 threads), one 128-query tile of one attention row at a time:
-//   warps 0-7   epilogue: warp w reads TMEM lanes 32(w%4).. (output channels
-//               32(w%4).., i.e. head w%4 of q, k, v and gate channels of that
-//               head) for queries 64(w/4)..+63, stages them and TMA-stores them:
-//               q, k, gate transposed to [query][32] rows, v^T as [32][query]
+//   warps 0-7   epilogue: warp w owns TMEM lanes 32(w%4)..: queries 32(w%4)..+31 of
+//               q, k and gate (D[query][channel]; heads 2(w/4), 2(w/4)+1) and
+//               channels of head w%4 of v (D[channel][query]; queries 64(w/4)..+63);
+//               it stages each output in its shared-memory tile (two 2 KB halves, so
+//               one TMA store drains while the next is written) and TMA-stores it
 //   warps 8-11  thread = query: scale-only LayerNorm of its row in place and the
 //               four pair-bias logits LN(z) . W_b[h]
 //   warp 12     TMA producer of z tiles (row tiles, or column tiles for the
 //               ending node), two stages
-//   warp 13     MMA issuer: D[out channel][query] = W_x . LN(z)^T for x = q, k
-//               (TMEM half 0, columns 0-255) and v, gate (half 1, 256-511)
+//   warp 13     MMA issuer: half 0 (TMEM columns 0-255) = LN(z) . [W_q | W_k]^T
+//               (M128 N256); half 1 = LN(z) . W_g^T (columns 256-383) and
+//               W_v . LN(z)^T (columns 384-511)
 constexpr int NOUT = 512;                   // w_qkvg rows: q, k, v, gate
 constexpr int W_BYTES = NOUT * C * 2;
 constexpr int PJ_EPI_WARPS = 8;
@@ -178,7 +182,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
       for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int st = it & 1;
         if (it >= 2) tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
-        const int b = (int)(tile / nqb), q0 = (int)((tile % nqb) * TILE);
+        const int b = (int)(tile / nqb), q0 = (int)((tile % nqb) * TILE);   // (projection tile coordinates)
         const int c1 = p.transpose ? b : q0;     // column coordinate
         const int c2 = p.transpose ? q0 : b;     // row coordinate
         uint8_t* dst = smem + OFF_JZ + st * A_BYTES;
@@ -190,30 +194,36 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
   } else if (warp == 13) {
     // ---- MMA issuer ----
     if (lane == 0) {
-      constexpr uint32_t IDESC = tc::idesc_bf16(128, 128);
+      constexpr uint32_t IDESC_QK = tc::idesc_bf16(128, 256), IDESC = tc::idesc_bf16(128, 128);
       uint32_t it = 0;
       for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int st = it & 1;
         tc::mbar_wait(&normed[st], (it >> 1) & 1, p.status, aborted);
         tc::tc_fence_after();
         const uint32_t zb = sb + OFF_JZ + st * A_BYTES;
+        auto wdesc = [&](int mtx, int ka, int kk) {   // rows 128 mtx.. of W (q, k, v, gate), K step (ka, kk)
+          return tc::smem_desc(sb + OFF_JW + ka * (NOUT * 128) + mtx * (128 * 128) + kk * 32, 1024, tc::kSW128);
+        };
+        // half 0: [q | k][query] = LN(z) . W_qk^T
+        if (it >= 1) tc::mbar_wait(&tfree[0], (it - 1) & 1, p.status, aborted);
+        tc::tc_fence_after();
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          if (it >= 1) tc::mbar_wait(&tfree[hh], (it - 1) & 1, p.status, aborted);
-          tc::tc_fence_after();
-#pragma unroll
-          for (int mt = 0; mt < 2; ++mt) {          // q, k | v, gate
-            const int mtx = 2 * hh + mt;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int ka = k >> 2, kk = k & 3;
-              tc::mma_bf16(tbase + hh * 256 + mt * 128,
-                           tc::smem_desc(sb + OFF_JW + ka * (NOUT * 128) + mtx * (128 * 128) + kk * 32, 1024, tc::kSW128),
-                           tc::smem_desc(zb + ka * ATOM + kk * 32, 1024, tc::kSW128), IDESC, k > 0);
-            }
-          }
-          tc::mma_commit(&tfull[hh]);
+        for (int k = 0; k < 8; ++k) {
+          const int ka = k >> 2, kk = k & 3;
+          tc::mma_bf16(tbase, tc::smem_desc(zb + ka * ATOM + kk * 32, 1024, tc::kSW128), wdesc(0, ka, kk), IDESC_QK, k > 0);
         }
+        tc::mma_commit(&tfull[0]);
+        // half 1: gate[query][channel] and v[channel][query]
+        if (it >= 1) tc::mbar_wait(&tfree[1], (it - 1) & 1, p.status, aborted);
+        tc::tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int ka = k >> 2, kk = k & 3;
+          const uint64_t zd = tc::smem_desc(zb + ka * ATOM + kk * 32, 1024, tc::kSW128);
+          tc::mma_bf16(tbase + 256, zd, wdesc(3, ka, kk), IDESC, k > 0);
+          tc::mma_bf16(tbase + 384, wdesc(2, ka, kk), zd, IDESC, k > 0);
+        }
+        tc::mma_commit(&tfull[1]);
         tc::mma_commit(&zfree[st]);
       }
     }
@@ -237,57 +247,89 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
       }
     }
   } else {
-    // ---- epilogue: head `quad`, queries q0 + 64 hf .. +63 ----
+    // ---- epilogue ----
     const int quad = warp & 3, hf = warp >> 2;
     const uint32_t lane_addr = tbase + ((uint32_t)(32 * quad) << 16);
     uint8_t* stg = smem + OFF_JST + warp * PJ_ST_BYTES;
+    int sh = 0;              // staging half for the next [32 queries][32 channels] store
+    bool full_used = false;  // the last store read the whole staging tile (v^T)
+    // one [32 queries][32 channels] tile (this lane = query row, 64B swizzle) into the next half, then stored
+    auto store_rows = [&](const float* v, const CUtensorMap* map, int c0, int c1) {
+      if (lane == 0) {
+        if (full_used) tc::bulk_wait_read0();
+        else tc::bulk_wait_read1();   // the store that used this half (two stores ago) has read it
+      }
+      __syncwarp();
+      uint8_t* half = stg + sh * 2048;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(half + tc::sw64_off(lane, c)) =
+            make_uint4(pack_bf2(v[8 * c], v[8 * c + 1]), pack_bf2(v[8 * c + 2], v[8 * c + 3]),
+                       pack_bf2(v[8 * c + 4], v[8 * c + 5]), pack_bf2(v[8 * c + 6], v[8 * c + 7]));
+      tc::fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tc::tma_store_2d(map, half, c0, c1);
+        tc::bulk_commit();
+      }
+      sh ^= 1;
+      full_used = false;
+    };
     uint32_t it = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
-      const int b = (int)(tile / nqb), q0 = (int)((tile % nqb) * TILE) + 64 * hf;
+      const int b = (int)(tile / nqb), qt0 = (int)((tile % nqb) * TILE);
+      const int qrow = qt0 + 32 * quad;   // first query of this warp's TMEM lanes
+      // ---- half 0: q and k, heads 2 hf, 2 hf + 1 ----
+      tc::mbar_wait(&tfull[0], it & 1, p.status, aborted);
+      tc::tc_fence_after();
 #pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        tc::mbar_wait(&tfull[hh], it & 1, p.status, aborted);
-        tc::tc_fence_after();
-#pragma unroll 1
-        for (int mt = 0; mt < 2; ++mt) {
-          const int o = 2 * hh + mt;   // 0 q, 1 k, 2 v, 3 gate
-          float v[64];
-          tc::tmem_ld64(lane_addr + hh * 256 + mt * 128 + 64 * hf, v);   // channel 32 quad + lane, 64 queries
-          if (mt == 1) {
-            // both TMEM columns of this half are in registers
-            tc::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&tfree[hh]);
-          }
-          if (o == 3) {
-#pragma unroll
-            for (int e = 0; e < 64; ++e) v[e] = sigmoid_tanh(v[e]);
-          }
-          if (lane == 0) tc::bulk_wait_read0();   // the previous store has read the staging tile
+      for (int i = 0; i < 4; ++i) {
+        const int t = i >> 1, hd = 2 * hf + (i & 1);   // t: 0 q, 1 k
+        float v[32];
+        tc::tmem_ld32(lane_addr + t * 128 + hd * D, v);
+        if (i == 3) {
+          tc::tc_fence_before();
           __syncwarp();
-          if (o == 2) {
-            // v^T: [32 channels][64 queries], 128B swizzle; this lane's row is its channel
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              *reinterpret_cast<uint4*>(stg + tc::sw128_off(lane, c)) =
-                  make_uint4(pack_bf2(v[8 * c], v[8 * c + 1]), pack_bf2(v[8 * c + 2], v[8 * c + 3]),
-                             pack_bf2(v[8 * c + 4], v[8 * c + 5]), pack_bf2(v[8 * c + 6], v[8 * c + 7]));
-          } else {
-            // q, k, gate: [64 queries][32 channels] rows of 64 bytes; this lane is column `lane`
-            bf16* st16 = reinterpret_cast<bf16*>(stg) + lane;
-#pragma unroll
-            for (int e = 0; e < 64; ++e) st16[e * D] = __float2bfloat16_rn(v[e]);
-          }
-          tc::fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) {
-            if (o == 0) tc::tma_store_2d(&tmQ, stg, 0, (int)(((int64_t)b * H + quad) * p.qp + q0));
-            else if (o == 1) tc::tma_store_2d(&tmK, stg, 0, (int)(((int64_t)b * H + quad) * p.qp + q0));
-            else if (o == 2) tc::tma_store_2d(&tmV, stg, q0, (b * H + quad) * D);
-            else tc::tma_store_2d(&tmG, stg, quad * D, (int)((int64_t)b * p.qp + q0));
-            tc::bulk_commit();
-          }
+          if (lane == 0) tc::mbar_arrive(&tfree[0]);
         }
+        store_rows(v, t == 0 ? &tmQ : &tmK, 0, (int)(((int64_t)b * H + hd) * p.qp + qrow));
+      }
+      // ---- half 1: gate (heads 2 hf, 2 hf + 1) and v^T (head quad, queries 64 hf ..) ----
+      tc::mbar_wait(&tfull[1], it & 1, p.status, aborted);
+      tc::tc_fence_after();
+#pragma unroll 1
+      for (int i = 0; i < 2; ++i) {
+        const int hd = 2 * hf + i;
+        float v[32];
+        tc::tmem_ld32(lane_addr + 256 + hd * D, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = sigmoid_tanh(v[e]);
+        store_rows(v, &tmG, hd * D, (int)((int64_t)b * p.qp + qrow));
+      }
+      {
+        float v[64];
+        tc::tmem_ld64(lane_addr + 384 + 64 * hf, v);   // channel 32 quad + lane, 64 queries
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&tfree[1]);
+          tc::bulk_wait_read0();   // v^T takes the whole staging tile
+        }
+        __syncwarp();
+        // [32 channels][64 queries], 128B swizzle; this lane's row is its channel
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(stg + tc::sw128_off(lane, c)) =
+              make_uint4(pack_bf2(v[8 * c], v[8 * c + 1]), pack_bf2(v[8 * c + 2], v[8 * c + 3]),
+                         pack_bf2(v[8 * c + 4], v[8 * c + 5]), pack_bf2(v[8 * c + 6], v[8 * c + 7]));
+        tc::fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_2d(&tmV, stg, qt0 + 64 * hf, (b * H + quad) * D);
+          tc::bulk_commit();
+        }
+        full_used = true;
+        sh = 0;
       }
     }
     if (lane == 0) tc::bulk_wait0();
@@ -782,11 +824,12 @@ int triatt_project_tc(const bf16* z, int64_t rows, int64_t cols, int transpose, 
   SF_TRY(set_smem(k_triatt_project_tc, SMEM_PROJ, attr));
   CUtensorMap mz, mq, mk, mv, mg;
   SF_TRY(make_pair_tmap(&mz, z, rows, cols, transpose != 0));
-  // stores of 64 queries per epilogue warp: Q, K [nb*H*qp][32], V^T [nb*H*32][qp], G [nb*qp][128]
-  SF_TRY(make_2d_tmap(&mq, q, D, nb * H * qp, D, 64, 0));
-  SF_TRY(make_2d_tmap(&mk, k, D, nb * H * qp, D, 64, 0));
+  // epilogue stores: Q, K [nb*H*qp][32] and G [nb*qp][128] as 32 queries x 32 channels (64B swizzle),
+  // V^T [nb*H*32][qp] as 32 channels x 64 queries (128B swizzle)
+  SF_TRY(make_2d_tmap(&mq, q, D, nb * H * qp, D, 32, 64));
+  SF_TRY(make_2d_tmap(&mk, k, D, nb * H * qp, D, 32, 64));
   SF_TRY(make_2d_tmap(&mv, vt, qp, nb * H * D, 64, D, 128));
-  SF_TRY(make_2d_tmap(&mg, g, C, nb * qp, D, 64, 0));
+  SF_TRY(make_2d_tmap(&mg, g, C, nb * qp, D, 32, 64));
   AttProjParams pp{ln_w, w_bias, bias, nb, nq, qp, transpose, compute_bias, status};
   const int64_t ntiles = nb * (qp / TILE);
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
