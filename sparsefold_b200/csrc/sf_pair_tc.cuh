@@ -200,6 +200,19 @@ __device__ __forceinline__ void load_weight_sw128(uint8_t* dst, const bf16* __re
   }
 }
 
+// acc + lo(a) lo(b) + hi(a) hi(b) for packed bf16 pairs a, b, accumulated in fp32
+// (the products of two bf16 values are exact in fp32).
+__device__ __forceinline__ float fma_bf16x2_f32(uint32_t a, uint32_t b, float acc) {
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+      "mov.b32 {al, ah}, %1;\n\t"
+      "mov.b32 {bl, bh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %0;\n\t"
+      "fma.rn.f32.bf16 %0, ah, bh, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(a), "r"(b));
+  return acc;
+}
+
 // Layer norm folded into the GEMM that follows it: with
 //   LN(x)[c] = (x[c] - mu) rho w[c] + b[c],
 //   LN(x) . W[o] = rho (x . W'[o] - mu s[o]) + b'[o],

@@ -117,12 +117,9 @@ __device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* _
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       u[j] = pack_bf2((bf_lo(u[j]) - mean) * rstd * wl[2 * j], (bf_hi(u[j]) - mean) * rstd * wl[2 * j + 1]);
-      const float y0 = bf_lo(u[j]), y1 = bf_hi(u[j]);   // the bias uses the bf16-rounded normalised row
+      // the bias uses the bf16-rounded normalised row: bf16 x bf16 products accumulated in fp32
 #pragma unroll
-      for (int h = 0; h < H; ++h) {
-        const uint32_t wp = reinterpret_cast<const uint32_t*>(&wv[h])[j];
-        bias[h] = fmaf(y0, bf_lo(wp), fmaf(y1, bf_hi(wp), bias[h]));
-      }
+      for (int h = 0; h < H; ++h) bias[h] = fma_bf16x2_f32(u[j], reinterpret_cast<const uint32_t*>(&wv[h])[j], bias[h]);
     }
     *reinterpret_cast<uint4*>(tile + off(i)) = v;
   }
