@@ -22,7 +22,7 @@
 //                       output projection, whose epilogue adds the residual.
 //
 // Intermediate layouts (qp = n rounded up to 128; padded query rows are zero):
-//   Q, K  [b][h][qp][32]    Vt [b][h][32][qp]    G = sigmoid(gate) [b][qp][128]
+//   Q, K  [b][h][qp][32] (Q times log2(e)/sqrt(32))    Vt [b][h][32][qp]    G = sigmoid(gate) [b][qp][128]
 //   bias  [q][h][qp] (bias[q][h][k] = log2(e) LN(z)[q,k] . W_b[h] in bf16, untransposed;
 //         rows q all-gathered from the row shards when the pair tensor is distributed)
 #include <cfloat>
@@ -36,9 +36,10 @@ using namespace pt;
 
 constexpr int H = 4, D = 32;
 constexpr float kLog2e = 1.4426950408889634f;
-// The pair bias is stored multiplied by log2(e): the core works in base 2 and forms
-// logit * log2(e) = (q.k) (log2(e) / sqrt(D)) + log2(e) b with one FMA per key.
+// The core works in base 2: Q is stored multiplied by log2(e) / sqrt(D) and the
+// pair bias by log2(e), so logit * log2(e) = q'.k + b' takes one add per key.
 constexpr float kBiasScale = kLog2e;
+constexpr float kQScale = 0.25503486f;   // log2(e) / sqrt(32)
 
 struct AttProjParams {
   const float* ln_w;      // act_norm scale [128]
@@ -289,6 +290,10 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
           __syncwarp();
           if (lane == 0) tc::mbar_arrive(&tfree[0]);
         }
+        if (t == 0) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] *= kQScale;   // q stored pre-scaled for the base-2 softmax
+        }
         store_rows(v, t == 0 ? &tmQ : &tmK, 0, (int)(((int64_t)b * H + hd) * p.qp + qrow));
       }
       // ---- half 1: gate (heads 2 hf, 2 hf + 1) and v^T (head quad, queries 64 hf ..) ----
@@ -352,7 +357,7 @@ struct AttCoreParams {
   int64_t nq, qp;         // queries = keys, pitch
   int64_t batch_offset;   // global token index of attention row 0 (row mask)
   int transpose;
-  float scale_log2;       // (1/sqrt(D)) * log2(e): S' = q.k + sqrt(D) b  ->  logit * log2(e) = S' * scale_log2
+  float scale_log2;       // (1/sqrt(D)) * log2(e), already applied to the stored Q
   uint32_t* status;
 };
 
@@ -370,6 +375,16 @@ constexpr int SMEM_CORE = OFF_BAR + 1024 + 1024;
 constexpr float kRescale = 8.0f;       // the running max moves only when a block exceeds it by 2^8
 constexpr int CORE_THREADS = (16 + 4) * 32;   // four softmax warpgroups + one issue warp per head
 
+// a0 += lo(w), a1 += hi(w) for a packed bf16 pair w (bf16 * 1.0 + fp32 in one instruction each).
+__device__ __forceinline__ void add_bf16x2(uint32_t w, float& a0, float& a1) {
+  asm("{\n\t.reg .b16 l, h, one;\n\t"
+      "mov.b32 {l, h}, %2;\n\t"
+      "mov.b16 one, 0x3F80;\n\t"
+      "fma.rn.f32.bf16 %0, l, one, %0;\n\t"
+      "fma.rn.f32.bf16 %1, h, one, %1;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(w));
+}
 __device__ __forceinline__ void wg_sync(int g) { asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory"); }
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -572,8 +587,8 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
 #pragma unroll
           for (int e2 = 0; e2 < 4; ++e2) {
             const int e = 8 * c + 2 * e2;
-            sv[e] = fmaf(sv[e], p.scale_log2, bf_lo(bw[e2]));
-            sv[e + 1] = fmaf(sv[e + 1], p.scale_log2, bf_hi(bw[e2]));
+            add_bf16x2(bw[e2], sv[e], sv[e + 1]);   // S (already in log2 units) + bias'
+
           }
         }
         if (vb != ~0u) {   // masked or padding keys in this block
