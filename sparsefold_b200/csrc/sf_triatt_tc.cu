@@ -375,6 +375,16 @@ constexpr int SMEM_CORE = OFF_BAR + 1024 + 1024;
 constexpr float kRescale = 8.0f;       // the running max moves only when a block exceeds it by 2^8
 constexpr int CORE_THREADS = (16 + 4) * 32;   // four softmax warpgroups + one issue warp per head
 
+// (a0, a1) += (b0, b1) as one packed fp32x2 add.
+__device__ __forceinline__ void add_f32x2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y;\n\t"
+      "mov.b64 x, {%0, %1};\n\t"
+      "mov.b64 y, {%2, %3};\n\t"
+      "add.rn.f32x2 x, x, y;\n\t"
+      "mov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
 // a0 += lo(w), a1 += hi(w) for a packed bf16 pair w (bf16 * 1.0 + fp32 in one instruction each).
 __device__ __forceinline__ void add_bf16x2(uint32_t w, float& a0, float& a1) {
   asm("{\n\t.reg .b16 l, h, one;\n\t"
@@ -621,10 +631,13 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
           for (int e = 0; e < KB; e += 4) {
             ma = tc::fmax3(ma, sv[e], sv[e + 1]);
             mb = tc::fmax3(mb, sv[e + 2], sv[e + 3]);
-            sv[e] = ex2(sv[e] - m_spec);
-            sv[e + 1] = ex2(sv[e + 1] - m_spec);
-            sv[e + 2] = ex2(sv[e + 2] - m_spec);
-            sv[e + 3] = ex2(sv[e + 3] - m_spec);
+            float d0 = sv[e], d1 = sv[e + 1], d2 = sv[e + 2], d3 = sv[e + 3];
+            add_f32x2(d0, d1, -m_spec, -m_spec);
+            add_f32x2(d2, d3, -m_spec, -m_spec);
+            sv[e] = ex2(d0);
+            sv[e + 1] = ex2(d1);
+            sv[e + 2] = ex2(d2);
+            sv[e + 3] = ex2(d3);
           }
           const float mx = fmaxf(ma, mb);
           const bool moves = mx > m_run + kRescale;          // also the first finite block after -inf
@@ -652,15 +665,15 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
       }
       // ---- P as bf16 pairs; the row sum ----
       uint32_t pk[KB / 2];
-      float ps0 = 0.f, ps1 = 0.f;
+      float ps0 = 0.f, ps1 = 0.f, ps2 = 0.f, ps3 = 0.f;
 #pragma unroll
       for (int e = 0; e < KB; e += 4) {
-        ps0 += sv[e] + sv[e + 1];
-        ps1 += sv[e + 2] + sv[e + 3];
+        add_f32x2(ps0, ps1, sv[e], sv[e + 1]);
+        add_f32x2(ps2, ps3, sv[e + 2], sv[e + 3]);
         pk[e >> 1] = pack_bf2(sv[e], sv[e + 1]);
         pk[(e >> 1) + 1] = pack_bf2(sv[e + 2], sv[e + 3]);
       }
-      l = l * corr + (ps0 + ps1);
+      l = l * corr + ((ps0 + ps1) + (ps2 + ps3));
       // P_j over S_j (S_j complete means P_{j-2} V_{j-2}, the last reader of this buffer, is done);
       // O is rescaled only after P_{j-1} V_{j-1}
       if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
