@@ -362,16 +362,18 @@ struct AttCoreParams {
 };
 
 constexpr int KB = 32;                 // keys per block
-constexpr int RING = 4;                // key blocks in flight: K, V^T and bias tile of each
+constexpr int RING = 4;                // key blocks in flight: K and bias tile of each
+constexpr int VRING = 5;               // V^T blocks: one more, so block j+3 lands where block j-2 was
 constexpr int K_BYTES = KB * D * 2;    // K block 32 keys x 64 B (64B swizzle)
 constexpr int V_BYTES = D * KB * 2;    // V^T block 32 dims x 64 B (64B swizzle)
 constexpr int BT_BYTES = TILE * KB * 2;  // bias tile of one head: 128 queries x 32 keys (64B swizzle)
-constexpr int SLOT_BYTES = K_BYTES + V_BYTES + BT_BYTES;
+constexpr int HEAD_BYTES = RING * (K_BYTES + BT_BYTES) + VRING * V_BYTES;   // one head's rings
 constexpr int MAX_QP = 32768;
-constexpr int OFF_RING = 0;                                   // [h][RING] slots: K | V^T | bias (residual, W_o, gated O at the end)
-constexpr int OFF_KBITS = OFF_RING + H * RING * SLOT_BYTES;   // key-valid bits, qp/32 words
+constexpr int OFF_RING = 0;                                   // [h]: K [RING] | bias [RING] (residual, W_o, gated O at the end) | V^T [VRING]
+constexpr int OFF_KBITS = OFF_RING + H * HEAD_BYTES;          // key-valid bits, qp/32 words
 constexpr int OFF_BAR = OFF_KBITS + MAX_QP / 8;
 constexpr int SMEM_CORE = OFF_BAR + 1024 + 1024;
+static_assert(SMEM_CORE <= 232448, "attention core shared memory");
 constexpr float kRescale = 8.0f;       // the running max moves only when a block exceeds it by 2^8
 constexpr int CORE_THREADS = (16 + 4) * 32;   // four softmax warpgroups + one issue warp per head
 
@@ -417,11 +419,14 @@ __device__ __forceinline__ float ex2(float x) {
 // TMEM once P_{j-1} V_{j-1} is done.  It writes P_j as bf16 and signals it.
 // One issue warp per head (warps 16-19; an issuing warp gets one tcgen05.mma
 // per ~130 cycles, which must not sit on the softmax warps) then issues
-// O += P_j V_j, refills the TMA rings and, once P_j V_j is done, issues S_{j+2}
-// into the same buffer, so the tensor core works two blocks ahead and S_j
-// complete also means P_{j-2} V_{j-2} complete.  The K block, V^T block and
-// bias tile of a key block arrive by TMA on one barrier, four blocks deep, which
-// the issue warp folds into the S barrier: a softmax warp waits once per block.
+// O += P_j V_j, refills the TMA rings and issues S_{j+2} into the same buffer
+// (MMAs of one thread run in issue order, so S_{j+2} writes after P_j V_j reads
+// P_j), so the tensor core works two blocks ahead and S_j complete also means
+// P_{j-2} V_{j-2} complete.  The K block, V^T block and
+// bias tile of a key block arrive by TMA on one barrier, four blocks deep (V^T in
+// a ring of five, so refilling a slot never waits for the P V that read it),
+// which the issue warp folds into the S barrier: a softmax warp waits once per
+// block.
 // A row whose token is masked attends uniformly to all N keys (every logit of
 // the reference is -FLT_MAX there).  Freed ring slots receive, near the end, the
 // residual tile z[queries][32h .. 32h+31] and the W_o columns of head h; the
@@ -493,10 +498,10 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
   // S buffers [0,32) and [32,64) (P_j written over the first 16 columns of S_j), O [64,96), Q [96,112)
   const uint32_t s_col = (uint32_t)g * 128, o_col = s_col + 64, qt_col = s_col + 96;
-  uint8_t* ring = smem + OFF_RING + g * RING * SLOT_BYTES;   // slot s: K at +0, V^T at +K_BYTES, bias at +K_BYTES+V_BYTES
-  auto k_of = [&](int jj) { return ring + (jj % RING) * SLOT_BYTES; };
-  auto v_of = [&](int jj) { return ring + (jj % RING) * SLOT_BYTES + K_BYTES; };
-  auto bt_of = [&](int jj) { return ring + (jj % RING) * SLOT_BYTES + K_BYTES + V_BYTES; };
+  uint8_t* ring = smem + OFF_RING + g * HEAD_BYTES;
+  auto k_of = [&](int jj) { return ring + (jj % RING) * K_BYTES; };
+  auto bt_of = [&](int jj) { return ring + RING * K_BYTES + (jj % RING) * BT_BYTES; };
+  auto v_of = [&](int jj) { return ring + RING * (K_BYTES + BT_BYTES) + (jj % VRING) * V_BYTES; };
   bool aborted = false;
   constexpr uint32_t IDESC = tc::idesc_bf16(128, 32);   // S (N = 32 keys) and O (N = 32 dims)
   if (!issuer) {
@@ -558,9 +563,11 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
           tc::mma_bf16_ts(tbase + o_col, tbase + s_col + (j & 1) * KB + kk * 8, tc::smem_desc(vs + kk * 32, 512, tc::kSW64),
                           IDESC, j > 0 || kk > 0);
         tc::mma_commit(&pvbar[g * 2 + (j & 1)]);
-        // the slot of block j-1 is free (S, P V and the bias read are done): block j+3, or the epilogue tiles
+        // block j+3, or the epilogue tiles
         if (j >= 1) {
           if (j + RING - 1 < nkb) {
+            // K and bias into the slots of block j-1 (S_{j-1} and its bias read are done), V^T into
+            // the V slot of block j-2 (P_{j-2} V_{j-2} is done: the softmax saw S_j complete)
             issue_load(j + RING - 1);
           } else if (j + RING - 1 == nkb) {
             tc::mbar_expect_tx(&rbar[g], TILE * D * 2);
@@ -571,11 +578,9 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
             tc::tma_load_2d(wstage, &tmW, &wbar[g], g * D, 0);
           }
         }
-        // S_{j+2} over P_j once P_j V_j has read it
-        if (j + 2 < nkb) {
-          tc::mbar_wait(&pvbar[g * 2 + (j & 1)], (j >> 1) & 1, p.status, aborted);
-          issue_s(j + 2);
-        }
+        // S_{j+2} over P_j: MMAs issued by one thread run in issue order, so its
+        // accumulator writes follow P_j V_j's read of P_j
+        if (j + 2 < nkb) issue_s(j + 2);
       }
     }
   } else {
@@ -729,8 +734,8 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
 #pragma unroll
     for (int k = 0; k < 2 * H; ++k) {
       const int h = k >> 1, kk = k & 1;
-      tc::mma_bf16(tbase, tc::smem_desc(os + h * RING * SLOT_BYTES + kk * 32, 512, tc::kSW64),
-                   tc::smem_desc(ws + h * RING * SLOT_BYTES + kk * 32, 512, tc::kSW64), IDESC_OUT, k > 0);
+      tc::mma_bf16(tbase, tc::smem_desc(os + h * HEAD_BYTES + kk * 32, 512, tc::kSW64),
+                   tc::smem_desc(ws + h * HEAD_BYTES + kk * 32, 512, tc::kSW64), IDESC_OUT, k > 0);
     }
     tc::mma_commit(outbar);
   }
