@@ -590,6 +590,9 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
       tc::tc_fence_after();
       float sv[KB];
       float corr = 1.f;
+      uint32_t pk[KB / 2];
+      float ps0 = 0.f, ps1 = 0.f, ps2 = 0.f, ps3 = 0.f;
+      bool packed = false;   // pk and the sums already hold this block's values
       const uint8_t* brow = bt_of(j);
       const uint32_t vb = kbits[j];
       // logit2 of key e: S scale + bias' (bias' = log2(e) bias), -inf where the key is excluded
@@ -643,7 +646,13 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
             sv[e + 1] = ex2(d1);
             sv[e + 2] = ex2(d2);
             sv[e + 3] = ex2(d3);
+            // packed and summed in the same pass (redone below in the rare case the max moves)
+            add_f32x2(ps0, ps1, sv[e], sv[e + 1]);
+            add_f32x2(ps2, ps3, sv[e + 2], sv[e + 3]);
+            pk[e >> 1] = pack_bf2(sv[e], sv[e + 1]);
+            pk[(e >> 1) + 1] = pack_bf2(sv[e + 2], sv[e + 3]);
           }
+          packed = true;
           const float mx = fmaxf(ma, mb);
           const bool moves = mx > m_run + kRescale;          // also the first finite block after -inf
           const bool redo = moves && !(mx <= m_run + 64.f);  // values up to 2^(mx - m) could overflow
@@ -657,26 +666,29 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
               corr = ex2(m_run - mx);
               m_run = mx;
             }
+            packed = false;
           } else if (moves) {
             corr = ex2(m_run - mx);
 #pragma unroll
             for (int e = 0; e < KB; ++e) sv[e] *= corr;
             m_run = mx;
+            packed = false;
           }
         }
       } else {
 #pragma unroll
         for (int e = 0; e < KB; ++e) sv[e] = ((int64_t)j * KB + e < p.nq) ? 1.f : 0.f;
       }
-      // ---- P as bf16 pairs; the row sum ----
-      uint32_t pk[KB / 2];
-      float ps0 = 0.f, ps1 = 0.f, ps2 = 0.f, ps3 = 0.f;
+      // ---- P as bf16 pairs; the row sum (unless the exponential pass made them) ----
+      if (!packed) {
+        ps0 = ps1 = ps2 = ps3 = 0.f;
 #pragma unroll
-      for (int e = 0; e < KB; e += 4) {
-        add_f32x2(ps0, ps1, sv[e], sv[e + 1]);
-        add_f32x2(ps2, ps3, sv[e + 2], sv[e + 3]);
-        pk[e >> 1] = pack_bf2(sv[e], sv[e + 1]);
-        pk[(e >> 1) + 1] = pack_bf2(sv[e + 2], sv[e + 3]);
+        for (int e = 0; e < KB; e += 4) {
+          add_f32x2(ps0, ps1, sv[e], sv[e + 1]);
+          add_f32x2(ps2, ps3, sv[e + 2], sv[e + 3]);
+          pk[e >> 1] = pack_bf2(sv[e], sv[e + 1]);
+          pk[(e >> 1) + 1] = pack_bf2(sv[e + 2], sv[e + 3]);
+        }
       }
       l = l * corr + ((ps0 + ps1) + (ps2 + ps3));
       // P_j over S_j (S_j complete means P_{j-2} V_{j-2}, the last reader of this buffer, is done);
