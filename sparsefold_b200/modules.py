@@ -605,6 +605,8 @@ class PairFormerIteration(torch.nn.Module):
     self.single_act_update = SingleActUpdate(c, seq_channels)
 
   def forward(self, act, *, seq_mask, single_act=None):
+    # every kernel reads the token mask as bytes: convert once, not once per op
+    seq_mask = ops.mask_u8(seq_mask)
     act = self.triangle_multiplication_outgoing(act, seq_mask)
     act = self.triangle_multiplication_incoming(act, seq_mask)
     act = self.pair_attention1(act, seq_mask)
@@ -708,6 +710,7 @@ class PairformerTrunk(torch.nn.Module):
     self.blocks = torch.nn.ModuleList(PairFormerIteration(num_channels, seq_channels) for _ in range(num_layers))
 
   def forward(self, pair, single, seq_mask):
+    seq_mask = ops.mask_u8(seq_mask)
     for blk in self.blocks:
       pair, single = blk(pair, seq_mask=seq_mask, single_act=single)
     return pair, single

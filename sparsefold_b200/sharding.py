@@ -223,11 +223,12 @@ def pairformer_block(block, z_loc: torch.Tensor, s_loc: torch.Tensor, mask: torc
   z_loc = tri_attention(block.pair_attention1, z_loc, m8, shard, group)
   z_loc = tri_attention(block.pair_attention2, z_loc, m8, shard, group)
   z_loc = block.pair_transition(z_loc)
-  s_loc = single_update(block.single_act_update, z_loc, s_loc, mask, shard, group)
+  s_loc = single_update(block.single_act_update, z_loc, s_loc, m8, shard, group)
   return z_loc, s_loc
 
 
 def pairformer_trunk(trunk, z_loc, s_loc, mask, shard: Shard, group=None):
+  mask = ops.mask_u8(mask)
   for blk in trunk.blocks:
     z_loc, s_loc = pairformer_block(blk, z_loc, s_loc, mask, shard, group)
   return z_loc, s_loc
