@@ -363,7 +363,7 @@ struct AttCoreParams {
 
 constexpr int KB = 32;                 // keys per block
 constexpr int RING = 4;                // key blocks in flight: K and bias tile of each
-constexpr int VRING = 5;               // V^T blocks: one more, so block j+3 lands where block j-2 was
+constexpr int VRING = 6;               // V^T blocks: two more, so block j+4 lands where block j-2 was
 constexpr int K_BYTES = KB * D * 2;    // K block 32 keys x 64 B (64B swizzle)
 constexpr int V_BYTES = D * KB * 2;    // V^T block 32 dims x 64 B (64B swizzle)
 constexpr int BT_BYTES = TILE * KB * 2;  // bias tile of one head: 128 queries x 32 keys (64B swizzle)
@@ -419,21 +419,22 @@ __device__ __forceinline__ float ex2(float x) {
 // TMEM once P_{j-1} V_{j-1} is done.  It writes P_j as bf16 and signals it.
 // One issue warp per head (warps 16-19; an issuing warp gets one tcgen05.mma
 // per ~130 cycles, which must not sit on the softmax warps) then issues
-// O += P_j V_j, refills the TMA rings and issues S_{j+2} into the same buffer
-// (MMAs of one thread run in issue order, so S_{j+2} writes after P_j V_j reads
-// P_j), so the tensor core works two blocks ahead and S_j complete also means
-// P_{j-2} V_{j-2} complete.  The K block, V^T block and
-// bias tile of a key block arrive by TMA on one barrier, four blocks deep (V^T in
-// a ring of five, so refilling a slot never waits for the P V that read it),
-// which the issue warp folds into the S barrier: a softmax warp waits once per
-// block.
+// O += P_j V_j and S_{j+2} into the same buffer (MMAs of one thread run in issue
+// order, so S_{j+2} writes after P_j V_j reads P_j; S_j complete thus also means
+// P_{j-2} V_{j-2} complete), and only then refills the TMA rings, so the next S
+// never waits behind a TMA issue.  The K block, V^T block and bias tile of a key
+// block arrive by TMA on one barrier, requested four blocks ahead (two blocks
+// before its S is issued; V^T in a ring of six, so a refill never waits for the
+// P V that read the slot), which the issue warp folds into the S barrier: a
+// softmax warp waits once per block.  The issue warps start the first loads
+// while the softmax warps move Q into TMEM.
 // A row whose token is masked attends uniformly to all N keys (every logit of
 // the reference is -FLT_MAX there).  Freed ring slots receive, near the end, the
 // residual tile z[queries][32h .. 32h+31] and the W_o columns of head h; the
-// gated, normalised O_h is staged in the last one, one more tcgen05 GEMM (K = 4
-// heads x 32) forms the output projection in columns [0,128), and each
-// warpgroup adds its 32 output channels to the residual tile in place and
-// TMA-stores it.
+// gated, normalised O_h is staged in the last one and head h's issue warp forms
+// its share of the output projection, O_h W_o[:, 32h .. 32h+31]^T, in the head's
+// own TMEM columns; each warpgroup sums the four heads' shares of its 32 output
+// channels, adds them to the residual tile in place and TMA-stores it.
 __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid_constant__ CUtensorMap tmK,
                                                            const __grid_constant__ CUtensorMap tmV,
                                                            const __grid_constant__ CUtensorMap tmB,
@@ -445,15 +446,15 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   // Block-indexed barriers come in pairs (block j uses [j & 1], phase j >> 1): a parity
   // wait only tells phases apart within one phase of the barrier, and the softmax warps,
   // the issue warp and the tensor core may each run up to a block ahead of one another.
-  uint64_t* sbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [H][2] S buffer written and its block landed (2 arrivals)
+  uint64_t* sbar = reinterpret_cast<uint64_t*>(smem + OFF_BAR);   // [H][2] S_j written and block j landed (2 arrivals)
   uint64_t* pvbar = sbar + 2 * H;                                  // [H][2] P_j V_j done
   uint64_t* pready = pvbar + 2 * H;                                // [H][2] P_j written (4 softmax warps)
   uint64_t* lbar = pready + 2 * H;                                 // [H][RING] K, V^T and bias of a block landed
   uint64_t* rbar = lbar + RING * H;                                // [H] residual tile landed
   uint64_t* wbar = rbar + H;                                       // [H] W_o columns landed
-  uint64_t* outbar = wbar + H;
-  constexpr int NBAR = (8 + RING) * H + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(outbar + 1);
+  uint64_t* ostaged = wbar + H;                                    // [H] gated O_h staged (4 softmax warps)
+  uint64_t* outbar = ostaged + H;                                  // [H] O_h W_o^T done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(outbar + H);
   uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool issuer = warp >= 16;
@@ -462,20 +463,46 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   const int nkb = (int)(p.qp / KB);   // >= 4
   const int64_t bh = b * H + g;
   const int64_t q = q0 + t;
+  uint8_t* ring = smem + OFF_RING + g * HEAD_BYTES;
+  auto k_of = [&](int jj) { return ring + (jj % RING) * K_BYTES; };
+  auto bt_of = [&](int jj) { return ring + RING * K_BYTES + (jj % RING) * BT_BYTES; };
+  auto v_of = [&](int jj) { return ring + RING * (K_BYTES + BT_BYTES) + (jj % VRING) * V_BYTES; };
+  bool aborted = false;
 
+  // this thread's query row of Q (64 B), for TMEM: requested first, it is the longest wait
+  uint4 qrow[4];
+  if (!issuer) {
+    const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (bh * p.qp + q) * D);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) qrow[c] = __ldg(qsrc + c);
+  }
+  auto issue_load = [&](int jj) {   // K, V^T and bias[q0..q0+127][g][32 jj .. 32 jj + 31] of block jj
+    uint64_t* bar = &lbar[g * RING + jj % RING];
+    tc::mbar_expect_tx(bar, K_BYTES + V_BYTES + BT_BYTES);
+    tc::tma_load_2d(k_of(jj), &tmK, bar, 0, (int)(bh * p.qp + (int64_t)jj * KB));
+    tc::tma_load_2d(v_of(jj), &tmV, bar, jj * KB, (int)(bh * D));
+    tc::tma_load_3d(bt_of(jj), &tmB, bar, jj * KB, g, (int)q0);
+  };
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
-  if (tid == 0) {
-    for (int i = 0; i < NBAR; ++i) tc::mbar_init(&sbar[i], i < 2 * H ? 2 : (i >= 4 * H && i < 6 * H) ? 4 : 1);
+  if (issuer && lane == 0) {
+    // each issue warp sets up its head's barriers and starts the first four blocks' loads at once
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&sbar[g * 2 + i], 2);
+      tc::mbar_init(&pvbar[g * 2 + i], 1);
+      tc::mbar_init(&pready[g * 2 + i], 4);
+    }
+    for (int i = 0; i < RING; ++i) tc::mbar_init(&lbar[g * RING + i], 1);
+    tc::mbar_init(&rbar[g], 1);
+    tc::mbar_init(&wbar[g], 1);
+    tc::mbar_init(&ostaged[g], 4);
+    tc::mbar_init(&outbar[g], 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmK);
     tc::prefetch_tmap(&tmV);
     tc::prefetch_tmap(&tmB);
-    tc::prefetch_tmap(&tmW);
-    tc::prefetch_tmap(&tmR);
-    tc::prefetch_tmap(&tmO);
   }
   // key k is attended iff mask[row] && mask[k] (pair mask, blocks.py:314); bits hold mask[k] && k < N
   for (int w = warp; w < (int)(p.qp / 32); w += CORE_THREADS / 32) {
@@ -483,26 +510,17 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
     const uint32_t bits = __ballot_sync(0xffffffffu, key < p.nq && p.mask[key] != 0);
     if (lane == 0) kbits[w] = bits;
   }
-  // this thread's query row of Q (64 B), for TMEM
-  uint4 qrow[4];
-  if (!issuer) {
-    const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (bh * p.qp + q) * D);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) qrow[c] = __ldg(qsrc + c);
-  }
   const bool uniform = p.mask[b + p.batch_offset] == 0;
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
+  // the first four blocks' loads, while the softmax warps move Q into TMEM
+  if (issuer && lane == 0)
+    for (int jj = 0; jj < RING; ++jj) issue_load(jj);   // nkb >= 4
   const uint32_t tbase = *tmem_slot;
   const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
   // S buffers [0,32) and [32,64) (P_j written over the first 16 columns of S_j), O [64,96), Q [96,112)
   const uint32_t s_col = (uint32_t)g * 128, o_col = s_col + 64, qt_col = s_col + 96;
-  uint8_t* ring = smem + OFF_RING + g * HEAD_BYTES;
-  auto k_of = [&](int jj) { return ring + (jj % RING) * K_BYTES; };
-  auto bt_of = [&](int jj) { return ring + RING * K_BYTES + (jj % RING) * BT_BYTES; };
-  auto v_of = [&](int jj) { return ring + RING * (K_BYTES + BT_BYTES) + (jj % VRING) * V_BYTES; };
-  bool aborted = false;
   constexpr uint32_t IDESC = tc::idesc_bf16(128, 32);   // S (N = 32 keys) and O (N = 32 dims)
   if (!issuer) {
     uint32_t qw[16];
@@ -517,13 +535,6 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
     tc::tmem_wait_st();
   }
 
-  auto issue_load = [&](int jj) {   // K, V^T and bias[q0..q0+127][g][32 jj .. 32 jj + 31] of block jj
-    uint64_t* bar = &lbar[g * RING + jj % RING];
-    tc::mbar_expect_tx(bar, K_BYTES + V_BYTES + BT_BYTES);
-    tc::tma_load_2d(k_of(jj), &tmK, bar, 0, (int)(bh * p.qp + (int64_t)jj * KB));
-    tc::tma_load_2d(v_of(jj), &tmV, bar, jj * KB, (int)(bh * D));
-    tc::tma_load_3d(bt_of(jj), &tmB, bar, jj * KB, g, (int)q0);
-  };
   auto issue_s = [&](int jj) {   // S_jj = Q K_jj^T into S buffer jj % 2, once block jj has landed
     tc::mbar_wait(&lbar[g * RING + jj % RING], (jj / RING) & 1, p.status, aborted);
     tc::mbar_arrive(&sbar[g * 2 + (jj & 1)]);   // the softmax reads the bias tile once S_jj is signalled
@@ -541,15 +552,14 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   uint8_t* resid = bt_of(nkb);        // bias part of the slot of block nkb-4
   uint8_t* wstage = bt_of(nkb + 1);   // ... of block nkb-3
   uint8_t* ostage = bt_of(nkb + 3);   // ... of block nkb-1
+  constexpr uint32_t IDESC_OUT = tc::idesc_bf16(128, 128);
 
-  // ---- prologue: K, V^T, bias of blocks 0-3; S_0, S_1 (issue warp of head g) ----
   tc::tc_fence_before();
   __syncthreads();   // Q is in TMEM
   float m_run = -INFINITY, l = 0.f;
   if (issuer) {
     if (lane == 0) {
       tc::tc_fence_after();
-      for (int jj = 0; jj < RING; ++jj) issue_load(jj);   // nkb >= 4
       issue_s(0);
       issue_s(1);
       for (int j = 0; j < nkb; ++j) {
@@ -563,31 +573,45 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
           tc::mma_bf16_ts(tbase + o_col, tbase + s_col + (j & 1) * KB + kk * 8, tc::smem_desc(vs + kk * 32, 512, tc::kSW64),
                           IDESC, j > 0 || kk > 0);
         tc::mma_commit(&pvbar[g * 2 + (j & 1)]);
-        // block j+3, or the epilogue tiles
-        if (j >= 1) {
-          if (j + RING - 1 < nkb) {
-            // K and bias into the slots of block j-1 (S_{j-1} and its bias read are done), V^T into
-            // the V slot of block j-2 (P_{j-2} V_{j-2} is done: the softmax saw S_j complete)
-            issue_load(j + RING - 1);
-          } else if (j + RING - 1 == nkb) {
-            tc::mbar_expect_tx(&rbar[g], TILE * D * 2);
-            tc::tma_load_3d(resid, &tmR, &rbar[g], g * D, rc1, rc2);
-          } else if (j + RING - 1 == nkb + 1) {
-            // W_o[:, 32g .. 32g+31] (K-major 128 x 32, 64B swizzle)
-            tc::mbar_expect_tx(&wbar[g], 8192);
-            tc::tma_load_2d(wstage, &tmW, &wbar[g], g * D, 0);
-          }
-        }
-        // S_{j+2} over P_j: MMAs issued by one thread run in issue order, so its
-        // accumulator writes follow P_j V_j's read of P_j
+        // S_{j+2} over P_j: MMAs issued by one thread run in issue order, so its accumulator
+        // writes follow P_j V_j's read of P_j
         if (j + 2 < nkb) issue_s(j + 2);
+        // then block j+4 (two blocks before its S), or an epilogue tile: K and bias into the slots
+        // of block j (S_j and the softmax of block j are done), V^T into the slot of block j-2
+        // (S_j complete means P_{j-2} V_{j-2}, issued before it, is done)
+        if (j + RING < nkb) {
+          issue_load(j + RING);
+        } else if (j + RING == nkb) {
+          tc::prefetch_tmap(&tmR);
+          tc::prefetch_tmap(&tmW);
+          tc::prefetch_tmap(&tmO);
+          tc::mbar_expect_tx(&rbar[g], TILE * D * 2);
+          tc::tma_load_3d(resid, &tmR, &rbar[g], g * D, rc1, rc2);
+        } else if (j + RING == nkb + 1) {
+          // W_o[:, 32g .. 32g+31] (K-major 128 x 32, 64B swizzle)
+          tc::mbar_expect_tx(&wbar[g], 8192);
+          tc::tma_load_2d(wstage, &tmW, &wbar[g], g * D, 0);
+        }
       }
+      // this head's share of the output projection, D_g = O_g W_o[:, 32g .. 32g+31]^T, into the
+      // head's own columns (its S, O, Q and P are dead once O_g is staged)
+      tc::mbar_wait(&ostaged[g], 0, p.status, aborted);
+      tc::mbar_wait(&wbar[g], 0, p.status, aborted);
+      tc::tc_fence_after();
+      const uint32_t os = tc::smem_u32(ostage), ws = tc::smem_u32(wstage);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk)
+        tc::mma_bf16(tbase + s_col, tc::smem_desc(os + kk * 32, 512, tc::kSW64),
+                     tc::smem_desc(ws + kk * 32, 512, tc::kSW64), IDESC_OUT, kk > 0);
+      tc::mma_commit(&outbar[g]);
     }
   } else {
+    const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
     for (int j = 0; j < nkb; ++j) {
       // S_j is written and block j (its bias tile) has landed
       tc::mbar_wait(&sbar[g * 2 + (j & 1)], (j >> 1) & 1, p.status, aborted);
       tc::tc_fence_after();
+      if (j == nkb - 2) asm volatile("prefetch.global.L2 [%0];" ::"l"(grow));   // the gate row for the epilogue
       float sv[KB];
       float corr = 1.f;
       uint32_t pk[KB / 2];
@@ -606,7 +630,6 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
           for (int e2 = 0; e2 < 4; ++e2) {
             const int e = 8 * c + 2 * e2;
             add_bf16x2(bw[e2], sv[e], sv[e + 1]);   // S (already in log2 units) + bias'
-
           }
         }
         if (vb != ~0u) {   // masked or padding keys in this block
@@ -709,11 +732,8 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&pready[g * 2 + (j & 1)]);
     }
-  }
 
-  // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) in the last bias slot ----
-  if (!issuer) {
-    const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
+    // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) in the last bias slot ----
     uint4 graw[D / 8];
 #pragma unroll
     for (int c = 0; c < D / 8; ++c) graw[c] = __ldg(grow + c);
@@ -722,58 +742,57 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
     tc::mbar_wait(&pvbar[g * 2 + ((nkb - 1) & 1)], ((nkb - 1) >> 1) & 1, p.status, aborted);
     tc::tc_fence_after();
     const float inv = l > 0.f ? 1.0f / l : 0.f;
-    float ov[D];
-    tc::tmem_ld32(lane_addr + o_col, ov);
+    {
+      float ov[D];
+      tc::tmem_ld32(lane_addr + o_col, ov);
 #pragma unroll
-    for (int cc = 0; cc < D / 8; ++cc) {
-      const uint4 gg = graw[cc];
-      const int d = cc * 8;
-      *reinterpret_cast<uint4*>(ostage + tc::sw64_off(t, cc)) =
-          make_uint4(pack_bf2(ov[d] * inv * bf_lo(gg.x), ov[d + 1] * inv * bf_hi(gg.x)),
-                     pack_bf2(ov[d + 2] * inv * bf_lo(gg.y), ov[d + 3] * inv * bf_hi(gg.y)),
-                     pack_bf2(ov[d + 4] * inv * bf_lo(gg.z), ov[d + 5] * inv * bf_hi(gg.z)),
-                     pack_bf2(ov[d + 6] * inv * bf_lo(gg.w), ov[d + 7] * inv * bf_hi(gg.w)));
+      for (int cc = 0; cc < D / 8; ++cc) {
+        const uint4 gg = graw[cc];
+        const int d = cc * 8;
+        *reinterpret_cast<uint4*>(ostage + tc::sw64_off(t, cc)) =
+            make_uint4(pack_bf2(ov[d] * inv * bf_lo(gg.x), ov[d + 1] * inv * bf_hi(gg.x)),
+                       pack_bf2(ov[d + 2] * inv * bf_lo(gg.y), ov[d + 3] * inv * bf_hi(gg.y)),
+                       pack_bf2(ov[d + 4] * inv * bf_lo(gg.z), ov[d + 5] * inv * bf_hi(gg.z)),
+                       pack_bf2(ov[d + 6] * inv * bf_lo(gg.w), ov[d + 7] * inv * bf_hi(gg.w)));
+      }
     }
-  }
-  tc::fence_proxy_async();
-  tc::tc_fence_before();
-  __syncthreads();
-  if (tid == 0) {
-    for (int h = 0; h < H; ++h) tc::mbar_wait(&wbar[h], 0, p.status, aborted);
+    tc::fence_proxy_async();
+    tc::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&ostaged[g]);
+
+    // ---- query q, output channels 32g .. 32g+31: the four heads' shares + residual, in place ----
+    for (int h = 0; h < H; ++h) tc::mbar_wait(&outbar[h], 0, p.status, aborted);
     tc::tc_fence_after();
-    constexpr uint32_t IDESC_OUT = tc::idesc_bf16(128, 128);
-    const uint32_t os = tc::smem_u32(ostage), ws = tc::smem_u32(wstage);   // head 0's slots (g = 0)
-#pragma unroll
-    for (int k = 0; k < 2 * H; ++k) {
-      const int h = k >> 1, kk = k & 1;
-      tc::mma_bf16(tbase, tc::smem_desc(os + h * HEAD_BYTES + kk * 32, 512, tc::kSW64),
-                   tc::smem_desc(ws + h * HEAD_BYTES + kk * 32, 512, tc::kSW64), IDESC_OUT, k > 0);
-    }
-    tc::mma_commit(outbar);
-  }
-  tc::mbar_wait(outbar, 0, p.status, aborted);
-  tc::tc_fence_after();
-  if (!issuer) {
-    // query q, output channels 32g .. 32g+31: residual + projection in place, then one TMA store
-    float ov[D];
-    tc::tmem_ld32(lane_addr + g * D, ov);
     tc::mbar_wait(&rbar[g], 0, p.status, aborted);
 #pragma unroll
-    for (int cc = 0; cc < D / 8; ++cc) {
-      uint4* zp = reinterpret_cast<uint4*>(resid + tc::sw64_off(t, cc));
-      const uint4 zz = *zp;
-      const int d = cc * 8;
-      *zp = make_uint4(pack_bf2(bf_lo(zz.x) + ov[d], bf_hi(zz.x) + ov[d + 1]),
-                       pack_bf2(bf_lo(zz.y) + ov[d + 2], bf_hi(zz.y) + ov[d + 3]),
-                       pack_bf2(bf_lo(zz.z) + ov[d + 4], bf_hi(zz.z) + ov[d + 5]),
-                       pack_bf2(bf_lo(zz.w) + ov[d + 6], bf_hi(zz.w) + ov[d + 7]));
+    for (int hf = 0; hf < 2; ++hf) {   // 16 channels at a time
+      float ov[16];
+      tc::tmem_ld16(lane_addr + g * D + hf * 16, ov);
+#pragma unroll
+      for (int h = 1; h < H; ++h) {
+        float oh[16];
+        tc::tmem_ld16(lane_addr + h * 128 + g * D + hf * 16, oh);
+#pragma unroll
+        for (int e = 0; e < 16; e += 2) add_f32x2(ov[e], ov[e + 1], oh[e], oh[e + 1]);
+      }
+#pragma unroll
+      for (int c2 = 0; c2 < 2; ++c2) {
+        uint4* zp = reinterpret_cast<uint4*>(resid + tc::sw64_off(t, 2 * hf + c2));
+        const uint4 zz = *zp;
+        const int d = c2 * 8;
+        *zp = make_uint4(pack_bf2(bf_lo(zz.x) + ov[d], bf_hi(zz.x) + ov[d + 1]),
+                         pack_bf2(bf_lo(zz.y) + ov[d + 2], bf_hi(zz.y) + ov[d + 3]),
+                         pack_bf2(bf_lo(zz.z) + ov[d + 4], bf_hi(zz.z) + ov[d + 5]),
+                         pack_bf2(bf_lo(zz.w) + ov[d + 6], bf_hi(zz.w) + ov[d + 7]));
+      }
     }
     tc::fence_proxy_async();
     wg_sync(g);
     if (t == 0) {
       tc::tma_store_3d(&tmO, resid, g * D, rc1, rc2);   // rows beyond N are clipped
       tc::bulk_commit();
-      tc::bulk_wait0();
+      tc::bulk_wait_read0();   // the tile must stay until the store has read it
     }
   }
   tc::tc_fence_before();
