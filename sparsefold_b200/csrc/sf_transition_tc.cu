@@ -5,17 +5,20 @@
 // tiles sharing every weight chunk) per pass.  The hidden layer is walked in 16
 // chunks of 32 units:
 //   warp 8      TMA producer: the x tiles of a pass, and per chunk the 64 rows of
-//               W1 (32 a + 32 b, 16 KB) and the 32 columns of W2 (8 KB), each in a
-//               4-stage ring
+//               W1 (32 a + 32 b, 16 KB) in a 4-stage ring
 //   warps 9, 11 GEMM1 issuers, one per tile (an issuing warp gets one MMA per
 //               ~126 cycles, so a single issuer of both tiles bounds the kernel):
 //               chunk c (M128 N64 K128) into one of two TMEM buffers as soon as
 //               the tile's half of the buffer and the weight chunk are free
 //   warp 10     GEMM2 issuer: chunk c (M128 N128 K32 per tile) from the hidden
-//               tile, accumulating the down projection in TMEM columns [256,512)
+//               tile, accumulating the down projection in TMEM columns [256,512);
+//               it also refills the 4-stage ring of W2 columns (8 KB per chunk), so
+//               W1 refills never wait for GEMM2, which runs a chunk or more behind
 //   warps 0-7   thread = position (warps 0-3 tile 0, 4-7 tile 1): LayerNorm of
-//               the pass in place, then per chunk swish(a) * b from TMEM into the
-//               64B-swizzled hidden tile, and finally y = x + acc.
+//               the pass in place (statistics in one shifted pass, scale and
+//               shift from shared memory), then per chunk swish(a) * b from TMEM
+//               into the 64B-swizzled hidden tile, and finally y = x + acc, staged
+//               by 64-channel halves in the free hidden buffers and TMA-stored.
 #include "sf_pair_tc.cuh"
 
 namespace sf {
@@ -24,7 +27,8 @@ namespace {
 using namespace pt;
 
 constexpr int I = 512, HC = 32, NCHUNK = I / HC;
-constexpr int TR_STAGES = 4;
+constexpr int W1_STAGES = 4;
+constexpr int W2_STAGES = 4;
 constexpr int X_BYTES = 2 * A_BYTES;           // two 128x128 input tiles
 constexpr int H_BYTES = TILE * HC * 2;         // one 128 x 32 hidden tile (8 KB)
 constexpr int W1C_BYTES = 2 * 64 * 128;        // 64 rows (32 a + 32 b) x 128 k, two 64-channel atoms
@@ -32,9 +36,50 @@ constexpr int W2C_BYTES = C * HC * 2;          // 128 out rows x 32 k (64B swizz
 constexpr int OFF_X = 0;
 constexpr int OFF_H = OFF_X + X_BYTES;                       // [2 buffers][2 tiles]
 constexpr int OFF_W1 = OFF_H + 4 * H_BYTES;                  // [stage]
-constexpr int OFF_W2 = OFF_W1 + TR_STAGES * W1C_BYTES;       // [stage]
-constexpr int OFF_BAR = OFF_W2 + TR_STAGES * W2C_BYTES;
+constexpr int OFF_W2 = OFF_W1 + W1_STAGES * W1C_BYTES;       // [stage]
+constexpr int OFF_LNP = OFF_W2 + W2_STAGES * W2C_BYTES;      // LayerNorm scale [128] and shift [128], fp32
+constexpr int OFF_BAR = OFF_LNP + 2 * C * 4;
 constexpr int SMEM_TR = OFF_BAR + 512 + 1024;
+static_assert(SMEM_TR <= 232448, "transition shared memory");
+
+// LayerNorm of row r of a 128 x 128 tile (128B swizzle) in place, one thread per row:
+// statistics in one pass over the row, shifted by its first value so that the
+// variance E[(x-k)^2] - E[x-k]^2 keeps its precision, with independent
+// accumulators; scale and shift come from shared memory.
+__device__ __forceinline__ void ln_row_shifted(uint8_t* tile, int r, const float* w_s, const float* b_s, float eps) {
+  auto off = [&](int i) -> uint32_t { return (uint32_t)(i >> 3) * ATOM + tc::sw128_off(r, i & 7); };
+  const float k = bf_lo(*reinterpret_cast<const uint32_t*>(tile + off(0)));
+  float s[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d0 = bf_lo(u[j]) - k, d1 = bf_hi(u[j]) - k;
+      s[j] += d0 + d1;
+      q[j] = fmaf(d0, d0, fmaf(d1, d1, q[j]));
+    }
+  }
+  const float dm = ((s[0] + s[1]) + (s[2] + s[3])) * (1.0f / C);
+  const float var = fmaxf(((q[0] + q[1]) + (q[2] + q[3])) * (1.0f / C) - dm * dm, 0.f);
+  const float mean = k + dm, rstd = rsqrtf(var + eps);
+#pragma unroll 2
+  for (int i = 0; i < 16; ++i) {
+    uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
+    uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+    const float4 w0 = *reinterpret_cast<const float4*>(w_s + 8 * i);
+    const float4 w1 = *reinterpret_cast<const float4*>(w_s + 8 * i + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(b_s + 8 * i);
+    const float4 b1 = *reinterpret_cast<const float4*>(b_s + 8 * i + 4);
+    u[0] = pack_bf2((bf_lo(u[0]) - mean) * rstd * w0.x + b0.x, (bf_hi(u[0]) - mean) * rstd * w0.y + b0.y);
+    u[1] = pack_bf2((bf_lo(u[1]) - mean) * rstd * w0.z + b0.z, (bf_hi(u[1]) - mean) * rstd * w0.w + b0.w);
+    u[2] = pack_bf2((bf_lo(u[2]) - mean) * rstd * w1.x + b1.x, (bf_hi(u[2]) - mean) * rstd * w1.y + b1.y);
+    u[3] = pack_bf2((bf_lo(u[3]) - mean) * rstd * w1.z + b1.z, (bf_hi(u[3]) - mean) * rstd * w1.w + b1.w);
+    *reinterpret_cast<uint4*>(tile + off(i)) = v;
+  }
+}
+__device__ __forceinline__ void tile_sync(int t2) { asm volatile("bar.sync %0, 128;" ::"r"(1 + t2) : "memory"); }
 constexpr int TR_THREADS = 12 * 32;
 
 struct TrParams {
@@ -48,7 +93,8 @@ struct TrParams {
 
 __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_constant__ CUtensorMap tmX,
                                                                  const __grid_constant__ CUtensorMap tmW1,
-                                                                 const __grid_constant__ CUtensorMap tmW2, TrParams p) {
+                                                                 const __grid_constant__ CUtensorMap tmW2,
+                                                                 const __grid_constant__ CUtensorMap tmY, TrParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -57,17 +103,19 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   uint64_t* xfree = bars + 2;                    // last GEMM1 of the pass done (both issuers)
   uint64_t* accfull = bars + 3;                  // last GEMM2 of the pass done
   uint64_t* accfree = bars + 4;                  // accumulators read (8 warps)
-  uint64_t* w1full = bars + 5;                   // [TR_STAGES]
-  uint64_t* w1free = w1full + TR_STAGES;         // both GEMM1 issuers done with the chunk
-  uint64_t* w2full = w1free + TR_STAGES;
-  uint64_t* w2free = w2full + TR_STAGES;
-  uint64_t* s1full = w2free + TR_STAGES;         // [2 buffers][2 tiles]
+  uint64_t* w1full = bars + 5;                   // [W1_STAGES]
+  uint64_t* w1free = w1full + W1_STAGES;         // both GEMM1 issuers done with the chunk
+  uint64_t* w2full = w1free + W1_STAGES;
+  uint64_t* w2free = w2full + W2_STAGES;
+  uint64_t* s1full = w2free + W2_STAGES;         // [2 buffers][2 tiles]
   uint64_t* s1free = s1full + 4;                 // [2 buffers][2 tiles] (4 warps)
   uint64_t* hfull = s1free + 4;                  // [2] (8 warps)
   uint64_t* hfree = hfull + 2;                   // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hfree + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t npasses = (p.M + 2 * TILE - 1) / (2 * TILE);
+  float* lnp = reinterpret_cast<float*>(smem + OFF_LNP);
+  if (tid < 2 * C) lnp[tid] = tid < C ? p.ln_w[tid] : (p.ln_b ? p.ln_b[tid - C] : 0.f);
 
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
@@ -79,9 +127,11 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
     tc::mbar_init(xfree, 2);
     tc::mbar_init(accfull, 1);
     tc::mbar_init(accfree, 8);
-    for (int s = 0; s < TR_STAGES; ++s) {
+    for (int s = 0; s < W1_STAGES; ++s) {
       tc::mbar_init(&w1full[s], 1);
       tc::mbar_init(&w1free[s], 2);
+    }
+    for (int s = 0; s < W2_STAGES; ++s) {
       tc::mbar_init(&w2full[s], 1);
       tc::mbar_init(&w2free[s], 1);
     }
@@ -97,6 +147,7 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
     tc::prefetch_tmap(&tmX);
     tc::prefetch_tmap(&tmW1);
     tc::prefetch_tmap(&tmW2);
+    tc::prefetch_tmap(&tmY);
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -117,18 +168,15 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
           for (int ka = 0; ka < 2; ++ka)
             tc::tma_load_2d(smem + OFF_X + t2 * A_BYTES + ka * ATOM, &tmX, xfull, ka * 64, (int)(m0 + t2 * TILE));
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
-          const int st = q % TR_STAGES;
-          const uint32_t ph = ((q / TR_STAGES) + 1) & 1;
-          if (q >= TR_STAGES) tc::mbar_wait(&w1free[st], ph, p.status, aborted);
+          const int st = q % W1_STAGES;
+          const uint32_t ph = ((q / W1_STAGES) + 1) & 1;
+          if (q >= W1_STAGES) tc::mbar_wait(&w1free[st], ph, p.status, aborted);
           uint8_t* w1 = smem + OFF_W1 + st * W1C_BYTES;
           tc::mbar_expect_tx(&w1full[st], W1C_BYTES);
           for (int ka = 0; ka < 2; ++ka) {
             tc::tma_load_2d(w1 + ka * 8192, &tmW1, &w1full[st], ka * 64, hc * HC);              // a rows
             tc::tma_load_2d(w1 + ka * 8192 + 4096, &tmW1, &w1full[st], ka * 64, I + hc * HC);   // b rows
           }
-          if (q >= TR_STAGES) tc::mbar_wait(&w2free[st], ph, p.status, aborted);
-          tc::mbar_expect_tx(&w2full[st], W2C_BYTES);
-          tc::tma_load_2d(smem + OFF_W2 + st * W2C_BYTES, &tmW2, &w2full[st], hc * HC, 0);
         }
       }
     }
@@ -141,8 +189,8 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
         tc::mbar_wait(xready, pi & 1, p.status, aborted);
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
-          const int st = q % TR_STAGES, sbuf = q & 1;
-          tc::mbar_wait(&w1full[st], (q / TR_STAGES) & 1, p.status, aborted);
+          const int st = q % W1_STAGES, sbuf = q & 1;
+          tc::mbar_wait(&w1full[st], (q / W1_STAGES) & 1, p.status, aborted);
           if (q >= 2) tc::mbar_wait(&s1free[sbuf * 2 + t2], ((q >> 1) + 1) & 1, p.status, aborted);
           tc::tc_fence_after();
           const uint32_t w1 = sb + OFF_W1 + st * W1C_BYTES;
@@ -160,16 +208,29 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       }
     }
   } else if (warp == 10) {
-    // ---- GEMM2 issuer: acc[t2] += H[t2] . W2 chunk^T ----
+    // ---- GEMM2 issuer: acc[t2] += H[t2] . W2 chunk^T; it also keeps the W2 ring filled (GEMM2
+    // runs a chunk or more behind GEMM1, and one producer for both rings held W1 to its pace) ----
     if (lane == 0) {
       constexpr uint32_t ID2 = tc::idesc_bf16(128, 128);
+      const uint32_t total = (uint32_t)((npasses - blockIdx.x + gridDim.x - 1) / gridDim.x) * NCHUNK;
+      auto load_w2 = [&](uint32_t c) {   // chunk c of this CTA into stage c % W2_STAGES
+        const int st = c % W2_STAGES;
+        tc::mbar_expect_tx(&w2full[st], W2C_BYTES);
+        tc::tma_load_2d(smem + OFF_W2 + st * W2C_BYTES, &tmW2, &w2full[st], (int)(c % NCHUNK) * HC, 0);
+      };
+      for (uint32_t c = 0; c < W2_STAGES && c < total; ++c) load_w2(c);
       uint32_t q = 0, pi = 0;
       for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
-          const int st = q % TR_STAGES, hb = q & 1;
+          const int st = q % W2_STAGES, hb = q & 1;
+          // chunk q-1+W2_STAGES into the stage of chunk q-1 once its GEMM2 is done (it usually is)
+          if (q >= 1 && q - 1 + W2_STAGES < total) {
+            tc::mbar_wait(&w2free[(q - 1) % W2_STAGES], ((q - 1) / W2_STAGES) & 1, p.status, aborted);
+            load_w2(q - 1 + W2_STAGES);
+          }
           if (hc == 0 && pi >= 1) tc::mbar_wait(accfree, (pi - 1) & 1, p.status, aborted);
           tc::mbar_wait(&hfull[hb], (q >> 1) & 1, p.status, aborted);
-          tc::mbar_wait(&w2full[st], (q / TR_STAGES) & 1, p.status, aborted);
+          tc::mbar_wait(&w2full[st], (q / W2_STAGES) & 1, p.status, aborted);
           tc::tc_fence_after();
           const uint32_t w2 = sb + OFF_W2 + st * W2C_BYTES;
           for (int t2 = 0; t2 < 2; ++t2)
@@ -192,13 +253,12 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
     for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
       const int64_t m0 = ps * 2 * TILE;
       tc::mbar_wait(xfull, pi & 1, p.status, aborted);
-      ln_row_inplace_lr(smem + OFF_X + t2 * A_BYTES, r, p.ln_w, p.ln_b, 1e-5f);
+      ln_row_shifted(smem + OFF_X + t2 * A_BYTES, r, lnp, lnp + C, 1e-5f);
       tc::fence_proxy_async();
       tc::mbar_arrive(xready);
       const int64_t m = m0 + t2 * TILE + r;
       const bool live = m < p.M;
       const uint4* xr = reinterpret_cast<const uint4*>(p.x + (live ? m : 0) * C);
-      uint4* yr = reinterpret_cast<uint4*>(p.y + (live ? m : 0) * C);
       uint4 xpre[16];
       for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
         const int sbuf = q & 1;
@@ -229,14 +289,18 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&hfull[sbuf]);
       }
-      // ---- residual epilogue: y = x + acc (the x row was prefetched during the last chunks) ----
+      // ---- residual epilogue: y = x + acc (the x row was prefetched during the last chunks), one
+      // 64-channel half at a time staged in the free hidden buffers (16 KB per tile, 128B swizzle)
+      // and TMA-stored: rows 256 B apart make per-thread 16-byte stores 32 transactions each ----
       tc::mbar_wait(accfull, pi & 1, p.status, aborted);
       tc::tc_fence_after();
+      uint8_t* ystage = smem + OFF_H + t2 * 2 * H_BYTES;
+      for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float v[32];
-        tc::tmem_ld32(lane_addr + 256 + t2 * 128 + 32 * i, v);
-        if (live) {
+        for (int i2 = 0; i2 < 2; ++i2) {
+          const int i = 2 * hh + i2;   // channels 32i .. 32i+31
+          float v[32];
+          tc::tmem_ld32(lane_addr + 256 + t2 * 128 + 32 * i, v);
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const uint4 xx = xpre[4 * i + c];
@@ -245,9 +309,17 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
 #pragma unroll
             for (int e = 0; e < 4; ++e)
               o[e] = pack_bf2(bf_lo(xu[e]) + v[8 * c + 2 * e], bf_hi(xu[e]) + v[8 * c + 2 * e + 1]);
-            yr[4 * i + c] = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(ystage + tc::sw128_off(r, 4 * i2 + c)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
+        tc::fence_proxy_async();
+        tile_sync(t2);
+        if (r == 0) {
+          tc::tma_store_2d(&tmY, ystage, hh * 64, (int)(m0 + t2 * TILE));   // rows past M are clipped
+          tc::bulk_commit();
+          tc::bulk_wait_read0();
+        }
+        tile_sync(t2);
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -301,8 +373,9 @@ int transition_tc(const bf16* x, const float* ln_w, const float* ln_b, const bf1
   SF_REQUIRE(M < (int64_t(1) << 31), "transition_tc: too many rows");
   SF_REQUIRE((reinterpret_cast<uintptr_t>(ln_w) & 15) == 0 && (reinterpret_cast<uintptr_t>(ln_b) & 15) == 0,
              "transition_tc: layer-norm parameters must be 16-byte aligned");
-  CUtensorMap mx, mw1, mw2;
+  CUtensorMap mx, mw1, mw2, my;
   SF_TRY(make_2d_tmap(&mx, x, C, M, 64, TILE));
+  SF_TRY(make_2d_tmap(&my, y, C, M, 64, TILE));
   SF_TRY(make_2d_tmap(&mw1, w1, C, 2 * I, 64, HC));         // W1 [1024][128]: 64 k x 32 rows
   SF_TRY(make_2d_tmap(&mw2, w2, I, C, HC, C, 64));          // W2 [128][512]: 32 k x 128 rows, 64B swizzle
   uint32_t* status = device_status_ptr();
@@ -321,7 +394,7 @@ int transition_tc(const bf16* x, const float* ln_w, const float* ln_b, const bf1
   TrParams p{x, y, ln_w, ln_b, M, status};
   const int64_t npairs = (M + 2 * TILE - 1) / (2 * TILE);
   const int grid = (int)(npairs < num_sms() ? npairs : num_sms());
-  k_transition_tc<<<grid, TR_THREADS, SMEM_TR, stream>>>(mx, mw1, mw2, p);
+  k_transition_tc<<<grid, TR_THREADS, SMEM_TR, stream>>>(mx, mw1, mw2, my, p);
   count_launch();
   return check_launch("transition_tc");
 }
