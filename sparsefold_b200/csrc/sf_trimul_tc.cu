@@ -42,8 +42,10 @@ constexpr int ST_BYTES = 32 * 128;                          // one epilogue warp
 constexpr int OFF_PW = 0;
 constexpr int OFF_PZ = W_BYTES;                             // two z stages
 constexpr int OFF_PST = OFF_PZ + 2 * A_BYTES;               // 8 staging tiles
-constexpr int OFF_PBAR = OFF_PST + EPI_WARPS * ST_BYTES;
+constexpr int OFF_PLN = OFF_PST + EPI_WARPS * ST_BYTES;    // LayerNorm scale and shift, 2 x 128 fp32
+constexpr int OFF_PBAR = OFF_PLN + 2 * C * 4;
 constexpr int SMEM_PROJ = OFF_PBAR + 256 + 1024;
+static_assert(SMEM_PROJ <= 232448, "trimul projection shared memory");
 
 __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __grid_constant__ CUtensorMap tmZ,
                                                                        const __grid_constant__ CUtensorMap tmA,
@@ -81,6 +83,8 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
     tc::prefetch_tmap(&tmB);
   }
   load_weight_sw128(smem + OFF_PW, w_glu, NOUT, tid, PROJ_THREADS);
+  float* lnp = reinterpret_cast<float*>(smem + OFF_PLN);
+  if (tid < 2 * C) lnp[tid] = tid < C ? p.ln_w[tid] : (p.ln_b ? p.ln_b[tid - C] : 0.f);
   tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();
@@ -142,7 +146,7 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       const int st = it & 1;
       tc::mbar_wait(&full[st], (it >> 1) & 1, p.status, aborted);
-      ln_half_row_inplace(smem + OFF_PZ + st * A_BYTES, r, half, p.ln_w, p.ln_b, 1e-5f);
+      ln_half_row_shifted(smem + OFF_PZ + st * A_BYTES, r, half, lnp, lnp + C, 1e-5f);
       tc::fence_proxy_async();
       tc::mbar_arrive(&normed[st]);
     }
