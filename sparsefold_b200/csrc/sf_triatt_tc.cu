@@ -73,44 +73,44 @@ constexpr int OFF_JW = 0;
 constexpr int OFF_JZ = W_BYTES;                            // [2] z tiles
 constexpr int OFF_JST = OFF_JZ + 2 * A_BYTES;              // [8] staging tiles
 constexpr int OFF_JWB = OFF_JST + PJ_EPI_WARPS * PJ_ST_BYTES;   // W_b [4][128] bf16
-constexpr int OFF_JBAR = OFF_JWB + H * C * 2;
+constexpr int OFF_JLN = OFF_JWB + H * C * 2;                  // LayerNorm scale [128] fp32
+constexpr int OFF_JBAR = OFF_JLN + C * 4;
 constexpr int SMEM_PROJ = OFF_JBAR + 256 + 1024;
 static_assert(SMEM_PROJ <= 232448, "projection shared memory");
 
 // Scale-only LayerNorm of tile row r in place (three passes over shared memory)
 // and the four pair-bias logits of the bf16-rounded normalised row.
-__device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* __restrict__ w, const bf16* wb_s,
-                                            float (&bias)[H]) {
+// Scale-only LayerNorm of tile row r in place (one thread per row) and the row's
+// pair bias LN(z) . W_b[h] (bf16 operands, fp32 sums): statistics in one pass,
+// shifted by the row's first value so E[(x-k)^2] - E[x-k]^2 keeps its precision,
+// independent accumulators throughout; the scale and W_b come from shared memory.
+__device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* w_s, const bf16* wb_s, float (&bias)[H]) {
   auto off = [&](int i) -> uint32_t { return (uint32_t)(i >> 3) * ATOM + tc::sw128_off(r, i & 7); };
-  float s = 0.f;
+  const float k = bf_lo(*reinterpret_cast<const uint32_t*>(tile + off(0)));
+  float s[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
   for (int i = 0; i < 16; ++i) {
     const uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) s += bf_lo(u[j]) + bf_hi(u[j]);
-  }
-  const float mean = s * (1.0f / C);
-  float q = 0.f;
-#pragma unroll 4
-  for (int i = 0; i < 16; ++i) {
-    const uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const float d0 = bf_lo(u[j]) - mean, d1 = bf_hi(u[j]) - mean;
-      q += d0 * d0 + d1 * d1;
+      const float d0 = bf_lo(u[j]) - k, d1 = bf_hi(u[j]) - k;
+      s[j] += d0 + d1;
+      q[j] = fmaf(d0, d0, fmaf(d1, d1, q[j]));
     }
   }
-  const float rstd = rsqrtf(q * (1.0f / C) + 1e-5f);
+  const float dm = ((s[0] + s[1]) + (s[2] + s[3])) * (1.0f / C);
+  const float mean = k + dm;
+  const float rstd = rsqrtf(fmaxf(((q[0] + q[1]) + (q[2] + q[3])) * (1.0f / C) - dm * dm, 0.f) + 1e-5f);
+  float b2[2][H];
 #pragma unroll
-  for (int h = 0; h < H; ++h) bias[h] = 0.f;
+  for (int h = 0; h < H; ++h) b2[0][h] = b2[1][h] = 0.f;
 #pragma unroll 2
   for (int i = 0; i < 16; ++i) {
     uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
     uint32_t* u = reinterpret_cast<uint32_t*>(&v);
-    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + 8 * i));
-    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + 8 * i + 4));
+    const float4 w0 = *reinterpret_cast<const float4*>(w_s + 8 * i);
+    const float4 w1 = *reinterpret_cast<const float4*>(w_s + 8 * i + 4);
     const float wl[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
     uint4 wv[H];
 #pragma unroll
@@ -120,10 +120,13 @@ __device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* _
       u[j] = pack_bf2((bf_lo(u[j]) - mean) * rstd * wl[2 * j], (bf_hi(u[j]) - mean) * rstd * wl[2 * j + 1]);
       // the bias uses the bf16-rounded normalised row: bf16 x bf16 products accumulated in fp32
 #pragma unroll
-      for (int h = 0; h < H; ++h) bias[h] = fma_bf16x2_f32(u[j], reinterpret_cast<const uint32_t*>(&wv[h])[j], bias[h]);
+      for (int h = 0; h < H; ++h)
+        b2[j & 1][h] = fma_bf16x2_f32(u[j], reinterpret_cast<const uint32_t*>(&wv[h])[j], b2[j & 1][h]);
     }
     *reinterpret_cast<uint4*>(tile + off(i)) = v;
   }
+#pragma unroll
+  for (int h = 0; h < H; ++h) bias[h] = b2[0][h] + b2[1][h];
 }
 
 __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __grid_constant__ CUtensorMap tmZ,
@@ -164,6 +167,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
   }
   for (int e = tid; e < H * C / 8; e += PJ_THREADS)
     reinterpret_cast<uint4*>(smem + OFF_JWB)[e] = __ldg(reinterpret_cast<const uint4*>(p.w_bias) + e);
+  if (tid < C) reinterpret_cast<float*>(smem + OFF_JLN)[tid] = p.ln_w[tid];
   load_weight_sw128(smem + OFF_JW, w_qkvg, NOUT, tid, PJ_THREADS);
   tc::fence_proxy_async();
   tc::tc_fence_before();
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
       const int st = it & 1;
       tc::mbar_wait(&full[st], (it >> 1) & 1, p.status, aborted);
       float bias[H];
-      ln_row_bias(smem + OFF_JZ + st * A_BYTES, r, p.ln_w, wb_s, bias);
+      ln_row_bias(smem + OFF_JZ + st * A_BYTES, r, reinterpret_cast<const float*>(smem + OFF_JLN), wb_s, bias);
       tc::fence_proxy_async();
       tc::mbar_arrive(&normed[st]);
       const int64_t b = tile / nqb, qi = (tile % nqb) * TILE + r;
