@@ -15,7 +15,7 @@ using namespace pt;
 
 constexpr int PL_HEADS = 16;                       // N of the MMA; weight rows beyond `heads` are zero
 constexpr int PL_W_BYTES = PL_HEADS * C * 2;       // two 64-channel atoms of 16 x 128 B
-constexpr int OFF_PLZ = 0, OFF_PLW = A_BYTES, OFF_PLBAR = OFF_PLW + PL_W_BYTES;
+constexpr int OFF_PLZ = 0, OFF_PLW = A_BYTES, OFF_PLLN = OFF_PLW + PL_W_BYTES, OFF_PLBAR = OFF_PLLN + 2 * C * 4;
 constexpr int SMEM_PL = OFF_PLBAR + 64 + 1024;
 
 struct PlParams {
@@ -55,13 +55,16 @@ __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ 
     if (r < p.heads) v = __ldg(reinterpret_cast<const uint4*>(p.w + (size_t)r * C + kc * 8));
     *reinterpret_cast<uint4*>(smem + OFF_PLW + (kc >> 3) * (PL_HEADS * 128) + tc::sw128_off(r, kc & 7)) = v;
   }
+  float* lnp = reinterpret_cast<float*>(smem + OFF_PLLN);   // LayerNorm scale and shift
+  lnp[tid] = p.ln_w[tid];
+  lnp[C + tid] = p.ln_b ? p.ln_b[tid] : 0.f;
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   bool aborted = false;
   tc::mbar_wait(ldbar, 0, p.status, aborted);
-  ln_row_inplace_lr(smem + OFF_PLZ, tid, p.ln_w, p.ln_b, 1e-5f);
+  ln_row_shifted(smem + OFF_PLZ, tid, lnp, lnp + C, 1e-5f);
   tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();

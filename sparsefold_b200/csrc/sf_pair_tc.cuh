@@ -187,6 +187,43 @@ __device__ __forceinline__ void ln_half_row_inplace(uint8_t* tile, int r, int h,
   }
 }
 
+// LayerNorm of row r of a 128 x 128 tile (128B swizzle) in place, one thread per row:
+// statistics in one pass over the row, shifted by its first value so that the
+// variance E[(x-k)^2] - E[x-k]^2 keeps its precision, with independent
+// accumulators; scale and shift come from shared memory.
+__device__ __forceinline__ void ln_row_shifted(uint8_t* tile, int r, const float* w_s, const float* b_s, float eps) {
+  auto off = [&](int i) -> uint32_t { return (uint32_t)(i >> 3) * ATOM + tc::sw128_off(r, i & 7); };
+  const float k = bf_lo(*reinterpret_cast<const uint32_t*>(tile + off(0)));
+  float s[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int i = 0; i < 16; ++i) {
+    const uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float d0 = bf_lo(u[j]) - k, d1 = bf_hi(u[j]) - k;
+      s[j] += d0 + d1;
+      q[j] = fmaf(d0, d0, fmaf(d1, d1, q[j]));
+    }
+  }
+  const float dm = ((s[0] + s[1]) + (s[2] + s[3])) * (1.0f / C);
+  const float var = fmaxf(((q[0] + q[1]) + (q[2] + q[3])) * (1.0f / C) - dm * dm, 0.f);
+  const float mean = k + dm, rstd = rsqrtf(var + eps);
+#pragma unroll 2
+  for (int i = 0; i < 16; ++i) {
+    uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
+    uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+    const float4 w0 = *reinterpret_cast<const float4*>(w_s + 8 * i);
+    const float4 w1 = *reinterpret_cast<const float4*>(w_s + 8 * i + 4);
+    const float4 b0 = *reinterpret_cast<const float4*>(b_s + 8 * i);
+    const float4 b1 = *reinterpret_cast<const float4*>(b_s + 8 * i + 4);
+    u[0] = pack_bf2((bf_lo(u[0]) - mean) * rstd * w0.x + b0.x, (bf_hi(u[0]) - mean) * rstd * w0.y + b0.y);
+    u[1] = pack_bf2((bf_lo(u[1]) - mean) * rstd * w0.z + b0.z, (bf_hi(u[1]) - mean) * rstd * w0.w + b0.w);
+    u[2] = pack_bf2((bf_lo(u[2]) - mean) * rstd * w1.x + b1.x, (bf_hi(u[2]) - mean) * rstd * w1.y + b1.y);
+    u[3] = pack_bf2((bf_lo(u[3]) - mean) * rstd * w1.z + b1.z, (bf_hi(u[3]) - mean) * rstd * w1.w + b1.w);
+    *reinterpret_cast<uint4*>(tile + off(i)) = v;
+  }
+}
 // The two-thread layer norm with the statistics in one pass over the row,
 // shifted by the row's first value k so that E[(x-k)^2] - E[x-k]^2 keeps its
 // precision, independent accumulators, and scale and shift read from shared
