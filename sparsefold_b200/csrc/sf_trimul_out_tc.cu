@@ -13,7 +13,10 @@
 //               swizzle: the M-major A operand of the update GEMM), two stages each
 //   warp 13     MMA issuer: gate = z W_gate'^T and update = P^T W_out'^T (M=N=K=128,
 //               folded weights resident) into one of two TMEM buffers of 256 columns
-//   warps 8-11  thread = position: mean and rstd of its z row and of its P column
+//   warps 8-11  per-position statistics, all as one pass of sums shifted by a
+//               value of the row or column: thread = position for its z row; for
+//               the P columns each thread sums a 16-byte chunk (8 positions) over 16
+//               channel rows and thread = position adds the 8 groups' partials
 //   warps 0-7   epilogue: warp w takes positions 32(w%4).. and channels 64(w/4)..,
 //               applies the folded norms, adds update * sigmoid(gate) to the raw z
 //               still in shared memory, in place, and TMA-stores that 32 x 64 block.
@@ -31,8 +34,10 @@ constexpr int OFF_Z = 2 * A_BYTES;              // [2] raw z tiles, then z_out s
 constexpr int OFF_P = OFF_Z + 2 * A_BYTES;      // [2] P tiles: two 64-position boxes of [128 ch][64 pos]
 constexpr int OFF_ST = OFF_P + 2 * A_BYTES;     // [2][4][128] floats: mean z, rstd z, mean P, rstd P
 constexpr int OFF_VEC = OFF_ST + 2 * 4 * C * 4; // [4][128] floats: s_gate, b_gate, s_out, b_out
-constexpr int OFF_BAR = OFF_VEC + 4 * C * 4;
+constexpr int OFF_PART = OFF_VEC + 4 * C * 4;   // [2][8 channel groups][2][128] floats: P column partial sums
+constexpr int OFF_BAR = OFF_PART + 2 * 8 * 2 * C * 4;
 constexpr int SMEM_OUT = OFF_BAR + 256 + 1024;
+static_assert(SMEM_OUT <= 232448, "trimul output shared memory");
 
 struct OutParams {
   const float *ln_w, *ln_b, *center_w, *center_b;
@@ -149,48 +154,80 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
       float* stats = reinterpret_cast<float*>(smem + OFF_ST) + st * 4 * C;
       tc::mbar_wait(&zfull[st], (it >> 1) & 1, p.status, aborted);
       {
-        // z row: mean, then the centred sum of squares (two passes over shared memory)
+        // z row: one pass of sums shifted by its first value (E[(x-k)^2] - E[x-k]^2 keeps its
+        // precision), four independent accumulator pairs
         const uint8_t* zs = smem + OFF_Z + st * A_BYTES;
-        float s = 0.f;
-#pragma unroll 4
-        for (int i = 0; i < 16; ++i) {
-          const uint4 v = *reinterpret_cast<const uint4*>(zs + (i >> 3) * ATOM + tc::sw128_off(pos, i & 7));
-          s += ((bf_lo(v.x) + bf_hi(v.x)) + (bf_lo(v.y) + bf_hi(v.y))) + ((bf_lo(v.z) + bf_hi(v.z)) + (bf_lo(v.w) + bf_hi(v.w)));
-        }
-        const float mean = s * (1.0f / C);
-        float q = 0.f;
+        const float k0 = bf_lo(*reinterpret_cast<const uint32_t*>(zs + tc::sw128_off(pos, 0)));
+        float s[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
         for (int i = 0; i < 16; ++i) {
           const uint4 v = *reinterpret_cast<const uint4*>(zs + (i >> 3) * ATOM + tc::sw128_off(pos, i & 7));
           const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float d0 = bf_lo(u[e]) - mean, d1 = bf_hi(u[e]) - mean;
-            q = fmaf(d0, d0, fmaf(d1, d1, q));
+            const float d0 = bf_lo(u[e]) - k0, d1 = bf_hi(u[e]) - k0;
+            s[e] += d0 + d1;
+            q[e] = fmaf(d0, d0, fmaf(d1, d1, q[e]));
           }
         }
-        stats[pos] = mean;
-        stats[C + pos] = rsqrtf(q * (1.0f / C) + 1e-5f);
+        const float md = ((s[0] + s[1]) + (s[2] + s[3])) * (1.0f / C);
+        stats[pos] = k0 + md;
+        stats[C + pos] = rsqrtf(fmaxf(((q[0] + q[1]) + (q[2] + q[3])) * (1.0f / C) - md * md, 0.f) + 1e-5f);
       }
       tc::mbar_wait(&pfull[st], (it >> 1) & 1, p.status, aborted);
       {
-        // P column: one pass of sums shifted by the first channel's value (avoids cancellation)
-        const uint8_t* pcol = smem + OFF_P + st * A_BYTES + (pos >> 6) * ATOM + (pos & 7) * 2;
-        const int chunk = (pos & 63) >> 3;
-        auto pval = [&](int c) {
-          return __bfloat162float(*reinterpret_cast<const bf16*>(pcol + c * 128 + ((chunk ^ (c & 7)) << 4)));
-        };
-        const float x0 = pval(0);
-        float s = 0.f, q = 0.f;
-#pragma unroll 16
-        for (int c = 0; c < C; ++c) {
-          const float d = pval(c) - x0;
-          s += d;
-          q = fmaf(d, d, q);
+        // P column sums shifted by the column's channel-0 value: thread t takes the 8 positions
+        // of one 16-byte chunk (group t % 16) over 16 channel rows (group t / 16), then thread
+        // pos adds the 8 groups' partials for its column
+        const int pg = pos & 15, cg = pos >> 4;
+        const uint8_t* pbox = smem + OFF_P + st * A_BYTES + (pg >> 3) * ATOM;
+        const int chunk = pg & 7;
+        auto prow = [&](int c) { return *reinterpret_cast<const uint4*>(pbox + c * 128 + ((chunk ^ (c & 7)) << 4)); };
+        float x0[8];
+        {
+          const uint4 v = prow(0);
+          const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            x0[2 * e] = bf_lo(u[e]);
+            x0[2 * e + 1] = bf_hi(u[e]);
+          }
         }
-        const float md = s * (1.0f / C);
-        stats[2 * C + pos] = x0 + md;
-        stats[3 * C + pos] = rsqrtf(fmaxf(q * (1.0f / C) - md * md, 0.f) + 1e-5f);
+        float s8[8], q8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s8[e] = q8[e] = 0.f;
+#pragma unroll 4
+        for (int c = 16 * cg; c < 16 * cg + 16; ++c) {
+          const uint4 v = prow(c);
+          const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float d0 = bf_lo(u[e]) - x0[2 * e], d1 = bf_hi(u[e]) - x0[2 * e + 1];
+            s8[2 * e] += d0;
+            s8[2 * e + 1] += d1;
+            q8[2 * e] = fmaf(d0, d0, q8[2 * e]);
+            q8[2 * e + 1] = fmaf(d1, d1, q8[2 * e + 1]);
+          }
+        }
+        float* part = reinterpret_cast<float*>(smem + OFF_PART) + st * 8 * 2 * C + cg * 2 * C;
+        *reinterpret_cast<float4*>(part + 8 * pg) = make_float4(s8[0], s8[1], s8[2], s8[3]);
+        *reinterpret_cast<float4*>(part + 8 * pg + 4) = make_float4(s8[4], s8[5], s8[6], s8[7]);
+        *reinterpret_cast<float4*>(part + C + 8 * pg) = make_float4(q8[0], q8[1], q8[2], q8[3]);
+        *reinterpret_cast<float4*>(part + C + 8 * pg + 4) = make_float4(q8[4], q8[5], q8[6], q8[7]);
+        asm volatile("bar.sync 1, 128;" ::: "memory");   // the four statistics warps
+        const float* pall = reinterpret_cast<const float*>(smem + OFF_PART) + st * 8 * 2 * C;
+        float ss = 0.f, qq = 0.f;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          ss += pall[g * 2 * C + pos];
+          qq += pall[g * 2 * C + C + pos];
+        }
+        // the shift of column pos is its own channel-0 value
+        const float x0p = __bfloat162float(*reinterpret_cast<const bf16*>(
+            smem + OFF_P + st * A_BYTES + (pos >> 6) * ATOM + ((((pos & 63) >> 3) ^ 0) << 4) + (pos & 7) * 2));
+        const float md = ss * (1.0f / C);
+        stats[2 * C + pos] = x0p + md;
+        stats[3 * C + pos] = rsqrtf(fmaxf(qq * (1.0f / C) - md * md, 0.f) + 1e-5f);
       }
       tc::mbar_arrive(&pfree[st]);
       tc::mbar_arrive(&sfull[st]);
@@ -223,14 +260,25 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
           uint4* zp = reinterpret_cast<uint4*>(zrow + tc::sw128_off(pos, 2 * k + h2));
           const uint4 zz = *zp;
           const uint32_t zu[4] = {zz.x, zz.y, zz.z, zz.w};
+          // the folded-norm vectors of these 8 channels, 16-byte loads (the same for every lane)
+          const int c0 = 16 * k + 8 * h2;
+          float vs[4][8];
+          const float* srcv[4] = {sg, bg, so, bo};
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            const float4 a = *reinterpret_cast<const float4*>(srcv[v4] + c0);
+            const float4 b = *reinterpret_cast<const float4*>(srcv[v4] + c0 + 4);
+            vs[v4][0] = a.x; vs[v4][1] = a.y; vs[v4][2] = a.z; vs[v4][3] = a.w;
+            vs[v4][4] = b.x; vs[v4][5] = b.y; vs[v4][6] = b.z; vs[v4][7] = b.w;
+          }
           uint32_t o[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int j = 8 * h2 + 2 * e, c = 16 * k + j;
-            const float g0 = fmaf(rz, fmaf(-mz, sg[c], g[j]), bg[c]);
-            const float g1 = fmaf(rz, fmaf(-mz, sg[c + 1], g[j + 1]), bg[c + 1]);
-            const float u0 = fmaf(rp, fmaf(-mp, so[c], u[j]), bo[c]);
-            const float u1 = fmaf(rp, fmaf(-mp, so[c + 1], u[j + 1]), bo[c + 1]);
+            const int j = 8 * h2 + 2 * e, c = 2 * e;
+            const float g0 = fmaf(rz, fmaf(-mz, vs[0][c], g[j]), vs[1][c]);
+            const float g1 = fmaf(rz, fmaf(-mz, vs[0][c + 1], g[j + 1]), vs[1][c + 1]);
+            const float u0 = fmaf(rp, fmaf(-mp, vs[2][c], u[j]), vs[3][c]);
+            const float u1 = fmaf(rp, fmaf(-mp, vs[2][c + 1], u[j + 1]), vs[3][c + 1]);
             o[e] = pack_bf2(fmaf(u0, sigmoid_tanh(g0), bf_lo(zu[e])), fmaf(u1, sigmoid_tanh(g1), bf_hi(zu[e])));
           }
           *zp = make_uint4(o[0], o[1], o[2], o[3]);
