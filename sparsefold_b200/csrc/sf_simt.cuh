@@ -183,8 +183,10 @@ constexpr int ATT_KPS = ATT_KT / ATT_NS;            // keys of a tile handled by
 // split's 16 keys, takes their max, rescales its running state once per tile and
 // spends one exp per key; the eight split states of a query are merged through
 // shared memory at the end.
+// Head dims up to 32 fit in 128 registers, which lets two blocks share an SM (with 256
+// blocks for a 512-token, 16-head call, one block per SM left it two latency-bound waves).
 template <typename T, typename TB, int DK, int DM>
-__global__ void __launch_bounds__(ATT_NS * 32) k_attention(sf_attention_args a) {
+__global__ void __launch_bounds__(ATT_NS * 32, (DM > 0 && DM <= 32) ? 2 : 1) k_attention(sf_attention_args a) {
   extern __shared__ float4 att_smem4[];
   float* att_smem = reinterpret_cast<float*>(att_smem4);
   const int D = DK > 0 ? DK : (int)a.head_dim;
