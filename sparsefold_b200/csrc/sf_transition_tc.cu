@@ -34,8 +34,9 @@ constexpr int H_BYTES = TILE * HC * 2;         // one 128 x 32 hidden tile (8 KB
 constexpr int W1C_BYTES = 2 * 64 * 128;        // 64 rows (32 a + 32 b) x 128 k, two 64-channel atoms
 constexpr int W2C_BYTES = C * HC * 2;          // 128 out rows x 32 k (64B swizzle)
 constexpr int OFF_X = 0;
-constexpr int OFF_H = OFF_X + X_BYTES;                       // [2 buffers][2 tiles]
-constexpr int OFF_W1 = OFF_H + 4 * H_BYTES;                  // [stage]
+constexpr int HBUF = 3;                                      // hidden tiles in flight
+constexpr int OFF_H = OFF_X + X_BYTES;                       // [HBUF buffers][2 tiles]
+constexpr int OFF_W1 = OFF_H + HBUF * 2 * H_BYTES;           // [stage]
 constexpr int OFF_W2 = OFF_W1 + W1_STAGES * W1C_BYTES;       // [stage]
 constexpr int OFF_LNP = OFF_W2 + W2_STAGES * W2C_BYTES;      // LayerNorm scale [128] and shift [128], fp32
 constexpr int OFF_BAR = OFF_LNP + 2 * C * 4;
@@ -72,9 +73,9 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   uint64_t* w2free = w2full + W2_STAGES;
   uint64_t* s1full = w2free + W2_STAGES;         // [2 buffers][2 tiles]
   uint64_t* s1free = s1full + 4;                 // [2 buffers][2 tiles] (4 warps)
-  uint64_t* hfull = s1free + 4;                  // [2] (8 warps)
-  uint64_t* hfree = hfull + 2;                   // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hfree + 2);
+  uint64_t* hfull = s1free + 4;                  // [HBUF] (8 warps)
+  uint64_t* hfree = hfull + HBUF;                // [HBUF]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hfree + HBUF);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t npasses = (p.M + 2 * TILE - 1) / (2 * TILE);
   float* lnp = reinterpret_cast<float*>(smem + OFF_LNP);
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       tc::mbar_init(&s1full[s], 1);
       tc::mbar_init(&s1free[s], 4);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < HBUF; ++s) {
       tc::mbar_init(&hfull[s], 8);
       tc::mbar_init(&hfree[s], 1);
     }
@@ -185,14 +186,14 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       uint32_t q = 0, pi = 0;
       for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
-          const int st = q % W2_STAGES, hb = q & 1;
+          const int st = q % W2_STAGES, hb = q % HBUF;
           // chunk q-1+W2_STAGES into the stage of chunk q-1 once its GEMM2 is done (it usually is)
           if (q >= 1 && q - 1 + W2_STAGES < total) {
             tc::mbar_wait(&w2free[(q - 1) % W2_STAGES], ((q - 1) / W2_STAGES) & 1, p.status, aborted);
             load_w2(q - 1 + W2_STAGES);
           }
           if (hc == 0 && pi >= 1) tc::mbar_wait(accfree, (pi - 1) & 1, p.status, aborted);
-          tc::mbar_wait(&hfull[hb], (q >> 1) & 1, p.status, aborted);
+          tc::mbar_wait(&hfull[hb], (q / HBUF) & 1, p.status, aborted);
           tc::mbar_wait(&w2full[st], (q / W2_STAGES) & 1, p.status, aborted);
           tc::tc_fence_after();
           const uint32_t w2 = sb + OFF_W2 + st * W2C_BYTES;
@@ -231,9 +232,10 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
         }
         tc::mbar_wait(&s1full[sbuf * 2 + t2], (q >> 1) & 1, p.status, aborted);
         tc::tc_fence_after();
-        float a[HC], bv[HC];
-        tc::tmem_ld32(lane_addr + sbuf * 128 + t2 * 64, a);
-        tc::tmem_ld32(lane_addr + sbuf * 128 + t2 * 64 + HC, bv);
+        float ab[2 * HC];   // a (swish input) then b, adjacent columns: one load, one wait
+        tc::tmem_ld64(lane_addr + sbuf * 128 + t2 * 64, ab);
+        const float* a = ab;
+        const float* bv = ab + HC;
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&s1free[sbuf * 2 + t2]);
@@ -242,15 +244,16 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
         for (int e = 0; e < HC / 2; ++e)
           hv[e] = pack_bf2(a[2 * e] * sigmoid_tanh(a[2 * e]) * bv[2 * e],
                            a[2 * e + 1] * sigmoid_tanh(a[2 * e + 1]) * bv[2 * e + 1]);
-        if (q >= 2) tc::mbar_wait(&hfree[sbuf], ((q >> 1) + 1) & 1, p.status, aborted);
-        uint8_t* hrow = smem + OFF_H + (sbuf * 2 + t2) * H_BYTES;
+        const int hbuf = q % HBUF;
+        if (q >= HBUF) tc::mbar_wait(&hfree[hbuf], ((q / HBUF) + 1) & 1, p.status, aborted);
+        uint8_t* hrow = smem + OFF_H + (hbuf * 2 + t2) * H_BYTES;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           *reinterpret_cast<uint4*>(hrow + tc::sw64_off(r, c)) =
               make_uint4(hv[4 * c], hv[4 * c + 1], hv[4 * c + 2], hv[4 * c + 3]);
         tc::fence_proxy_async();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&hfull[sbuf]);
+        if (lane == 0) tc::mbar_arrive(&hfull[hbuf]);
       }
       // ---- residual epilogue: y = x + acc (the x row was prefetched during the last chunks), one
       // 64-channel half at a time staged in the free hidden buffers (16 KB per tile, 128B swizzle)
