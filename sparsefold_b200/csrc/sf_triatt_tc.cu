@@ -379,6 +379,7 @@ constexpr int OFF_BAR = OFF_KBITS + MAX_QP / 8;
 constexpr int SMEM_CORE = OFF_BAR + 1024 + 1024;
 static_assert(SMEM_CORE <= 232448, "attention core shared memory");
 constexpr float kRescale = 8.0f;       // the running max moves only when a block exceeds it by 2^8
+constexpr float kSumLimit = 256.0f;    // a block sum up to 2^8 leaves the running max where it is
 constexpr int CORE_THREADS = (16 + 4) * 32;   // four softmax warpgroups + one issue warp per head
 
 // (a0, a1) += (b0, b1) as one packed fp32x2 add.
@@ -417,10 +418,11 @@ __device__ __forceinline__ float ex2(float x) {
 // keys] tile and each thread adds its query's row on the CUDA cores: logit2 =
 // S scale + bias'.  Per block j a warpgroup reads S_j and its bias row, sets
 // masked and padding keys to -inf and forms 2^(logit2 - m) against the running
-// max m while it tracks the block max in the same pass (exponentials and
-// CUDA-core work interleave); when the block max exceeds m by more than 2^8 the
-// block's values are rescaled (or, past 2^64, recomputed) and O is rescaled in
-// TMEM once P_{j-1} V_{j-1} is done.  It writes P_j as bf16 and signals it.
+// max m, summing and packing them in the same pass; no value exceeds the block's
+// sum, so while that sum stays <= 2^8 the running max stands, and otherwise the
+// block max is taken from S and the bias (the max moves when the block max
+// exceeds m by more than 2^8, the values are redone and O is rescaled in TMEM
+// once P_{j-1} V_{j-1} is done).  It writes P_j as bf16 and signals it.
 // One issue warp per head (warps 16-19; an issuing warp gets one tcgen05.mma
 // per ~130 cycles, which must not sit on the softmax warps) then issues
 // O += P_j V_j and S_{j+2} into the same buffer (MMAs of one thread run in issue
@@ -670,13 +672,10 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
           for (int e = 0; e < KB; ++e) sv[e] = ex2(sv[e] - mu);
           m_run = mx;
         } else {
-          // exponentials against the running max (+inf while no key has counted: all 0) while the
-          // block max is tracked
+          // exponentials against the running max (+inf while no key has counted: all 0)
           const float m_spec = m_run == -INFINITY ? INFINITY : m_run;
 #pragma unroll
           for (int e = 0; e < KB; e += 4) {
-            ma = tc::fmax3(ma, sv[e], sv[e + 1]);
-            mb = tc::fmax3(mb, sv[e + 2], sv[e + 3]);
             float d0 = sv[e], d1 = sv[e + 1], d2 = sv[e + 2], d3 = sv[e + 3];
             add_f32x2(d0, d1, -m_spec, -m_spec);
             add_f32x2(d2, d3, -m_spec, -m_spec);
@@ -691,12 +690,21 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
             pk[(e >> 1) + 1] = pack_bf2(sv[e + 2], sv[e + 3]);
           }
           packed = true;
-          const float mx = fmaxf(ma, mb);
-          const bool moves = mx > m_run + kRescale;          // also the first finite block after -inf
-          const bool redo = moves && !(mx <= m_run + 64.f);  // values up to 2^(mx - m) could overflow
-          if (__any_sync(0xffffffffu, redo)) {
-            // recompute the whole warp's values from S and the bias tile
+          // No exponential exceeds the block's sum: while that sum stays <= 2^8 the running max
+          // stands, and no per-key max is needed.  A larger (or infinite, or NaN) sum, or a row
+          // with no key counted yet, takes the exact path: the block max from S and the bias,
+          // the running max moved when the block max exceeds it by more than 2^8, values redone.
+          const float tot = (ps0 + ps1) + (ps2 + ps3);
+          const bool exact = !(tot <= kSumLimit) || m_run == -INFINITY;
+          if (__any_sync(0xffffffffu, exact)) {   // warp-uniform: tcgen05.ld is warp-collective
             load_logits();
+#pragma unroll
+            for (int e = 0; e < KB; e += 4) {
+              ma = tc::fmax3(ma, sv[e], sv[e + 1]);
+              mb = tc::fmax3(mb, sv[e + 2], sv[e + 3]);
+            }
+            const float mx = fmaxf(ma, mb);
+            const bool moves = mx > m_run + kRescale;   // also the first finite block after -inf
             const float mr = moves ? mx : (m_run == -INFINITY ? 0.f : m_run);
 #pragma unroll
             for (int e = 0; e < KB; ++e) sv[e] = ex2(sv[e] - mr);
@@ -704,12 +712,6 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
               corr = ex2(m_run - mx);
               m_run = mx;
             }
-            packed = false;
-          } else if (moves) {
-            corr = ex2(m_run - mx);
-#pragma unroll
-            for (int e = 0; e < KB; ++e) sv[e] *= corr;
-            m_run = mx;
             packed = false;
           }
         }
