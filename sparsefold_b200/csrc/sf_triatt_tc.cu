@@ -422,7 +422,8 @@ __device__ __forceinline__ float ex2(float x) {
 // sum, so while that sum stays <= 2^8 the running max stands, and otherwise the
 // block max is taken from S and the bias (the max moves when the block max
 // exceeds m by more than 2^8, the values are redone and O is rescaled in TMEM
-// once P_{j-1} V_{j-1} is done).  It writes P_j as bf16 and signals it.
+// once P_{j-1} V_{j-1} is done).  It writes P_j as bf16 and signals it at the
+// start of the next block, once that block's S wait has covered the store.
 // One issue warp per head (warps 16-19; an issuing warp gets one tcgen05.mma
 // per ~130 cycles, which must not sit on the softmax warps) then issues
 // O += P_j V_j and S_{j+2} into the same buffer (MMAs of one thread run in issue
@@ -628,6 +629,14 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
       // S_j is written and block j (its bias tile) has landed
       tc::mbar_wait(&sbar[g * 2 + (j & 1)], (j >> 1) & 1, p.status, aborted);
       tc::tc_fence_after();
+      // P_{j-1}, stored at the end of the previous block, is signalled only now: its store
+      // latency overlaps the wait above
+      if (j >= 1) {
+        tc::tmem_wait_st();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&pready[g * 2 + ((j - 1) & 1)]);
+      }
       if (j == nkb - 2) asm volatile("prefetch.global.L2 [%0];" ::"l"(grow));   // the gate row for the epilogue
       float sv[KB];
       float corr = 1.f;
@@ -744,11 +753,11 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
         tc::tmem_st32(lane_addr + o_col, r);
       }
       tc::tmem_st16(lane_addr + s_col + (j & 1) * KB, pk);
-      tc::tmem_wait_st();
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&pready[g * 2 + (j & 1)]);
     }
+    tc::tmem_wait_st();
+    tc::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&pready[g * 2 + ((nkb - 1) & 1)]);
 
     // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) in the last bias slot ----
     uint4 graw[D / 8];
