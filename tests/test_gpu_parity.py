@@ -197,3 +197,23 @@ def test_larger_block_bf16():
   zr, sr = orc.pairformer_block(z.to(dt).float(), s.to(dt).float(), mask, _round(p, dt))
   assert max_rel_err(zo.float().cpu(), zr) < 2e-2
   assert max_rel_err(so.float().cpu(), sr) < 2e-2
+
+
+@pytest.mark.parametrize("op", ["tri_att_start", "tri_att_end"])
+def test_triangle_attention_wide_logits_bf16(op):
+  """Query/key and pair-bias weights scaled up so each row's logits span tens of units: later
+  key blocks exceed the running max by more than 2^8 and block sums pass 2^8, which sends the
+  attention core through its exact path (block max from S and the bias, running max moved,
+  O rescaled).  Same bf16 tolerance as every other parity test."""
+  n, n_real = 200, 187
+  z, _, mask = synth.pair_inputs(n, n_real=n_real, seed=21)
+  m = _make(op)
+  p = synth.init_params(m, seed=13)
+  for name in ("q_projection.weight", "k_projection.weight", "pair_bias_projection.weight"):
+    p[name] = p[name] * 2.0
+  m = _native_module(op, p)
+  dt = torch.bfloat16
+  got = _run(m, op, z.to(dt).cuda(), mask.cuda())
+  ref = _oracle(op, _round(p, dt), z.to(dt).float(), mask)
+  assert max_rel_err(got.float().cpu(), ref) < TOL[dt]
+  assert _native.device_status() == 0
