@@ -250,19 +250,74 @@ __global__ void __launch_bounds__(ATT_NS * 32, (DM > 0 && DM <= 32) ? 2 : 1) k_a
   float mrun = -INFINITY, lrun = 0.f;
   for (int64_t k0 = 0; k0 < a.k_len; k0 += ATT_KT) {
     const int kn = (a.k_len - k0) < ATT_KT ? (int)(a.k_len - k0) : ATT_KT;
-    for (int r = warp; r < kn; r += ATT_NS) {         // one key row per warp, lanes along d
-      const T* kr = kp + (k0 + r) * a.k_sk;
-      const T* vr = vp + (k0 + r) * a.v_sk;
-      for (int c = lane; c < D; c += 32) {
-        ks[r * D + c] = ld(kr + c);
-        vs[r * D + c] = ld(vr + c);
+    // With 16-bit K/V (head dim a multiple of 8) and 16-byte aligned rows, every thread first
+    // issues all its 16-byte loads of the tile, then converts and stores them.
+    constexpr bool CHUNKED = DK > 0 && DK % 8 == 0 && sizeof(T) == 2;
+    constexpr int NT = ATT_NS * 32;
+    const bool kv_chunked =
+        CHUNKED && ((reinterpret_cast<uintptr_t>(kp) | reinterpret_cast<uintptr_t>(vp) | (uintptr_t)(a.k_sk * 2) |
+                     (uintptr_t)(a.v_sk * 2)) & 15) == 0;
+    if (kv_chunked) {
+      constexpr int CPR = DK > 0 ? DK / 8 : 1, KVC = ATT_KT * CPR, PER = (2 * KVC + NT - 1) / NT;
+      uint4 buf[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = threadIdx.x + i * NT, w = e / KVC, rem = e - w * KVC, r = rem / CPR, c = rem - r * CPR;
+        if (e < 2 * KVC && r < kn)
+          buf[i] = __ldg(reinterpret_cast<const uint4*>((w ? vp + (k0 + r) * a.v_sk : kp + (k0 + r) * a.k_sk) + 8 * c));
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = threadIdx.x + i * NT, w = e / KVC, rem = e - w * KVC, r = rem / CPR, c = rem - r * CPR;
+        if (e < 2 * KVC && r < kn) {
+          float4* dst = reinterpret_cast<float4*>((w ? vs : ks) + r * D + 8 * c);
+          dst[0] = make_float4(__uint_as_float(buf[i].x << 16), __uint_as_float(buf[i].x & 0xffff0000u),
+                               __uint_as_float(buf[i].y << 16), __uint_as_float(buf[i].y & 0xffff0000u));
+          dst[1] = make_float4(__uint_as_float(buf[i].z << 16), __uint_as_float(buf[i].z & 0xffff0000u),
+                               __uint_as_float(buf[i].w << 16), __uint_as_float(buf[i].w & 0xffff0000u));
+        }
+      }
+    } else {
+      for (int r = warp; r < kn; r += ATT_NS) {         // one key row per warp, lanes along d
+        const T* kr = kp + (k0 + r) * a.k_sk;
+        const T* vr = vp + (k0 + r) * a.v_sk;
+        for (int c = lane; c < D; c += 32) {
+          ks[r * D + c] = ld(kr + c);
+          vs[r * D + c] = ld(vr + c);
+        }
       }
     }
     if (bbase) {
-      for (int qq = warp; qq < ATT_QB; qq += ATT_NS) {
-        if (q0 + qq >= a.q_len) continue;
-        const TB* br = bbase + (q0 + qq) * a.b_sq + k0;
-        for (int k = lane; k < kn; k += 32) bs[qq * (ATT_KT + 1) + k] = ld(br + k);
+      const bool b_chunked = sizeof(TB) == 2 && kn % 8 == 0 &&
+                             ((reinterpret_cast<uintptr_t>(bbase) | (uintptr_t)(a.b_sq * 2)) & 15) == 0;
+      if (b_chunked) {   // the bias tile the same way, 8 keys per 16-byte load
+        constexpr int CPQ = ATT_KT / 8, BC = ATT_QB * CPQ, BPER = (BC + NT - 1) / NT;
+        uint4 bb[BPER];
+#pragma unroll
+        for (int i = 0; i < BPER; ++i) {
+          const int e = threadIdx.x + i * NT, qq = e / CPQ, k = 8 * (e - qq * CPQ);
+          if (e < BC && q0 + qq < a.q_len && k < kn)
+            bb[i] = __ldg(reinterpret_cast<const uint4*>(bbase + (q0 + qq) * a.b_sq + k0 + k));
+        }
+#pragma unroll
+        for (int i = 0; i < BPER; ++i) {
+          const int e = threadIdx.x + i * NT, qq = e / CPQ, k = 8 * (e - qq * CPQ);
+          if (e < BC && q0 + qq < a.q_len && k < kn) {
+            float* dst = bs + qq * (ATT_KT + 1) + k;
+            const uint32_t u[4] = {bb[i].x, bb[i].y, bb[i].z, bb[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              dst[2 * j] = __uint_as_float(u[j] << 16);
+              dst[2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+            }
+          }
+        }
+      } else {
+        for (int qq = warp; qq < ATT_QB; qq += ATT_NS) {
+          if (q0 + qq >= a.q_len) continue;
+          const TB* br = bbase + (q0 + qq) * a.b_sq + k0;
+          for (int k = lane; k < kn; k += 32) bs[qq * (ATT_KT + 1) + k] = ld(br + k);
+        }
       }
     }
     for (int r = threadIdx.x; r < kn; r += blockDim.x)
