@@ -1,12 +1,11 @@
 // Pair-logit projection of SingleActUpdate (blocks.py:745-749), bf16 track, on tcgen05:
 //   logits[h][m] = LN(z[m]) . W[h],   z [M][128], W [heads <= 16][128], logits [heads][M].
 //
-// One CTA (8 warps) per 128-position tile, several CTAs per SM: TMA brings the z
-// tile (128B swizzle), two threads per row layer-norm it in place (rounded to
+// One CTA (4 warps) per 128-position tile, several CTAs per SM: TMA brings the z
+// tile (128B swizzle), each thread layer-norms its row in place (rounded to
 // bf16 as the reference does before the projection), one thread issues 8
-// tcgen05.mma (M128 N16 K16) against the 16-row weight tile, and each thread of
-// warps 0-3 reads its row's 16 logits from TMEM and writes them head-major
-// (coalesced per head).
+// tcgen05.mma (M128 N16 K16) against the 16-row weight tile, and each thread
+// reads its 16 logits from TMEM and writes them head-major (coalesced per head).
 #include "sf_pair_tc.cuh"
 
 namespace sf {
@@ -28,7 +27,7 @@ struct PlParams {
   uint32_t* status;
 };
 
-__global__ void __launch_bounds__(256) k_pair_logits_tc(const __grid_constant__ CUtensorMap tmZ, PlParams p) {
+__global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ CUtensorMap tmZ, PlParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* ldbar = reinterpret_cast<uint64_t*>(smem + OFF_PLBAR);
@@ -50,21 +49,22 @@ __global__ void __launch_bounds__(256) k_pair_logits_tc(const __grid_constant__ 
     tc::tma_load_2d(smem + OFF_PLZ + ATOM, &tmZ, ldbar, 64, (int)m0);
   }
   // weight rows h < heads, zero rows after: K-major, 128B swizzle, atom ka at ka * 16 rows * 128 B
-  for (int e = tid; e < PL_HEADS * 16; e += 256) {
+  for (int e = tid; e < PL_HEADS * 16; e += 128) {
     const int r = e >> 4, kc = e & 15;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (r < p.heads) v = __ldg(reinterpret_cast<const uint4*>(p.w + (size_t)r * C + kc * 8));
     *reinterpret_cast<uint4*>(smem + OFF_PLW + (kc >> 3) * (PL_HEADS * 128) + tc::sw128_off(r, kc & 7)) = v;
   }
   float* lnp = reinterpret_cast<float*>(smem + OFF_PLLN);   // LayerNorm scale and shift
-  lnp[tid] = tid < C ? p.ln_w[tid] : (p.ln_b ? p.ln_b[tid - C] : 0.f);
+  lnp[tid] = p.ln_w[tid];
+  lnp[C + tid] = p.ln_b ? p.ln_b[tid] : 0.f;
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   bool aborted = false;
   tc::mbar_wait(ldbar, 0, p.status, aborted);
-  ln_half_row_shifted(smem + OFF_PLZ, tid >> 1, tid & 1, lnp, lnp + C, 1e-5f);
+  ln_row_shifted(smem + OFF_PLZ, tid, lnp, lnp + C, 1e-5f);
   tc::fence_proxy_async();
   tc::tc_fence_before();
   __syncthreads();
@@ -82,15 +82,13 @@ __global__ void __launch_bounds__(256) k_pair_logits_tc(const __grid_constant__ 
   }
   tc::mbar_wait(mmabar, 0, p.status, aborted);
   tc::tc_fence_after();
-  if (warp < 4) {
-    float v[16];
-    tc::tmem_ld16(tbase + ((uint32_t)(32 * warp) << 16), v);
-    const int64_t m = m0 + tid;
-    if (m < p.M) {
+  float v[16];
+  tc::tmem_ld16(tbase + ((uint32_t)(32 * warp) << 16), v);
+  const int64_t m = m0 + tid;
+  if (m < p.M) {
 #pragma unroll
-      for (int h = 0; h < PL_HEADS; ++h)
-        if (h < p.heads) p.logits[(int64_t)h * p.M + m] = __float2bfloat16_rn(v[h]);
-    }
+    for (int h = 0; h < PL_HEADS; ++h)
+      if (h < p.heads) p.logits[(int64_t)h * p.M + m] = __float2bfloat16_rn(v[h]);
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -127,7 +125,7 @@ int pair_logits_tc(const bf16* z, const float* ln_w, const float* ln_b, const bf
     attr[dev & 63] = true;
   }
   PlParams pp{ln_w, ln_b, w, logits, M, heads, status};
-  k_pair_logits_tc<<<(unsigned)((M + TILE - 1) / TILE), 256, SMEM_PL, stream>>>(mz, pp);
+  k_pair_logits_tc<<<(unsigned)((M + TILE - 1) / TILE), 128, SMEM_PL, stream>>>(mz, pp);
   count_launch();
   return check_launch("pair_logits_tc");
 }

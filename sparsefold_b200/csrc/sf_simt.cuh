@@ -39,54 +39,10 @@ __global__ void k_layernorm(const Tin* __restrict__ x, Tout* __restrict__ y,
   }
 }
 
-// The same layer norm with the row held in registers (cols a multiple of 32, at most 32 * VPL):
-// one read of the row instead of three, the same summation order, so the same results.
-template <typename Tin, typename Tout, int VPL>
-__global__ void k_layernorm_reg(const Tin* __restrict__ x, Tout* __restrict__ y, const float* __restrict__ w,
-                                const float* __restrict__ b, int64_t rows, int cols, float eps) {
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const int nv = cols / 32;
-  const Tin* xr = x + row * cols;
-  float xv[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) xv[i] = i < nv ? ld(xr + lane + 32 * i) : 0.f;
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) s += xv[i];
-  const float mean = warp_sum(s) / cols;
-  float v = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i)
-    if (i < nv) {
-      const float d = xv[i] - mean;
-      v += d * d;
-    }
-  const float rstd = rsqrtf(warp_sum(v) / cols + eps);
-  Tout* yr = y + row * cols;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i)
-    if (i < nv) {
-      const int c = lane + 32 * i;
-      float o = (xv[i] - mean) * rstd;
-      if (w) o *= w[c];
-      if (b) o += b[c];
-      st(yr + c, o);
-    }
-}
-
 template <typename Tin, typename Tout>
 inline int launch_layernorm(const Tin* x, Tout* y, const float* w, const float* b, int64_t rows,
                             int cols, float eps, cudaStream_t s) {
   if (rows == 0) return SF_OK;
-  if (cols % 32 == 0 && cols <= 512) {
-    constexpr int warps = 4;
-    k_layernorm_reg<Tin, Tout, 16><<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, s>>>(x, y, w, b, rows,
-                                                                                                 cols, eps);
-    count_launch();
-    return check_launch("layernorm");
-  }
   int warps = 8;
   k_layernorm<Tin, Tout><<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, s>>>(x, y, w, b, rows, cols, eps);
   count_launch();
