@@ -77,6 +77,8 @@ int make_2d_tmap(CUtensorMap* map, const void* base, int64_t inner, int64_t oute
                  uint32_t box_outer, int swizzle_bytes = 128);
 int pair_logits_tc(const bf16* z, const float* ln_w, const float* ln_b, const bf16* w, bf16* logits, int64_t M,
                    int heads, cudaStream_t stream);
+int pair_rows_bias_tc(const bf16* z, int64_t rows, int64_t n, const float* ln_w, const bf16* w, int heads, float scale,
+                      bf16* bias, int64_t ldb, cudaStream_t stream);
 int transition_tc(const bf16* x, const float* ln_w, const float* ln_b, const bf16* w1, const bf16* w2, bf16* y,
                   int64_t M, cudaStream_t stream);
 int trimul_output_tc(const bf16* z, const bf16* P, int64_t rows, int64_t n, const float* ln_w, const float* ln_b,

@@ -25,6 +25,8 @@ struct PlParams {
   int64_t M;
   int heads;
   uint32_t* status;
+  int64_t ncols, ldb;   // ldb > 0: position m = r * ncols + s goes to logits[(r * heads + h) * ldb + s]
+  float scale;          // ... times scale
 };
 
 __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ CUtensorMap tmZ, PlParams p) {
@@ -86,9 +88,16 @@ __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ 
   tc::tmem_ld16(tbase + ((uint32_t)(32 * warp) << 16), v);
   const int64_t m = m0 + tid;
   if (m < p.M) {
+    if (p.ldb > 0) {
+      const int64_t r = m / p.ncols, sc = m - r * p.ncols;
 #pragma unroll
-    for (int h = 0; h < PL_HEADS; ++h)
-      if (h < p.heads) p.logits[(int64_t)h * p.M + m] = __float2bfloat16_rn(v[h]);
+      for (int h = 0; h < PL_HEADS; ++h)
+        if (h < p.heads) p.logits[(r * p.heads + h) * p.ldb + sc] = __float2bfloat16_rn(v[h] * p.scale);
+    } else {
+#pragma unroll
+      for (int h = 0; h < PL_HEADS; ++h)
+        if (h < p.heads) p.logits[(int64_t)h * p.M + m] = __float2bfloat16_rn(v[h]);
+    }
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -100,9 +109,10 @@ __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ 
 
 }  // namespace
 
-// logits [heads][M] = LN(z) W^T for z [M][128] bf16, heads <= 16.
-int pair_logits_tc(const bf16* z, const float* ln_w, const float* ln_b, const bf16* w, bf16* logits, int64_t M,
-                   int heads, cudaStream_t stream) {
+// LN(z) W^T for z [M][128] bf16 and heads <= 16: logits [heads][M] (ldb = 0), or, with the
+// positions as rows of ncols, rows [M / ncols][heads][ldb] times scale.
+static int pair_logits_launch(const bf16* z, const float* ln_w, const float* ln_b, const bf16* w, bf16* logits,
+                              int64_t M, int heads, int64_t ncols, int64_t ldb, float scale, cudaStream_t stream) {
   if (M == 0) return SF_OK;
   SF_REQUIRE(heads >= 1 && heads <= PL_HEADS, "pair_logits_tc: %d heads (1..16)", heads);
   SF_REQUIRE(M < (int64_t(1) << 31), "pair_logits_tc: too many positions");
@@ -124,10 +134,25 @@ int pair_logits_tc(const bf16* z, const float* ln_w, const float* ln_b, const bf
     }
     attr[dev & 63] = true;
   }
-  PlParams pp{ln_w, ln_b, w, logits, M, heads, status};
+  PlParams pp{ln_w, ln_b, w, logits, M, heads, status, ncols, ldb, scale};
   k_pair_logits_tc<<<(unsigned)((M + TILE - 1) / TILE), 128, SMEM_PL, stream>>>(mz, pp);
   count_launch();
   return check_launch("pair_logits_tc");
+}
+
+// logits [heads][M] = LN(z) W^T for z [M][128] bf16, heads <= 16.
+int pair_logits_tc(const bf16* z, const float* ln_w, const float* ln_b, const bf16* w, bf16* logits, int64_t M,
+                   int heads, cudaStream_t stream) {
+  return pair_logits_launch(z, ln_w, ln_b, w, logits, M, heads, 1, 0, 1.0f, stream);
+}
+
+// bias [rows][heads][ldb] = scale * LN(z[r][s]) . W[h] for the pair rows z [rows][n][128]: the same
+// kernel with row-major output (the pair bias of a row block for triangle attention).
+int pair_rows_bias_tc(const bf16* z, int64_t rows, int64_t n, const float* ln_w, const bf16* w, int heads, float scale,
+                      bf16* bias, int64_t ldb, cudaStream_t stream) {
+  if (rows == 0 || n == 0) return SF_OK;
+  SF_REQUIRE(ldb >= n, "pair_rows_bias_tc: ldb %lld < n %lld", (long long)ldb, (long long)n);
+  return pair_logits_launch(z, ln_w, nullptr, w, bias, rows * n, heads, n, ldb, scale, stream);
 }
 
 }  // namespace sf

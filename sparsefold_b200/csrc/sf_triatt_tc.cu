@@ -844,39 +844,6 @@ int set_smem(K kernel, int bytes, bool* done) {
   return SF_OK;
 }
 
-// Pair bias of the local pair rows only: bias[(r*H + h)*ldb + s] = LN(z[r,s]) . W_b[h]
-// (blocks.py:317-320), one warp per position.  Used when the attention runs on a
-// transposed block whose own positions are not the rows the bias needs.
-__global__ void k_triatt_bias(const bf16* __restrict__ z, const float* __restrict__ ln_w, const bf16* __restrict__ wb,
-                              bf16* __restrict__ bias, int64_t rows, int64_t n, int64_t ldb) {
-  const int64_t pos = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (pos >= rows * n) return;
-  const bf16* zr = z + pos * C;
-  float x[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) x[e] = __bfloat162float(zr[lane * 4 + e]);
-  const float mean = warp_sum(x[0] + x[1] + x[2] + x[3]) * (1.0f / C);
-  float v = 0.f;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) v += (x[e] - mean) * (x[e] - mean);
-  const float rstd = rsqrtf(warp_sum(v) * (1.0f / C) + 1e-5f);
-  float acc[H] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int c = lane * 4 + e;
-    const float y = __bfloat162float(__float2bfloat16_rn((x[e] - mean) * rstd * ln_w[c]));
-#pragma unroll
-    for (int h = 0; h < H; ++h) acc[h] += y * __bfloat162float(wb[h * C + c]);
-  }
-#pragma unroll
-  for (int h = 0; h < H; ++h) acc[h] = warp_sum(acc[h]);
-  if (lane == 0) {
-    const int64_t r = pos / n, sc = pos % n;
-#pragma unroll
-    for (int h = 0; h < H; ++h) bias[(r * H + h) * ldb + sc] = __float2bfloat16_rn(acc[h] * kBiasScale);
-  }
-}
 
 }  // namespace
 
@@ -884,12 +851,8 @@ int64_t triatt_query_pitch(int64_t nq) { return (nq + 127) / 128 * 128; }
 
 int triatt_bias_tc(const bf16* z, int64_t rows, int64_t n, const float* ln_w, const bf16* w_bias, bf16* bias,
                    int64_t ldb, cudaStream_t stream) {
-  if (rows == 0 || n == 0) return SF_OK;
-  SF_REQUIRE(ldb >= n, "triatt_bias: ldb %lld < n %lld", (long long)ldb, (long long)n);
-  const int64_t total = rows * n;
-  k_triatt_bias<<<(unsigned)((total + 7) / 8), 256, 0, stream>>>(z, ln_w, w_bias, bias, rows, n, ldb);
-  count_launch();
-  return check_launch("triatt_bias");
+  // the pair-logit kernel: scale-only LN in place (rounded to bf16), M128 N16 K128 MMA, row-major stores
+  return pair_rows_bias_tc(z, rows, n, ln_w, w_bias, H, kBiasScale, bias, ldb, stream);
 }
 
 int triatt_project_tc(const bf16* z, int64_t rows, int64_t cols, int transpose, int compute_bias, const float* ln_w,

@@ -217,3 +217,34 @@ def test_triangle_attention_wide_logits_bf16(op):
   ref = _oracle(op, _round(p, dt), z.to(dt).float(), mask)
   assert max_rel_err(got.float().cpu(), ref) < TOL[dt]
   assert _native.device_status() == 0
+
+
+def test_tri_attention_row_bias_bf16():
+  """sf_tri_attention_bias (the pair bias of a block of pair rows, which the ending-node attention of a
+  row shard needs) against the projection's own bias for the same rows and against
+  log2(e) * bf16(LN(z)) . W_b in fp32, on a ragged block."""
+  from sparsefold_b200 import sharding
+  rows, n = 37, 130
+  z = (torch.randn(rows, n, 128, generator=torch.Generator().manual_seed(11)) * 1.5 + 0.3).to(torch.bfloat16)
+  m = _make("tri_att_start")
+  p = synth.init_params(m, seed=5)
+  modules.prepare(m)
+  m = m.cuda()
+  w = m.native_weights(torch.bfloat16)
+  lib = _native.load()
+  qp = int(lib.sf_tri_attention_query_pitch(n))
+  zc = z.cuda()
+  got = torch.zeros(rows, 4, qp, dtype=torch.bfloat16, device="cuda")
+  _native.call("sf_tri_attention_bias", _native.SF_BF16, sharding._p(zc), rows, n, sharding.C.byref(w), sharding._p(got),
+               qp, sharding._stream())
+  _, q, k, vt, g = sharding._att_buffers(rows, n, torch.bfloat16, zc.device)
+  ref_proj = torch.zeros_like(got)
+  _native.call("sf_tri_attention_project", _native.SF_BF16, sharding._p(zc), rows, n, 0, 1, sharding.C.byref(w),
+               sharding._p(q), sharding._p(k), sharding._p(vt), sharding._p(g), sharding._p(ref_proj), sharding._stream())
+  torch.cuda.synchronize()
+  assert _native.device_status() == 0
+  got_v = got[:, :, :n].float().cpu()
+  assert max_rel_err(got_v, ref_proj[:, :, :n].float().cpu()) < 1e-2
+  ln = (torch.nn.functional.layer_norm(z.float(), (128,), eps=1e-5) * p["act_norm.weight"]).to(torch.bfloat16).float()
+  ref = torch.einsum("rsc,ch->rhs", ln, p["pair_bias_projection.weight"].to(torch.bfloat16).float()) * 1.4426950408889634
+  assert max_rel_err(got_v, ref) < TOL[torch.bfloat16]
