@@ -11,9 +11,11 @@ With --gpus N > 1 the pair rows are sharded over the N ranks (NCCL
 all-gathers / all-to-alls as in the reference's distributed blocks) on the same
 workload (strong scaling); --n-token 2048 selects configs[4] (1931 real tokens).
 
-``--impl reference`` times the reference's CPU algorithm (the oracle
-restatement in oracle/pairformer.py of the reference Torch CPU math path) on
-this host's cores, on a bounded sample, and prints the same JSON line.
+``--impl reference`` times the reference's own CPU path (its
+blocks.PairFormerIteration from the package installed under baseline/_ref,
+backend "torch" on the CPU; the oracle restatement oracle/pairformer.py where
+that package is absent) on this host's cores, one exact block of the same
+workload per step, and prints the same JSON line.
 """
 from __future__ import annotations
 
@@ -280,20 +282,15 @@ def run_b200(args) -> None:
   peaks = load_peaks()
   flops = tri_attention_op_flops(N_TOKEN)
   achieved = flops / (probe_ms * 1e-3) / 1e12 if probe_ms > 0 else 0.0
-  cpu = cpu_baseline_sample() if rank == 0 and world == 1 and not args.no_cpu_baseline else None
+  cpu = cpu_baseline_sample(n_tok, n_real) if rank == 0 and world == 1 and not args.no_cpu_baseline else None
   if rank == 0:
     line = {
         "metric": METRIC, "value": round(ms_block, 4), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
         "higher_is_better": False, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) pair/single, random-init AF3-shaped weights)",
-        "config": {"workload": (f"{'configs[1]' if n_tok == 512 else 'configs[4]' if n_tok == 2048 else 'custom'}: "
-                                f"48-block Pairformer trunk, N_token={n_tok} ({n_real} real), c_z=128, c_s=384"),
-                   "n_token": n_tok, "n_real": n_real, "blocks": N_BLOCKS,
-                   "block_gflop": round(block_flops(n_tok) / 1e9, 1),
-                   "trunk_tflop_per_s": round(block_flops(n_tok) / (ms_block * 1e-3) / 1e12, 2),
-                   "l2": "flushed (256 MiB write) before every timed step",
-                   "parallelism": f"pair rows sharded over {world} GPUs (NCCL)" if world > 1 else "single"},
+        "config": workload_config(n_tok, n_real, world),
+        "trunk_tflop_per_s": round(block_flops(n_tok) / (ms_block * 1e-3) / 1e12, 2),
         "e2e": {"value": round(e2e_ms / N_BLOCKS, 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
@@ -316,8 +313,11 @@ def run_b200(args) -> None:
 
 
 # ---------------------------------------------------------------------------
-# CPU side: the reference algorithm (oracle restatement of the Torch CPU math
-# path, oracle/pairformer.py) on this host's cores.
+# CPU side: the reference's own PairFormerIteration (the pip-installed package
+# under baseline/_ref, backend "torch" on the CPU with math SDPA: the path the
+# reference runs without a GPU) on this host's cores.  Where that package is
+# absent, the oracle restatement of the same path (oracle/pairformer.py) runs
+# instead and the line says kind "port".
 # ---------------------------------------------------------------------------
 def _cpu_threads() -> int:
   import torch
@@ -326,58 +326,109 @@ def _cpu_threads() -> int:
   return torch.get_num_threads()
 
 
-def _cpu_block_seconds(n: int, repeats: int = 1, warmup: int = 0) -> list:
+def _reference_package() -> bool:
+  """Put the installed reference (baseline/_ref) on sys.path; False when it is not there."""
+  import types
+  src = os.path.join(REPO, "baseline", "_ref")
+  if not os.path.isdir(os.path.join(src, "sparsefold")):
+    return False
+  if src not in sys.path:
+    sys.path.insert(0, src)
+  try:
+    import zstandard  # noqa: F401  (only checkpoint reading uses it)
+  except ImportError:
+    sys.modules["zstandard"] = types.ModuleType("zstandard")
+  return True
+
+
+def cpu_block_runner(n: int, n_real: int):
+  """(run, kind, what): run() is one Pairformer block forward at N=n on the CPU in bf16."""
   import torch
-  from oracle import pairformer as orc
-  from sparsefold_b200 import modules, synth
+  from sparsefold_b200 import synth
   dt = torch.bfloat16
-  blk = modules.PairFormerIteration(C_Z, C_S)
-  p = {k: v.to(dt) for k, v in synth.init_params(blk, seed=0).items()}
-  z, s, mask = synth.pair_inputs(n, C_Z, C_S, n_real=max(1, n * N_REAL // N_TOKEN), seed=0)
+  z, s, mask = synth.pair_inputs(n, C_Z, C_S, n_real=n_real, seed=0)
   z, s = z.to(dt), s.to(dt)
-  out = []
-  with torch.no_grad():
-    for i in range(warmup + repeats):
-      t0 = time.perf_counter()
+  if _reference_package():
+    from sparsefold.runtime import config
+    from sparsefold import backends
+    config.configure_runtime(backend="torch", device="cpu", sdpa_implementation="math", enable_sharding=False,
+                             enable_compile=False, logs=set())
+    backends.init()
+    from sparsefold.model.trunk import blocks, network
+    from sparsefold.model import config as mc
+    blk = blocks.PairFormerIteration(network.Evoformer.Config().pairformer, mc.GlobalConfig(), with_single=True,
+                                     num_channels=C_Z, seq_channels=C_S)
+    synth.init_params(blk, seed=0)
+    blk = blk.to(dt).eval()
+
+    def run():
+      with torch.no_grad():
+        blk(z, seq_mask=mask, single_act=s)
+    return run, "reference", ("the reference's own blocks.PairFormerIteration (baseline/_ref, backend torch, "
+                              "device cpu, math SDPA), bf16 weights and activations")
+  from oracle import pairformer as orc
+  from sparsefold_b200 import modules
+  holder = modules.PairFormerIteration(C_Z, C_S)
+  p = {k: v.to(dt) for k, v in synth.init_params(holder, seed=0).items()}
+
+  def run():
+    with torch.no_grad():
       orc.pairformer_block(z, s, mask, p)
-      if i >= warmup:
-        out.append(time.perf_counter() - t0)
+  return run, "port", "oracle/pairformer.py restatement of the reference Torch CPU math path, bf16 tensors"
+
+
+def _time_cpu(run, steps: int, warmup: int) -> list:
+  out = []
+  for i in range(warmup + steps):
+    t0 = time.perf_counter()
+    run()
+    if i >= warmup:
+      out.append(time.perf_counter() - t0)
   return out
 
 
-def cpu_baseline_sample() -> dict:
-  """One Pairformer block on the host; exact at N=512 when that fits ~30 s, else N=256 scaled by FLOPs."""
+def cpu_baseline_sample(n_tok: int, n_real: int) -> dict:
+  """One exact Pairformer block of the bench workload on the host (after one untimed block)."""
   cores = _cpu_threads()
-  t256 = min(_cpu_block_seconds(256))
-  scale = block_flops(N_TOKEN) / block_flops(256)
-  if t256 * scale <= 30.0:
-    t = min(_cpu_block_seconds(N_TOKEN))
-    sample = "1 Pairformer block at N=512 (oracle port, bf16 tensors), timed exactly"
-  else:
-    t = t256 * scale
-    sample = f"1 Pairformer block at N=256 (oracle port, bf16 tensors), x{scale:.2f} FLOP ratio to N=512"
-  return {"value": round(t * 1e3, 2), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+  run, kind, what = cpu_block_runner(n_tok, n_real)
+  t = min(_time_cpu(run, 1, 1))
+  return {"value": round(t * 1e3, 2), "unit": UNIT, "cores": cores, "kind": kind,
+          "sample": f"1 Pairformer block at N={n_tok} ({n_real} real) timed exactly: {what}"}
+
+
+def workload_config(n_tok: int, n_real: int, world: int) -> dict:
+  """The `config` object both arms print (the driver compares them)."""
+  tag = "configs[1]" if n_tok == 512 else "configs[4]" if n_tok == 2048 else "custom"
+  return {"workload": f"{tag}: 48-block Pairformer trunk, N_token={n_tok} ({n_real} real), c_z=128, c_s=384",
+          "n_token": n_tok, "n_real": n_real, "blocks": N_BLOCKS,
+          "block_gflop": round(block_flops(n_tok) / 1e9, 1),
+          "l2": "b200 arm: flushed (256 MiB write) before every timed step",
+          "parallelism": f"pair rows sharded over {world} GPUs (NCCL)" if world > 1 else "single"}
 
 
 def run_reference(args) -> None:
+  """The reference arm: one exact Pairformer block of the workload per step on the host cores."""
   rank = int(os.environ.get("RANK", "0"))
   world = int(os.environ.get("WORLD_SIZE", "1"))
   if rank != 0:
     return
   cores = _cpu_threads()
-  n_sample = 256
-  times = _cpu_block_seconds(n_sample, repeats=args.steps, warmup=args.warmup)
-  scale = block_flops(N_TOKEN) / block_flops(n_sample)
-  ms_block = statistics.median(times) * scale * 1e3
-  sample = (f"per step 1 Pairformer block at N={n_sample} (oracle port of the reference Torch CPU math path, "
-            f"bf16 tensors), scaled x{scale:.2f} by FLOPs to N=512")
+  n_tok = args.n_token
+  n_real = {512: N_REAL, 2048: 1931}.get(n_tok, n_tok)
+  n_s = args.sample_n or n_tok
+  n_real_s = n_real if n_s == n_tok else max(1, n_s * n_real // n_tok)
+  run, kind, what = cpu_block_runner(n_s, n_real_s)
+  times = _time_cpu(run, args.steps, args.warmup)
+  ms_block = statistics.median(times) * 1e3
+  sample = f"per step 1 Pairformer block at N={n_s} ({n_real_s} real) timed exactly: {what}"
   line = {
       "metric": METRIC, "value": round(ms_block, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-      "warmup": args.warmup, "ms_per_step": round(ms_block * N_BLOCKS, 1), "higher_is_better": False,
-      "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-      "config": {"workload": "configs[1]: 48-block Pairformer trunk, N_token=512 (475 real)", "n_token": N_TOKEN},
+      "warmup": args.warmup, "ms_per_step": round(ms_block, 1), "higher_is_better": False,
+      "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+      "data": "synthetic (seeded N(0,1) pair/single, random-init AF3-shaped weights)",
+      "config": workload_config(n_tok, n_real, 1),
       "impl": "reference",
-      "cpu_baseline": {"value": round(ms_block, 2), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+      "cpu_baseline": {"value": round(ms_block, 2), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
       "e2e": {"value": round(ms_block, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
   }
   print(json.dumps(line), flush=True)
@@ -451,6 +502,8 @@ def main():
   ap.add_argument("--op", choices=OPS, default=None, help="time one op alone instead of the trunk")
   ap.add_argument("--n", type=int, default=N_TOKEN, help="N_token for --op")
   ap.add_argument("--n-token", type=int, default=N_TOKEN, help="N_token of the trunk (512 = configs[1], 2048 = configs[4])")
+  ap.add_argument("--sample-n", type=int, default=None,
+                  help="reference arm only: time blocks of this N instead of the workload's (quick CPU checks)")
   args = ap.parse_args()
   if args.op:
     run_op(args)

@@ -5,8 +5,14 @@
  * counts and a CUDA stream, returns an `int` status (SF_OK == 0), and never
  * throws.  On failure `sf_last_error()` returns a message for the calling
  * thread.  The caller allocates every input, output and workspace buffer; the
- * library allocates and frees nothing and keeps no device state.  Work is
- * enqueued asynchronously on `stream`.
+ * library calls no cudaMalloc or cudaFree.  Its only device state is two
+ * file-scope `__device__` arrays that every GPU loading the library holds
+ * until the process exits: a 4-byte status word per device (see
+ * sf_device_status) and the fixed 16 MiB scratch array of
+ * sf_transition_noalloc (see the notes at that entry point).  Their device
+ * addresses are looked up once per device and cached; calls made after
+ * cudaDeviceReset() on a device are not supported.  Work is enqueued
+ * asynchronously on `stream`.
  *
  * Conventions
  *  - dtype (`SF_F32` / `SF_BF16`) is the element type of the activation

@@ -1,6 +1,7 @@
 // Runtime plumbing of the C ABI: per-thread error messages, launch accounting,
 // device check, version.
 #include <cstring>
+#include <mutex>
 
 #include "sf_common.cuh"
 
@@ -12,6 +13,7 @@ static std::atomic<uint64_t> g_launches{0};
 // waits record a timeout here instead of hanging.
 static __device__ uint32_t g_device_status;
 static uint32_t* g_status_ptr[64] = {nullptr};
+static std::mutex g_status_mu;
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -34,6 +36,7 @@ int check_launch(const char* what) {
 uint32_t* device_status_ptr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_status_mu);
   if (!g_status_ptr[dev]) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_device_status);

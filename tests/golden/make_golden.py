@@ -228,5 +228,8 @@ def diffusion_and_msa():
 
 
 if __name__ == "__main__":
-  main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+  src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPARSEFOLD_REF_SRC")
+  if not src:
+    raise SystemExit("usage: make_golden.py <path of the reference's src/ directory> (or set SPARSEFOLD_REF_SRC)")
+  main(src)
   diffusion_and_msa()

@@ -1,28 +1,19 @@
 """The b200 backend behind the reference's own plugin API (backends/__init__.py:28-102).
 
-Runs only where the reference source is importable (it is absent on GPU boxes);
-it checks factory replacement, class identity, and that preparing a reference
-PairFormerIteration keeps its state_dict contract.
+Runs only where the reference package is importable ($SPARSEFOLD_REF_SRC or the
+pip-installed copy under baseline/_ref, see tests/refsrc.py); it checks factory
+replacement, class identity, and that preparing a reference PairFormerIteration
+keeps its state_dict contract.
 """
-import os
-import sys
-import types
-
 import pytest
 
-REF_SRC = os.environ.get("SPARSEFOLD_REF_SRC", "/root/reference/src")
+from tests.refsrc import import_reference
 
 
 @pytest.fixture(scope="module")
 def ref():
-  if not os.path.isdir(os.path.join(REF_SRC, "sparsefold")):
-    pytest.skip("reference source tree not present")
-  if REF_SRC not in sys.path:
-    sys.path.insert(0, REF_SRC)
-  try:
-    import zstandard  # noqa: F401
-  except ImportError:
-    sys.modules["zstandard"] = types.ModuleType("zstandard")
+  if import_reference() is None:
+    pytest.skip("reference package not present")
   from sparsefold.runtime import config
   from sparsefold import backends
   import sparsefold_b200.backend as b200

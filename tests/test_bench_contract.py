@@ -10,8 +10,9 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def test_reference_arm_json_line():
-  out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0"],
-                       cwd=REPO, capture_output=True, text=True, timeout=600)
+  # --sample-n keeps the CPU block small here; the driver's run times exact blocks of the workload
+  out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0",
+                        "--sample-n", "64"], cwd=REPO, capture_output=True, text=True, timeout=600)
   assert out.returncode == 0, out.stderr[-2000:]
   lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
   assert len(lines) == 1, out.stdout
@@ -23,6 +24,9 @@ def test_reference_arm_json_line():
   assert d["metric"] == "pairformer_ms_per_block" and d["unit"] == "ms/block"
   assert d["higher_is_better"] is False and d["value"] > 0 and d["steps"] == 1 and d["n_gpus"] == 1
   assert "workload" in d["config"]
+  sys.path.insert(0, REPO)
+  import bench
+  assert d["config"] == bench.workload_config(512, 475, 1)   # the b200 arm prints the same object
   cb = d["cpu_baseline"]
   assert cb["kind"] in ("port", "reference") and cb["cores"] >= 1 and cb["value"] == d["value"] and cb["sample"]
   assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
