@@ -72,6 +72,13 @@ uint64_t sf_launch_count(void);
 /* Reads (and with clear != 0 resets) the current device's status word: 0, or
  * SF_ERR_TIMEOUT when a kernel's bounded wait gave up.  Synchronises the device. */
 int sf_device_status(uint32_t* out, int clear);
+/* Self-test of the bounded device-side wait (no counterpart in the reference: it
+ * exercises this library's failure detection).  Launches one warp that waits on an
+ * mbarrier with a bound of `polls` polls (1 .. 2^22); with arrive == 0 nothing
+ * ever arrives, the wait gives up, the kernel records SF_ERR_TIMEOUT in the status
+ * word read by sf_device_status() and returns.  With arrive != 0 the barrier
+ * completes and the status word is left unchanged. */
+int sf_selftest_wait(uint32_t polls, int arrive, sf_stream_t stream);
 
 /* ---- generic attention: sdpa.py:22-121 ---------------------------------
  * out[b,q,h,:] = softmax_k(scale * q.k + bias[b,h,q,k] + maskbias) @ v
@@ -93,6 +100,7 @@ typedef struct sf_attention_args {
   const uint8_t* mask_row;
   const void* gate; int64_t g_sb, g_sh, g_sq;
   float scale;
+  int64_t value_dim;   /* head dim of v, out and gate; 0 = head_dim (sdpa.py allows Dv != Dqk) */
 } sf_attention_args;
 int sf_attention(const sf_attention_args* args, sf_stream_t stream);
 

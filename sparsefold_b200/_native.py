@@ -34,6 +34,7 @@ class AttentionArgs(C.Structure):
       ("mask_row", _vp),
       ("gate", _vp), ("g_sb", _i64), ("g_sh", _i64), ("g_sq", _i64),
       ("scale", C.c_float),
+      ("value_dim", _i64),
   ]
 
 
@@ -54,6 +55,7 @@ _SIGNATURES = {
     "sf_launch_count": (C.c_uint64, []),
     "sf_pair_pitch": (C.c_int64, [_i64]),
     "sf_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
+    "sf_selftest_wait": (C.c_int, [C.c_uint32, C.c_int, _vp]),
     "sf_attention": (C.c_int, [C.POINTER(AttentionArgs), _vp]),
     "sf_layernorm": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, C.c_float, _vp]),
     "sf_linear": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, C.c_int, _vp]),

@@ -53,7 +53,8 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
   uint64_t* empty = full + STAGES;
   uint64_t* accf = empty + STAGES;
   uint64_t* acce = accf + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  uint64_t* drain = acce + 2;                    // MMA issuer's drain barrier (abort path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   const int64_t mt = (p.rows + BM - 1) / BM, nt = (p.cols + BN - 1) / BN;
@@ -73,6 +74,7 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
       tc::mbar_init(&accf[a], 1);
       tc::mbar_init(&acce[a], 128);
     }
+    tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmA);
     tc::prefetch_tmap(&tmB);
@@ -82,16 +84,17 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
   tc::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   bool aborted = false;
+  uint32_t loads = 0;   // TMA loads issued by the producer (abort-path drain)
 
   if (warp == 4 && lane == 0) {
-    // ---- TMA producer ----
-    uint32_t q = 0;
-    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    // ---- TMA producer (stops at its first failed wait) ----
+    uint32_t& q = loads;
+    for (int64_t t = blockIdx.x; t < ntiles && !aborted; t += gridDim.x) {
       const int64_t c = t / (mt * nt), rem = t % (mt * nt);
       const int i0 = (int)((rem / nt) * BM), j0 = (int)((rem % nt) * BN);
       for (int kb = 0; kb < nk; ++kb, ++q) {
         const int s = q % STAGES;
-        tc::mbar_wait(&empty[s], ((q / STAGES) & 1) ^ 1, p.status, aborted);
+        if (!tc::mbar_wait(&empty[s], ((q / STAGES) & 1) ^ 1, p.status, aborted)) break;
         uint8_t* st = smem + s * STAGE_BYTES;
         tc::mbar_expect_tx(&full[s], STAGE_BYTES);
         // K index -> (chunk, offset in chunk); chunks hold whole 64-wide K blocks
@@ -101,17 +104,17 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
       }
     }
   } else if (warp == 5 && lane == 0) {
-    // ---- MMA issuer ----
+    // ---- MMA issuer (stops at its first failed wait) ----
     constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN);
     const uint32_t sbase = tc::smem_u32(smem);
     uint32_t q = 0, u = 0;
-    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++u) {
+    for (int64_t t = blockIdx.x; t < ntiles && !aborted; t += gridDim.x, ++u) {
       const uint32_t acc = u & 1;
-      tc::mbar_wait(&acce[acc], ((u >> 1) & 1) ^ 1, p.status, aborted);
+      if (!tc::mbar_wait(&acce[acc], ((u >> 1) & 1) ^ 1, p.status, aborted)) break;
       tc::tc_fence_after();
       for (int kb = 0; kb < nk; ++kb, ++q) {
         const int s = q % STAGES;
-        tc::mbar_wait(&full[s], (q / STAGES) & 1, p.status, aborted);
+        if (!tc::mbar_wait(&full[s], (q / STAGES) & 1, p.status, aborted)) break;
         tc::tc_fence_after();
         const uint32_t sa = sbase + s * STAGE_BYTES, sb = sa + SA_BYTES;
 #pragma unroll
@@ -122,6 +125,7 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
         }
         tc::mma_commit(&empty[s]);
       }
+      if (aborted) break;
       tc::mma_commit(&accf[acc]);
     }
   } else if (warp < 4) {
@@ -183,7 +187,12 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
       tc::mbar_arrive(&acce[acc]);
     }
   }
-  __syncthreads();
+  tc::tc_fence_before();
+  if (__syncthreads_or(aborted)) {   // abort path: drain the producer's loads and the issuer's MMAs
+    if (warp == 4 && lane == 0) tc::drain_ring(full, STAGES, loads, p.status);
+    if (warp == 5 && lane == 0) tc::drain_mma(drain, p.status);
+    __syncthreads();
+  }
   if (warp == 0) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tbase, Tile<BN>::TMEM_COLS);

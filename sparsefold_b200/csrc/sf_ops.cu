@@ -327,6 +327,9 @@ int sf_attention(const sf_attention_args* a, sf_stream_t stream) {
   SF_REQUIRE(a && a->q && a->k && a->v && a->out, "sf_attention: null tensor");
   SF_REQUIRE(a->head_dim > 0 && a->head_dim <= ATT_DMAX, "sf_attention: head_dim %lld outside (0, %d]",
              (long long)a->head_dim, ATT_DMAX);
+  SF_REQUIRE(a->value_dim >= 0 && a->value_dim <= ATT_DMAX, "sf_attention: value_dim %lld outside [0, %d]",
+             (long long)a->value_dim, ATT_DMAX);
+  const int dv = a->value_dim > 0 ? (int)a->value_dim : (int)a->head_dim;
   SF_REQUIRE(a->batch >= 0 && a->heads > 0 && a->q_len >= 0 && a->k_len >= 0, "sf_attention: bad sizes");
   SF_REQUIRE(a->batch <= 65535 && a->heads <= 65535, "sf_attention: batch/heads exceed grid limits");
   if (a->batch == 0 || a->q_len == 0) return SF_OK;
@@ -334,13 +337,13 @@ int sf_attention(const sf_attention_args* a, sf_stream_t stream) {
   SF_REQUIRE(!a->bias || a->bias_dtype == SF_F32 || a->bias_dtype == a->dtype, "sf_attention: bias dtype");
   SF_REQUIRE((a->q_len + ATT_QB - 1) / ATT_QB <= 0x7fffffff, "sf_attention: q_len too large");
   dim3 grid((unsigned)((a->q_len + ATT_QB - 1) / ATT_QB), (unsigned)a->heads, (unsigned)a->batch);
-  const size_t smem = attention_smem_bytes((int)a->head_dim);
+  const size_t smem = attention_smem_bytes((int)a->head_dim, dv);
   SF_DISPATCH(a->dtype, {
     const bool f32bias = a->bias && a->bias_dtype == SF_F32;
     using K = void (*)(sf_attention_args);
     // compile-time head dims for the common sizes; the generic kernel takes any D <= 64
     const int hd = (int)a->head_dim;
-    const int di = hd == 16 ? 0 : hd == 24 ? 1 : hd == 32 ? 2 : hd == 48 ? 3 : hd == 64 ? 4 : 5;
+    const int di = dv != hd ? 5 : hd == 16 ? 0 : hd == 24 ? 1 : hd == 32 ? 2 : hd == 48 ? 3 : hd == 64 ? 4 : 5;
     static const K kerns[2][6] = {
         {k_attention<T, T, 16, 16>, k_attention<T, T, 24, 24>, k_attention<T, T, 32, 32>,
          k_attention<T, T, 48, 48>, k_attention<T, T, 64, 64>, k_attention<T, T, 0, 64>},
@@ -351,7 +354,7 @@ int sf_attention(const sf_attention_args* a, sf_stream_t stream) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_done[dev & 63][f32bias ? 1 : 0][di]) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem_bytes(64));
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attention_smem_bytes(64, 64));
       attr_done[dev & 63][f32bias ? 1 : 0][di] = true;
     }
     kern<<<grid, ATT_NS * 32, smem, stream>>>(*a);

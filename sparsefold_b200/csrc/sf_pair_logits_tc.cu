@@ -34,7 +34,8 @@ __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ 
   uint8_t* smem = align1024(smem_raw);
   uint64_t* ldbar = reinterpret_cast<uint64_t*>(smem + OFF_PLBAR);
   uint64_t* mmabar = ldbar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ldbar + 2);
+  uint64_t* drain = ldbar + 2;                   // MMA drain barrier (abort path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ldbar + 3);
   const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t m0 = (int64_t)blockIdx.x * TILE;
 
@@ -45,6 +46,7 @@ __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ 
   if (tid == 0) {
     tc::mbar_init(ldbar, 1);
     tc::mbar_init(mmabar, 1);
+    tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
     tc::mbar_expect_tx(ldbar, A_BYTES);
     tc::tma_load_2d(smem + OFF_PLZ, &tmZ, ldbar, 0, (int)m0);
@@ -69,8 +71,9 @@ __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ 
   ln_row_shifted(smem + OFF_PLZ, tid, lnp, lnp + C, 1e-5f);
   tc::fence_proxy_async();
   tc::tc_fence_before();
-  __syncthreads();
-  if (tid == 0) {
+  // the tile is only used by the tensor core if every thread saw it land (abort path)
+  const bool loaded = !__syncthreads_or(aborted);
+  if (tid == 0 && loaded) {
     tc::tc_fence_after();
     const uint32_t sb = tc::smem_u32(smem);
     constexpr uint32_t IDESC = tc::idesc_bf16(128, PL_HEADS);
@@ -82,7 +85,7 @@ __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ 
     }
     tc::mma_commit(mmabar);
   }
-  tc::mbar_wait(mmabar, 0, p.status, aborted);
+  if (loaded) tc::mbar_wait(mmabar, 0, p.status, aborted);
   tc::tc_fence_after();
   float v[16];
   tc::tmem_ld16(tbase + ((uint32_t)(32 * warp) << 16), v);
@@ -100,7 +103,13 @@ __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ 
     }
   }
   tc::tc_fence_before();
-  __syncthreads();
+  if (__syncthreads_or(aborted)) {   // abort path: the tile load and the MMAs must be done before exit
+    if (tid == 0) {
+      tc::mbar_wait_drain(ldbar, 0, p.status);
+      if (loaded) tc::drain_mma(drain, p.status);
+    }
+    __syncthreads();
+  }
   if (warp == 0) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tbase, 32);

@@ -190,10 +190,12 @@ __global__ void __launch_bounds__(ATT_NS * 32, (DM > 0 && DM <= 32) ? 2 : 1) k_a
   extern __shared__ float4 att_smem4[];
   float* att_smem = reinterpret_cast<float*>(att_smem4);
   const int D = DK > 0 ? DK : (int)a.head_dim;
+  // value head dim: the query/key dim unless value_dim says otherwise (runtime-dim kernel only)
+  const int DV = DK > 0 ? DK : (a.value_dim > 0 ? (int)a.value_dim : D);
   constexpr bool VEC = DK > 0 && DK % 4 == 0;
   float* ks = att_smem;                               // [KT][D]
-  float* vs = ks + ATT_KT * D;                        // [KT][D]
-  float* bs = vs + ATT_KT * D;                        // [QB][KT + 1]
+  float* vs = ks + ATT_KT * D;                        // [KT][DV]
+  float* bs = vs + ATT_KT * DV;                       // [QB][KT + 1]
   uint8_t* kvalid = reinterpret_cast<uint8_t*>(bs + ATT_QB * (ATT_KT + 1));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t b = blockIdx.z, h = blockIdx.y;
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(ATT_NS * 32, (DM > 0 && DM <= 32) ? 2 : 1) k_a
     } else {
 #pragma unroll
       for (int d = 0; d < DM; ++d)
-        if (d < D) acc[d] = fmaf(pr, vr[d], acc[d]);
+        if (d < DV) acc[d] = fmaf(pr, vr[d], acc[d]);
     }
   };
   float mrun = -INFINITY, lrun = 0.f;
@@ -281,10 +283,8 @@ __global__ void __launch_bounds__(ATT_NS * 32, (DM > 0 && DM <= 32) ? 2 : 1) k_a
       for (int r = warp; r < kn; r += ATT_NS) {         // one key row per warp, lanes along d
         const T* kr = kp + (k0 + r) * a.k_sk;
         const T* vr = vp + (k0 + r) * a.v_sk;
-        for (int c = lane; c < D; c += 32) {
-          ks[r * D + c] = ld(kr + c);
-          vs[r * D + c] = ld(vr + c);
-        }
+        for (int c = lane; c < D; c += 32) ks[r * D + c] = ld(kr + c);
+        for (int c = lane; c < DV; c += 32) vs[r * DV + c] = ld(vr + c);
       }
     }
     if (bbase) {
@@ -352,7 +352,7 @@ __global__ void __launch_bounds__(ATT_NS * 32, (DM > 0 && DM <= 32) ? 2 : 1) k_a
         if (kk < kn) {
           const float pr = expf(sc[j] - mnew);
           lrun += pr;
-          axpy(pr, vs + kk * D);
+          axpy(pr, vs + kk * DV);
         }
       }
       mrun = mnew;
@@ -362,12 +362,12 @@ __global__ void __launch_bounds__(ATT_NS * 32, (DM > 0 && DM <= 32) ? 2 : 1) k_a
   // merge the key splits of each query (the K/V area is free now)
   float* ms = att_smem;                               // [NS][QB]
   float* ls = ms + ATT_NS * ATT_QB;                   // [NS][QB]
-  float* as = ls + ATT_NS * ATT_QB;                   // [NS][QB][D]
+  float* as = ls + ATT_NS * ATT_QB;                   // [NS][QB][DV]
   ms[warp * ATT_QB + lane] = mrun;
   ls[warp * ATT_QB + lane] = lrun;
 #pragma unroll
   for (int d = 0; d < DM; ++d)
-    if (d < D) as[(warp * ATT_QB + lane) * D + d] = acc[d];
+    if (d < DV) as[(warp * ATT_QB + lane) * DV + d] = acc[d];
   __syncthreads();
   const int qq = threadIdx.x % ATT_QB, d0 = threadIdx.x / ATT_QB;
   const int64_t qo = q0 + qq;
@@ -385,19 +385,19 @@ __global__ void __launch_bounds__(ATT_NS * 32, (DM > 0 && DM <= 32) ? 2 : 1) k_a
   const float inv = l > 0.f ? 1.f / l : 0.f;
   T* op = static_cast<T*>(a.out) + b * a.o_sb + h * a.o_sh + qo * a.o_sq;
   const T* gp = a.gate ? static_cast<const T*>(a.gate) + b * a.g_sb + h * a.g_sh + qo * a.g_sq : nullptr;
-  for (int d = d0; d < D; d += ATT_NS) {
+  for (int d = d0; d < DV; d += ATT_NS) {
     float o = 0.f;
 #pragma unroll
-    for (int sp = 0; sp < ATT_NS; ++sp) o += as[(sp * ATT_QB + qq) * D + d] * wgt[sp];
+    for (int sp = 0; sp < ATT_NS; ++sp) o += as[(sp * ATT_QB + qq) * DV + d] * wgt[sp];
     o *= inv;
     if (gp) o *= sigmoid_f(ld(gp + d));
     st(op + d, o);
   }
 }
 
-inline size_t attention_smem_bytes(int D) {
-  const size_t main = (size_t)(2 * ATT_KT * D + ATT_QB * (ATT_KT + 1)) * sizeof(float) + ATT_KT;
-  const size_t merge = (size_t)ATT_NS * ATT_QB * (D + 2) * sizeof(float);
+inline size_t attention_smem_bytes(int D, int DV) {
+  const size_t main = (size_t)(ATT_KT * (D + DV) + ATT_QB * (ATT_KT + 1)) * sizeof(float) + ATT_KT;
+  const size_t merge = (size_t)ATT_NS * ATT_QB * (DV + 2) * sizeof(float);
   return main > merge ? main : merge;
 }
 

@@ -63,11 +63,34 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
 // Bounded wait.  On timeout sets *status (first error wins) and returns false;
 // once this thread has timed out (`aborted`), later waits poll only once so the
 // kernel still reaches its end in bounded time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, bool& aborted) {
-  const uint32_t limit = aborted ? 1u : kWaitLimit;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status, bool& aborted,
+                                          uint32_t wait_limit = kWaitLimit) {
+  const uint32_t limit = aborted ? 1u : wait_limit;
   for (uint32_t i = 0; i < limit; ++i)
     if (mbar_try(bar, parity)) return true;
   aborted = true;
+  if (status) atomicCAS(status, 0u, (uint32_t)SF_ERR_TIMEOUT);
+  return false;
+}
+
+// ---- the abort path -------------------------------------------------------------
+// Once a wait has given up, the data or the buffer it waited for may never arrive,
+// so a thread that issues asynchronous work (TMA loads, tcgen05.mma) stops issuing
+// at its first failed wait.  Work it issued before that may still be in flight, and
+// other threads may have given up without waiting for it; so before TMEM is freed
+// and the CTA exits, every issuing thread drains what it issued whenever any thread
+// of the CTA gave up (the kernels test that with __syncthreads_or over `aborted`):
+//  * tcgen05.mma: one more tcgen05.commit, on the thread's own drain barrier (count
+//    1, otherwise unused), and a wait for it: a commit tracks every earlier MMA of
+//    the thread;
+//  * TMA loads into a ring of `stages` slots: a wait for the last phase issued into
+//    each slot (one load per slot can be outstanding, as each refill waited for the
+//    slot to be freed first).
+// The drain waits have their own bound and do not depend on earlier timeouts; if
+// one gives up as well, the kernel still ends (its status word says so).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try(bar, parity)) return true;
   if (status) atomicCAS(status, 0u, (uint32_t)SF_ERR_TIMEOUT);
   return false;
 }
@@ -200,6 +223,20 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+// Abort path: waits until every tcgen05.mma this thread issued has completed.
+// `drain_bar` is the thread's own barrier (count 1), used once.
+__device__ __forceinline__ void drain_mma(uint64_t* drain_bar, uint32_t* status) {
+  mma_commit(drain_bar);
+  mbar_wait_drain(drain_bar, 0, status);
+}
+// Abort path: waits for the last of `issued` TMA loads made in order q = 0, 1, ...
+// into slot q % stages of a ring whose landing barriers are full[0..stages) (load q
+// completes phase q / stages of its slot's barrier).
+__device__ __forceinline__ void drain_ring(uint64_t* full, uint32_t stages, uint32_t issued, uint32_t* status) {
+  const uint32_t first = issued > stages ? issued - stages : 0u;
+  for (uint32_t q = first; q < issued; ++q) mbar_wait_drain(&full[q % stages], (q / stages) & 1u, status);
 }
 
 // ---- TMEM -> registers: lane = row (warp w reads lanes 32*(w%4)..+31) -----------------

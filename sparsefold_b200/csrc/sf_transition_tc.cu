@@ -75,7 +75,8 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   uint64_t* s1free = s1full + 4;                 // [2 buffers][2 tiles] (4 warps)
   uint64_t* hfull = s1free + 4;                  // [HBUF] (8 warps)
   uint64_t* hfree = hfull + HBUF;                // [HBUF]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hfree + HBUF);
+  uint64_t* drain = hfree + HBUF;                // [3] drain barriers of the MMA issuers, warps 9-11 (abort path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 3);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t npasses = (p.M + 2 * TILE - 1) / (2 * TILE);
   float* lnp = reinterpret_cast<float*>(smem + OFF_LNP);
@@ -107,6 +108,7 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       tc::mbar_init(&hfull[s], 8);
       tc::mbar_init(&hfree[s], 1);
     }
+    for (int s = 0; s < 3; ++s) tc::mbar_init(&drain[s], 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmX);
     tc::prefetch_tmap(&tmW1);
@@ -119,22 +121,25 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   const uint32_t tbase = *tmem_slot;
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
+  uint32_t xloads = 0, w1loads = 0, w2loads = 0;   // TMA loads issued per ring (abort-path drain)
 
   if (warp == 8) {
-    // ---- TMA producer ----
+    // ---- TMA producer (stops at its first failed wait) ----
     if (lane == 0) {
-      uint32_t q = 0, pi = 0;
-      for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
+      uint32_t& q = w1loads;
+      uint32_t pi = 0;
+      for (int64_t ps = blockIdx.x; ps < npasses && !aborted; ps += gridDim.x, ++pi) {
         const int64_t m0 = ps * 2 * TILE;
-        if (pi >= 1) tc::mbar_wait(xfree, (pi - 1) & 1, p.status, aborted);
+        if (pi >= 1 && !tc::mbar_wait(xfree, (pi - 1) & 1, p.status, aborted)) break;
         tc::mbar_expect_tx(xfull, X_BYTES);
         for (int t2 = 0; t2 < 2; ++t2)
           for (int ka = 0; ka < 2; ++ka)
             tc::tma_load_2d(smem + OFF_X + t2 * A_BYTES + ka * ATOM, &tmX, xfull, ka * 64, (int)(m0 + t2 * TILE));
+        ++xloads;
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
           const int st = q % W1_STAGES;
           const uint32_t ph = ((q / W1_STAGES) + 1) & 1;
-          if (q >= W1_STAGES) tc::mbar_wait(&w1free[st], ph, p.status, aborted);
+          if (q >= W1_STAGES && !tc::mbar_wait(&w1free[st], ph, p.status, aborted)) break;
           uint8_t* w1 = smem + OFF_W1 + st * W1C_BYTES;
           tc::mbar_expect_tx(&w1full[st], W1C_BYTES);
           for (int ka = 0; ka < 2; ++ka) {
@@ -145,17 +150,17 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       }
     }
   } else if (warp == 9 || warp == 11) {
-    // ---- GEMM1 issuer of tile t2 ----
+    // ---- GEMM1 issuer of tile t2 (stops at its first failed wait) ----
     if (lane == 0) {
       const int t2 = warp == 9 ? 0 : 1;
       constexpr uint32_t ID1 = tc::idesc_bf16(128, 2 * HC);
       uint32_t q = 0, pi = 0;
-      for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
-        tc::mbar_wait(xready, pi & 1, p.status, aborted);
+      for (int64_t ps = blockIdx.x; ps < npasses && !aborted; ps += gridDim.x, ++pi) {
+        if (!tc::mbar_wait(xready, pi & 1, p.status, aborted)) break;
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
           const int st = q % W1_STAGES, sbuf = q & 1;
-          tc::mbar_wait(&w1full[st], (q / W1_STAGES) & 1, p.status, aborted);
-          if (q >= 2) tc::mbar_wait(&s1free[sbuf * 2 + t2], ((q >> 1) + 1) & 1, p.status, aborted);
+          if (!tc::mbar_wait(&w1full[st], (q / W1_STAGES) & 1, p.status, aborted)) break;
+          if (q >= 2 && !tc::mbar_wait(&s1free[sbuf * 2 + t2], ((q >> 1) + 1) & 1, p.status, aborted)) break;
           tc::tc_fence_after();
           const uint32_t w1 = sb + OFF_W1 + st * W1C_BYTES;
 #pragma unroll
@@ -177,24 +182,25 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
     if (lane == 0) {
       constexpr uint32_t ID2 = tc::idesc_bf16(128, 128);
       const uint32_t total = (uint32_t)((npasses - blockIdx.x + gridDim.x - 1) / gridDim.x) * NCHUNK;
-      auto load_w2 = [&](uint32_t c) {   // chunk c of this CTA into stage c % W2_STAGES
+      auto load_w2 = [&](uint32_t c) {   // chunk c of this CTA into stage c % W2_STAGES (c == w2loads)
         const int st = c % W2_STAGES;
         tc::mbar_expect_tx(&w2full[st], W2C_BYTES);
         tc::tma_load_2d(smem + OFF_W2 + st * W2C_BYTES, &tmW2, &w2full[st], (int)(c % NCHUNK) * HC, 0);
+        ++w2loads;
       };
       for (uint32_t c = 0; c < W2_STAGES && c < total; ++c) load_w2(c);
       uint32_t q = 0, pi = 0;
-      for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
+      for (int64_t ps = blockIdx.x; ps < npasses && !aborted; ps += gridDim.x, ++pi) {
         for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
           const int st = q % W2_STAGES, hb = q % HBUF;
           // chunk q-1+W2_STAGES into the stage of chunk q-1 once its GEMM2 is done (it usually is)
           if (q >= 1 && q - 1 + W2_STAGES < total) {
-            tc::mbar_wait(&w2free[(q - 1) % W2_STAGES], ((q - 1) / W2_STAGES) & 1, p.status, aborted);
+            if (!tc::mbar_wait(&w2free[(q - 1) % W2_STAGES], ((q - 1) / W2_STAGES) & 1, p.status, aborted)) break;
             load_w2(q - 1 + W2_STAGES);
           }
-          if (hc == 0 && pi >= 1) tc::mbar_wait(accfree, (pi - 1) & 1, p.status, aborted);
-          tc::mbar_wait(&hfull[hb], (q / HBUF) & 1, p.status, aborted);
-          tc::mbar_wait(&w2full[st], (q / W2_STAGES) & 1, p.status, aborted);
+          if (hc == 0 && pi >= 1 && !tc::mbar_wait(accfree, (pi - 1) & 1, p.status, aborted)) break;
+          if (!tc::mbar_wait(&hfull[hb], (q / HBUF) & 1, p.status, aborted)) break;
+          if (!tc::mbar_wait(&w2full[st], (q / W2_STAGES) & 1, p.status, aborted)) break;
           tc::tc_fence_after();
           const uint32_t w2 = sb + OFF_W2 + st * W2C_BYTES;
           for (int t2 = 0; t2 < 2; ++t2)
@@ -206,6 +212,7 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
           tc::mma_commit(&hfree[hb]);
           tc::mma_commit(&w2free[st]);
         }
+        if (aborted) break;
         tc::mma_commit(accfull);
       }
     }
@@ -293,7 +300,18 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
     }
   }
   tc::tc_fence_before();
-  __syncthreads();
+  if (__syncthreads_or(aborted)) {   // abort path: drain every ring's loads and every issuer's MMAs
+    if (lane == 0) {
+      if (warp == 8) {
+        tc::drain_ring(xfull, 1, xloads, p.status);
+        tc::drain_ring(w1full, W1_STAGES, w1loads, p.status);
+      } else if (warp >= 9 && warp <= 11) {
+        if (warp == 10) tc::drain_ring(w2full, W2_STAGES, w2loads, p.status);
+        tc::drain_mma(&drain[warp - 9], p.status);
+      }
+    }
+    __syncthreads();
+  }
   if (warp == 0) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tbase, 512);

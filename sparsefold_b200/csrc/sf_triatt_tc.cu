@@ -142,7 +142,8 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
   uint64_t* zfree = normed + 2;                                     // [2] MMAs of the stage done
   uint64_t* tfull = zfree + 2;                                      // [2] TMEM half written
   uint64_t* tfree = tfull + 2;                                      // [2] TMEM half read (8 warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
+  uint64_t* drain = tfree + 2;                                      // MMA drain barrier (abort path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t nqb = p.qp / TILE, ntiles = p.nb * nqb;
 
@@ -158,6 +159,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
       tc::mbar_init(&tfull[s], 1);
       tc::mbar_init(&tfree[s], PJ_EPI_WARPS);
     }
+    tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmZ);
     tc::prefetch_tmap(&tmQ);
@@ -176,14 +178,15 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
   const uint32_t tbase = *tmem_slot;
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
+  uint32_t loads = 0;   // z tiles requested by the producer (abort-path drain)
 
   if (warp == 12) {
-    // ---- TMA producer ----
+    // ---- TMA producer (stops at its first failed wait) ----
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t& it = loads;
       for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int st = it & 1;
-        if (it >= 2) tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
+        if (it >= 2 && !tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted)) break;
         const int b = (int)(tile / nqb), q0 = (int)((tile % nqb) * TILE);   // (projection tile coordinates)
         const int c1 = p.transpose ? b : q0;     // column coordinate
         const int c2 = p.transpose ? q0 : b;     // row coordinate
@@ -194,20 +197,20 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
       }
     }
   } else if (warp == 13) {
-    // ---- MMA issuer ----
+    // ---- MMA issuer (stops at its first failed wait) ----
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = tc::idesc_bf16(128, 256), IDESC = tc::idesc_bf16(128, 128);
       uint32_t it = 0;
       for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int st = it & 1;
-        tc::mbar_wait(&normed[st], (it >> 1) & 1, p.status, aborted);
+        if (!tc::mbar_wait(&normed[st], (it >> 1) & 1, p.status, aborted)) break;
         tc::tc_fence_after();
         const uint32_t zb = sb + OFF_JZ + st * A_BYTES;
         auto wdesc = [&](int mtx, int ka, int kk) {   // rows 128 mtx.. of W (q, k, v, gate), K step (ka, kk)
           return tc::smem_desc(sb + OFF_JW + ka * (NOUT * 128) + mtx * (128 * 128) + kk * 32, 1024, tc::kSW128);
         };
         // half 0: [q | k][query] = LN(z) . W_qk^T
-        if (it >= 1) tc::mbar_wait(&tfree[0], (it - 1) & 1, p.status, aborted);
+        if (it >= 1 && !tc::mbar_wait(&tfree[0], (it - 1) & 1, p.status, aborted)) break;
         tc::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -216,7 +219,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
         }
         tc::mma_commit(&tfull[0]);
         // half 1: gate[query][channel] and v[channel][query]
-        if (it >= 1) tc::mbar_wait(&tfree[1], (it - 1) & 1, p.status, aborted);
+        if (it >= 1 && !tc::mbar_wait(&tfree[1], (it - 1) & 1, p.status, aborted)) break;
         tc::tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -341,7 +344,11 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
     if (lane == 0) tc::bulk_wait0();
   }
   tc::tc_fence_before();
-  __syncthreads();
+  if (__syncthreads_or(aborted)) {   // abort path: drain the producer's loads and the issuer's MMAs
+    if (warp == 12 && lane == 0) tc::drain_ring(full, 2, loads, p.status);
+    if (warp == 13 && lane == 0) tc::drain_mma(drain, p.status);
+    __syncthreads();
+  }
   if (warp == 0) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tbase, 512);
@@ -462,7 +469,8 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   uint64_t* wbar = rbar + H;                                       // [H] W_o columns landed
   uint64_t* ostaged = wbar + H;                                    // [H] gated O_h staged (4 softmax warps)
   uint64_t* outbar = ostaged + H;                                  // [H] O_h W_o^T done
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(outbar + H);
+  uint64_t* drainb = outbar + H;                                   // [H] issue warps' MMA drain (abort path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drainb + H);
   uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + OFF_KBITS);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool issuer = warp >= 16;
@@ -476,6 +484,8 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   auto bt_of = [&](int jj) { return ring + RING * K_BYTES + (jj % RING) * BT_BYTES; };
   auto v_of = [&](int jj) { return ring + RING * (K_BYTES + BT_BYTES) + (jj % VRING) * V_BYTES; };
   bool aborted = false;
+  uint32_t loads = 0;                    // key blocks requested by this head's issue thread (abort-path drain)
+  bool rload = false, wload = false;     // residual tile / W_o columns requested
 
   // this thread's query row of Q (64 B), for TMEM: requested first, it is the longest wait
   uint4 qrow[4];
@@ -484,7 +494,8 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
 #pragma unroll
     for (int c = 0; c < 4; ++c) qrow[c] = __ldg(qsrc + c);
   }
-  auto issue_load = [&](int jj) {   // K, V^T and bias[q0..q0+127][g][32 jj .. 32 jj + 31] of block jj
+  auto issue_load = [&](int jj) {   // K, V^T and bias[q0..q0+127][g][32 jj .. 32 jj + 31] of block jj (jj == loads)
+    ++loads;
     uint64_t* bar = &lbar[g * RING + jj % RING];
     tc::mbar_expect_tx(bar, K_BYTES + V_BYTES + BT_BYTES);
     tc::tma_load_2d(k_of(jj), &tmK, bar, 0, (int)(bh * p.qp + (int64_t)jj * KB));
@@ -507,6 +518,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
     tc::mbar_init(&wbar[g], 1);
     tc::mbar_init(&ostaged[g], 4);
     tc::mbar_init(&outbar[g], 1);
+    tc::mbar_init(&drainb[g], 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmK);
     tc::prefetch_tmap(&tmV);
@@ -544,7 +556,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   }
 
   auto issue_s = [&](int jj) {   // S_jj = Q K_jj^T into S buffer jj % 2, once block jj has landed
-    tc::mbar_wait(&lbar[g * RING + jj % RING], (jj / RING) & 1, p.status, aborted);
+    if (!tc::mbar_wait(&lbar[g * RING + jj % RING], (jj / RING) & 1, p.status, aborted)) return;
     tc::mbar_arrive(&sbar[g * 2 + (jj & 1)]);   // the softmax reads the bias tile once S_jj is signalled
     tc::tc_fence_after();
     const uint32_t ks = tc::smem_u32(k_of(jj));
@@ -576,13 +588,14 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
         while (clock64() < until) {
         }
       }
+      // (the issue thread stops issuing at its first failed wait)
       issue_s(0);
-      issue_load(2);
-      issue_s(1);
-      issue_load(3);
-      for (int j = 0; j < nkb; ++j) {
+      if (!aborted) issue_load(2);
+      if (!aborted) issue_s(1);
+      if (!aborted) issue_load(3);
+      for (int j = 0; j < nkb && !aborted; ++j) {
         // P_j is in TMEM: S_j and bias_j have been read, P_{j-1} V_{j-1} awaited by the softmax
-        tc::mbar_wait(&pready[g * 2 + (j & 1)], (j >> 1) & 1, p.status, aborted);
+        if (!tc::mbar_wait(&pready[g * 2 + (j & 1)], (j >> 1) & 1, p.status, aborted)) break;
         tc::tc_fence_after();
         // O += P_j V_j (P_j over S_j; V^T of block j landed before S_j was signalled)
         const uint32_t vs = tc::smem_u32(v_of(j));
@@ -594,6 +607,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
         // S_{j+2} over P_j: MMAs issued by one thread run in issue order, so its accumulator
         // writes follow P_j V_j's read of P_j
         if (j + 2 < nkb) issue_s(j + 2);
+        if (aborted) break;
         // then block j+4 (two blocks before its S), or an epilogue tile: K and bias into the slots
         // of block j (S_j and the softmax of block j are done), V^T into the slot of block j-2
         // (S_j complete means P_{j-2} V_{j-2}, issued before it, is done)
@@ -605,23 +619,26 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
           tc::prefetch_tmap(&tmO);
           tc::mbar_expect_tx(&rbar[g], TILE * D * 2);
           tc::tma_load_3d(resid, &tmR, &rbar[g], g * D, rc1, rc2);
+          rload = true;
         } else if (j + RING == nkb + 1) {
           // W_o[:, 32g .. 32g+31] (K-major 128 x 32, 64B swizzle)
           tc::mbar_expect_tx(&wbar[g], 8192);
           tc::tma_load_2d(wstage, &tmW, &wbar[g], g * D, 0);
+          wload = true;
         }
       }
       // this head's share of the output projection, D_g = O_g W_o[:, 32g .. 32g+31]^T, into the
       // head's own columns (its S, O, Q and P are dead once O_g is staged)
-      tc::mbar_wait(&ostaged[g], 0, p.status, aborted);
-      tc::mbar_wait(&wbar[g], 0, p.status, aborted);
-      tc::tc_fence_after();
-      const uint32_t os = tc::smem_u32(ostage), ws = tc::smem_u32(wstage);
+      if (!aborted && tc::mbar_wait(&ostaged[g], 0, p.status, aborted) &&
+          tc::mbar_wait(&wbar[g], 0, p.status, aborted)) {
+        tc::tc_fence_after();
+        const uint32_t os = tc::smem_u32(ostage), ws = tc::smem_u32(wstage);
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk)
-        tc::mma_bf16(tbase + s_col, tc::smem_desc(os + kk * 32, 512, tc::kSW64),
-                     tc::smem_desc(ws + kk * 32, 512, tc::kSW64), IDESC_OUT, kk > 0);
-      tc::mma_commit(&outbar[g]);
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc::mma_bf16(tbase + s_col, tc::smem_desc(os + kk * 32, 512, tc::kSW64),
+                       tc::smem_desc(ws + kk * 32, 512, tc::kSW64), IDESC_OUT, kk > 0);
+        tc::mma_commit(&outbar[g]);
+      }
     }
   } else {
     const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
@@ -822,7 +839,15 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
     }
   }
   tc::tc_fence_before();
-  __syncthreads();
+  if (__syncthreads_or(aborted)) {   // abort path: drain each head's loads and MMAs
+    if (issuer && lane == 0) {
+      tc::drain_ring(&lbar[g * RING], RING, loads, p.status);
+      if (rload) tc::mbar_wait_drain(&rbar[g], 0, p.status);
+      if (wload) tc::mbar_wait_drain(&wbar[g], 0, p.status);
+      tc::drain_mma(&drainb[g], p.status);
+    }
+    __syncthreads();
+  }
   if (warp == 0) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tbase, 512);

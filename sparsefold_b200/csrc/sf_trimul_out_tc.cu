@@ -59,7 +59,8 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
   uint64_t* sfull = pfree + 2;                                      // [2] stats written (128)
   uint64_t* tfull = sfull + 2;                                      // [2] TMEM buffer written
   uint64_t* tfree = tfull + 2;                                      // [2] TMEM buffer read (8 warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
+  uint64_t* drain = tfree + 2;                                      // MMA drain barrier (abort path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t nb = (p.n + TILE - 1) / TILE, ntiles = p.rows * nb;
   float* vec = reinterpret_cast<float*>(smem + OFF_VEC);
@@ -78,6 +79,7 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
       tc::mbar_init(&tfull[s], 1);
       tc::mbar_init(&tfree[s], OUT_EPI_WARPS);
     }
+    tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmZ);
     tc::prefetch_tmap(&tmP);
@@ -99,37 +101,40 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
   const uint32_t tbase = *tmem_slot;
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
+  uint32_t zloads = 0, ploads = 0;   // z and P tiles requested by the producer (abort-path drain)
 
   if (warp == 12) {
-    // ---- TMA producer ----
+    // ---- TMA producer (stops at its first failed wait) ----
     if (lane == 0) {
       uint32_t it = 0;
       for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int st = it & 1;
         const int64_t r = tile / nb, s0 = (tile % nb) * TILE;
-        if (it >= 2) tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
+        if (it >= 2 && !tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted)) break;
         uint8_t* zs = smem + OFF_Z + st * A_BYTES;
         tc::mbar_expect_tx(&zfull[st], A_BYTES);
         tc::tma_load_3d(zs, &tmZ, &zfull[st], 0, (int)s0, (int)r);
         tc::tma_load_3d(zs + ATOM, &tmZ, &zfull[st], 64, (int)s0, (int)r);
-        if (it >= 2) tc::mbar_wait(&pfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
+        ++zloads;
+        if (it >= 2 && !tc::mbar_wait(&pfree[st], ((it >> 1) + 1) & 1, p.status, aborted)) break;
         uint8_t* ps = smem + OFF_P + st * A_BYTES;
         tc::mbar_expect_tx(&pfull[st], A_BYTES);
         tc::tma_load_3d(ps, &tmP, &pfull[st], (int)s0, 0, (int)r);
         tc::tma_load_3d(ps + ATOM, &tmP, &pfull[st], (int)s0 + 64, 0, (int)r);
+        ++ploads;
       }
     }
   } else if (warp == 13) {
-    // ---- MMA issuer ----
+    // ---- MMA issuer (stops at its first failed wait) ----
     if (lane == 0) {
       constexpr uint32_t IDESC_G = tc::idesc_bf16(128, 128);
       constexpr uint32_t IDESC_U = tc::idesc_bf16(128, 128) | (1u << 15);   // A (P) M-major
       uint32_t it = 0;
       for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int st = it & 1, buf = it & 1;
-        tc::mbar_wait(&zfull[st], (it >> 1) & 1, p.status, aborted);
-        tc::mbar_wait(&pfull[st], (it >> 1) & 1, p.status, aborted);
-        if (it >= 2) tc::mbar_wait(&tfree[buf], ((it >> 1) + 1) & 1, p.status, aborted);
+        if (!tc::mbar_wait(&zfull[st], (it >> 1) & 1, p.status, aborted)) break;
+        if (!tc::mbar_wait(&pfull[st], (it >> 1) & 1, p.status, aborted)) break;
+        if (it >= 2 && !tc::mbar_wait(&tfree[buf], ((it >> 1) + 1) & 1, p.status, aborted)) break;
         tc::tc_fence_after();
         const uint32_t zb = sb + OFF_Z + st * A_BYTES, pb = sb + OFF_P + st * A_BYTES;
 #pragma unroll
@@ -300,7 +305,14 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
     if (lane == 0) tc::bulk_wait0();
   }
   tc::tc_fence_before();
-  __syncthreads();
+  if (__syncthreads_or(aborted)) {   // abort path: drain the producer's loads and the issuer's MMAs
+    if (warp == 12 && lane == 0) {
+      tc::drain_ring(zfull, 2, zloads, p.status);
+      tc::drain_ring(pfull, 2, ploads, p.status);
+    }
+    if (warp == 13 && lane == 0) tc::drain_mma(drain, p.status);
+    __syncthreads();
+  }
   if (warp == 0) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tbase, 512);

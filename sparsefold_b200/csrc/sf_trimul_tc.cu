@@ -58,7 +58,8 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
   uint64_t* zfree = normed + 2;                                     // [2] MMAs of the stage done
   uint64_t* tfull = zfree + 2;                                      // [2] TMEM half written
   uint64_t* tfree = tfull + 2;                                      // [2] TMEM half read (8 warps)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfree + 2);
+  uint64_t* drain = tfree + 2;                                      // MMA drain barrier (abort path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   const int64_t span = p.incoming ? p.rows : p.n;              // positions along a tile's axis
@@ -77,6 +78,7 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
       tc::mbar_init(&tfull[s], 1);
       tc::mbar_init(&tfree[s], EPI_WARPS);
     }
+    tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmZ);
     tc::prefetch_tmap(&tmA);
@@ -92,14 +94,15 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
   const uint32_t tbase = *tmem_slot;
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
+  uint32_t loads = 0;   // z tiles requested by the producer (abort-path drain)
 
   if (warp == EPI_WARPS + LN_WARPS) {
-    // ---- TMA producer ----
+    // ---- TMA producer (stops at its first failed wait) ----
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t& it = loads;
       for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
         const int st = it & 1;
-        if (it >= 2) tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted);
+        if (it >= 2 && !tc::mbar_wait(&zfree[st], ((it >> 1) + 1) & 1, p.status, aborted)) break;
         const int64_t major = tile / nb, minor = (tile % nb) * TILE;
         const int c1 = (int)(p.incoming ? major : minor);    // tensor coordinates (channel, column, row)
         const int c2 = (int)(p.incoming ? minor : major);
@@ -110,18 +113,18 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
       }
     }
   } else if (warp == EPI_WARPS + LN_WARPS + 1) {
-    // ---- MMA issuer ----
+    // ---- MMA issuer (stops at its first failed wait) ----
     if (lane == 0) {
       constexpr uint32_t IDESC = tc::idesc_bf16(128, 128);
       uint32_t it = 0;
-      for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      for (int64_t tile = blockIdx.x; tile < ntiles && !aborted; tile += gridDim.x, ++it) {
         const int st = it & 1;
-        tc::mbar_wait(&normed[st], (it >> 1) & 1, p.status, aborted);
+        if (!tc::mbar_wait(&normed[st], (it >> 1) & 1, p.status, aborted)) break;
         tc::tc_fence_after();
         const uint32_t zb = sb + OFF_PZ + st * A_BYTES;
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          if (it >= 1) tc::mbar_wait(&tfree[hh], (it - 1) & 1, p.status, aborted);
+          if (it >= 1 && !tc::mbar_wait(&tfree[hh], (it - 1) & 1, p.status, aborted)) break;
           tc::tc_fence_after();
 #pragma unroll
           for (int mt = 0; mt < 2; ++mt) {          // gate, value of operand hh
@@ -136,6 +139,7 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
           }
           tc::mma_commit(&tfull[hh]);
         }
+        if (aborted) break;
         tc::mma_commit(&zfree[st]);
       }
     }
@@ -220,7 +224,11 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
     if (lane == 0) tc::bulk_wait0();
   }
   tc::tc_fence_before();
-  __syncthreads();
+  if (__syncthreads_or(aborted)) {   // abort path: drain the producer's loads and the issuer's MMAs
+    if (warp == EPI_WARPS + LN_WARPS && lane == 0) tc::drain_ring(full, 2, loads, p.status);
+    if (warp == EPI_WARPS + LN_WARPS + 1 && lane == 0) tc::drain_mma(drain, p.status);
+    __syncthreads();
+  }
   if (warp == 0) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tbase, 512);

@@ -75,26 +75,27 @@ def attention(q, k, v, *, scale=None, mask_q=None, mask_k=None, bias=None, gate=
               mask_row=None) -> torch.Tensor:
   """Drop-in for backends/torch/attention/sdpa.py:22 dot_product_attention.
 
-  q [..., Q, H, D], k/v [..., K, H, D], masks [..., Q] / [..., K] (broadcast),
-  bias broadcastable to [..., H, Q, K]; optional gate [..., Q, H, D] applies
-  sigmoid(gate) to the output.  Returns [..., Q, H, D] in q's dtype.
+  q [..., Q, H, D], k [..., K, H, D], v [..., K, H, Dv] (Dv may differ from D,
+  as sdpa.py allows), masks [..., Q] / [..., K] (broadcast), bias broadcastable
+  to [..., H, Q, K]; optional gate [..., Q, H, Dv] applies sigmoid(gate) to the
+  output.  Returns [..., Q, H, Dv] in q's dtype.
   """
   _cuda(q, k, v)
   batch = q.shape[:-3]
   Q, H, D = q.shape[-3:]
   K = k.shape[-3]
-  if v.shape[-1] != D:
-    raise ValueError("sf_attention requires value dim == query dim")
+  Dv = v.shape[-1]
   B = math.prod(batch) if batch else 1
   dt = _dt(q)
   q3 = q.reshape(B, Q, H, D)
   k3 = k.expand(*batch, K, H, D).reshape(B, K, H, D)
-  v3 = v.expand(*batch, K, H, D).reshape(B, K, H, D)
+  v3 = v.expand(*batch, K, H, Dv).reshape(B, K, H, Dv)
   q3, k3, v3 = (t if t.stride(-1) == 1 else t.contiguous() for t in (q3, k3, v3))
-  out = torch.empty(B, Q, H, D, dtype=q.dtype, device=q.device)
+  out = torch.empty(B, Q, H, Dv, dtype=q.dtype, device=q.device)
   a = N.AttentionArgs()
   a.dtype = dt
   a.batch, a.heads, a.q_len, a.k_len, a.head_dim = B, H, Q, K, D
+  a.value_dim = Dv
   a.q, a.q_sb, a.q_sh, a.q_sq = _p(q3), q3.stride(0), q3.stride(2), q3.stride(1)
   a.k, a.k_sb, a.k_sh, a.k_sk = _p(k3), k3.stride(0), k3.stride(2), k3.stride(1)
   a.v, a.v_sb, a.v_sh, a.v_sk = _p(v3), v3.stride(0), v3.stride(2), v3.stride(1)
@@ -125,12 +126,12 @@ def attention(q, k, v, *, scale=None, mask_q=None, mask_k=None, bias=None, gate=
     a.mask_row = _p(mr)
     keep.append(mr)
   if gate is not None:
-    g3 = gate.reshape(B, Q, H, D)
+    g3 = gate.reshape(B, Q, H, Dv)
     a.gate, a.g_sb, a.g_sh, a.g_sq = _p(g3), g3.stride(0), g3.stride(2), g3.stride(1)
     keep.append(g3)
   a.scale = float(1.0 / math.sqrt(D) if scale is None else scale)
   N.call("sf_attention", C.byref(a), _stream())
-  return out.reshape(*batch, Q, H, D)
+  return out.reshape(*batch, Q, H, Dv)
 
 
 # ---------------------------------------------------------------------------

@@ -71,6 +71,38 @@ class Shard:
     return x.narrow(dim, self.offset(), self.size())
 
 
+class RankFailure(RuntimeError):
+  """A peer rank did not reach a step of the sharded path within the time limit."""
+
+
+def step_barrier(store, step: int, rank: int, world: int, timeout_s: float = 10.0, prefix: str = "sf_step") -> None:
+  """Host-side liveness check before the collectives of one sharded step.
+
+  Every rank posts ``{prefix}/{step}/{rank}`` in the process group's key-value
+  store and waits, at most ``timeout_s`` seconds, for the other ranks' keys.  A
+  rank that raised, exited or never started is reported by index with
+  ``RankFailure`` before any collective or kernel of the step is launched, so
+  the surviving ranks leave between steps with nothing in flight on their GPUs
+  (the reference detects a lost rank only when a collective times out).
+  """
+  import datetime
+  import time
+  store.set(f"{prefix}/{step}/{rank}", "1")
+  deadline = time.monotonic() + timeout_s
+  missing = [r for r in range(world) if r != rank]
+  while missing:
+    left = deadline - time.monotonic()
+    if left <= 0:
+      raise RankFailure(f"step {step}: ranks {missing} did not arrive within {timeout_s:.1f} s")
+    try:
+      store.wait([f"{prefix}/{step}/{missing[0]}"], datetime.timedelta(seconds=max(left, 0.05)))
+      missing.pop(0)
+    except Exception:   # the store's own timeout (DistStoreError) or a closed connection
+      if time.monotonic() >= deadline:
+        raise RankFailure(f"step {step}: ranks {missing} did not arrive within {timeout_s:.1f} s") from None
+      time.sleep(0.05)
+
+
 def world_size(group=None) -> int:
   return dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
 

@@ -158,14 +158,30 @@ def test_attention_golden_semantics():
   for bi in range(3):
     for masked in (0, 1):
       t = f"b{bi}_m{masked}"
-      q, k, v = (arrays[f"{t}_{x}"] for x in "qkv")
-      if v.shape[-1] != q.shape[-1]:
-        continue  # the kernel needs Dv == Dqk (all hot-path heads); checked against the oracle below
+      q, k, v = (arrays[f"{t}_{x}"] for x in "qkv")   # includes the reference's Dv != Dqk cases
       got = ops.attention(q.cuda(), k.cuda(), v.cuda(), scale=0.4,
                           mask_q=None if not masked else arrays[f"{t}_mask_q"].cuda(),
                           mask_k=None if not masked else arrays[f"{t}_mask_k"].cuda(),
                           bias=arrays[f"{t}_bias"].cuda())
       torch.testing.assert_close(got.cpu(), arrays[f"{t}_out"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("dq,dv", [(16, 12), (24, 32), (8, 40)])
+def test_attention_value_dim_differs(dq, dv, dtype):
+  """sdpa.py:22-121 takes v with its own head dim; out and gate follow v."""
+  g = torch.Generator().manual_seed(dq * 100 + dv)
+  q = torch.randn(2, 37, 3, dq, generator=g).to(dtype)
+  k = torch.randn(2, 45, 3, dq, generator=g).to(dtype)
+  v = torch.randn(2, 45, 3, dv, generator=g).to(dtype)
+  bias = torch.randn(2, 3, 37, 45, generator=g).to(dtype)
+  gate = torch.randn(2, 37, 3, dv, generator=g).to(dtype)
+  mk = torch.rand(2, 45, generator=g) > 0.2
+  ref = orc.dot_product_attention(q.float(), k.float(), v.float(), mask_k=mk, bias=bias.float())
+  ref = ref * torch.sigmoid(gate.float())
+  got = ops.attention(q.cuda(), k.cuda(), v.cuda(), mask_k=mk.cuda(), bias=bias.cuda(), gate=gate.cuda())
+  assert got.shape == (2, 37, 3, dv)
+  assert max_rel_err(got.float().cpu(), ref) < TOL[dtype]
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
