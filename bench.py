@@ -435,60 +435,160 @@ def run_reference(args) -> None:
 
 
 OPS = ("tri_attention_start", "tri_attention_end", "tri_mult_outgoing", "tri_mult_incoming", "pair_transition",
-       "single_update")
+       "single_update", "single_attention", "diffusion_transformer", "atom_transformer", "msa_attention",
+       "outer_product_mean")
 
 
 def op_flops(op: str, n: int) -> float:
+  """Algorithmic FLOPs of one op at its workload (pair ops at N_token = n)."""
   if op.startswith("tri_attention"):
     return tri_attention_op_flops(n)
   if op.startswith("tri_mult"):
     return 256.0 * n**3 + n * n * 2.0 * 128 * (512 + 128 + 128)
   if op == "pair_transition":
     return n * n * 2.0 * 128 * (1024 + 512)
+  if op == "single_attention":           # 16 heads x 24: 4 N^2 d H
+    return 4.0 * n * n * 24 * 16
   return 0.0
 
 
+def _diffusion_token_flops(s: int, n: int, c: int, h: int, d: int, blocks: int, sc: int, pc: int) -> float:
+  """One denoising step of the token transformer (diffusion/transformer.py:348-477), s samples."""
+  per = (2.0 * s * n * c * 4 * c          # q, k, v, gate
+         + 4.0 * s * h * n * n * d        # attention core
+         + 2.0 * s * n * c * c            # adaptive-zero transition2 of the attention
+         + 2.0 * s * n * c * 4 * c        # transition W1 (2 x 2c)
+         + 2.0 * s * n * 2 * c * c        # transition W2
+         + 2 * (2.0 * 2 * n * sc * c)     # AdaLN scale and bias of both sub-blocks
+         + 2 * 2.0 * n * sc * c)          # adaptive-zero gates
+  return blocks * per + 2.0 * n * n * pc * blocks * h
+
+
+def _atom_flops(s: int, nsub: int, q: int, k: int, c: int, h: int, d: int, blocks: int) -> float:
+  """CrossAttTransformer (transformer.py:588-693): s samples, nsub windows of q queries x k keys."""
+  nq, nk = nsub * q, nsub * k
+  per = (2.0 * s * nq * c * 2 * h * d     # q and gate
+         + 2.0 * s * nk * c * 2 * h * d   # k and v of the gathered windows
+         + 4.0 * s * nsub * h * q * k * d # attention core
+         + 2.0 * s * nq * h * d * c       # adaptive-zero transition2
+         + 2.0 * s * nq * c * 4 * c       # transition W1
+         + 2.0 * s * nq * 2 * c * c       # transition W2
+         + 2.0 * (2 * nq + 2 * nk) * c * c + 4.0 * nq * c * c)   # AdaLN (queries, keys) and gates
+  return blocks * per
+
+
+def _workload_op(op: str, n: int):
+  """(run, flops, what) for the workload ops of configs[2] and configs[3] and the single attention."""
+  import types
+  import torch
+  from sparsefold_b200 import modules, ops, synth
+  dt = torch.bfloat16
+  g = torch.Generator().manual_seed(4)
+  rn = lambda *shape: torch.randn(*shape, generator=g).to("cuda", dt)
+  if op == "single_attention":
+    h, d = 16, 24
+    y = rn(n, 4, h, d)
+    bias = rn(h, n, n)
+    mk = (torch.arange(n) < max(1, N_REAL * n // N_TOKEN)).cuda()
+    return (lambda: ops.attention(y[:, 0], y[:, 1], y[:, 2], mask_k=mk, bias=bias, gate=y[:, 3]), op_flops(op, n),
+            f"Pairformer single attention core (sf_attention), N={n}, 16 heads x 24, pair-logit bias, gate")
+  if op == "diffusion_transformer":
+    s_, n_, c, sc, pc = 5, 768, 768, 384, 128
+    m = modules.DiffusionTransformer(c, sc, pc, num_head=16, num_blocks=24, super_block_size=4)
+    synth.init_params(m, seed=4)
+    m = m.cuda()
+    modules.prepare(m)
+    act, single, pair = rn(s_, n_, c), rn(n_, sc), rn(n_, n_, pc)
+    mask = torch.ones(n_, dtype=torch.bool, device="cuda")
+    return (lambda: m(act, mask, single, pair), _diffusion_token_flops(s_, n_, c, 16, 48, 24, sc, pc),
+            "configs[2] token transformer, one denoising step: 24 blocks, 5 samples, N=768, c=768, 16 x 48, "
+            "pair-logit pack from z [768,768,128]")
+  if op == "atom_transformer":
+    s_, nsub, q_, k_, c, pc = 5, 192, 32, 128, 128, 16
+    m = modules.CrossAttTransformer(c, pc, num_head=4, key_dim=128, num_blocks=3, num_intermediate_factor=2)
+    synth.init_params(m, seed=4)
+    m = m.cuda()
+    modules.prepare(m)
+    starts = torch.clamp(32 * torch.arange(nsub) + 16 - 64, 0, nsub * q_ - k_)
+    idx = (starts[:, None] + torch.arange(k_)[None, :]).to(torch.int32).cuda()
+    info = types.SimpleNamespace(gather_idxs=idx, gather_mask=torch.ones(nsub, k_, dtype=torch.bool, device="cuda"))
+    qact, qsc, ksc, pcq = rn(s_, nsub, q_, c), rn(nsub, q_, c), rn(nsub, k_, c), rn(nsub, q_, k_, pc)
+    qmask = torch.ones(nsub, q_, dtype=torch.bool, device="cuda")
+    kmask = torch.ones(nsub, k_, dtype=torch.bool, device="cuda")
+    return (lambda: m(qact, qmask, info, kmask, qsc, ksc, pcq), _atom_flops(s_, nsub, q_, k_, c, 4, 32, 3),
+            "configs[2] atom encoder: 3 blocks, 5 samples, 6144 atoms in 192 windows of 32 queries x 128 keys, "
+            "c_atom=128, 4 x 32")
+  if op in ("msa_attention", "outer_product_mean"):
+    m_, n_ = 1024, 768
+    act = torch.nn.functional.one_hot(torch.randint(0, 32, (m_, n_), generator=g), 32).float()
+    act = torch.cat([act, torch.randn(m_, n_, 32, generator=g)], -1).to("cuda", dt)   # c_m = 64
+    mask = (torch.rand(m_, n_, generator=g) > 0.15).cuda()
+    if op == "msa_attention":
+      m = modules.MSAAttention(64, 128, 8)
+      synth.init_params(m, seed=4)
+      m = m.cuda()
+      modules.prepare(m)
+      pair = rn(n_, n_, 128)
+      fl = 2.0 * 8 * m_ * 8 * n_ * n_ + 3 * 2.0 * m_ * n_ * 64 * 64 + 2.0 * n_ * n_ * 128 * 8
+      return (lambda: m(act, mask, pair), fl,
+              "configs[3] MSA pair-weighted averaging (MSAAttention), 1024 MSA rows x 768 tokens, 8 x 8")
+    m = modules.OuterProductMean(64, 128, 32)
+    synth.init_params(m, seed=4)
+    m = m.cuda()
+    modules.prepare(m)
+    fl = 2.0 * m_ * (n_ * 32) ** 2 + 2.0 * n_ * n_ * 1024 * 128 + 2 * 2.0 * m_ * n_ * 64 * 32
+    return (lambda: m(act, mask), fl, "configs[3] outer-product mean, 1024 MSA rows x 768 tokens, c=32 -> 128")
+  raise ValueError(op)
+
+
 def run_op(args) -> None:
-  """Time one hot-path op alone at N_token (for per-kernel rooflines and small ncu captures)."""
+  """Time one op alone (per-kernel rooflines, small ncu captures, the configs[2]/[3] workloads)."""
   import torch
   from sparsefold_b200 import _native, modules, synth
   _native.check(_native.load().sf_device_check(), "sf_device_check")
   n = args.n
-  make = {
+  pair_ops = {
       "tri_attention_start": lambda: modules.GridSelfAttention(128, 4, transpose=False),
       "tri_attention_end": lambda: modules.GridSelfAttention(128, 4, transpose=True),
       "tri_mult_outgoing": lambda: modules.TriangleMultiplication(128, "...ikc,...jkc->...ijc"),
       "tri_mult_incoming": lambda: modules.TriangleMultiplication(128, "...kjc,...kic->...ijc"),
       "pair_transition": lambda: modules.TransitionBlock(128, 4),
       "single_update": lambda: modules.SingleActUpdate(128, 384),
-  }[args.op]
-  m = make()
-  synth.init_params(m, seed=4)
-  m = m.cuda()
-  modules.prepare(m)
-  z, s, mask = synth.pair_inputs(n, n_real=max(1, N_REAL * n // N_TOKEN), seed=4)
-  z, s, mask = z.to("cuda", torch.bfloat16), s.to("cuda", torch.bfloat16), mask.cuda()
-  run = {
-      "pair_transition": lambda: m(z),
-      "single_update": lambda: m(z, s, mask),
-  }.get(args.op, lambda: m(z, mask))
+  }
+  if args.op in pair_ops:
+    m = pair_ops[args.op]()
+    synth.init_params(m, seed=4)
+    m = m.cuda()
+    modules.prepare(m)
+    z, s, mask = synth.pair_inputs(n, n_real=max(1, N_REAL * n // N_TOKEN), seed=4)
+    z, s, mask = z.to("cuda", torch.bfloat16), s.to("cuda", torch.bfloat16), mask.cuda()
+    run = {
+        "pair_transition": lambda: m(z),
+        "single_update": lambda: m(z, s, mask),
+    }.get(args.op, lambda: m(z, mask))
+    fl, what = op_flops(args.op, n), f"{args.op}, N={n}"
+  else:
+    run, fl, what = _workload_op(args.op, n)
   with torch.no_grad():
     for _ in range(args.warmup):
       run()
     st = torch.cuda.current_stream()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     torch.cuda.synchronize()
+    l0 = _native.launch_count()
     for a, b in ev:
       a.record(st)
       run()
       b.record(st)
     torch.cuda.synchronize()
+    launches = (_native.launch_count() - l0) // max(1, args.steps)
   ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
-  fl = op_flops(args.op, n)
   peaks = load_peaks()
-  print(json.dumps({"op": args.op, "n_token": n, "ms": round(ms, 4),
+  print(json.dumps({"op": args.op, "what": what, "n_token": n, "ms": round(ms, 4),
+                    "gflop": round(fl / 1e9, 2) if fl else None,
                     "tflop_per_s": round(fl / (ms * 1e-3) / 1e12, 2) if fl else None,
                     "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4) if fl else None,
+                    "peak_source": peaks["source"], "launches_per_call": int(launches),
                     "device_status": _native.device_status()}), flush=True)
 
 

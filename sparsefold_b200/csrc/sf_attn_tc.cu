@@ -1,0 +1,377 @@
+// Pair-biased gated attention on tcgen05 (bf16, fp32 accumulation): the
+// dot_product_attention of the single, token and atom attentions
+// (backends/torch/attention/sdpa.py:22-121 with the gate of
+// diffusion/transformer.py:306-345 and :549-585):
+//   out[b,q,h,:] = sigmoid(gate[b,q,h,:]) * softmax_k(scale q.k + bias[b,h,q,k] + maskbias) v
+// with maskbias = -FLT_MAX for a masked query row or key (the reference's
+// -finfo.max bias: a fully masked row averages v uniformly over every key).
+//
+// One CTA per (128 queries, head h, batch b); head dims D <= 64 (a multiple of
+// 8) are zero-padded to 64 in shared memory and TMEM.
+//   warps 0-3  softmax / epilogue, thread = query row: Q (pre-scaled by
+//              scale * log2 e) into TMEM, then per 64-key block the S row from
+//              TMEM + bias * log2 e from global memory, exp2 against a running
+//              max that moves only when a block exceeds it by 2^8 (then O is
+//              rescaled in TMEM), P as bf16 written over S; finally O / l,
+//              times the gate, stored with 16-byte stores.
+//   warp 4     producer: K and V rows of each key block, 16-byte loads, into a
+//              4-slot ring of 128B-swizzled [64 keys][64 dims] tiles (K read by
+//              the tensor core K-major, V as an MN-major B operand, so V needs
+//              no transpose); padding dims and keys beyond k_len are zero.
+//   warp 5     one thread issues S_j = Q K_j^T (A from TMEM) and O += P_j V_j
+//              (A = P_j from TMEM), S_{j+2} right after P_j V_j into the same
+//              TMEM buffer (MMAs of one thread complete in issue order).
+// TMEM: S/P double buffer [0,128), O [128,192), Q [192,224) of 256 columns.
+#include <cfloat>
+
+#include "sf_pair_tc.cuh"
+
+namespace sf {
+namespace {
+
+using namespace pt;
+
+constexpr int MH_KB = 64;                       // keys per block
+constexpr int MH_DP = 64;                       // padded head dim
+constexpr int MH_RING = 4;                      // key blocks staged ahead
+constexpr int MH_TILE_BYTES = MH_KB * MH_DP * 2;   // one [64][64] bf16 tile (8 KB)
+constexpr int MH_SLOT_BYTES = 2 * MH_TILE_BYTES;   // K then V
+constexpr int MH_MAX_KEYS = 65536;              // key-valid bits kept in shared memory
+constexpr int MH_OFF_RING = 0;
+constexpr int MH_OFF_KBITS = MH_OFF_RING + MH_RING * MH_SLOT_BYTES;
+constexpr int MH_OFF_BAR = MH_OFF_KBITS + MH_MAX_KEYS / 8;
+// one CTA's dynamic shared memory; kept above a third of the SM so at most two
+// CTAs (2 x 256 TMEM columns) share an SM
+constexpr int MH_SMEM = 80 * 1024 + 1024;
+static_assert(MH_OFF_BAR + 256 + 1024 <= MH_SMEM, "attention shared memory");
+constexpr int MH_THREADS = 6 * 32;
+constexpr float MH_RESCALE = 8.0f;
+
+struct MhaParams {
+  sf_attention_args a;
+  int bias_f32;
+  uint32_t* status;
+};
+
+__device__ __forceinline__ uint32_t tile_off(int r, int c) { return (uint32_t)r * 128u + (uint32_t)((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(MhaParams P) {
+  const sf_attention_args& a = P.a;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* kvfull = reinterpret_cast<uint64_t*>(smem + MH_OFF_BAR);   // [RING] K and V of a block staged (32)
+  uint64_t* kvfree = kvfull + MH_RING;                                  // [RING] P V of the slot's block done
+  uint64_t* sbar = kvfree + MH_RING;                                    // [2] S_j written
+  uint64_t* pready = sbar + 2;                                          // [2] P_j written (4 warps)
+  uint64_t* pvbar = pready + 2;                                         // [2] P_j V_j done
+  uint64_t* drain = pvbar + 2;                                          // issuer's drain barrier (abort path)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + MH_OFF_KBITS);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t b = blockIdx.z, h = blockIdx.y, q0 = (int64_t)blockIdx.x * TILE;
+  const int D = (int)a.head_dim;
+  const int nkb = (int)((a.k_len + MH_KB - 1) / MH_KB);
+  const int nkw = (int)((a.k_len + 31) / 32);
+  const bf16* kbase = static_cast<const bf16*>(a.k) + b * a.k_sb + h * a.k_sh;
+  const bf16* vbase = static_cast<const bf16*>(a.v) + b * a.v_sb + h * a.v_sh;
+  bool aborted = false;
+
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_relinquish();
+  }
+  if (tid == 5 * 32) {
+    for (int s = 0; s < MH_RING; ++s) {
+      tc::mbar_init(&kvfull[s], 32);
+      tc::mbar_init(&kvfree[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      tc::mbar_init(&sbar[s], 1);
+      tc::mbar_init(&pready[s], 4);
+      tc::mbar_init(&pvbar[s], 1);
+    }
+    tc::mbar_init(drain, 1);
+    tc::fence_mbar_init();
+  }
+  // key k counts iff k < k_len and mask_k[b, k] (sdpa.py:61-80); one bit per key
+  for (int w = warp; w < nkw; w += MH_THREADS / 32) {
+    const int64_t key = (int64_t)w * 32 + lane;
+    const bool ok = key < a.k_len && (!a.mask_k || a.mask_k[b * a.mk_sb + key] != 0);
+    const uint32_t bits = __ballot_sync(0xffffffffu, ok);
+    if (lane == 0) kbits[w] = bits;
+  }
+  // the query row of this thread (softmax warps): scaled by scale * log2 e into TMEM
+  const int64_t q = q0 + tid;
+  const bool qin = warp < 4 && q < a.q_len;
+  bool row_ok = qin;
+  if (qin && a.mask_row) row_ok = a.mask_row[b] != 0;
+  if (qin && a.mask_q) row_ok = row_ok && a.mask_q[b * a.mq_sb + q] != 0;
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  constexpr uint32_t S_COL = 0, O_COL = 128, Q_COL = 192;
+
+  if (warp < 4) {
+    const uint32_t lane_addr = tbase + ((uint32_t)(32 * warp) << 16);
+    {
+      uint32_t qw[32];
+      const float qs = a.scale * 1.4426950408889634f;
+      const bf16* qp = static_cast<const bf16*>(a.q) + b * a.q_sb + h * a.q_sh + (qin ? q : 0) * a.q_sq;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (qin && 8 * c < D) v = __ldg(reinterpret_cast<const uint4*>(qp + 8 * c));
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) qw[4 * c + e] = pack_bf2(bf_lo(u[e]) * qs, bf_hi(u[e]) * qs);
+      }
+      tc::tmem_st32(lane_addr + Q_COL, qw);
+      tc::tmem_wait_st();
+    }
+    tc::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) tc::mbar_arrive(&pready[1]);   // "Q is in TMEM": phase 0 of pready[1] (4 warps)
+
+    const bool use_bias = a.bias != nullptr && row_ok;
+    const char* brow = nullptr;
+    if (use_bias) {
+      const int64_t esz = P.bias_f32 ? 4 : 2;
+      brow = static_cast<const char*>(a.bias) + (b * a.b_sb + h * a.b_sh + q * a.b_sq) * esz;
+    }
+    float m_run = -INFINITY, l = 0.f;
+    for (int j = 0; j < nkb; ++j) {
+      const int64_t k0 = (int64_t)j * MH_KB;
+      // bias of this row and block (log2 units), read before the wait
+      float bv[MH_KB];
+      if (use_bias) {
+        const bool full = k0 + MH_KB <= a.k_len;
+        if (!P.bias_f32) {
+          const bf16* br = reinterpret_cast<const bf16*>(brow) + k0;
+          if (full && ((reinterpret_cast<uintptr_t>(br) & 15) == 0)) {
+#pragma unroll
+            for (int c = 0; c < MH_KB / 8; ++c) {
+              const uint4 v = __ldg(reinterpret_cast<const uint4*>(br) + c);
+              const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                bv[8 * c + 2 * e] = bf_lo(u[e]);
+                bv[8 * c + 2 * e + 1] = bf_hi(u[e]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < MH_KB; ++e) bv[e] = k0 + e < a.k_len ? __bfloat162float(br[e]) : 0.f;
+          }
+        } else {
+          const float* br = reinterpret_cast<const float*>(brow) + k0;
+#pragma unroll
+          for (int e = 0; e < MH_KB; ++e) bv[e] = k0 + e < a.k_len ? __ldg(br + e) : 0.f;
+        }
+      }
+      tc::mbar_wait(&sbar[j & 1], (j >> 1) & 1, P.status, aborted);
+      tc::tc_fence_after();
+      float sv[MH_KB];
+      tc::tmem_ld64(lane_addr + S_COL + (j & 1) * MH_KB, sv);
+      const uint32_t vb0 = kbits[2 * j], vb1 = (2 * j + 1 < nkw) ? kbits[2 * j + 1] : 0u;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < MH_KB; ++e) {
+        const bool inb = k0 + e < a.k_len;
+        const bool valid = ((e < 32 ? vb0 >> e : vb1 >> (e - 32)) & 1u) != 0;
+        float s = -INFINITY;                         // beyond the last key: no part at all
+        if (inb) s = (row_ok && valid) ? (use_bias ? fmaf(bv[e], 1.4426950408889634f, sv[e]) : sv[e]) : -FLT_MAX;
+        sv[e] = s;
+        mx = fmaxf(mx, s);
+      }
+      // the running max moves only when the block exceeds it by 2^8 (values stay <= 2^8)
+      const bool moves = m_run == -INFINITY ? mx != -INFINITY : mx > m_run + MH_RESCALE;
+      float corr = 1.f;
+      if (moves) {
+        corr = m_run == -INFINITY ? 0.f : ex2f(m_run - mx);
+        m_run = mx;
+      }
+      const float mref = m_run == -INFINITY ? 0.f : m_run;
+      uint32_t pk[MH_KB / 2];
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int e = 0; e < MH_KB; e += 2) {
+        const float p0 = ex2f(sv[e] - mref), p1 = ex2f(sv[e + 1] - mref);
+        ps0 += p0;
+        ps1 += p1;
+        pk[e >> 1] = pack_bf2(p0, p1);
+      }
+      l = l * corr + (ps0 + ps1);
+      // O holds P V up to block j-1: rescale it once P_{j-1} V_{j-1} is done (warp-uniform branch)
+      if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+        tc::mbar_wait(&pvbar[(j - 1) & 1], ((j - 1) >> 1) & 1, P.status, aborted);
+        tc::tc_fence_after();
+        float ov[MH_DP];
+        tc::tmem_ld64(lane_addr + O_COL, ov);
+        uint32_t r0[32], r1[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          r0[e] = __float_as_uint(ov[e] * corr);
+          r1[e] = __float_as_uint(ov[32 + e] * corr);
+        }
+        tc::tmem_st32(lane_addr + O_COL, r0);
+        tc::tmem_st32(lane_addr + O_COL + 32, r1);
+      }
+      tc::tmem_st32(lane_addr + S_COL + (j & 1) * MH_KB, pk);   // P_j over S_j
+      tc::tmem_wait_st();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&pready[j & 1]);
+    }
+    // ---- O / l, gate, store ----
+    if (nkb >= 2) tc::mbar_wait(&pvbar[(nkb - 2) & 1], ((nkb - 2) >> 1) & 1, P.status, aborted);
+    tc::mbar_wait(&pvbar[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, P.status, aborted);
+    tc::tc_fence_after();
+    float ov[MH_DP];
+    tc::tmem_ld64(lane_addr + O_COL, ov);
+    if (qin) {
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      bf16* op = static_cast<bf16*>(a.out) + b * a.o_sb + h * a.o_sh + q * a.o_sq;
+      const bf16* gp = a.gate ? static_cast<const bf16*>(a.gate) + b * a.g_sb + h * a.g_sh + q * a.g_sq : nullptr;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        if (8 * c < D) {
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = ov[8 * c + e] * inv;
+          if (gp) {
+            const uint4 g = __ldg(reinterpret_cast<const uint4*>(gp + 8 * c));
+            const uint32_t gu[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              o[2 * e] *= fast_sigmoid(bf_lo(gu[e]));
+              o[2 * e + 1] *= fast_sigmoid(bf_hi(gu[e]));
+            }
+          }
+          *reinterpret_cast<uint4*>(op + 8 * c) =
+              make_uint4(pack_bf2(o[0], o[1]), pack_bf2(o[2], o[3]), pack_bf2(o[4], o[5]), pack_bf2(o[6], o[7]));
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ---- producer: K and V rows of block j into slot j % RING (stops at its first failed wait) ----
+    const int nch = D / 8;   // 16-byte chunks of a row that hold data
+    for (int j = 0; j < nkb && !aborted; ++j) {
+      const int slot = j % MH_RING;
+      if (j >= MH_RING && !tc::mbar_wait(&kvfree[slot], ((j / MH_RING) + 1) & 1, P.status, aborted)) break;
+      uint8_t* kt = smem + MH_OFF_RING + slot * MH_SLOT_BYTES;
+      uint8_t* vt = kt + MH_TILE_BYTES;
+      const int64_t k0 = (int64_t)j * MH_KB;
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {   // 32 key rows at a time: lane = key row, 8 chunks each
+        const int r = half * 32 + lane;
+        const int64_t key = k0 + r;
+        const bool live = key < a.k_len;
+        uint4 kv[8], vv[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          kv[c] = make_uint4(0u, 0u, 0u, 0u);
+          vv[c] = make_uint4(0u, 0u, 0u, 0u);
+          if (live && c < nch) {
+            kv[c] = __ldg(reinterpret_cast<const uint4*>(kbase + key * a.k_sk) + c);
+            vv[c] = __ldg(reinterpret_cast<const uint4*>(vbase + key * a.v_sk) + c);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          *reinterpret_cast<uint4*>(kt + tile_off(r, c)) = kv[c];
+          *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = vv[c];
+        }
+      }
+      tc::fence_proxy_async();   // the generic-proxy stores, seen by the tensor core
+      tc::mbar_arrive(&kvfull[slot]);
+    }
+  } else if (lane == 0) {
+    // ---- warp 5: MMA issuer (stops at its first failed wait) ----
+    constexpr uint32_t ID_S = tc::idesc_bf16(128, MH_KB);
+    constexpr uint32_t ID_PV = tc::idesc_bf16(128, MH_DP) | (1u << 16);   // B (V) MN-major
+    const uint32_t sb = tc::smem_u32(smem);
+    auto issue_s = [&](int jj) {   // S_jj = Q K_jj^T into buffer jj & 1
+      const int slot = jj % MH_RING;
+      if (!tc::mbar_wait(&kvfull[slot], (jj / MH_RING) & 1, P.status, aborted)) return;
+      tc::tc_fence_after();
+      const uint32_t kt = sb + MH_OFF_RING + slot * MH_SLOT_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < MH_DP / 16; ++kk)
+        tc::mma_bf16_ts(tbase + S_COL + (jj & 1) * MH_KB, tbase + Q_COL + kk * 8,
+                        tc::smem_desc(kt + kk * 32, 1024, tc::kSW128), ID_S, kk > 0);
+      tc::mma_commit(&sbar[jj & 1]);
+    };
+    // Q must be in TMEM before the first S
+    if (tc::mbar_wait(&pready[1], 0, P.status, aborted)) {
+      tc::tc_fence_after();
+      issue_s(0);
+      if (!aborted && nkb > 1) issue_s(1);
+    }
+    for (int j = 0; j < nkb && !aborted; ++j) {
+      // pready[1] completed one extra phase for Q: block j's phase is (j >> 1) + (j & 1)
+      const uint32_t ph = ((j >> 1) + (j & 1)) & 1;
+      if (!tc::mbar_wait(&pready[j & 1], ph, P.status, aborted)) break;
+      tc::tc_fence_after();
+      const uint32_t vt = sb + MH_OFF_RING + (j % MH_RING) * MH_SLOT_BYTES + MH_TILE_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < MH_KB / 16; ++kk)
+        tc::mma_bf16_ts(tbase + O_COL, tbase + S_COL + (j & 1) * MH_KB + kk * 8,
+                        tc::smem_desc_mn(vt + kk * 2048, MH_TILE_BYTES, 1024, tc::kSW128), ID_PV, j > 0 || kk > 0);
+      tc::mma_commit(&pvbar[j & 1]);
+      tc::mma_commit(&kvfree[j % MH_RING]);
+      if (j + 2 < nkb) issue_s(j + 2);
+    }
+  }
+  tc::tc_fence_before();
+  if (__syncthreads_or(aborted)) {   // abort path: the issuer's MMAs must be done before TMEM is freed
+    if (warp == 5 && lane == 0) tc::drain_mma(drain, P.status);
+    __syncthreads();
+  }
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tbase, 256);
+  }
+}
+
+}  // namespace
+
+// Returns SF_OK after launching, or SF_ERR_ARG (with no message) when the call is outside what
+// this kernel takes, so that the caller uses the CUDA-core kernel instead.
+int attention_tc(const sf_attention_args* a, cudaStream_t stream) {
+  const int64_t D = a->head_dim;
+  const bool f32bias = a->bias && a->bias_dtype == SF_F32;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool ok = a->dtype == SF_BF16 && D % 8 == 0 && D <= MH_DP && (a->value_dim == 0 || a->value_dim == D) &&
+                  a->k_len > 0 && a->k_len <= MH_MAX_KEYS && al16(a->q) && al16(a->k) && al16(a->v) && al16(a->out) &&
+                  (!a->gate || al16(a->gate)) && (a->q_sb | a->q_sh | a->q_sq | a->k_sb | a->k_sh | a->k_sk | a->v_sb |
+                                                  a->v_sh | a->v_sk | a->o_sb | a->o_sh | a->o_sq) % 8 == 0 &&
+                  (!a->gate || (a->g_sb | a->g_sh | a->g_sq) % 8 == 0) && a->q_len <= (int64_t(1) << 31) - TILE;
+  if (!ok) return SF_ERR_ARG;
+  uint32_t* status = device_status_ptr();
+  if (!status) return SF_ERR_CUDA;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(k_mha_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, MH_SMEM);
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute(attention): %s", cudaGetErrorString(e));
+      return SF_ERR_CUDA;
+    }
+    attr[dev & 63] = true;
+  }
+  MhaParams p{*a, f32bias ? 1 : 0, status};
+  dim3 grid((unsigned)((a->q_len + TILE - 1) / TILE), (unsigned)a->heads, (unsigned)a->batch);
+  k_mha_tc<<<grid, MH_THREADS, MH_SMEM, stream>>>(p);
+  count_launch();
+  return check_launch("attention_tc");
+}
+
+}  // namespace sf

@@ -88,6 +88,9 @@ int linear_tc(const bf16* x, const bf16* wt, const float* bias, const bf16* resi
               int64_t N, int post_op, cudaStream_t stream);
 int contract_tc(const bf16* a_op, const bf16* b_op, bf16* P, int64_t channels, int64_t rows, int64_t cols,
                 int64_t kdim, cudaStream_t stream);
+// Generic pair-biased gated attention on tcgen05 (bf16, head dim <= 64, a multiple of 8);
+// SF_ERR_ARG without a message when the call is outside what it takes.
+int attention_tc(const sf_attention_args* a, cudaStream_t stream);
 int trimul_project_tc(const bf16* z, const uint8_t* mask, int64_t rows, int64_t n, int64_t row_offset, int incoming,
                       const float* ln_w, const float* ln_b, const bf16* w_glu, bf16* a_op, bf16* b_op,
                       cudaStream_t stream);

@@ -336,6 +336,10 @@ int sf_attention(const sf_attention_args* a, sf_stream_t stream) {
   SF_REQUIRE(a->k_len > 0, "sf_attention: k_len must be positive");
   SF_REQUIRE(!a->bias || a->bias_dtype == SF_F32 || a->bias_dtype == a->dtype, "sf_attention: bias dtype");
   SF_REQUIRE((a->q_len + ATT_QB - 1) / ATT_QB <= 0x7fffffff, "sf_attention: q_len too large");
+  {
+    const int st = attention_tc(a, stream);   // bf16, head dim <= 64: the tensor-core kernel
+    if (st != SF_ERR_ARG) return st;
+  }
   dim3 grid((unsigned)((a->q_len + ATT_QB - 1) / ATT_QB), (unsigned)a->heads, (unsigned)a->batch);
   const size_t smem = attention_smem_bytes((int)a->head_dim, dv);
   SF_DISPATCH(a->dtype, {
