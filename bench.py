@@ -197,6 +197,55 @@ def time_kernel_probe(n: int, dtype, iters: int = 10) -> float:
   return sum(a.elapsed_time(b) for a, b in ev) / iters
 
 
+def measure_configs4(trunk, world: int, rank: int, dev, l2_flush, steps: int = 2, warmup: int = 1) -> dict:
+  """configs[4] beside the headline: the 48-block trunk at N_token=2048 (1931 real), pair rows sharded over
+  the job's ranks, device time per block (max over ranks, L2 flushed before each step); with more than one
+  rank, rank 0 also times the unsharded trunk alone on its GPU in the same run, so the parallel efficiency
+  T1 / (P * TP) comes from one run on one box."""
+  import torch
+  from sparsefold_b200 import sharding, synth
+  n4, r4 = 2048, 1931
+  dt = torch.bfloat16
+  shard = sharding.Shard(n4, world, rank)
+  z_h, s_h, m_h = synth.pair_inputs(n4, C_Z, C_S, n_real=r4, seed=0)
+  mask = m_h.to(dev)
+
+  def timed(z, s, sharded):
+    run = (lambda: sharding.pairformer_trunk(trunk, z, s, mask, shard)) if sharded else (lambda: trunk(z, s, mask))
+    for _ in range(warmup):
+      run()
+    st = torch.cuda.current_stream()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for a, b in evs:
+      flush_l2(l2_flush)
+      a.record(st)
+      run()
+      b.record(st)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / steps / N_BLOCKS
+
+  if world > 1:
+    zl, sl = shard.shard(z_h).contiguous().to(dev, dt), shard.shard(s_h).contiguous().to(dev, dt)
+    barrier(world)
+    tp = max_over_ranks(timed(zl, sl, True), world)
+    del zl, sl
+  t1 = None
+  if rank == 0:
+    t1 = timed(z_h.to(dev, dt), s_h.to(dev, dt), False)
+    torch.cuda.empty_cache()
+  barrier(world)
+  if world == 1:
+    tp = t1
+  out = {"workload": "configs[4]: 48-block Pairformer trunk, N_token=2048 (1931 real), 4 chains of 512, bf16",
+         "n_gpus": world, "ms_per_block": round(tp, 3), "steps": steps, "warmup": warmup,
+         "block_gflop": round(block_flops(n4) / 1e9, 1), "trunk_tflop_per_s": round(block_flops(n4) / (tp * 1e-3) / 1e12, 2)}
+  if rank == 0 and world > 1:
+    out["ms_per_block_1gpu_same_run"] = round(t1, 3)
+    out["efficiency_vs_1gpu_same_run"] = round(t1 / (world * tp), 4)
+  return out
+
+
 def run_b200(args) -> None:
   import torch
   from sparsefold_b200 import _native, synth
@@ -279,6 +328,9 @@ def run_b200(args) -> None:
     # ---- dominant-kernel roofline: triangle attention core ----
     probe_ms = time_kernel_probe(N_TOKEN, dt) if rank == 0 else 0.0
 
+    # ---- the N=2048 trunk (1931 real tokens), rows sharded over the same ranks ----
+    c4 = measure_configs4(trunk, world, rank, dev, l2_flush) if args.configs4 else None
+
   peaks = load_peaks()
   flops = tri_attention_op_flops(N_TOKEN)
   achieved = flops / (probe_ms * 1e-3) / 1e12 if probe_ms > 0 else 0.0
@@ -305,6 +357,7 @@ def run_b200(args) -> None:
                      "exp2_bound_ms": round(tri_attention_exp2_count(N_TOKEN) / (16 * 148 * 1.9e9) * 1e3, 4)},
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
+        "configs4": c4,
     }
     print(json.dumps(line), flush=True)
   if world > 1:
@@ -599,6 +652,8 @@ def main():
   ap.add_argument("--warmup", type=int, default=3)
   ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
   ap.add_argument("--no-cpu-baseline", action="store_true")
+  ap.add_argument("--no-configs4", dest="configs4", action="store_false",
+                  help="skip the configs[4] (N_token=2048) trunk measured beside the headline")
   ap.add_argument("--op", choices=OPS, default=None, help="time one op alone instead of the trunk")
   ap.add_argument("--n", type=int, default=N_TOKEN, help="N_token for --op")
   ap.add_argument("--n-token", type=int, default=N_TOKEN, help="N_token of the trunk (512 = configs[1], 2048 = configs[4])")

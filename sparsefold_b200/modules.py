@@ -71,11 +71,29 @@ class B200Module:
     return self._buffers[f"_sf_{name}"]
 
 
-def _check_pair(act: torch.Tensor, mask: torch.Tensor, c: int) -> None:
-  if act.ndim != 3 or act.shape[0] != act.shape[1] or act.shape[2] != c:
-    raise ValueError(f"pair activation must be [N, N, {c}] on one device, got {tuple(act.shape)}")
-  if mask.shape != (act.shape[0],):
+def _check_pair(act: torch.Tensor, mask: torch.Tensor, c: int, shard=None) -> None:
+  rows = act.shape[1] if shard is None else shard.size()
+  if act.ndim != 3 or act.shape[0] != rows or act.shape[2] != c:
+    raise ValueError(f"pair activation must be [{'N' if shard is None else 'N/P'}, N, {c}], got {tuple(act.shape)}")
+  if mask.shape != (act.shape[1],):
     raise ValueError(f"mask must be [N], got {tuple(mask.shape)}")
+
+
+def _reference_shard(mod):
+  """The row shard of the reference's distributed mode, or None.
+
+  A reference module built with ``distributed=True`` while the reference's
+  runtime/dist.py is initialised reads ``dist.current_shard`` (trunk/blocks.py:309-314,
+  :499-503); the B200 mixins then run the sharded phase entry points with the same
+  partition (``sharding.Shard`` follows the reference's even / ragged rule)."""
+  if not getattr(mod, "distributed", False):
+    return None
+  from sparsefold.runtime import dist as rdist   # only reference-built modules get here
+  cs = rdist.current_shard
+  if cs is None:
+    return None
+  from sparsefold_b200 import sharding
+  return sharding.Shard(cs.length, rdist.get_world_size(), rdist.get_rank(), even=cs.is_even)
 
 
 # ---------------------------------------------------------------------------
@@ -113,7 +131,11 @@ class TriangleMultiplicationB200(B200Module):
 
   @_require_prepared
   def forward(self, act: torch.Tensor, mask: torch.Tensor):
-    _check_pair(act, mask, self.num_channels)
+    shard = _reference_shard(self)
+    _check_pair(act, mask, self.num_channels, shard)
+    if shard is not None:   # rows sharded over the ranks (blocks.py:540-556)
+      from sparsefold_b200 import sharding
+      return sharding.tri_mult(self, act.contiguous(), ops.mask_u8(mask), shard)
     w = self.native_weights(act.dtype)
     return ops.tri_mult(act.contiguous(), ops.mask_u8(mask), w, self.incoming)
 
@@ -148,7 +170,11 @@ class GridSelfAttentionB200(B200Module):
 
   @_require_prepared
   def forward(self, act: torch.Tensor, seq_mask: torch.Tensor):
-    _check_pair(act, seq_mask, self.num_channels)
+    shard = _reference_shard(self)
+    _check_pair(act, seq_mask, self.num_channels, shard)
+    if shard is not None:   # rows sharded over the ranks (blocks.py:309-346)
+      from sparsefold_b200 import sharding
+      return sharding.tri_attention(self, act.contiguous(), ops.mask_u8(seq_mask), shard)
     w = self.native_weights(act.dtype)
     return ops.tri_attention(act.contiguous(), ops.mask_u8(seq_mask), w, bool(self.transpose))
 
@@ -244,6 +270,11 @@ class SelfAttentionB200(B200Module):
     y = ops.linear(xn, self._packed("qkvg", dt), bias=self._kept("qkvg_bias"))   # [..., N, 4*H*D]
     y = y.view(*x.shape[:-1], 4, h, d)
     q, k, v, g = (y[..., i, :, :] for i in range(4))
+    shard = _reference_shard(self)
+    if shard is not None:   # keys and values of every rank's rows (diffusion/transformer.py:322-330)
+      from sparsefold_b200 import sharding
+      yf = sharding.all_gather_rows(y.reshape(y.shape[-4], -1)).view(-1, 4, h, d)
+      k, v = yf[:, 1], yf[:, 2]
     o = ops.attention(q, k, v, mask_k=mask, bias=pair_logits, gate=g)
     return _apply_zero_init(self, self.zero_init, o.reshape(*x.shape[:-1], h * d), single_cond, x)
 

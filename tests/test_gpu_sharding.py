@@ -93,5 +93,9 @@ def test_two_gpu_sharded_block_matches_block():
     p.start()
   for p in procs:
     p.join(300)
+  for p in procs:   # a rank still waiting after the limit is ended, not left behind
+    if p.is_alive():
+      p.kill()
+      p.join(10)
   assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
   assert q.get(timeout=10) == "ok"
