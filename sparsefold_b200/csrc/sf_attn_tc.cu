@@ -6,21 +6,22 @@
 // with maskbias = -FLT_MAX for a masked query row or key (the reference's
 // -finfo.max bias: a fully masked row averages v uniformly over every key).
 //
-// One CTA per (128 queries, head h, batch b); head dims D <= 64 (a multiple of
-// 8) are zero-padded to 64 in shared memory and TMEM.
-//   warps 0-3  softmax / epilogue, thread = query row: Q (pre-scaled by
-//              scale * log2 e) into TMEM, then per 64-key block the S row from
-//              TMEM + bias * log2 e from global memory, exp2 against a running
-//              max that moves only when a block exceeds it by 2^8 (then O is
-//              rescaled in TMEM), P as bf16 written over S; finally O / l,
-//              times the gate, stored with 16-byte stores.
-//   warp 4     producer: K and V rows of each key block, 16-byte loads, into a
-//              4-slot ring of 128B-swizzled [64 keys][64 dims] tiles (K read by
-//              the tensor core K-major, V as an MN-major B operand, so V needs
-//              no transpose); padding dims and keys beyond k_len are zero.
-//   warp 5     one thread issues S_j = Q K_j^T (A from TMEM) and O += P_j V_j
-//              (A = P_j from TMEM), S_{j+2} right after P_j V_j into the same
-//              TMEM buffer (MMAs of one thread complete in issue order).
+// One CTA per (128 queries, head h, batch b); head dims D <= 64 (a multiple of 8).
+//   one thread  TMA producer: per 64-key block the K tile [64 keys][32 or 64 dims]
+//               (64B or 128B swizzle), the V tile [64 keys][64 dims] (128B swizzle)
+//               and the bf16 bias tile [128 queries][64 keys] (128B swizzle) into a
+//               3-slot ring; dims beyond D and keys beyond k_len arrive as zeros
+//               (the tensor maps' bounds), so nothing is staged by hand.
+//   warps 0-3   softmax / epilogue, thread = query row: Q (pre-scaled by
+//               scale * log2 e) into TMEM, then per block the S row from TMEM plus
+//               the bias row from shared memory times log2 e, exp2 against a running
+//               max that moves only when a block exceeds it by 2^8 (then O is
+//               rescaled in TMEM), P as bf16 written over S; finally O / l, times
+//               the gate, stored with 16-byte stores.
+//   warp 5      one thread issues S_j = Q K_j^T (A from TMEM) and O += P_j V_j (A =
+//               P_j from TMEM, V as an MN-major B operand, so V needs no transpose),
+//               S_{j+2} right after P_j V_j into the same TMEM buffer (MMAs of one
+//               thread complete in issue order).
 // TMEM: S/P double buffer [0,128), O [128,192), Q [192,224) of 256 columns.
 #include <cfloat>
 
@@ -31,29 +32,27 @@ namespace {
 
 using namespace pt;
 
-constexpr int MH_KB = 64;                       // keys per block
-constexpr int MH_DP = 64;                       // padded head dim
-constexpr int MH_RING = 4;                      // key blocks staged ahead
-constexpr int MH_TILE_BYTES = MH_KB * MH_DP * 2;   // one [64][64] bf16 tile (8 KB)
-constexpr int MH_SLOT_BYTES = 2 * MH_TILE_BYTES;   // K then V
-constexpr int MH_MAX_KEYS = 65536;              // key-valid bits kept in shared memory
+constexpr int MH_KB = 64;                          // keys per block
+constexpr int MH_DP = 64;                          // padded head dim of V, O (and of K when D > 32)
+constexpr int MH_RING = 3;                         // key blocks staged ahead
+constexpr int MH_K_BYTES = MH_KB * 128;            // K tile (64 rows of up to 128 B)
+constexpr int MH_V_BYTES = MH_KB * 128;            // V tile [64 keys][64 dims]
+constexpr int MH_B_BYTES = TILE * MH_KB * 2;       // bias tile [128 queries][64 keys]
+constexpr int MH_SLOT_BYTES = MH_K_BYTES + MH_V_BYTES + MH_B_BYTES;   // 32 KB
+constexpr int MH_MAX_KEYS = 65536;                 // key-valid bits kept in shared memory
 constexpr int MH_OFF_RING = 0;
 constexpr int MH_OFF_KBITS = MH_OFF_RING + MH_RING * MH_SLOT_BYTES;
 constexpr int MH_OFF_BAR = MH_OFF_KBITS + MH_MAX_KEYS / 8;
-// one CTA's dynamic shared memory; kept above a third of the SM so at most two
-// CTAs (2 x 256 TMEM columns) share an SM
-constexpr int MH_SMEM = 80 * 1024 + 1024;
-static_assert(MH_OFF_BAR + 256 + 1024 <= MH_SMEM, "attention shared memory");
+constexpr int MH_SMEM = MH_OFF_BAR + 256 + 1024;
+static_assert(MH_SMEM <= 232448 / 2, "two attention CTAs per SM");
 constexpr int MH_THREADS = 6 * 32;
 constexpr float MH_RESCALE = 8.0f;
 
 struct MhaParams {
   sf_attention_args a;
-  int bias_f32;
+  int bias_batched;   // the bias map has a batch dimension (else one bias for every batch entry)
   uint32_t* status;
 };
-
-__device__ __forceinline__ uint32_t tile_off(int r, int c) { return (uint32_t)r * 128u + (uint32_t)((c ^ (r & 7)) << 4); }
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -61,13 +60,18 @@ __device__ __forceinline__ float ex2f(float x) {
   return y;
 }
 
-__global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(MhaParams P) {
+// KSW: swizzle of the K tile, 64 (rows of 32 dims, D <= 32) or 128 (rows of 64 dims).
+template <int KSW>
+__global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant__ CUtensorMap tmK,
+                                                          const __grid_constant__ CUtensorMap tmV,
+                                                          const __grid_constant__ CUtensorMap tmB, MhaParams P) {
+  constexpr int DK = KSW / 2;                     // padded head dim of K (32 or 64)
   const sf_attention_args& a = P.a;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint64_t* kvfull = reinterpret_cast<uint64_t*>(smem + MH_OFF_BAR);   // [RING] K and V of a block staged (32)
+  uint64_t* kvfull = reinterpret_cast<uint64_t*>(smem + MH_OFF_BAR);   // [RING] K, V and bias of a block landed
   uint64_t* kvfree = kvfull + MH_RING;                                  // [RING] P V of the slot's block done
-  uint64_t* sbar = kvfree + MH_RING;                                    // [2] S_j written
+  uint64_t* sbar = kvfree + MH_RING;                                    // [2] S_j written and block j landed (2)
   uint64_t* pready = sbar + 2;                                          // [2] P_j written (4 warps)
   uint64_t* pvbar = pready + 2;                                         // [2] P_j V_j done
   uint64_t* drain = pvbar + 2;                                          // issuer's drain barrier (abort path)
@@ -78,26 +82,46 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(MhaParams P) {
   const int D = (int)a.head_dim;
   const int nkb = (int)((a.k_len + MH_KB - 1) / MH_KB);
   const int nkw = (int)((a.k_len + 31) / 32);
-  const bf16* kbase = static_cast<const bf16*>(a.k) + b * a.k_sb + h * a.k_sh;
-  const bf16* vbase = static_cast<const bf16*>(a.v) + b * a.v_sb + h * a.v_sh;
+  const bool has_bias = a.bias != nullptr;
   bool aborted = false;
+  uint32_t loads = 0;   // key blocks requested by the producer (abort-path drain)
+  auto slot_of = [&](int jj) { return smem + MH_OFF_RING + (jj % MH_RING) * MH_SLOT_BYTES; };
+  auto issue_load = [&](int jj) {   // block jj into slot jj % RING (jj == loads)
+    ++loads;
+    uint8_t* sl = slot_of(jj);
+    uint64_t* bar = &kvfull[jj % MH_RING];
+    tc::mbar_expect_tx(bar, MH_KB * KSW + MH_V_BYTES + (has_bias ? MH_B_BYTES : 0));
+    tc::tma_load_4d(sl, &tmK, bar, 0, jj * MH_KB, (int)h, (int)b);
+    tc::tma_load_4d(sl + MH_K_BYTES, &tmV, bar, 0, jj * MH_KB, (int)h, (int)b);
+    if (has_bias) {
+      if (P.bias_batched)
+        tc::tma_load_4d(sl + MH_K_BYTES + MH_V_BYTES, &tmB, bar, jj * MH_KB, (int)q0, (int)h, (int)b);
+      else
+        tc::tma_load_3d(sl + MH_K_BYTES + MH_V_BYTES, &tmB, bar, jj * MH_KB, (int)q0, (int)h);
+    }
+  };
 
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 256);
     tc::tmem_relinquish();
   }
-  if (tid == 5 * 32) {
+  if (tid == 4 * 32) {
     for (int s = 0; s < MH_RING; ++s) {
-      tc::mbar_init(&kvfull[s], 32);
+      tc::mbar_init(&kvfull[s], 1);
       tc::mbar_init(&kvfree[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
-      tc::mbar_init(&sbar[s], 1);
+      tc::mbar_init(&sbar[s], 2);
       tc::mbar_init(&pready[s], 4);
       tc::mbar_init(&pvbar[s], 1);
     }
     tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmK);
+    tc::prefetch_tmap(&tmV);
+    if (has_bias) tc::prefetch_tmap(&tmB);
+    // the ring's first blocks at once, under the Q and mask loads
+    for (int jj = 0; jj < MH_RING && jj < nkb; ++jj) issue_load(jj);
   }
   // key k counts iff k < k_len and mask_k[b, k] (sdpa.py:61-80); one bit per key
   for (int w = warp; w < nkw; w += MH_THREADS / 32) {
@@ -106,7 +130,7 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(MhaParams P) {
     const uint32_t bits = __ballot_sync(0xffffffffu, ok);
     if (lane == 0) kbits[w] = bits;
   }
-  // the query row of this thread (softmax warps): scaled by scale * log2 e into TMEM
+  // the query row of this thread (softmax warps)
   const int64_t q = q0 + tid;
   const bool qin = warp < 4 && q < a.q_len;
   bool row_ok = qin;
@@ -120,7 +144,7 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(MhaParams P) {
 
   if (warp < 4) {
     const uint32_t lane_addr = tbase + ((uint32_t)(32 * warp) << 16);
-    {
+    {   // Q row, scaled by scale * log2 e, into TMEM (zero beyond D)
       uint32_t qw[32];
       const float qs = a.scale * 1.4426950408889634f;
       const bf16* qp = static_cast<const bf16*>(a.q) + b * a.q_sb + h * a.q_sh + (qin ? q : 0) * a.q_sq;
@@ -139,54 +163,35 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(MhaParams P) {
     __syncwarp();
     if (lane == 0) tc::mbar_arrive(&pready[1]);   // "Q is in TMEM": phase 0 of pready[1] (4 warps)
 
-    const bool use_bias = a.bias != nullptr && row_ok;
-    const char* brow = nullptr;
-    if (use_bias) {
-      const int64_t esz = P.bias_f32 ? 4 : 2;
-      brow = static_cast<const char*>(a.bias) + (b * a.b_sb + h * a.b_sh + q * a.b_sq) * esz;
-    }
+    const bool use_bias = has_bias && row_ok;
     float m_run = -INFINITY, l = 0.f;
     for (int j = 0; j < nkb; ++j) {
       const int64_t k0 = (int64_t)j * MH_KB;
-      // bias of this row and block (log2 units), read before the wait
-      float bv[MH_KB];
-      if (use_bias) {
-        const bool full = k0 + MH_KB <= a.k_len;
-        if (!P.bias_f32) {
-          const bf16* br = reinterpret_cast<const bf16*>(brow) + k0;
-          if (full && ((reinterpret_cast<uintptr_t>(br) & 15) == 0)) {
-#pragma unroll
-            for (int c = 0; c < MH_KB / 8; ++c) {
-              const uint4 v = __ldg(reinterpret_cast<const uint4*>(br) + c);
-              const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                bv[8 * c + 2 * e] = bf_lo(u[e]);
-                bv[8 * c + 2 * e + 1] = bf_hi(u[e]);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < MH_KB; ++e) bv[e] = k0 + e < a.k_len ? __bfloat162float(br[e]) : 0.f;
-          }
-        } else {
-          const float* br = reinterpret_cast<const float*>(brow) + k0;
-#pragma unroll
-          for (int e = 0; e < MH_KB; ++e) bv[e] = k0 + e < a.k_len ? __ldg(br + e) : 0.f;
-        }
-      }
+      // S_j is written and block j (its bias tile) has landed
       tc::mbar_wait(&sbar[j & 1], (j >> 1) & 1, P.status, aborted);
       tc::tc_fence_after();
       float sv[MH_KB];
       tc::tmem_ld64(lane_addr + S_COL + (j & 1) * MH_KB, sv);
+      if (use_bias) {
+        const uint8_t* brow = slot_of(j) + MH_K_BYTES + MH_V_BYTES;
+#pragma unroll
+        for (int c = 0; c < MH_KB / 8; ++c) {
+          const uint4 v = *reinterpret_cast<const uint4*>(brow + tc::sw128_off(tid, c));
+          const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            sv[8 * c + 2 * e] = fmaf(bf_lo(u[e]), 1.4426950408889634f, sv[8 * c + 2 * e]);
+            sv[8 * c + 2 * e + 1] = fmaf(bf_hi(u[e]), 1.4426950408889634f, sv[8 * c + 2 * e + 1]);
+          }
+        }
+      }
       const uint32_t vb0 = kbits[2 * j], vb1 = (2 * j + 1 < nkw) ? kbits[2 * j + 1] : 0u;
       float mx = -INFINITY;
 #pragma unroll
       for (int e = 0; e < MH_KB; ++e) {
         const bool inb = k0 + e < a.k_len;
         const bool valid = ((e < 32 ? vb0 >> e : vb1 >> (e - 32)) & 1u) != 0;
-        float s = -INFINITY;                         // beyond the last key: no part at all
-        if (inb) s = (row_ok && valid) ? (use_bias ? fmaf(bv[e], 1.4426950408889634f, sv[e]) : sv[e]) : -FLT_MAX;
+        const float s = !inb ? -INFINITY : (row_ok && valid) ? sv[e] : -FLT_MAX;   // beyond k_len: no part at all
         sv[e] = s;
         mx = fmaxf(mx, s);
       }
@@ -260,52 +265,28 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(MhaParams P) {
       }
     }
   } else if (warp == 4) {
-    // ---- producer: K and V rows of block j into slot j % RING (stops at its first failed wait) ----
-    const int nch = D / 8;   // 16-byte chunks of a row that hold data
-    for (int j = 0; j < nkb && !aborted; ++j) {
-      const int slot = j % MH_RING;
-      if (j >= MH_RING && !tc::mbar_wait(&kvfree[slot], ((j / MH_RING) + 1) & 1, P.status, aborted)) break;
-      uint8_t* kt = smem + MH_OFF_RING + slot * MH_SLOT_BYTES;
-      uint8_t* vt = kt + MH_TILE_BYTES;
-      const int64_t k0 = (int64_t)j * MH_KB;
-#pragma unroll 1
-      for (int half = 0; half < 2; ++half) {   // 32 key rows at a time: lane = key row, 8 chunks each
-        const int r = half * 32 + lane;
-        const int64_t key = k0 + r;
-        const bool live = key < a.k_len;
-        uint4 kv[8], vv[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          kv[c] = make_uint4(0u, 0u, 0u, 0u);
-          vv[c] = make_uint4(0u, 0u, 0u, 0u);
-          if (live && c < nch) {
-            kv[c] = __ldg(reinterpret_cast<const uint4*>(kbase + key * a.k_sk) + c);
-            vv[c] = __ldg(reinterpret_cast<const uint4*>(vbase + key * a.v_sk) + c);
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          *reinterpret_cast<uint4*>(kt + tile_off(r, c)) = kv[c];
-          *reinterpret_cast<uint4*>(vt + tile_off(r, c)) = vv[c];
-        }
+    // ---- TMA producer: block j + RING into the slot of block j once P_j V_j is done ----
+    if (lane == 0) {
+      for (int jj = MH_RING; jj < nkb; ++jj) {
+        if (!tc::mbar_wait(&kvfree[jj % MH_RING], ((jj / MH_RING) + 1) & 1, P.status, aborted)) break;
+        issue_load(jj);
       }
-      tc::fence_proxy_async();   // the generic-proxy stores, seen by the tensor core
-      tc::mbar_arrive(&kvfull[slot]);
     }
   } else if (lane == 0) {
     // ---- warp 5: MMA issuer (stops at its first failed wait) ----
     constexpr uint32_t ID_S = tc::idesc_bf16(128, MH_KB);
     constexpr uint32_t ID_PV = tc::idesc_bf16(128, MH_DP) | (1u << 16);   // B (V) MN-major
+    constexpr tc::Swizzle KSWZ = KSW == 128 ? tc::kSW128 : tc::kSW64;
     const uint32_t sb = tc::smem_u32(smem);
-    auto issue_s = [&](int jj) {   // S_jj = Q K_jj^T into buffer jj & 1
-      const int slot = jj % MH_RING;
-      if (!tc::mbar_wait(&kvfull[slot], (jj / MH_RING) & 1, P.status, aborted)) return;
+    auto issue_s = [&](int jj) {   // S_jj = Q K_jj^T into buffer jj & 1, once block jj has landed
+      if (!tc::mbar_wait(&kvfull[jj % MH_RING], (jj / MH_RING) & 1, P.status, aborted)) return;
+      tc::mbar_arrive(&sbar[jj & 1]);   // the softmax reads the bias tile once S_jj is signalled
       tc::tc_fence_after();
-      const uint32_t kt = sb + MH_OFF_RING + slot * MH_SLOT_BYTES;
+      const uint32_t kt = sb + MH_OFF_RING + (jj % MH_RING) * MH_SLOT_BYTES;
 #pragma unroll
-      for (int kk = 0; kk < MH_DP / 16; ++kk)
+      for (int kk = 0; kk < DK / 16; ++kk)
         tc::mma_bf16_ts(tbase + S_COL + (jj & 1) * MH_KB, tbase + Q_COL + kk * 8,
-                        tc::smem_desc(kt + kk * 32, 1024, tc::kSW128), ID_S, kk > 0);
+                        tc::smem_desc(kt + kk * 32, 8 * KSW, KSWZ), ID_S, kk > 0);
       tc::mma_commit(&sbar[jj & 1]);
     };
     // Q must be in TMEM before the first S
@@ -319,18 +300,19 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(MhaParams P) {
       const uint32_t ph = ((j >> 1) + (j & 1)) & 1;
       if (!tc::mbar_wait(&pready[j & 1], ph, P.status, aborted)) break;
       tc::tc_fence_after();
-      const uint32_t vt = sb + MH_OFF_RING + (j % MH_RING) * MH_SLOT_BYTES + MH_TILE_BYTES;
+      const uint32_t vt = sb + MH_OFF_RING + (j % MH_RING) * MH_SLOT_BYTES + MH_K_BYTES;
 #pragma unroll
       for (int kk = 0; kk < MH_KB / 16; ++kk)
         tc::mma_bf16_ts(tbase + O_COL, tbase + S_COL + (j & 1) * MH_KB + kk * 8,
-                        tc::smem_desc_mn(vt + kk * 2048, MH_TILE_BYTES, 1024, tc::kSW128), ID_PV, j > 0 || kk > 0);
+                        tc::smem_desc_mn(vt + kk * 2048, MH_V_BYTES, 1024, tc::kSW128), ID_PV, j > 0 || kk > 0);
       tc::mma_commit(&pvbar[j & 1]);
       tc::mma_commit(&kvfree[j % MH_RING]);
       if (j + 2 < nkb) issue_s(j + 2);
     }
   }
   tc::tc_fence_before();
-  if (__syncthreads_or(aborted)) {   // abort path: the issuer's MMAs must be done before TMEM is freed
+  if (__syncthreads_or(aborted)) {   // abort path: the producer's loads and the issuer's MMAs done before exit
+    if (warp == 4 && lane == 0) tc::drain_ring(kvfull, MH_RING, loads, P.status);
     if (warp == 5 && lane == 0) tc::drain_mma(drain, P.status);
     __syncthreads();
   }
@@ -340,36 +322,82 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(MhaParams P) {
   }
 }
 
+// Tensor map over a strided bf16 tensor of up to 4 dims (dim 0 contiguous); dims of extent 1
+// get a placeholder stride.  False (no message) when TMA cannot address it.
+bool strided_tmap(CUtensorMap* map, const void* base, int rank, const int64_t* dims, const int64_t* strides,
+                  const uint32_t* box, CUtensorMapSwizzle sw) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  cuuint64_t gd[4], gs[3];
+  cuuint32_t bx[4], es[4] = {1, 1, 1, 1};
+  int64_t prev = dims[0] * 2;
+  for (int i = 0; i < rank; ++i) {
+    if (dims[i] < 1 || dims[i] > (int64_t(1) << 32)) return false;
+    gd[i] = (cuuint64_t)dims[i];
+    bx[i] = box[i];
+    if (i > 0) {
+      int64_t st = strides[i - 1] * 2;   // bytes
+      if (dims[i] == 1) st = (prev + 15) / 16 * 16;
+      if (st <= 0 || st % 16 != 0 || st >= (int64_t(1) << 40)) return false;
+      gs[i - 1] = (cuuint64_t)st;
+      prev = st * dims[i];
+    }
+  }
+  auto encode = tensor_map_encoder();
+  if (!encode) return false;
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), gd, gs, bx, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 // Returns SF_OK after launching, or SF_ERR_ARG (with no message) when the call is outside what
 // this kernel takes, so that the caller uses the CUDA-core kernel instead.
 int attention_tc(const sf_attention_args* a, cudaStream_t stream) {
   const int64_t D = a->head_dim;
-  const bool f32bias = a->bias && a->bias_dtype == SF_F32;
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  const bool ok = a->dtype == SF_BF16 && D % 8 == 0 && D <= MH_DP && (a->value_dim == 0 || a->value_dim == D) &&
-                  a->k_len > 0 && a->k_len <= MH_MAX_KEYS && al16(a->q) && al16(a->k) && al16(a->v) && al16(a->out) &&
-                  (!a->gate || al16(a->gate)) && (a->q_sb | a->q_sh | a->q_sq | a->k_sb | a->k_sh | a->k_sk | a->v_sb |
-                                                  a->v_sh | a->v_sk | a->o_sb | a->o_sh | a->o_sq) % 8 == 0 &&
-                  (!a->gate || (a->g_sb | a->g_sh | a->g_sq) % 8 == 0) && a->q_len <= (int64_t(1) << 31) - TILE;
+  bool ok = a->dtype == SF_BF16 && D % 8 == 0 && D <= MH_DP && (a->value_dim == 0 || a->value_dim == D) &&
+            a->k_len > 0 && a->k_len <= MH_MAX_KEYS && al16(a->q) && al16(a->out) && (!a->gate || al16(a->gate)) &&
+            (a->q_sb | a->q_sh | a->q_sq | a->o_sb | a->o_sh | a->o_sq) % 8 == 0 &&
+            (!a->gate || (a->g_sb | a->g_sh | a->g_sq) % 8 == 0) && a->q_len <= (int64_t(1) << 31) - TILE &&
+            (!a->bias || a->bias_dtype == SF_BF16);
   if (!ok) return SF_ERR_ARG;
+  const int ksw = D <= 32 ? 64 : 128;
+  CUtensorMap mk, mv, mb;
+  {
+    const int64_t dk[4] = {D, a->k_len, a->heads, a->batch}, sk[3] = {a->k_sk, a->k_sh, a->k_sb};
+    const int64_t sv[3] = {a->v_sk, a->v_sh, a->v_sb};
+    const uint32_t bk[4] = {(uint32_t)(ksw / 2), (uint32_t)MH_KB, 1, 1}, bv[4] = {64, (uint32_t)MH_KB, 1, 1};
+    if (!strided_tmap(&mk, a->k, 4, dk, sk, bk, ksw == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !strided_tmap(&mv, a->v, 4, dk, sv, bv, CU_TENSOR_MAP_SWIZZLE_128B))
+      return SF_ERR_ARG;
+  }
+  int batched = 0;
+  if (a->bias) {
+    const uint32_t bb[4] = {(uint32_t)MH_KB, (uint32_t)TILE, 1, 1};
+    batched = a->b_sb != 0 && a->batch > 1;
+    const int64_t db[4] = {a->k_len, a->q_len, a->heads, a->batch}, sbs[3] = {a->b_sq, a->b_sh, a->b_sb};
+    if (!strided_tmap(&mb, a->bias, batched ? 4 : 3, db, sbs, bb, CU_TENSOR_MAP_SWIZZLE_128B)) return SF_ERR_ARG;
+  } else {
+    mb = mk;   // unused
+  }
   uint32_t* status = device_status_ptr();
   if (!status) return SF_ERR_CUDA;
-  static bool attr[64] = {false};
+  static bool attr[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(k_mha_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, MH_SMEM);
+  auto kern = ksw == 64 ? k_mha_tc<64> : k_mha_tc<128>;
+  if (!attr[dev & 63][ksw == 64]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MH_SMEM);
     if (e != cudaSuccess) {
       set_error("cudaFuncSetAttribute(attention): %s", cudaGetErrorString(e));
       return SF_ERR_CUDA;
     }
-    attr[dev & 63] = true;
+    attr[dev & 63][ksw == 64] = true;
   }
-  MhaParams p{*a, f32bias ? 1 : 0, status};
+  MhaParams p{*a, batched, status};
   dim3 grid((unsigned)((a->q_len + TILE - 1) / TILE), (unsigned)a->heads, (unsigned)a->batch);
-  k_mha_tc<<<grid, MH_THREADS, MH_SMEM, stream>>>(p);
+  kern<<<grid, MH_THREADS, MH_SMEM, stream>>>(mk, mv, mb, p);
   count_launch();
   return check_launch("attention_tc");
 }
