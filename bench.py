@@ -625,19 +625,41 @@ def run_op(args) -> None:
   with torch.no_grad():
     for _ in range(args.warmup):
       run()
+    torch.cuda.synchronize()
+    l0 = _native.launch_count()
+    run()
+    torch.cuda.synchronize()
+    launches = _native.launch_count() - l0
+    # device time per call: the call captured once in a CUDA graph and replayed, so that the host's
+    # Python and ctypes work between launches (which a small op cannot hide) is not timed
+    graph = None
+    if not args.no_graph:
+      try:
+        cap = torch.cuda.Stream()
+        cap.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cap):
+          run()
+        torch.cuda.current_stream().wait_stream(cap)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+          run()
+        graph.replay()
+        torch.cuda.synchronize()
+      except Exception:   # an op that cannot be captured is timed eagerly
+        graph = None
     st = torch.cuda.current_stream()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     torch.cuda.synchronize()
-    l0 = _native.launch_count()
     for a, b in ev:
       a.record(st)
-      run()
+      graph.replay() if graph is not None else run()
       b.record(st)
     torch.cuda.synchronize()
-    launches = (_native.launch_count() - l0) // max(1, args.steps)
   ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
   peaks = load_peaks()
   print(json.dumps({"op": args.op, "what": what, "n_token": n, "ms": round(ms, 4),
+                    "timing": "CUDA graph replay" if graph is not None else "eager launches",
                     "gflop": round(fl / 1e9, 2) if fl else None,
                     "tflop_per_s": round(fl / (ms * 1e-3) / 1e12, 2) if fl else None,
                     "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4) if fl else None,
@@ -656,6 +678,7 @@ def main():
                   help="skip the configs[4] (N_token=2048) trunk measured beside the headline")
   ap.add_argument("--op", choices=OPS, default=None, help="time one op alone instead of the trunk")
   ap.add_argument("--n", type=int, default=N_TOKEN, help="N_token for --op")
+  ap.add_argument("--no-graph", action="store_true", help="--op: time eager launches instead of a graph replay")
   ap.add_argument("--n-token", type=int, default=N_TOKEN, help="N_token of the trunk (512 = configs[1], 2048 = configs[4])")
   ap.add_argument("--sample-n", type=int, default=None,
                   help="reference arm only: time blocks of this N instead of the workload's (quick CPU checks)")

@@ -232,13 +232,16 @@ size_t sf_pair_logits_workspace(int dtype, int64_t rows, int64_t n, int64_t c);
 
 /* ---- diffusion-transformer and MSA helpers ----------------------------- */
 /* y = scale * LN(x) + bias (norm without affine): AdaptiveLayerNorm with
- * single_cond (model/diffusion/transformer.py:80-93); x, scale, bias, y [rows][cols]. */
+ * single_cond (model/diffusion/transformer.py:80-93); x, y [rows][cols]; scale, bias
+ * [cond_rows][cols], repeated every cond_rows rows of x (one conditioning for every
+ * diffusion sample; rows must be a multiple of cond_rows). */
 int sf_adaln(int dtype, const void* x, const void* scale, const void* bias, void* y, int64_t rows,
-             int64_t cols, sf_stream_t stream);
-/* out = base + u * gate, elementwise (base may be null): AdaptiveZeroInit gating and
- * residual (transformer.py:138-154, :345, :585), MSAAttention gate (trunk/blocks.py:182-183). */
+             int64_t cols, int64_t cond_rows, sf_stream_t stream);
+/* out[e] = base[e] + u[e] * gate[e % gate_period] (base may be null): AdaptiveZeroInit gating
+ * and residual (transformer.py:138-154, :345, :585), MSAAttention gate (trunk/blocks.py:182-183);
+ * n must be a multiple of gate_period. */
 int sf_gated_residual(int dtype, const void* base, const void* u, const void* gate, void* out, int64_t n,
-                      sf_stream_t stream);
+                      int64_t gate_period, sf_stream_t stream);
 /* out[b][i][:] = mask[i] ? src[b][idx[i]][:] : 0 — atom_layout.convert
  * (schema/atom_layout.py:52-83) for the atom key windows (transformer.py:671-673). */
 int sf_gather_rows(int dtype, const void* src, int64_t batch, int64_t src_rows, const int32_t* idx,

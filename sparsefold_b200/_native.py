@@ -75,8 +75,8 @@ _SIGNATURES = {
     "sf_transition_noalloc_max_scratch": (C.c_size_t, []),
     "sf_pair_logits": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, C.c_size_t, _vp]),
     "sf_pair_logits_workspace": (C.c_size_t, [C.c_int, _i64, _i64, _i64]),
-    "sf_adaln": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
-    "sf_gated_residual": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "sf_adaln": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "sf_gated_residual": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "sf_gather_rows": (C.c_int, [C.c_int, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _vp]),
     "sf_mask_rows": (C.c_int, [C.c_int, _vp, _vp, _i64, _i64, _vp]),
     "sf_softmax_rows": (C.c_int, [C.c_int, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),

@@ -13,7 +13,7 @@ namespace {
 // single_cond branch of AdaptiveLayerNorm (diffusion/transformer.py:85-93).
 template <typename T>
 __global__ void k_adaln(const T* __restrict__ x, const T* __restrict__ scale, const T* __restrict__ bias,
-                        T* __restrict__ y, int64_t rows, int cols, float eps) {
+                        T* __restrict__ y, int64_t rows, int cols, int64_t cond_rows, float eps) {
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -27,21 +27,21 @@ __global__ void k_adaln(const T* __restrict__ x, const T* __restrict__ scale, co
     v += d * d;
   }
   const float rstd = rsqrtf(warp_sum(v) / cols + eps);
+  const int64_t cr = (row % cond_rows) * cols;   // scale and bias repeat every cond_rows rows
   for (int c = lane; c < cols; c += 32) {
-    const int64_t o = row * cols + c;
     // the reference rounds LN(x) and the scale/bias to the activation dtype first
     const float xn = ld_round<T>((ld(xr + c) - mean) * rstd);
-    st(y + o, ld(scale + o) * xn + ld(bias + o));
+    st(y + row * cols + c, ld(scale + cr + c) * xn + ld(bias + cr + c));
   }
 }
 
 // out = base + u * gate (base may be null)
 template <typename T>
 __global__ void k_gated_residual(const T* __restrict__ base, const T* __restrict__ u, const T* __restrict__ gate,
-                                 T* __restrict__ out, int64_t n) {
+                                 T* __restrict__ out, int64_t n, int64_t gate_period) {
   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (e >= n) return;
-  const float v = ld(u + e) * ld(gate + e);
+  const float v = ld(u + e) * ld(gate + e % gate_period);
   st(out + e, base ? ld(base + e) + v : v);
 }
 
@@ -183,23 +183,26 @@ using namespace sf;
 extern "C" {
 
 int sf_adaln(int dtype, const void* x, const void* scale, const void* bias, void* y, int64_t rows, int64_t cols,
-             sf_stream_t stream) {
-  SF_REQUIRE(x && scale && bias && y && rows >= 0 && cols > 0, "sf_adaln: bad arguments");
+             int64_t cond_rows, sf_stream_t stream) {
+  SF_REQUIRE(x && scale && bias && y && rows >= 0 && cols > 0 && cond_rows > 0 && rows % cond_rows == 0,
+             "sf_adaln: bad arguments");
   if (rows == 0) return SF_OK;
   SF_DISPATCH(dtype, {
     k_adaln<T><<<blocks_for(rows, 8), 256, 0, stream>>>((const T*)x, (const T*)scale, (const T*)bias, (T*)y, rows,
-                                                        (int)cols, 1e-5f);
+                                                        (int)cols, cond_rows, 1e-5f);
     count_launch();
     return check_launch("sf_adaln");
   });
 }
 
 int sf_gated_residual(int dtype, const void* base, const void* u, const void* gate, void* out, int64_t n,
-                      sf_stream_t stream) {
-  SF_REQUIRE(u && gate && out && n >= 0, "sf_gated_residual: bad arguments");
+                      int64_t gate_period, sf_stream_t stream) {
+  SF_REQUIRE(u && gate && out && n >= 0 && gate_period > 0 && n % gate_period == 0,
+             "sf_gated_residual: bad arguments");
   if (n == 0) return SF_OK;
   SF_DISPATCH(dtype, {
-    k_gated_residual<T><<<blocks_for(n), 256, 0, stream>>>((const T*)base, (const T*)u, (const T*)gate, (T*)out, n);
+    k_gated_residual<T><<<blocks_for(n), 256, 0, stream>>>((const T*)base, (const T*)u, (const T*)gate, (T*)out, n,
+                                                           gate_period);
     count_launch();
     return check_launch("sf_gated_residual");
   });

@@ -386,9 +386,12 @@ class CrossAttTransformerB200(B200Module):
 
   def prepare_native(self):
     w = self.pair_logits_projection.weight.detach().float()                        # [P, blocks, H]
-    self._pack("pl_w", w.reshape(w.shape[0], -1).T)
+    wt = w.reshape(w.shape[0], -1).T                                               # [blocks * H, P]
+    width = (wt.shape[0] + 7) // 8 * 8   # output width padded to 8 so the projection runs on tcgen05
+    self._pack("pl_w", torch.cat([wt, wt.new_zeros(width - wt.shape[0], wt.shape[1])], 0))
     self._keep("pair_ln_w", self.pair_input_layer_norm.weight)
     self._bh = (w.shape[1], w.shape[2])
+    self._plw = width
     self._native_prepared = True
 
   @_require_prepared
@@ -398,11 +401,12 @@ class CrossAttTransformerB200(B200Module):
     dt = queries_act.dtype
     s_, q_, k_, _ = pair_cond.shape
     x = ops.layer_norm(pair_cond.to(dt), self._kept("pair_ln_w"), None)
-    lg = ops.linear(x, self._packed("pl_w", dt)).reshape(s_ * q_ * k_, nb * h)
+    wd = self._plw
+    lg = ops.linear(x, self._packed("pl_w", dt)).reshape(s_ * q_ * k_, wd)      # columns (b, h), padded to wd
     # "s q k b h -> b s h q k" (transformer.py:661)
     pl = torch.empty(nb, s_, h, q_, k_, dtype=dt, device=lg.device)
     qk = q_ * k_
-    ops.transpose_(lg, pl, s_, nb, qk, h, qk * nb * h, h, nb * h, h * qk, s_ * h * qk, qk)
+    ops.transpose_(lg, pl, s_, nb, qk, h, qk * wd, h, wd, h * qk, s_ * h * qk, qk)
     idx = queries_to_keys.gather_idxs
     gmask = queries_to_keys.gather_mask
     lead = queries_act.shape[:-3]

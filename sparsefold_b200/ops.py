@@ -206,27 +206,45 @@ def pair_logits(z: torch.Tensor, ln_w, ln_b, w, heads: int) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 # diffusion-transformer and MSA helpers
 # ---------------------------------------------------------------------------
+def _trailing_period(t: torch.Tensor, like: torch.Tensor):
+  """(t, period) with t contiguous and like's trailing shape: the elements of t repeat every
+  `period` elements of like (t broadcasts over like's leading dims), or t expanded in full."""
+  t = t.to(like.dtype)
+  lead = like.ndim - t.ndim
+  if lead >= 0 and tuple(t.shape) == tuple(like.shape[lead:]):
+    t = t.contiguous()
+    return t, t.numel()
+  t = t.expand_as(like).contiguous()
+  return t, t.numel()
+
+
 def adaln(x: torch.Tensor, scale: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
-  """scale * LN(x) + bias, all [..., C] of x's dtype (AdaptiveLayerNorm with single_cond)."""
+  """scale * LN(x) + bias, all [..., C] of x's dtype (AdaptiveLayerNorm with single_cond); scale and
+  bias may have fewer leading dims than x (one conditioning for every sample) and are not copied then."""
   _cuda(x, scale, bias)
   x = x.contiguous()
-  scale = scale.to(x.dtype).expand_as(x).contiguous()
-  bias = bias.to(x.dtype).expand_as(x).contiguous()
-  y = torch.empty_like(x)
   c = x.shape[-1]
-  N.call("sf_adaln", _dt(x), _p(x), _p(scale), _p(bias), _p(y), x.numel() // c, c, _stream())
+  if scale.shape != bias.shape:
+    scale, bias = torch.broadcast_tensors(scale, bias)
+  scale, per = _trailing_period(scale, x)
+  bias, per_b = _trailing_period(bias, x)
+  if per_b != per:
+    scale, per = scale.expand_as(x).contiguous(), x.numel()
+    bias = bias.expand_as(x).contiguous()
+  y = torch.empty_like(x)
+  N.call("sf_adaln", _dt(x), _p(x), _p(scale), _p(bias), _p(y), x.numel() // c, c, per // c, _stream())
   return y
 
 
 def gated_residual(base, u: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
-  """base + u * gate (base may be None); gate broadcast to u's shape."""
+  """base + u * gate (base may be None); gate broadcasts to u's shape (over leading dims without a copy)."""
   _cuda(u, gate, base)
   u = u.contiguous()
-  gate = gate.to(u.dtype).expand_as(u).contiguous()
+  gate, per = _trailing_period(gate, u)
   if base is not None:
     base = base.to(u.dtype).expand_as(u).contiguous()
   out = torch.empty_like(u)
-  N.call("sf_gated_residual", _dt(u), _p(base), _p(u), _p(gate), _p(out), u.numel(), _stream())
+  N.call("sf_gated_residual", _dt(u), _p(base), _p(u), _p(gate), _p(out), u.numel(), per, _stream())
   return out
 
 
