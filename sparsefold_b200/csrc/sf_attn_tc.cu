@@ -61,11 +61,20 @@ __device__ __forceinline__ float ex2f(float x) {
 }
 
 // KSW: swizzle of the K tile, 64 (rows of 32 dims, D <= 32) or 128 (rows of 64 dims).
-template <int KSW>
+// G: batch entries per CTA.  G = 1: 128 query rows of one entry, 64-key blocks.  G = 4
+// (entries of at most 32 queries, the atom windows): warp w holds the 32 query rows of
+// entry 4 * blockIdx.z + w, and each 64-key block is 16 keys of each of the four entries
+// (their own key windows); a warp reads only its entry's 16 columns of S and writes zeros
+// over the other entries' columns of P, so one M128 N64 MMA for S and one K=64 P V serve
+// all four entries.
+template <int KSW, int G>
 __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant__ CUtensorMap tmK,
                                                           const __grid_constant__ CUtensorMap tmV,
                                                           const __grid_constant__ CUtensorMap tmB, MhaParams P) {
   constexpr int DK = KSW / 2;                     // padded head dim of K (32 or 64)
+  constexpr int KBG = MH_KB / G;                  // keys of one entry in a 64-key block
+  constexpr int QG = TILE / G;                    // query rows of one entry
+  constexpr int BIAS_BOX = KBG * QG * 2;          // bytes of one entry's bias box
   const sf_attention_args& a = P.a;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -76,11 +85,13 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant_
   uint64_t* pvbar = pready + 2;                                         // [2] P_j V_j done
   uint64_t* drain = pvbar + 2;                                          // issuer's drain barrier (abort path)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + MH_OFF_KBITS);
+  uint32_t* kbits = reinterpret_cast<uint32_t*>(smem + MH_OFF_KBITS);   // [G][nkw]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t b = blockIdx.z, h = blockIdx.y, q0 = (int64_t)blockIdx.x * TILE;
+  const int64_t h = blockIdx.y;
+  const int64_t bz = (int64_t)blockIdx.z * G;                           // first batch entry of the CTA
+  const int64_t q0 = G == 1 ? (int64_t)blockIdx.x * TILE : 0;
   const int D = (int)a.head_dim;
-  const int nkb = (int)((a.k_len + MH_KB - 1) / MH_KB);
+  const int nkb = (int)((a.k_len + KBG - 1) / KBG);
   const int nkw = (int)((a.k_len + 31) / 32);
   const bool has_bias = a.bias != nullptr;
   bool aborted = false;
@@ -90,14 +101,19 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant_
     ++loads;
     uint8_t* sl = slot_of(jj);
     uint64_t* bar = &kvfull[jj % MH_RING];
-    tc::mbar_expect_tx(bar, MH_KB * KSW + MH_V_BYTES + (has_bias ? MH_B_BYTES : 0));
-    tc::tma_load_4d(sl, &tmK, bar, 0, jj * MH_KB, (int)h, (int)b);
-    tc::tma_load_4d(sl + MH_K_BYTES, &tmV, bar, 0, jj * MH_KB, (int)h, (int)b);
-    if (has_bias) {
-      if (P.bias_batched)
-        tc::tma_load_4d(sl + MH_K_BYTES + MH_V_BYTES, &tmB, bar, jj * MH_KB, (int)q0, (int)h, (int)b);
-      else
-        tc::tma_load_3d(sl + MH_K_BYTES + MH_V_BYTES, &tmB, bar, jj * MH_KB, (int)q0, (int)h);
+    tc::mbar_expect_tx(bar, MH_KB * KSW + MH_V_BYTES + (has_bias ? G * BIAS_BOX : 0));
+#pragma unroll
+    for (int g = 0; g < G; ++g) {   // entry g's keys: rows g * KBG .. of the K and V tiles
+      const int be = (int)(bz + g);
+      tc::tma_load_4d(sl + g * KBG * KSW, &tmK, bar, 0, jj * KBG, (int)h, be);
+      tc::tma_load_4d(sl + MH_K_BYTES + g * KBG * 128, &tmV, bar, 0, jj * KBG, (int)h, be);
+      if (has_bias) {   // G = 1: one [128 q][64 k] tile; G = 4: four [32 q][16 k] tiles
+        uint8_t* bt = sl + MH_K_BYTES + MH_V_BYTES + g * (MH_B_BYTES / G);
+        if (P.bias_batched)
+          tc::tma_load_4d(bt, &tmB, bar, jj * KBG, (int)q0, (int)h, be);
+        else
+          tc::tma_load_3d(bt, &tmB, bar, jj * KBG, (int)q0, (int)h);
+      }
     }
   };
 
@@ -123,19 +139,22 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant_
     // the ring's first blocks at once, under the Q and mask loads
     for (int jj = 0; jj < MH_RING && jj < nkb; ++jj) issue_load(jj);
   }
-  // key k counts iff k < k_len and mask_k[b, k] (sdpa.py:61-80); one bit per key
-  for (int w = warp; w < nkw; w += MH_THREADS / 32) {
-    const int64_t key = (int64_t)w * 32 + lane;
-    const bool ok = key < a.k_len && (!a.mask_k || a.mask_k[b * a.mk_sb + key] != 0);
+  // key k of entry g counts iff k < k_len and mask_k[g, k] (sdpa.py:61-80); one bit per key
+  for (int w = warp; w < G * nkw; w += MH_THREADS / 32) {
+    const int g = w / nkw;
+    const int64_t key = (int64_t)(w - g * nkw) * 32 + lane, be = bz + g;
+    const bool ok = be < a.batch && key < a.k_len && (!a.mask_k || a.mask_k[be * a.mk_sb + key] != 0);
     const uint32_t bits = __ballot_sync(0xffffffffu, ok);
     if (lane == 0) kbits[w] = bits;
   }
-  // the query row of this thread (softmax warps)
-  const int64_t q = q0 + tid;
-  const bool qin = warp < 4 && q < a.q_len;
+  // the query row of this thread (softmax warps): entry bz + ge, query q
+  const int ge = G == 1 ? 0 : warp;
+  const int64_t be = bz + ge;
+  const int64_t q = q0 + (G == 1 ? tid : lane);
+  const bool qin = warp < 4 && be < a.batch && q < a.q_len && (G == 1 || lane < QG);
   bool row_ok = qin;
-  if (qin && a.mask_row) row_ok = a.mask_row[b] != 0;
-  if (qin && a.mask_q) row_ok = row_ok && a.mask_q[b * a.mq_sb + q] != 0;
+  if (qin && a.mask_row) row_ok = a.mask_row[be] != 0;
+  if (qin && a.mask_q) row_ok = row_ok && a.mask_q[be * a.mq_sb + q] != 0;
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -147,7 +166,7 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant_
     {   // Q row, scaled by scale * log2 e, into TMEM (zero beyond D)
       uint32_t qw[32];
       const float qs = a.scale * 1.4426950408889634f;
-      const bf16* qp = static_cast<const bf16*>(a.q) + b * a.q_sb + h * a.q_sh + (qin ? q : 0) * a.q_sq;
+      const bf16* qp = static_cast<const bf16*>(a.q) + (qin ? be * a.q_sb + h * a.q_sh + q * a.q_sq : 0);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -164,19 +183,25 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant_
     if (lane == 0) tc::mbar_arrive(&pready[1]);   // "Q is in TMEM": phase 0 of pready[1] (4 warps)
 
     const bool use_bias = has_bias && row_ok;
+    const uint32_t* kb = kbits + ge * nkw;
     float m_run = -INFINITY, l = 0.f;
     for (int j = 0; j < nkb; ++j) {
-      const int64_t k0 = (int64_t)j * MH_KB;
+      const int64_t k0 = (int64_t)j * KBG;
       // S_j is written and block j (its bias tile) has landed
       tc::mbar_wait(&sbar[j & 1], (j >> 1) & 1, P.status, aborted);
       tc::tc_fence_after();
-      float sv[MH_KB];
-      tc::tmem_ld64(lane_addr + S_COL + (j & 1) * MH_KB, sv);
+      float sv[KBG];
+      if constexpr (G == 1) {
+        tc::tmem_ld64(lane_addr + S_COL + (j & 1) * MH_KB, sv);
+      } else {
+        tc::tmem_ld16(lane_addr + S_COL + (j & 1) * MH_KB + ge * KBG, sv);   // warp-uniform column
+      }
       if (use_bias) {
-        const uint8_t* brow = slot_of(j) + MH_K_BYTES + MH_V_BYTES;
+        const uint8_t* bt = slot_of(j) + MH_K_BYTES + MH_V_BYTES;
 #pragma unroll
-        for (int c = 0; c < MH_KB / 8; ++c) {
-          const uint4 v = *reinterpret_cast<const uint4*>(brow + tc::sw128_off(tid, c));
+        for (int c = 0; c < KBG / 8; ++c) {
+          const uint4 v = G == 1 ? *reinterpret_cast<const uint4*>(bt + tc::sw128_off(tid, c))
+                                 : *reinterpret_cast<const uint4*>(bt + ge * (MH_B_BYTES / G) + lane * (KBG * 2) + 16 * c);
           const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -185,15 +210,22 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant_
           }
         }
       }
-      const uint32_t vb0 = kbits[2 * j], vb1 = (2 * j + 1 < nkw) ? kbits[2 * j + 1] : 0u;
+      uint32_t vb = kb[(k0 >> 5)];                // KBG divides 32: one word covers the block
+      if constexpr (G == 1) (void)vb;
       float mx = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < MH_KB; ++e) {
-        const bool inb = k0 + e < a.k_len;
-        const bool valid = ((e < 32 ? vb0 >> e : vb1 >> (e - 32)) & 1u) != 0;
-        const float s = !inb ? -INFINITY : (row_ok && valid) ? sv[e] : -FLT_MAX;   // beyond k_len: no part at all
-        sv[e] = s;
-        mx = fmaxf(mx, s);
+      for (int e = 0; e < KBG; ++e) {
+        const int64_t key = k0 + e;
+        const bool inb = key < a.k_len;
+        bool valid;
+        if constexpr (G == 1) {
+          valid = ((kb[2 * j + (e >> 5)] >> (e & 31)) & 1u) != 0;
+        } else {
+          valid = ((vb >> ((int)(k0 & 31) + e)) & 1u) != 0;
+        }
+        const float sc = !inb ? -INFINITY : (row_ok && valid) ? sv[e] : -FLT_MAX;   // beyond k_len: no part at all
+        sv[e] = sc;
+        mx = fmaxf(mx, sc);
       }
       // the running max moves only when the block exceeds it by 2^8 (values stay <= 2^8)
       const bool moves = m_run == -INFINITY ? mx != -INFINITY : mx > m_run + MH_RESCALE;
@@ -204,13 +236,22 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant_
       }
       const float mref = m_run == -INFINITY ? 0.f : m_run;
       uint32_t pk[MH_KB / 2];
+#pragma unroll
+      for (int e = 0; e < MH_KB / 2; ++e) pk[e] = 0u;   // G > 1: the other entries' columns stay zero
       float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
-      for (int e = 0; e < MH_KB; e += 2) {
+      for (int e = 0; e < KBG; e += 2) {
         const float p0 = ex2f(sv[e] - mref), p1 = ex2f(sv[e + 1] - mref);
         ps0 += p0;
         ps1 += p1;
-        pk[e >> 1] = pack_bf2(p0, p1);
+        const uint32_t pp = pack_bf2(p0, p1);
+        if constexpr (G == 1) {
+          pk[e >> 1] = pp;
+        } else {
+#pragma unroll
+          for (int g = 0; g < G; ++g)
+            if (g == ge) pk[g * (KBG / 2) + (e >> 1)] = pp;   // static indices, warp-uniform choice
+        }
       }
       l = l * corr + (ps0 + ps1);
       // O holds P V up to block j-1: rescale it once P_{j-1} V_{j-1} is done (warp-uniform branch)
@@ -242,8 +283,8 @@ __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant_
     tc::tmem_ld64(lane_addr + O_COL, ov);
     if (qin) {
       const float inv = l > 0.f ? 1.0f / l : 0.f;
-      bf16* op = static_cast<bf16*>(a.out) + b * a.o_sb + h * a.o_sh + q * a.o_sq;
-      const bf16* gp = a.gate ? static_cast<const bf16*>(a.gate) + b * a.g_sb + h * a.g_sh + q * a.g_sq : nullptr;
+      bf16* op = static_cast<bf16*>(a.out) + be * a.o_sb + h * a.o_sh + q * a.o_sq;
+      const bf16* gp = a.gate ? static_cast<const bf16*>(a.gate) + be * a.g_sb + h * a.g_sh + q * a.g_sq : nullptr;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         if (8 * c < D) {
@@ -363,40 +404,48 @@ int attention_tc(const sf_attention_args* a, cudaStream_t stream) {
             (!a->bias || a->bias_dtype == SF_BF16);
   if (!ok) return SF_ERR_ARG;
   const int ksw = D <= 32 ? 64 : 128;
+  // entries of at most 32 queries (the atom windows) go four to a CTA
+  const int G = (a->q_len <= TILE / 4 && a->batch > 1 && ksw == 64 && a->k_len <= MH_MAX_KEYS / 4) ? 4 : 1;
+  const uint32_t kbg = (uint32_t)(MH_KB / G);
   CUtensorMap mk, mv, mb;
   {
     const int64_t dk[4] = {D, a->k_len, a->heads, a->batch}, sk[3] = {a->k_sk, a->k_sh, a->k_sb};
     const int64_t sv[3] = {a->v_sk, a->v_sh, a->v_sb};
-    const uint32_t bk[4] = {(uint32_t)(ksw / 2), (uint32_t)MH_KB, 1, 1}, bv[4] = {64, (uint32_t)MH_KB, 1, 1};
+    const uint32_t bk[4] = {(uint32_t)(ksw / 2), kbg, 1, 1}, bv[4] = {64, kbg, 1, 1};
     if (!strided_tmap(&mk, a->k, 4, dk, sk, bk, ksw == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) ||
         !strided_tmap(&mv, a->v, 4, dk, sv, bv, CU_TENSOR_MAP_SWIZZLE_128B))
       return SF_ERR_ARG;
   }
   int batched = 0;
   if (a->bias) {
-    const uint32_t bb[4] = {(uint32_t)MH_KB, (uint32_t)TILE, 1, 1};
+    // G = 1: [128 queries][64 keys] boxes, 128B swizzle; G = 4: [32 queries][16 keys], unswizzled
+    const uint32_t bb[4] = {kbg, (uint32_t)(TILE / G), 1, 1};
     batched = a->b_sb != 0 && a->batch > 1;
     const int64_t db[4] = {a->k_len, a->q_len, a->heads, a->batch}, sbs[3] = {a->b_sq, a->b_sh, a->b_sb};
-    if (!strided_tmap(&mb, a->bias, batched ? 4 : 3, db, sbs, bb, CU_TENSOR_MAP_SWIZZLE_128B)) return SF_ERR_ARG;
+    if (!strided_tmap(&mb, a->bias, batched ? 4 : 3, db, sbs, bb,
+                      G == 1 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE))
+      return SF_ERR_ARG;
   } else {
     mb = mk;   // unused
   }
   uint32_t* status = device_status_ptr();
   if (!status) return SF_ERR_CUDA;
-  static bool attr[64][2] = {};
+  static bool attr[64][3] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  auto kern = ksw == 64 ? k_mha_tc<64> : k_mha_tc<128>;
-  if (!attr[dev & 63][ksw == 64]) {
+  const int ki = G == 4 ? 2 : ksw == 64 ? 1 : 0;
+  auto kern = G == 4 ? k_mha_tc<64, 4> : ksw == 64 ? k_mha_tc<64, 1> : k_mha_tc<128, 1>;
+  if (!attr[dev & 63][ki]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MH_SMEM);
     if (e != cudaSuccess) {
       set_error("cudaFuncSetAttribute(attention): %s", cudaGetErrorString(e));
       return SF_ERR_CUDA;
     }
-    attr[dev & 63][ksw == 64] = true;
+    attr[dev & 63][ki] = true;
   }
   MhaParams p{*a, batched, status};
-  dim3 grid((unsigned)((a->q_len + TILE - 1) / TILE), (unsigned)a->heads, (unsigned)a->batch);
+  dim3 grid(G == 1 ? (unsigned)((a->q_len + TILE - 1) / TILE) : 1u, (unsigned)a->heads,
+            (unsigned)((a->batch + G - 1) / G));
   kern<<<grid, MH_THREADS, MH_SMEM, stream>>>(mk, mv, mb, p);
   count_launch();
   return check_launch("attention_tc");

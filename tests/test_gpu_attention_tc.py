@@ -116,3 +116,24 @@ def test_masked_query_rows_and_rows_without_valid_keys():
   got = ops.attention(q.cuda(), k.cuda(), v.cuda(), mask_q=mq.cuda(), mask_k=mk.cuda(), bias=bias.cuda())
   ref = _ref(q, k, v, None, mq, mk, bias, None)
   assert max_rel_err(got.float().cpu(), ref) < TOL
+
+
+@pytest.mark.parametrize("nsub,q,k,d", [(10, 32, 128, 32), (4, 32, 128, 16), (7, 20, 100, 24), (2, 1, 16, 8)])
+def test_windows_four_per_cta(nsub, q, k, d):
+  """Entries of at most 32 queries (atom windows: 32 queries x 128 keys of their own) run four to a
+  CTA; a batch that is not a multiple of four, ragged keys, per-window masks, a fully masked window."""
+  g = torch.Generator().manual_seed(nsub * 100 + q + k + d)
+  H, dt = 4, torch.bfloat16
+  qq = torch.randn(2, nsub, q, H, d, generator=g).to(dt)      # 2 samples x nsub windows
+  kk = torch.randn(2, nsub, k, H, d, generator=g).to(dt)
+  vv = torch.randn(2, nsub, k, H, d, generator=g).to(dt)
+  gate = torch.randn(2, nsub, q, H, d, generator=g).to(dt)
+  bias = torch.randn(nsub, H, q, k, generator=g).to(dt)          # per window, shared by the samples
+  mq = torch.rand(nsub, q, generator=g) > 0.1
+  mk = torch.rand(nsub, k, generator=g) > 0.2
+  mk[nsub // 2] = False
+  got = ops.attention(qq.cuda(), kk.cuda(), vv.cuda(), mask_q=mq.cuda(), mask_k=mk.cuda(), bias=bias.cuda(),
+                      gate=gate.cuda())
+  ref = _ref(qq, kk, vv, None, mq.expand(2, nsub, q), mk.expand(2, nsub, k), bias, gate)
+  assert max_rel_err(got.float().cpu(), ref) < TOL
+  assert _native.device_status() == 0
