@@ -488,8 +488,8 @@ def run_reference(args) -> None:
 
 
 OPS = ("tri_attention_start", "tri_attention_end", "tri_mult_outgoing", "tri_mult_incoming", "pair_transition",
-       "single_update", "single_attention", "diffusion_transformer", "atom_transformer", "msa_attention",
-       "outer_product_mean")
+       "single_update", "single_attention", "diffusion_transformer", "diffusion_step", "atom_transformer",
+       "msa_attention", "outer_product_mean")
 
 
 def op_flops(op: str, n: int) -> float:
@@ -545,7 +545,7 @@ def _workload_op(op: str, n: int):
     mk = (torch.arange(n) < max(1, N_REAL * n // N_TOKEN)).cuda()
     return (lambda: ops.attention(y[:, 0], y[:, 1], y[:, 2], mask_k=mk, bias=bias, gate=y[:, 3]), op_flops(op, n),
             f"Pairformer single attention core (sf_attention), N={n}, 16 heads x 24, pair-logit bias, gate")
-  if op == "diffusion_transformer":
+  if op in ("diffusion_transformer", "diffusion_step"):
     s_, n_, c, sc, pc = 5, 768, 768, 384, 128
     m = modules.DiffusionTransformer(c, sc, pc, num_head=16, num_blocks=24, super_block_size=4)
     synth.init_params(m, seed=4)
@@ -553,6 +553,13 @@ def _workload_op(op: str, n: int):
     modules.prepare(m)
     act, single, pair = rn(s_, n_, c), rn(n_, sc), rn(n_, n_, pc)
     mask = torch.ones(n_, dtype=torch.bool, device="cuda")
+    if op == "diffusion_step":   # the pack computed once, as for every step of a denoising loop
+      with torch.no_grad():
+        pack = m.pair_logits_pack(pair, dt)
+      fl = _diffusion_token_flops(s_, n_, c, 16, 48, 24, sc, pc) - 2.0 * n_ * n_ * pc * 24 * 16
+      return (lambda: m(act, mask, single, pair_logits_pack=pack), fl,
+              "configs[2] token transformer, one step of a denoising loop: pair-logit pack cached, 24 blocks, "
+              "5 samples, N=768, c=768, 16 x 48")
     return (lambda: m(act, mask, single, pair), _diffusion_token_flops(s_, n_, c, 16, 48, 24, sc, pc),
             "configs[2] token transformer, one denoising step: 24 blocks, 5 samples, N=768, c=768, 16 x 48, "
             "pair-logit pack from z [768,768,128]")

@@ -370,9 +370,13 @@ class DiffusionTransformerB200(B200Module):
     return out.view(nsb, sbs, h, n, n)
 
   @_require_prepared
-  def forward(self, act, mask, single_cond, pair_cond=None):
+  def forward(self, act, mask, single_cond, pair_cond=None, *, pair_logits_pack=None):
+    """transformer.py:422-477.  ``pair_logits_pack`` (from ``pair_logits_pack(pair_cond)``) lets a
+    denoising loop compute the pack once for all its steps, as pair_cond does not change between them."""
     nsb, sbs, _ = self._shape
-    pack = self.pair_logits_pack(pair_cond, act.dtype) if pair_cond is not None else None
+    pack = pair_logits_pack
+    if pack is None and pair_cond is not None:
+      pack = self.pair_logits_pack(pair_cond, act.dtype)
     for sb in range(nsb):
       for s in range(sbs):
         act = self.self_attention[sb][s](act, mask, pair_logits=None if pack is None else pack[sb, s],
