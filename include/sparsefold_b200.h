@@ -271,6 +271,12 @@ int sf_opm_repack(int dtype, const void* o, int64_t pitch, int64_t n_res, int64_
                   sf_stream_t stream);
 /* x[r][:] *= s[r] (the OPM normaliser, trunk/blocks.py:689). */
 int sf_scale_rows(int dtype, void* x, const float* s, int64_t rows, int64_t cols, sf_stream_t stream);
+/* dst[b*dbs + r*drs + c] = src[b*sbs + r*srs + c] for nblk blocks of rows x width_bytes (all in bytes,
+ * multiples of 16): the packing of the pair tensor between row and column shards around the all-to-all
+ * of the ending-node attention (runtime/dist.py:477-565 reshard, trunk/blocks.py:335-346). */
+int sf_copy_blocks(void* dst, const void* src, int64_t nblk, int64_t rows, int64_t width_bytes,
+                   int64_t src_blk_stride, int64_t src_row_stride, int64_t dst_blk_stride,
+                   int64_t dst_row_stride, sf_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -45,6 +45,18 @@ __global__ void k_gated_residual(const T* __restrict__ base, const T* __restrict
   st(out + e, base ? ld(base + e) + v : v);
 }
 
+// Strided block copy in 16-byte units: block b, row r, chunk c of dst <- the same of src,
+// with independent block and row strides (the row-shard <-> column-shard packing of the pair
+// tensor around the all-to-all of the ending-node attention).
+__global__ void k_copy_blocks(uint4* __restrict__ dst, const uint4* __restrict__ src, int64_t nblk, int64_t rows,
+                              int64_t width, int64_t sbs, int64_t srs, int64_t dbs, int64_t drs) {
+  const int64_t per_blk = rows * width, total = nblk * per_blk;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = e / per_blk, rem = e - b * per_blk, r = rem / width, c = rem - r * width;
+    dst[b * dbs + r * drs + c] = __ldg(src + b * sbs + r * srs + c);
+  }
+}
+
 // out[b][i][:] = mask[i] ? src[b][idx[i]][:] : 0   (atom_layout.convert, schema/atom_layout.py:52-83)
 template <typename T>
 __global__ void k_gather_rows(const T* __restrict__ src, const int32_t* __restrict__ idx,
@@ -300,6 +312,23 @@ int sf_swiglu(int dtype, const void* h, void* out, int64_t rows, int64_t inter, 
     count_launch();
     return check_launch("sf_swiglu");
   });
+}
+
+int sf_copy_blocks(void* dst, const void* src, int64_t nblk, int64_t rows, int64_t width_bytes, int64_t src_blk_stride,
+                   int64_t src_row_stride, int64_t dst_blk_stride, int64_t dst_row_stride, sf_stream_t stream) {
+  SF_REQUIRE(dst && src && nblk >= 0 && rows >= 0 && width_bytes >= 0, "sf_copy_blocks: bad arguments");
+  const int64_t all = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | width_bytes |
+                      src_blk_stride | src_row_stride | dst_blk_stride | dst_row_stride;
+  SF_REQUIRE((all & 15) == 0, "sf_copy_blocks: pointers, width and strides must be multiples of 16 bytes");
+  const int64_t total = nblk * rows * (width_bytes / 16);
+  if (total == 0) return SF_OK;
+  const int64_t want = (total + 255) / 256;
+  const unsigned grid = (unsigned)(want < 148 * 16 ? want : 148 * 16);
+  k_copy_blocks<<<grid, 256, 0, stream>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src), nblk, rows,
+                                          width_bytes / 16, src_blk_stride / 16, src_row_stride / 16,
+                                          dst_blk_stride / 16, dst_row_stride / 16);
+  count_launch();
+  return check_launch("sf_copy_blocks");
 }
 
 int sf_scale_rows(int dtype, void* x, const float* s, int64_t rows, int64_t cols, sf_stream_t stream) {

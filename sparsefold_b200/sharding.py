@@ -128,20 +128,41 @@ def all_to_all_rows(send: torch.Tensor, group=None) -> torch.Tensor:
   return recv
 
 
+def _pack_blocks(dst: torch.Tensor, src: torch.Tensor, nblk: int, rows: int, width: int, sbs: int, srs: int,
+                 dbs: int, drs: int) -> None:
+  """Strided block copy (element strides) on the device: one sf_copy_blocks launch when the layout allows
+  16-byte chunks (CUDA tensors), else a torch copy of the same views (CPU ranks)."""
+  es = src.element_size()
+  if src.is_cuda and (width * es) % 16 == 0 and all((v * es) % 16 == 0 for v in (sbs, srs, dbs, drs)) \
+      and src.data_ptr() % 16 == 0 and dst.data_ptr() % 16 == 0:
+    N.call("sf_copy_blocks", _p(dst), _p(src), nblk, rows, width * es, sbs * es, srs * es, dbs * es, drs * es,
+           _stream())
+    return
+  d = dst.as_strided((nblk, rows, width), (dbs, drs, 1))
+  d.copy_(src.as_strided((nblk, rows, width), (sbs, srs, 1)))
+
+
 def pair_transpose_to_columns(z_loc: torch.Tensor, shard: Shard, group=None) -> torch.Tensor:
-  """[rows_loc, N, C] (row shard) -> [N, cols_loc, C] (column shard)."""
+  """[rows_loc, N, C] (row shard) -> [N, cols_loc, C] (column shard), the reshard of
+  runtime/dist.py:477-565: block q of the send buffer holds my rows x the columns of rank q."""
   p = shard.num_shards
   r, n, c = z_loc.shape
-  send = z_loc.view(r, p, n // p, c).transpose(0, 1)             # block q: my rows x columns of rank q
-  return all_to_all_rows(send.reshape(p * r, n // p, c), group).view(n, n // p, c)
+  cl = n // p
+  z_loc = z_loc.contiguous()
+  send = torch.empty(p * r, cl, c, dtype=z_loc.dtype, device=z_loc.device)
+  _pack_blocks(send, z_loc, p, r, cl * c, cl * c, n * c, r * cl * c, cl * c)
+  return all_to_all_rows(send, group).view(n, cl, c)
 
 
 def pair_transpose_to_rows(z_col: torch.Tensor, shard: Shard, group=None) -> torch.Tensor:
   """[N, cols_loc, C] (column shard) -> [rows_loc, N, C] (row shard)."""
   p = shard.num_shards
   n, cl, c = z_col.shape
-  recv = all_to_all_rows(z_col, group).view(p, n // p, cl, c)   # block q: my rows x columns of rank q
-  return recv.transpose(0, 1).reshape(n // p, n, c)
+  r = n // p
+  recv = all_to_all_rows(z_col, group)              # block q: my rows x columns of rank q, [p][r][cl][c]
+  out = torch.empty(r, n, c, dtype=z_col.dtype, device=z_col.device)
+  _pack_blocks(out, recv, p, r, cl * c, r * cl * c, cl * c, cl * c, n * c)
+  return out
 
 
 def _stream() -> int:
