@@ -176,12 +176,86 @@ def _p(t):
 # ---------------------------------------------------------------------------
 # sharded ops (bf16)
 # ---------------------------------------------------------------------------
+# Triangle multiplication on P ranks moves its operands one of two ways:
+#  * "rows" (the reference's choreography, blocks.py:541-555): every rank all-gathers the
+#    whole b (outgoing) or a^T (incoming) operand, (P-1)/P of [N][C][N] per rank and op;
+#  * "channels": every rank contracts C/P channels over all N x N positions; a and b go out
+#    by channel block and the product comes back by row block, three all-to-alls of
+#    (P-1)/P of the rank's [rows][C][N] each, i.e. 3/P of what "rows" moves (fewer bytes from
+#    P = 4 on).
+CHANNELS_FROM_RANKS = 4
+
+
+def tri_mult_mode(p: int) -> str:
+  """"rows" or "channels" for P ranks; SF_TRIMULT_SHARDING=rows|channels overrides the choice."""
+  import os
+  forced = os.environ.get("SF_TRIMULT_SHARDING", "").strip().lower()
+  if forced in ("rows", "channels"):
+    return forced
+  return "channels" if p >= CHANNELS_FROM_RANKS else "rows"
+
+
+def channel_blocks_out(op: torch.Tensor, p: int, group=None) -> torch.Tensor:
+  """op [m][C][kp] (this rank's rows of a contraction operand) -> [P][m_src][C/P][kp]: channel block r
+  of every rank's op on rank r (all-to-all; block q of the send buffer = channels q C/P ..)."""
+  m, c, kp = op.shape
+  cl = c // p
+  send = torch.empty(p, m, cl, kp, dtype=op.dtype, device=op.device)
+  _pack_blocks(send, op.contiguous(), p, m, cl * kp, cl * kp, c * kp, m * cl * kp, cl * kp)
+  return all_to_all_rows(send.view(p * m, cl, kp), group).view(p, m, cl, kp)
+
+
+def channel_blocks_back(prod_c: torch.Tensor, p: int, rows: int, c: int, group=None) -> torch.Tensor:
+  """prod_c [N][C/P][pn] (this rank's channels, all rows) -> [rows][C][pn] (all channels, this rank's rows)."""
+  n, cl, pn = prod_c.shape
+  recv = all_to_all_rows(prod_c.contiguous().view(n, cl, pn), group)      # [P (channel block)][rows][cl][pn]
+  out = torch.empty(rows, c, pn, dtype=prod_c.dtype, device=prod_c.device)
+  _pack_blocks(out, recv, p, rows, cl * pn, rows * cl * pn, cl * pn, cl * pn, c * pn)
+  return out
+
+
+def _tri_mult_channels(mod, z_loc, mask_u8, shard: Shard, w, group=None) -> torch.Tensor:
+  rows, n, c = z_loc.shape
+  p = shard.num_shards
+  if not shard.is_even or c % p:
+    raise ValueError("channel-sharded triangle multiplication needs an even row split and C divisible by P")
+  dt = N.SF_BF16
+  cl = c // p
+  if not mod.incoming:
+    pitch = ops.pitch(n)
+    a_op = torch.empty(rows, c, pitch, dtype=z_loc.dtype, device=z_loc.device)
+    b_op = torch.empty_like(a_op)
+    N.call("sf_tri_mult_project_rows", dt, _p(z_loc), _p(mask_u8), rows, n, shard.offset(), 0, C.byref(w), _p(a_op),
+           _p(b_op), _stream())
+    a_c = channel_blocks_out(a_op, p, group)               # [P][rows][cl][pitch] = all rows i of my channels
+    b_c = channel_blocks_out(b_op, p, group)
+    chunks = 1
+  else:
+    if rows % 64 or ops.pitch(rows) != rows:
+      raise ValueError(f"incoming triangle multiplication needs shard rows ({rows}) that are multiples of 64")
+    a_send = torch.empty(n, c, rows, dtype=z_loc.dtype, device=z_loc.device)   # b^T: [i][C][k_loc]
+    b_send = torch.empty_like(a_send)                                          # a^T: [j][C][k_loc]
+    N.call("sf_tri_mult_project_rows", dt, _p(z_loc), _p(mask_u8), rows, n, shard.offset(), 1, C.byref(w),
+           _p(a_send), _p(b_send), _stream())
+    a_c = channel_blocks_out(a_send, p, group)             # [P (k chunk)][N][cl][k_loc]
+    b_c = channel_blocks_out(b_send, p, group)
+    chunks = p
+  prod_c = torch.empty(n, cl, ops.pitch(n), dtype=z_loc.dtype, device=z_loc.device)
+  N.call("sf_tri_mult_contract_chunked", dt, _p(a_c), chunks, _p(b_c), chunks, _p(prod_c), cl, n, n, n, _stream())
+  prod = channel_blocks_back(prod_c, p, rows, c, group)
+  out = torch.empty_like(z_loc)
+  N.call("sf_tri_mult_output", dt, _p(z_loc), _p(prod), rows, n, C.byref(w), _p(out), None, 0, _stream())
+  return out
+
+
 def tri_mult(mod, z_loc: torch.Tensor, mask_u8: torch.Tensor, shard: Shard, group=None) -> torch.Tensor:
   """TriangleMultiplication (blocks.py:484-566) on a row shard."""
   rows, n, c = z_loc.shape
   p = shard.num_shards
   w = mod.native_weights(z_loc.dtype)
   dt = N.SF_BF16
+  if p > 1 and tri_mult_mode(p) == "channels":
+    return _tri_mult_channels(mod, z_loc, mask_u8, shard, w, group)
   if not mod.incoming:
     pitch = ops.pitch(n)
     a_op = torch.empty(rows, c, pitch, dtype=z_loc.dtype, device=z_loc.device)

@@ -54,10 +54,10 @@ def _free_port():
     return sk.getsockname()[1]
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, mode="rows"):
   import datetime
   import torch.distributed as dist
-  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", SF_TRIMULT_SHARDING=mode)
   torch.cuda.set_device(rank)
   dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                           device_id=torch.device("cuda", rank))
@@ -84,11 +84,14 @@ def _rank(rank, world, port, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_sharded_block_matches_block():
+@pytest.mark.parametrize("mode", ["rows", "channels"])
+def test_two_gpu_sharded_block_matches_block(mode):
+  """Both ways of moving the triangle-multiplication operands: all-gathers of whole operands ("rows", the
+  reference's choreography) and channel blocks out / product rows back ("channels")."""
   ctx = mp.get_context("spawn")
   q = ctx.Queue()
   port = _free_port()
-  procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+  procs = [ctx.Process(target=_rank, args=(r, 2, port, q, mode)) for r in range(2)]
   for p in procs:
     p.start()
   for p in procs:

@@ -104,3 +104,33 @@ def _incoming_choreography(rank, world):
 
 def test_incoming_triangle_multiplication_choreography_two_ranks():
   _run(_incoming_choreography)
+
+
+def _channel_choreography(rank, world):
+  """Channel-sharded triangle multiplication (the "channels" mode of sharding.tri_mult): a and b leave by
+  channel block, each rank contracts its channels over all positions, the product returns by row block.
+  The contraction is emulated with einsum; everything else is the module's own data movement."""
+  from sparsefold_b200.sharding import channel_blocks_back, channel_blocks_out
+  g = torch.Generator().manual_seed(2)
+  n, c = 8, 4 * world
+  a = torch.randn(n, c, n, generator=g)           # A[i][c][k] (outgoing operand layout, rows i)
+  b = torch.randn(n, c, n, generator=g)           # B[j][c][k]
+  ref = torch.einsum("ick,jck->icj", a, b)        # P[i][c][j]
+  sh = Shard(n, world, rank)
+  rows, off = sh.size(), sh.offset()
+  a_c = channel_blocks_out(a[off:off + rows].contiguous(), world).reshape(n, c // world, n)   # all i, my channels
+  b_c = channel_blocks_out(b[off:off + rows].contiguous(), world).reshape(n, c // world, n)
+  cl = c // world
+  assert torch.equal(a_c, a[:, rank * cl:(rank + 1) * cl])
+  prod_c = torch.einsum("ick,jck->icj", a_c, b_c)                                          # [N][my channels][N]
+  prod = channel_blocks_back(prod_c, world, rows, c)
+  assert torch.allclose(prod, ref[off:off + rows], atol=1e-5)
+  # incoming: operands hold K in per-rank chunks ([i][C][k_loc] on every rank)
+  at = torch.randn(n, c, rows, generator=torch.Generator().manual_seed(10 + rank))
+  got = channel_blocks_out(at, world)                                                      # [P][N][cl][k_loc]
+  full = all_gather_rows(at.unsqueeze(0)).view(world, n, c, rows)                          # every rank's chunk
+  assert torch.equal(got, full[:, :, rank * cl:(rank + 1) * cl, :])
+
+
+def test_channel_sharded_triangle_multiplication_choreography_two_ranks():
+  _run(_channel_choreography)
