@@ -92,6 +92,21 @@ def prepare(module: torch.nn.Module) -> dict[str, int]:
   return _m.prepare(module)
 
 
+def load_and_prepare(module: torch.nn.Module, checkpoint, *, strict: bool = True):
+  """Load AF3 parameters with the reference's own loader, then pack them for the kernels.
+
+  ``checkpoint`` is what ``sparsefold.weights.load_checkpoint`` takes (weights/loading.py:145):
+  a ``Checkpoint`` read from disk or the nested ``{scope: {name: tensor}}`` mapping of the AF3
+  parameter layout (bf16 in the released weights).  The reference assigns the tensors to the
+  module's parameters (state_dict keys and shapes unchanged by the b200 factories), and
+  ``prepare`` then packs the weight matrices as bf16 (and fp32) "out x in" buffers and keeps the
+  LayerNorm parameters and biases in fp32.  Returns the loader's report."""
+  from sparsefold.weights import load_checkpoint
+  report = load_checkpoint(module, checkpoint, strict=strict)
+  _m.prepare(module)
+  return report
+
+
 def materialize(*, parallelism: int | None = None) -> int:
   return 0
 

@@ -75,3 +75,31 @@ def test_reference_pairformer_block_on_b200(ref_blocks, dtype, tol):
   with torch.no_grad():
     zm, sm = mine(z.to(dtype).cuda(), seq_mask=mask.cuda(), single_act=s.to(dtype).cuda())
   assert torch.equal(zm, zo) and torch.equal(sm, so)
+
+
+def test_af3_layout_checkpoint_through_the_reference_loader_on_b200(ref_blocks):
+  """Weights in the AF3 layout (bf16, tests/af3_layout.py) loaded by the reference's own loader into its
+  PairFormerIteration, packed by prepare(), run on the GPU in bf16 against the oracle on the same values."""
+  blocks, network, mc, backends = ref_blocks
+  from sparsefold_b200 import backend, synth
+  from tests.af3_layout import checkpoint_from_module
+
+  def make():
+    return blocks.PairFormerIteration(network.Evoformer.Config().pairformer, mc.GlobalConfig(), with_single=True,
+                                      num_channels=128, seq_channels=384)
+  src = make()
+  synth.init_params(src, 11)
+  blk = make()
+  report = backend.load_and_prepare(blk, checkpoint_from_module(src))
+  assert report.complete
+  blk = blk.cuda()
+  z, s, mask = synth.pair_inputs(64, n_real=57, seed=12)
+  dt = torch.bfloat16
+  with torch.no_grad():
+    zo, so = blk(z.to(dt).cuda(), seq_mask=mask.cuda(), single_act=s.to(dt).cuda())
+  torch.cuda.synchronize()
+  assert _native.device_status() == 0
+  p = {k: v.to(dt).float() for k, v in src.state_dict().items()}   # the checkpoint's bf16 values
+  zr, sr = orc.pairformer_block(z.to(dt).float(), s.to(dt).float(), mask, p)
+  assert max_rel_err(zo.float().cpu(), zr) < 2e-2
+  assert max_rel_err(so.float().cpu(), sr) < 2e-2
