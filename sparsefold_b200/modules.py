@@ -487,6 +487,10 @@ class OuterProductMeanB200(B200Module):
   def prepare_native(self):
     self._pack("left", self.left_projection.weight.detach().float().T)     # [32, C]
     self._pack("right", self.right_projection.weight.detach().float().T)
+    if "output_w" not in self._parameters:
+      # the reference creates output_w / output_b when its weights are set (blocks.py:608-628)
+      raise RuntimeError(f"{getattr(self, 'name', type(self).__name__)}: output_w / output_b are not loaded; "
+                         "load the weights before backends.prepare(model)")
     w = self.output_w.detach().float()                                       # [32, 32, C2]
     self._pack("out", w.reshape(-1, w.shape[-1]).T)                          # [C2, 1024]
     self._keep("out_b", self.output_b)

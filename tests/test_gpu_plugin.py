@@ -99,7 +99,7 @@ def test_af3_layout_checkpoint_through_the_reference_loader_on_b200(ref_blocks):
     zo, so = blk(z.to(dt).cuda(), seq_mask=mask.cuda(), single_act=s.to(dt).cuda())
   torch.cuda.synchronize()
   assert _native.device_status() == 0
-  p = {k: v.to(dt).float() for k, v in src.state_dict().items()}   # the checkpoint's bf16 values
+  p = {k: v.to(dt).float().cpu() for k, v in src.state_dict().items()}   # the checkpoint's bf16 values
   zr, sr = orc.pairformer_block(z.to(dt).float(), s.to(dt).float(), mask, p)
   assert max_rel_err(zo.float().cpu(), zr) < 2e-2
   assert max_rel_err(so.float().cpu(), sr) < 2e-2
