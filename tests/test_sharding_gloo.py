@@ -1,4 +1,4 @@
-"""Host logic of the row-sharded path on CPU ranks (gloo, world size 2).
+"""Host logic of the row-sharded path on CPU ranks (gloo, world sizes 2 and 4).
 
 The kernels are CUDA-only; these tests cover the partition rule, the collective
 helpers, the pair transpose between row and column shards, and the layout
@@ -77,8 +77,9 @@ def _collectives(rank, world):
   assert recv.flatten().tolist() == [2 * rank + 100 * p + e for p in range(world) for e in range(2)]
 
 
-def test_collectives_and_pair_transpose_two_ranks():
-  _run(_collectives)
+@pytest.mark.parametrize("world", [2, 4])
+def test_collectives_and_pair_transpose(world):
+  _run(_collectives, world)
 
 
 def _incoming_choreography(rank, world):
@@ -102,8 +103,9 @@ def _incoming_choreography(rank, world):
   assert torch.allclose(p, ref[:, off:off + kl, :].permute(1, 0, 2), atol=1e-5)
 
 
-def test_incoming_triangle_multiplication_choreography_two_ranks():
-  _run(_incoming_choreography)
+@pytest.mark.parametrize("world", [2, 4])
+def test_incoming_triangle_multiplication_choreography(world):
+  _run(_incoming_choreography, world)
 
 
 def _channel_choreography(rank, world):
@@ -132,5 +134,6 @@ def _channel_choreography(rank, world):
   assert torch.equal(got, full[:, :, rank * cl:(rank + 1) * cl, :])
 
 
-def test_channel_sharded_triangle_multiplication_choreography_two_ranks():
-  _run(_channel_choreography)
+@pytest.mark.parametrize("world", [2, 4])
+def test_channel_sharded_triangle_multiplication_choreography(world):
+  _run(_channel_choreography, world)
