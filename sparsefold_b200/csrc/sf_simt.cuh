@@ -39,10 +39,96 @@ __global__ void k_layernorm(const Tin* __restrict__ x, Tout* __restrict__ y,
   }
 }
 
+// Eight consecutive elements as fp32 (one 16-byte load for bf16, two for fp32).
+__device__ __forceinline__ void ld8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void ld8(const bf16* p, float (&v)[8]) {
+  const uint4 q = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void st8(bf16* p, const float (&v)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    w[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// The same LayerNorm for rows of G * 8 elements (G = 1 .. 32, a power of two): a group of G
+// lanes per row, eight elements per lane held in registers, statistics over the group with
+// shuffles (same two passes, mean then the centred squares), one coalesced read and write.
+template <typename Tin, typename Tout, int G>
+__global__ void k_layernorm_vec(const Tin* __restrict__ x, Tout* __restrict__ y, const float* __restrict__ w,
+                                const float* __restrict__ b, int64_t rows, float eps) {
+  constexpr int COLS = 8 * G;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / G;
+  const int sub = threadIdx.x % G;
+  const bool live = row < rows;
+  float v[8];
+  if (live) ld8(x + row * COLS + sub * 8, v);
+  else
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = 0.f;
+  float s = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o, G);
+  const float mean = s / COLS;
+  float q = 0.f;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float d = v[e] - mean;
+    q = fmaf(d, d, q);
+  }
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o, G);
+  const float rstd = rsqrtf(q / COLS + eps);
+  if (!live) return;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const int c = sub * 8 + e;
+    float o = (v[e] - mean) * rstd;
+    if (w) o *= w[c];
+    if (b) o += b[c];
+    v[e] = o;
+  }
+  st8(y + row * COLS + sub * 8, v);
+}
+
+template <typename Tin, typename Tout, int G>
+inline int launch_layernorm_vec(const Tin* x, Tout* y, const float* w, const float* b, int64_t rows, float eps,
+                                cudaStream_t s) {
+  const int64_t threads = rows * G;
+  k_layernorm_vec<Tin, Tout, G><<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, y, w, b, rows, eps);
+  count_launch();
+  return check_launch("layernorm");
+}
+
 template <typename Tin, typename Tout>
 inline int launch_layernorm(const Tin* x, Tout* y, const float* w, const float* b, int64_t rows,
                             int cols, float eps, cudaStream_t s) {
   if (rows == 0) return SF_OK;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (aligned && (rows * cols) / 8 < (int64_t(1) << 31)) {
+    switch (cols) {
+      case 64: return launch_layernorm_vec<Tin, Tout, 8>(x, y, w, b, rows, eps, s);
+      case 128: return launch_layernorm_vec<Tin, Tout, 16>(x, y, w, b, rows, eps, s);
+      case 256: return launch_layernorm_vec<Tin, Tout, 32>(x, y, w, b, rows, eps, s);
+      default: break;
+    }
+  }
   int warps = 8;
   k_layernorm<Tin, Tout><<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, s>>>(x, y, w, b, rows, cols, eps);
   count_launch();
