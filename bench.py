@@ -489,7 +489,7 @@ def run_reference(args) -> None:
 
 OPS = ("tri_attention_start", "tri_attention_end", "tri_mult_outgoing", "tri_mult_incoming", "pair_transition",
        "single_update", "single_attention", "diffusion_transformer", "diffusion_step", "atom_transformer",
-       "msa_attention", "outer_product_mean")
+       "msa_attention", "outer_product_mean", "pair_embedding", "diffusion_pair_cond")
 
 
 def op_flops(op: str, n: int) -> float:
@@ -530,6 +530,29 @@ def _atom_flops(s: int, nsub: int, q: int, k: int, c: int, h: int, d: int, block
   return blocks * per
 
 
+def op_bytes(op: str, n: int) -> float:
+  """Algorithmic HBM bytes of one call of the bandwidth-bound ops (each input read once, the result
+  written once, bf16)."""
+  if op == "pair_embedding":     # relative encoding (139) + contact (1) + previous pair in, pair out
+    return n * n * 2.0 * (139 + 1 + 128 + 128)
+  if op == "diffusion_pair_cond":   # [pair | relative encoding] (128 + 139) in, pair_cond out
+    return n * n * 2.0 * (128 + 139 + 128)
+  return 0.0
+
+
+def _one_hot_rel(n: int, g):
+  """Relative-encoding-shaped features [n, n, 139]: one-hot position (66), token (66), chain (6) bins and a
+  0/1 same-entity flag (trunk/network.py:171-186)."""
+  import torch
+  x = torch.zeros(n, n, 139)
+  i = torch.arange(n)
+  x[i[:, None], i[None, :], torch.clamp(i[:, None] - i[None, :] + 32, 0, 64)] = 1.0
+  x[i[:, None], i[None, :], 66 + torch.clamp(i[:, None] - i[None, :] + 32, 0, 64)] = 1.0
+  x[..., 132] = 1.0
+  x[i[:, None], i[None, :], 133 + torch.randint(0, 6, (n, n), generator=g)] = 1.0
+  return x
+
+
 def _workload_op(op: str, n: int):
   """(run, flops, what) for the workload ops of configs[2] and configs[3] and the single attention."""
   import types
@@ -538,6 +561,49 @@ def _workload_op(op: str, n: int):
   dt = torch.bfloat16
   g = torch.Generator().manual_seed(4)
   rn = lambda *shape: torch.randn(*shape, generator=g).to("cuda", dt)
+  if op == "pair_embedding":
+    # Evoformer pair embedding (computed once per prediction) and one recycling step
+    # (trunk/network.py:344-372) on the b200 kernels, N = n tokens, bf16
+    tf = rn(n, 447)
+    wl, wr = rn(128, 447) * 0.05, rn(128, 447) * 0.05
+    w_pos = (torch.randn(139, 128, generator=g) * 0.1).cuda()
+    w_bond = (torch.randn(1, 128, generator=g) * 0.1).cuda()
+    rel = _one_hot_rel(n, g).to("cuda", dt)
+    contact = (torch.rand(n, n, 1, generator=g) > 0.99).to("cuda", dt)
+    prev = rn(n, n, 128)
+    ln_w, ln_b = torch.ones(128, device="cuda"), torch.zeros(128, device="cuda")
+    wp = rn(128, 128) * 0.09
+
+    def run():
+      pos = ops.pair_sparse_linear(rel, w_pos)
+      pair = ops.pair_outer_sum(ops.linear(tf, wl), ops.linear(tf, wr), addend=pos)
+      pair = ops.pair_sparse_linear(contact, w_bond, residual=pair)
+      return ops.linear(ops.layer_norm(prev, ln_w, ln_b), wp, residual=pair)
+    return (run, 0.0, f"Evoformer pair embedding (outer sum of the single projections + relative-position "
+                      f"encoding 139 one-hot + bonds) and one recycling step (LayerNorm + linear + residual), N={n}")
+  if op == "diffusion_pair_cond":
+    # DiffusionHead._get_base_cond, the pair half (diffusion/generator.py:367-391) at configs[2]'s N=768:
+    # LayerNorm over [pair | relative encoding] (267), the fp32 ("highest") projection, two transitions
+    n_ = 768
+    pair, rel = rn(n_, n_, 128), _one_hot_rel(n_, g).to("cuda", dt)
+    w_ln = torch.ones(267, device="cuda")
+    w_proj = (torch.randn(128, 267, generator=g) * 0.06).cuda()
+    tr = [modules.DiffusionTransitionBlock(128, 2) for _ in range(2)]
+    for i, t in enumerate(tr):
+      synth.init_params(t, seed=4 + i)
+    tr = [t.cuda() for t in tr]
+    for t in tr:
+      modules.prepare(t)
+
+    def run():
+      f2 = torch.cat((pair, rel), dim=-1)
+      pc = ops.linear(ops.layer_norm(f2, w_ln, None).float(), w_proj).to(dt)
+      for t in tr:
+        pc = t(pc)
+      return pc
+    fl = 2.0 * n_ * n_ * 267 * 128 + 2 * (2.0 * n_ * n_ * 128 * 512 + 2.0 * n_ * n_ * 256 * 128)
+    return (run, fl, "DiffusionHead pair conditioning at N=768: LayerNorm(267) + fp32 projection 267->128 + "
+                     "2 transitions")
   if op == "single_attention":
     h, d = 16, 24
     y = rn(n, 4, h, d)
@@ -665,7 +731,10 @@ def run_op(args) -> None:
     torch.cuda.synchronize()
   ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
   peaks = load_peaks()
-  print(json.dumps({"op": args.op, "what": what, "n_token": n, "ms": round(ms, 4),
+  nbytes = op_bytes(args.op, n)
+  hbm = ({"gbytes": round(nbytes / 1e9, 4), "gb_per_s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+          "frac_of_hbm_peak": round(nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)} if nbytes else {})
+  print(json.dumps({"op": args.op, "what": what, "n_token": n, "ms": round(ms, 4), **hbm,
                     "timing": "CUDA graph replay" if graph is not None else "eager launches",
                     "gflop": round(fl / 1e9, 2) if fl else None,
                     "tflop_per_s": round(fl / (ms * 1e-3) / 1e12, 2) if fl else None,

@@ -277,6 +277,19 @@ int sf_scale_rows(int dtype, void* x, const float* s, int64_t rows, int64_t cols
 int sf_copy_blocks(void* dst, const void* src, int64_t nblk, int64_t rows, int64_t width_bytes,
                    int64_t src_blk_stride, int64_t src_row_stride, int64_t dst_blk_stride,
                    int64_t dst_row_stride, sf_stream_t stream);
+/* out[i][j][:] = left[i][:] + right[j][:] (+ addend[i][j][:] when not NULL), rows x cols x channels:
+ * the sequence pair embedding left_single(target_feat_shard)[:, None] + right_single(target_feat)[None, :]
+ * of Evoformer._get_seq_pair_embedding (trunk/network.py:195-212).  fp32 sum, rounded once. */
+int sf_pair_outer_sum(int dtype, const void* left, const void* right, const void* addend, void* out,
+                      int64_t rows, int64_t cols, int64_t channels, sf_stream_t stream);
+/* out[p][:] = sum_k x[p][k] w[k][:] (+ residual[p][:] when not NULL) for `positions` rows of x [positions][k]:
+ * the pair-side linear layers whose inputs are one-hot or 0/1 features, the relative-position encoding
+ * (Evoformer._get_position_feat, trunk/network.py:188-193, k = 139) and the bond contact map
+ * (Evoformer._get_bonds_act, :214-256, k = 1).  w is fp32 [k][channels] (the reference Linear's
+ * input_shape + output_shape layout); channels 32, 64, 128 or 256.  Only nonzero x[p][k] contribute
+ * (a zero feature skips its term), in increasing k, fp32 sums rounded once to dtype. */
+int sf_pair_sparse_linear(int dtype, const void* x, const float* w, const void* residual, void* out,
+                          int64_t positions, int64_t k, int64_t channels, sf_stream_t stream);
 
 #ifdef __cplusplus
 }

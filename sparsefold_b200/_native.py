@@ -87,6 +87,8 @@ _SIGNATURES = {
     "sf_opm_repack": (C.c_int, [C.c_int, _vp, _i64, _i64, _i64, _vp, _vp]),
     "sf_scale_rows": (C.c_int, [C.c_int, _vp, _vp, _i64, _i64, _vp]),
     "sf_copy_blocks": (C.c_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
+    "sf_pair_outer_sum": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "sf_pair_sparse_linear": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "sf_tri_mult_project_rows": (C.c_int, [C.c_int, _vp, _vp, _i64, _i64, _i64, C.c_int, C.POINTER(TriMultWeights),
                                            _vp, _vp, _vp]),
     "sf_tri_mult_contract_chunked": (C.c_int, [C.c_int, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),

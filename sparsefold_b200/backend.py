@@ -46,6 +46,10 @@ def replacement_map():
     orig[name] = _reference_base(getattr(blocks, name))
   diff = {name: _reference_base(getattr(transformer, name))
           for name in ("SelfAttention", "TransitionBlock", "CrossAttention", "Transformer", "CrossAttTransformer")}
+  from sparsefold.model.trunk import network
+  from sparsefold.model.diffusion import generator
+  evoformer = _reference_base(network.Evoformer)
+  head = _reference_base(generator.DiffusionHead)
   return [
       (blocks, "GridSelfAttention", _native_class(orig["GridSelfAttention"], _m.GridSelfAttentionB200)),
       (blocks, "TriangleMultiplication", _native_class(orig["TriangleMultiplication"], _m.TriangleMultiplicationB200)),
@@ -58,6 +62,8 @@ def replacement_map():
       (transformer, "CrossAttention", _native_class(diff["CrossAttention"], _m.CrossAttentionB200)),
       (transformer, "Transformer", _native_class(diff["Transformer"], _m.DiffusionTransformerB200)),
       (transformer, "CrossAttTransformer", _native_class(diff["CrossAttTransformer"], _m.CrossAttTransformerB200)),
+      (network, "Evoformer", _native_class(evoformer, _m.EvoformerB200)),
+      (generator, "DiffusionHead", _native_class(head, _m.DiffusionHeadB200)),
   ]
 
 

@@ -520,6 +520,135 @@ class OuterProductMeanB200(B200Module):
 
 
 # ---------------------------------------------------------------------------
+# Embedding-side pair layers (trunk/network.py:195-285, diffusion/generator.py:367-391).
+# The Evoformer and the DiffusionHead hold plain primitives (Linear, LayerNorm) for their
+# pair-side embeddings; at prepare time those instances take a B200 class of their own
+# (``(LinearB200, primitives.Linear)``), so the reference's methods run unchanged and call
+# the kernels, and parameters and state_dict keys stay where they were.
+# ---------------------------------------------------------------------------
+_ADOPTED: dict[tuple[type, type], type] = {}
+
+
+def _adopt(mod: torch.nn.Module, mixin: type) -> torch.nn.Module:
+  """Give one module instance the class (mixin, its class); returns it."""
+  if not isinstance(mod, mixin):
+    base = type(mod)
+    key = (base, mixin)
+    if key not in _ADOPTED:
+      _ADOPTED[key] = type(base.__name__ + "B200", (mixin, base), {"__module__": __name__})
+    mod.__class__ = _ADOPTED[key]
+  return mod
+
+
+class LinearB200(B200Module):
+  """``Linear`` (layers/primitives.py:192-365) with one input and one output axis on the C ABI.
+
+  Dense mode: ``sf_linear`` (tcgen05 for bf16 with K, N multiples of 8, CUDA cores otherwise) in the
+  activation dtype, or in fp32 where the reference asks ``precision="highest"``; bias, residual and
+  post_op in the reference's order (output + bias + residual, then post_op, primitives.py:347-365).
+  Sparse mode (``_sf_sparse``, for one-hot or 0/1 inputs): ``sf_pair_sparse_linear`` over the nonzero
+  features with the fp32 weight.  The result has the input's dtype, as the reference's.
+  """
+  _sf_sparse = False
+
+  def prepare_native(self):
+    if len(self.input_shape) != 1 or len(self.output_shape) != 1:
+      raise ValueError(f"{self.name}: B200 Linear takes one input and one output axis, got "
+                       f"{self.input_shape} -> {self.output_shape}")
+    w = self.weight.detach().float()
+    w_kc = w.T if self.transpose_weights else w                     # [K, C]
+    if self._sf_sparse and (self.use_bias or w_kc.shape[1] not in (32, 64, 128, 256)):
+      raise ValueError(f"{self.name}: sparse pair linear needs no bias and 32/64/128/256 outputs")
+    self._keep("w_kc", w_kc)
+    self._pack("wt", w_kc.T)                                        # [C, K] per activation dtype
+    if self.use_bias:
+      self._keep("bias", self.bias)
+    self._native_prepared = True
+
+  @_require_prepared
+  def forward(self, inputs: torch.Tensor, *, post_op=None, residual: torch.Tensor | None = None):
+    dt = inputs.dtype
+    if self._sf_sparse:
+      if post_op is not None:
+        raise ValueError(f"{self.name}: post_op on a sparse pair linear")
+      return ops.pair_sparse_linear(inputs, self._kept("w_kc"), residual)
+    cdt = torch.float32 if getattr(self, "precision", None) == "highest" else dt
+    bias = self._kept("bias") if self.use_bias else None
+    res = None if residual is None else residual.to(cdt)
+    return ops.linear(inputs.to(cdt), self._packed("wt", cdt), bias, residual=res, post_op=post_op).to(dt)
+
+
+class LayerNormB200(B200Module):
+  """``LayerNorm`` (layers/primitives.py:368-497) over the last axis on ``sf_layernorm`` (fp32
+  statistics, affine parameters in fp32, output in the input's dtype)."""
+
+  def prepare_native(self):
+    if len(self.normalized_shape) != 1:
+      raise ValueError(f"{self.name}: B200 LayerNorm normalises one axis")
+    if self.weight is not None:
+      self._keep("w", self.weight)
+    if self.bias is not None:
+      self._keep("b", self.bias)
+    self._native_prepared = True
+
+  @_require_prepared
+  def forward(self, input: torch.Tensor) -> torch.Tensor:
+    if self.dim not in (-1, input.ndim - 1):
+      raise ValueError(f"{self.name}: B200 LayerNorm normalises the last axis only (dim={self.dim})")
+    w = self._kept("w") if self.weight is not None else None
+    b = self._kept("b") if self.bias is not None else None
+    return ops.layer_norm(input, w, b, self.eps)
+
+
+class EvoformerB200(B200Module):
+  """The pair embedding of ``Evoformer`` (trunk/network.py:195-285, :344-376) on the C ABI.
+
+  * ``_get_seq_pair_embedding``: left_single / right_single on ``sf_linear``, then one
+    ``sf_pair_outer_sum`` pass for left[:, None] + right[None, :] (network.py:195-212);
+  * ``_get_position_feat`` and ``_get_bonds_act`` run the reference's code, whose
+    ``position_activations`` (139 one-hot features) and ``bond_embedding`` (one 0/1 feature) are
+    sparse B200 Linears (``sf_pair_sparse_linear``);
+  * the recycling step prev_embedding(LayerNorm(prev pair), residual=pair) (:369-372) runs on
+    ``sf_layernorm`` and ``sf_linear`` with the residual in its epilogue.
+  The template, MSA and Pairformer stacks are the reference's, built from the B200 factories.
+  """
+  _LINEARS = {"left_single": False, "right_single": False, "prev_embedding": False,
+              "position_activations": True, "bond_embedding": True}
+  _NORMS = ("prev_embedding_layer_norm",)
+
+  def prepare_native(self):
+    for name, sparse in self._LINEARS.items():
+      sub = _adopt(getattr(self, name), LinearB200)
+      sub._sf_sparse = sparse
+      sub.prepare_native()
+    for name in self._NORMS:
+      _adopt(getattr(self, name), LayerNormB200).prepare_native()
+    self._native_prepared = True
+
+  @_require_prepared
+  def _get_seq_pair_embedding(self, token_features, target_feat: torch.Tensor, target_feat_shard: torch.Tensor):
+    left = self.left_single(target_feat_shard)    # (B, C)
+    right = self.right_single(target_feat)        # (N, C)
+    return ops.pair_outer_sum(left, right)        # (B, N, C)
+
+
+class DiffusionHeadB200(B200Module):
+  """The base conditioning of ``DiffusionHead._get_base_cond`` (diffusion/generator.py:367-391): the
+  LayerNorms over [pair embedding | 139 relative features] and [single | target features] on
+  ``sf_layernorm`` and the two ``precision="highest"`` projections on ``sf_linear`` in fp32; the
+  pair transitions are the B200 diffusion TransitionBlock of the factory swap."""
+  _LINEARS = ("pair_cond_initial_projection", "single_cond_initial_projection")
+  _NORMS = ("pair_cond_initial_norm", "single_cond_initial_norm")
+
+  def prepare_native(self):
+    for name in self._LINEARS:
+      _adopt(getattr(self, name), LinearB200).prepare_native()
+    for name in self._NORMS:
+      _adopt(getattr(self, name), LayerNormB200).prepare_native()
+    self._native_prepared = True
+
+
+# ---------------------------------------------------------------------------
 # Standalone modules: the reference module trees (same attribute names, shapes
 # and state_dict keys) built from the parameter holders of layers.py.
 # ---------------------------------------------------------------------------

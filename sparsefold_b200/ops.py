@@ -334,3 +334,33 @@ def swiglu(h: torch.Tensor) -> torch.Tensor:
   out = torch.empty(*h.shape[:-1], i2 // 2, dtype=h.dtype, device=h.device)
   N.call("sf_swiglu", _dt(h), _p(h), _p(out), h.numel() // i2, i2 // 2, _stream())
   return out
+
+
+def pair_outer_sum(left: torch.Tensor, right: torch.Tensor, addend=None) -> torch.Tensor:
+  """out[i, j] = left[i] + right[j] (+ addend[i, j]): [B, C] x [N, C] -> [B, N, C] in left's dtype
+  (Evoformer._get_seq_pair_embedding, trunk/network.py:195-212)."""
+  _cuda(left, right, addend)
+  assert left.ndim == 2 and right.ndim == 2 and left.shape[1] == right.shape[1] and left.dtype == right.dtype
+  b, c = left.shape
+  n = right.shape[0]
+  left, right = left.contiguous(), right.contiguous()
+  if addend is not None:
+    addend = addend.to(left.dtype).expand(b, n, c).contiguous()
+  out = torch.empty(b, n, c, dtype=left.dtype, device=left.device)
+  N.call("sf_pair_outer_sum", _dt(left), _p(left), _p(right), _p(addend), _p(out), b, n, c, _stream())
+  return out
+
+
+def pair_sparse_linear(x: torch.Tensor, w_kc: torch.Tensor, residual=None) -> torch.Tensor:
+  """out[..., :] = sum over the nonzero x[..., k] of x[..., k] * w_kc[k, :] (+ residual): the linear layers
+  on one-hot / 0-1 pair features (trunk/network.py:188-193, :214-256).  w_kc is fp32 [K, C]."""
+  _cuda(x, w_kc, residual)
+  assert w_kc.dtype == torch.float32 and w_kc.ndim == 2 and x.shape[-1] == w_kc.shape[0]
+  x = x.contiguous()
+  k, c = w_kc.shape
+  out = torch.empty(*x.shape[:-1], c, dtype=x.dtype, device=x.device)
+  if residual is not None:
+    residual = residual.to(x.dtype).expand_as(out).contiguous()
+  N.call("sf_pair_sparse_linear", _dt(x), _p(x), _p(w_kc.contiguous()), _p(residual), _p(out), x.numel() // k, k, c,
+         _stream())
+  return out

@@ -44,6 +44,11 @@ def _setup_reference(src: str):
   from sparsefold import backends
   backends.init()
   torch.set_float32_matmul_precision("highest")
+  # A Linear built with precision="highest" restores the reference's default fp32 matmul
+  # precision ("medium", runtime/util.py:28) after its einsum (layers/primitives.py:359-364);
+  # the fixtures keep every fp32 matmul at "highest".
+  from sparsefold.runtime import util
+  util.DEFAULT_FP32_MATMUL_PRECISION = "highest"
 
 
 def _spec(module) -> list:
@@ -227,9 +232,79 @@ def diffusion_and_msa():
   _save("outer_product_mean", _spec(mod), seed, act=act, mask=msa_mask, out=out)
 
 
+def _spec_sub(module, names) -> list:
+  """The parameter spec of the named submodules only, with their full names."""
+  out = []
+  for name in names:
+    for full, shape, kind, fan in _spec(getattr(module, name)):
+      out.append([f"{name}.{full}", shape, kind, fan])
+  return out
+
+
+def embedding():
+  """Fixture of the embedding-side pair ops: the Evoformer's pair embedding and recycling step and the
+  DiffusionHead's base conditioning, N=16 tokens in two chains, the reference's own relative encoding."""
+  import types as _types
+  from sparsefold.model.trunk import network
+  from sparsefold.model.diffusion import generator
+  from sparsefold.model.embeddings import features as emb
+  from sparsefold.model import config as mc
+  gc = mc.GlobalConfig()
+  seed = 0
+  g = torch.Generator().manual_seed(13)
+  rn = lambda *s: torch.randn(*s, generator=g)
+  n, tf_size = 16, 447
+  tok = _types.SimpleNamespace(
+      token_index=torch.arange(n), residue_index=torch.cat([torch.arange(10), torch.arange(6)]),
+      asym_id=torch.cat([torch.zeros(10), torch.ones(6)]).long(), entity_id=torch.cat([torch.zeros(10), torch.ones(6)]).long(),
+      sym_id=torch.zeros(n).long())
+  rel = emb.create_relative_encoding(tok, 32, 2).float()
+  assert rel.shape == (n, n, 139)
+  evo = network.Evoformer(network.Evoformer.Config(), gc, target_feat_size=tf_size)
+  names = ("left_single", "right_single", "position_activations", "bond_embedding", "prev_embedding_layer_norm",
+           "prev_embedding")
+  for name in names:
+    synth.init_params(getattr(evo, name), seed, prefix=f"{name}.")
+  target_feat = rn(n, tf_size)
+  pl_idx = torch.tensor([[2, 12], [5, 14], [0, 0]], dtype=torch.int32)
+  pl_mask = torch.tensor([[1, 1], [1, 1], [0, 1]], dtype=torch.int32)
+  ll_idx = torch.tensor([[12, 13], [14, 15]], dtype=torch.int32)
+  ll_mask = torch.tensor([[1, 1], [1, 0]], dtype=torch.int32)
+  batch = _types.SimpleNamespace(
+      token_features=tok,
+      polymer_ligand_bond_info=_types.SimpleNamespace(
+          tokens_to_polymer_ligand_bonds=_types.SimpleNamespace(gather_idxs=pl_idx, gather_mask=pl_mask)),
+      ligand_ligand_bond_info=_types.SimpleNamespace(
+          tokens_to_ligand_ligand_bonds=_types.SimpleNamespace(gather_idxs=ll_idx, gather_mask=ll_mask)))
+  prev_pair = rn(n, n, 128)
+  with torch.no_grad():
+    seq_pair = evo._get_seq_pair_embedding(tok, target_feat, target_feat)
+    pos = evo._get_position_feat(rel, torch.float32)
+    bonds = evo._get_bonds_act(batch, torch.float32)
+    pair = seq_pair + pos + bonds
+    prev_out = evo.prev_embedding(evo.prev_embedding_layer_norm(prev_pair), residual=pair)
+  spec = _spec_sub(evo, names)
+
+  head = generator.DiffusionHead(generator.DiffusionHead.Config(), gc, pair_channels=128, seq_channels=384,
+                                 target_feat_size=tf_size)
+  hnames = ("pair_cond_initial_norm", "pair_cond_initial_projection", "pair_transitions", "single_cond_initial_norm",
+            "single_cond_initial_projection")
+  for name in hnames:
+    synth.init_params(getattr(head, name), seed, prefix=f"head.{name}.")
+  single = rn(n, 384)
+  with torch.no_grad():
+    sc, pc = head._get_base_cond(rel, {"single": single, "pair": prev_out, "target_feat": target_feat}, True)
+  spec_h = [[f"head.{f}", s, k, fan] for f, s, k, fan in _spec_sub(head, hnames)]
+  meta_seed = seed
+  _save("embedding_n16", spec + spec_h, meta_seed, target_feat=target_feat, rel_features=rel, pl_idx=pl_idx,
+        pl_mask=pl_mask, ll_idx=ll_idx, ll_mask=ll_mask, prev_pair=prev_pair, seq_pair=seq_pair, position_feat=pos,
+        bonds_act=bonds, prev_out=prev_out, single=single, single_cond=sc, pair_cond=pc)
+
+
 if __name__ == "__main__":
   src = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SPARSEFOLD_REF_SRC")
   if not src:
     raise SystemExit("usage: make_golden.py <path of the reference's src/ directory> (or set SPARSEFOLD_REF_SRC)")
   main(src)
   diffusion_and_msa()
+  embedding()

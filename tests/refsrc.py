@@ -40,3 +40,17 @@ def import_reference() -> str | None:
   except ImportError:
     sys.modules["zstandard"] = types.ModuleType("zstandard")
   return src
+
+
+def loaded_shapes(module):
+  """The reference's OuterProductMean creates output_w / output_b only when weights are loaded
+  (trunk/blocks.py:608-628, set_parameters); give them their loaded shapes so a module built without a
+  checkpoint carries every parameter."""
+  import torch
+  for mod in module.modules():
+    if type(mod).__name__.startswith("OuterProductMean") and "output_w" not in mod._parameters:
+      outer, dev = tuple(mod.left_projection.output_shape), mod.left_projection.weight.device
+      mod.output_w = torch.nn.Parameter(torch.empty(*outer, *outer, mod.num_output_channel, device=dev),
+                                        requires_grad=False)
+      mod.output_b = torch.nn.Parameter(torch.empty(mod.num_output_channel, device=dev), requires_grad=False)
+  return module

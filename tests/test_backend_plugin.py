@@ -7,7 +7,7 @@ keeps its state_dict contract.
 """
 import pytest
 
-from tests.refsrc import import_reference
+from tests.refsrc import import_reference, loaded_shapes
 
 
 @pytest.fixture(scope="module")
@@ -61,3 +61,36 @@ def test_reference_block_prepares_with_same_state_dict(ref):
   mine.load_state_dict(blk.state_dict(), strict=True)
   for k, v in mine.state_dict().items():
     torch.testing.assert_close(v, blk.state_dict()[k], rtol=0, atol=0)
+
+
+def test_evoformer_and_diffusion_head_pair_layers_take_b200_classes(ref):
+  """The embedding-side pair layers (trunk/network.py:195-285, diffusion/generator.py:367-391): prepare()
+  gives the Evoformer's and the DiffusionHead's pair-side Linear / LayerNorm instances B200 classes, keeps
+  the state_dict, and the product path refuses host tensors (no CPU fallback)."""
+  import torch
+  from sparsefold.model.trunk import network
+  from sparsefold.model.diffusion import generator
+  from sparsefold.model import config as mc
+  from sparsefold_b200 import modules
+  assert issubclass(network.Evoformer, modules.EvoformerB200)
+  assert issubclass(generator.DiffusionHead, modules.DiffusionHeadB200)
+  evo = loaded_shapes(network.Evoformer(network.Evoformer.Config(), mc.GlobalConfig(), target_feat_size=447))
+  head = generator.DiffusionHead(generator.DiffusionHead.Config(), mc.GlobalConfig(), pair_channels=128,
+                                 seq_channels=384, target_feat_size=447)
+  for mod in (evo, head):
+    with torch.no_grad():
+      for p in mod.parameters():
+        p.normal_(0.0, 0.02)
+    keys = set(mod.state_dict())
+    ref.prepare(mod)
+    assert set(mod.state_dict()) == keys
+  for name, sparse in modules.EvoformerB200._LINEARS.items():
+    sub = getattr(evo, name)
+    assert isinstance(sub, modules.LinearB200) and sub._sf_sparse == sparse, name
+  assert isinstance(evo.prev_embedding_layer_norm, modules.LayerNormB200)
+  assert isinstance(head.pair_cond_initial_projection, modules.LinearB200)
+  assert isinstance(head.pair_cond_initial_norm, modules.LayerNormB200)
+  with pytest.raises(ValueError, match="CUDA tensors only"):
+    evo._get_position_feat(torch.zeros(4, 4, 139), torch.float32)
+  with pytest.raises(ValueError, match="CUDA tensors only"):
+    evo._get_seq_pair_embedding(None, torch.zeros(4, 447), torch.zeros(4, 447))

@@ -16,7 +16,7 @@ import torch
 
 from sparsefold_b200 import _native, synth
 from tests.golden_io import max_rel_err
-from tests.refsrc import import_reference
+from tests.refsrc import import_reference, loaded_shapes
 
 pytestmark = pytest.mark.gpu
 TOL = {torch.float32: 1e-4, torch.bfloat16: 2e-2}
@@ -51,27 +51,15 @@ def _kernel_values(p, dtype):
   return {k: (v.float() if keep(k) else v.to(dtype).float()) for k, v in p.items()}
 
 
-def _loaded_shapes(module):
-  """The reference's OuterProductMean creates output_w / output_b only when weights are loaded
-  (blocks.py:608-628, set_parameters); give them their loaded shapes so both copies carry them."""
-  for mod in module.modules():
-    if type(mod).__name__.startswith("OuterProductMean") and "output_w" not in mod._parameters:
-      outer, dev = tuple(mod.left_projection.output_shape), mod.left_projection.weight.device
-      mod.output_w = torch.nn.Parameter(torch.empty(*outer, *outer, mod.num_output_channel, device=dev),
-                                        requires_grad=False)
-      mod.output_b = torch.nn.Parameter(torch.empty(mod.num_output_channel, device=dev), requires_grad=False)
-  return module
-
-
 def _twins(ref, make, seed):
   """(module under b200, module of the reference's own Torch path on the CPU) with the same parameters."""
   blocks, network, mc, backends, b200 = ref
-  mine = _loaded_shapes(make())
+  mine = loaded_shapes(make())
   p = synth.init_params(mine, seed)
   backends.prepare(mine)
   b200.unapply()                      # the reference's own classes for the second copy
   try:
-    theirs = _loaded_shapes(make()).cpu()
+    theirs = loaded_shapes(make()).cpu()
   finally:
     b200.apply()
   return mine, theirs, p

@@ -108,3 +108,22 @@ def test_msa_attention_golden():
 def test_outer_product_mean_golden():
   a, p = load("outer_product_mean")
   assert max_rel_err(dif.outer_product_mean(a["act"], a["mask"], p), a["out"]) < 2e-6
+
+
+def test_embedding_golden():
+  """The embedding-side pair ops: Evoformer pair embedding + recycling step and the DiffusionHead base
+  conditioning, against the reference's own outputs (N=16, two chains, its relative encoding)."""
+  from oracle import embedding as emb
+  a, p = load("embedding_n16")
+  n = a["target_feat"].shape[0]
+  assert max_rel_err(emb.seq_pair_embedding(a["target_feat"], a["target_feat"], p), a["seq_pair"]) < 1e-6
+  assert max_rel_err(emb.position_feat(a["rel_features"], p), a["position_feat"]) < 1e-6
+  contact = emb.contact_matrix(n, a["pl_idx"], a["pl_mask"], a["ll_idx"], a["ll_mask"])
+  assert int(contact.sum()) == 3 and contact[0, 0] == 0
+  assert max_rel_err(emb.bonds_act(contact, p), a["bonds_act"]) < 1e-6
+  pair = a["seq_pair"] + a["position_feat"] + a["bonds_act"]
+  assert max_rel_err(emb.prev_embedding(a["prev_pair"], pair, p), a["prev_out"]) < 2e-6
+  hp = {k[len("head."):]: v for k, v in p.items() if k.startswith("head.")}
+  sc, pc = emb.base_cond(a["rel_features"], a["single"], a["prev_out"], a["target_feat"], True, hp)
+  assert max_rel_err(sc, a["single_cond"]) < 2e-6
+  assert max_rel_err(pc, a["pair_cond"]) < 2e-6
