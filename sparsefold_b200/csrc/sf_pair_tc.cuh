@@ -34,86 +34,104 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// LayerNorm of row r of a 128 x 128 tile (128B swizzle) in place, one thread per row:
-// statistics in one pass over the row, shifted by its first value so that the
-// variance E[(x-k)^2] - E[x-k]^2 keeps its precision, with independent
-// accumulators; scale and shift come from shared memory.
+// Packed fp32 pairs (one instruction for two lanes of arithmetic, each IEEE as its
+// scalar form): (a0, a1) - (b0, b1), (a0, a1) * (b0, b1), (a0, a1) * (b0, b1) + (c0, c1).
+__device__ __forceinline__ void sub2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\t"
+      "sub.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void mul2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\t"
+      "mul.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\t"
+      "add.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a0), "+f"(a1) : "f"(b0), "f"(b1));
+}
+// (d0, d1) = (a0, a1) * (b0, b1) + (d0, d1)
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tmov.b64 z, {%0, %1};\n\t"
+      "fma.rn.f32x2 z, x, y, z;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "+f"(d0), "+f"(d1) : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// The shifted one-pass statistics of 8 bf16 values (one 16-byte chunk) as packed pairs:
+// s += (x - k), q += (x - k)^2 over the pairs (even, odd) of the chunk.
+__device__ __forceinline__ void ln_accumulate(const uint4 v, float k, float (&s)[2], float (&q)[2]) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float d0 = bf_lo(u[j]), d1 = bf_hi(u[j]);
+    sub2(d0, d1, k, k);
+    add2(s[0], s[1], d0, d1);
+    fma2(q[0], q[1], d0, d1, d0, d1);
+  }
+}
+// One normalised chunk: ((x - mean) * rstd) * w + b for 8 values, packed to bf16.
+__device__ __forceinline__ uint4 ln_apply(const uint4 v, float mean, float rstd, const float* w, const float* b) {
+  const float4 w0 = *reinterpret_cast<const float4*>(w), w1 = *reinterpret_cast<const float4*>(w + 4);
+  const float4 b0 = *reinterpret_cast<const float4*>(b), b1 = *reinterpret_cast<const float4*>(b + 4);
+  const float wl[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+  const float bl[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float x0 = bf_lo(u[j]), x1 = bf_hi(u[j]);
+    sub2(x0, x1, mean, mean);
+    mul2(x0, x1, rstd, rstd);
+    float y0 = bl[2 * j], y1 = bl[2 * j + 1];
+    fma2(y0, y1, x0, x1, wl[2 * j], wl[2 * j + 1]);
+    o[j] = pack_bf2(y0, y1);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// LayerNorm of tile row r in place, one thread per row (128 channels in two 64-channel
+// atoms of the 128B-swizzled K-major layout): statistics in one pass shifted by the row's
+// first value k so that E[(x-k)^2] - E[x-k]^2 keeps its precision, then the normalised,
+// rounded row written back; arithmetic on packed fp32 pairs, scale and shift (128 floats
+// each) from shared memory.
 __device__ __forceinline__ void ln_row_shifted(uint8_t* tile, int r, const float* w_s, const float* b_s, float eps) {
   auto off = [&](int i) -> uint32_t { return (uint32_t)(i >> 3) * ATOM + tc::sw128_off(r, i & 7); };
   const float k = bf_lo(*reinterpret_cast<const uint32_t*>(tile + off(0)));
-  float s[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
+  float s[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, q[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    ln_accumulate(*reinterpret_cast<const uint4*>(tile + off(i)), k, s[i & 1], q[i & 1]);
+  const float dm = ((s[0][0] + s[0][1]) + (s[1][0] + s[1][1])) * (1.0f / C);
+  const float var = fmaxf(((q[0][0] + q[0][1]) + (q[1][0] + q[1][1])) * (1.0f / C) - dm * dm, 0.f);
+  const float mean = k + dm, rstd = rsqrtf(var + eps);
 #pragma unroll 4
   for (int i = 0; i < 16; ++i) {
-    const uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
-    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float d0 = bf_lo(u[j]) - k, d1 = bf_hi(u[j]) - k;
-      s[j] += d0 + d1;
-      q[j] = fmaf(d0, d0, fmaf(d1, d1, q[j]));
-    }
-  }
-  const float dm = ((s[0] + s[1]) + (s[2] + s[3])) * (1.0f / C);
-  const float var = fmaxf(((q[0] + q[1]) + (q[2] + q[3])) * (1.0f / C) - dm * dm, 0.f);
-  const float mean = k + dm, rstd = rsqrtf(var + eps);
-#pragma unroll 2
-  for (int i = 0; i < 16; ++i) {
-    uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
-    uint32_t* u = reinterpret_cast<uint32_t*>(&v);
-    const float4 w0 = *reinterpret_cast<const float4*>(w_s + 8 * i);
-    const float4 w1 = *reinterpret_cast<const float4*>(w_s + 8 * i + 4);
-    const float4 b0 = *reinterpret_cast<const float4*>(b_s + 8 * i);
-    const float4 b1 = *reinterpret_cast<const float4*>(b_s + 8 * i + 4);
-    u[0] = pack_bf2((bf_lo(u[0]) - mean) * rstd * w0.x + b0.x, (bf_hi(u[0]) - mean) * rstd * w0.y + b0.y);
-    u[1] = pack_bf2((bf_lo(u[1]) - mean) * rstd * w0.z + b0.z, (bf_hi(u[1]) - mean) * rstd * w0.w + b0.w);
-    u[2] = pack_bf2((bf_lo(u[2]) - mean) * rstd * w1.x + b1.x, (bf_hi(u[2]) - mean) * rstd * w1.y + b1.y);
-    u[3] = pack_bf2((bf_lo(u[3]) - mean) * rstd * w1.z + b1.z, (bf_hi(u[3]) - mean) * rstd * w1.w + b1.w);
-    *reinterpret_cast<uint4*>(tile + off(i)) = v;
+    uint4* p = reinterpret_cast<uint4*>(tile + off(i));
+    *p = ln_apply(*p, mean, rstd, w_s + 8 * i, b_s + 8 * i);
   }
 }
-// The two-thread layer norm with the statistics in one pass over the row,
-// shifted by the row's first value k so that E[(x-k)^2] - E[x-k]^2 keeps its
-// precision, independent accumulators, and scale and shift read from shared
-// memory (w_s, b_s: 128 floats each; b_s may be null).
+// The same with two threads per row (thread h takes channels 64h..64h+63, the
+// statistics meet through a shuffle with the partner lane); b_s may be null.
 __device__ __forceinline__ void ln_half_row_shifted(uint8_t* tile, int r, int h, const float* w_s, const float* b_s,
                                                     float eps) {
   uint8_t* base = tile + h * ATOM;
   auto off = [&](int i) -> uint32_t { return tc::sw128_off(r, (i + 4 * h) & 7); };
   const float k = bf_lo(*reinterpret_cast<const uint32_t*>(tile + tc::sw128_off(r, 0)));
-  float s[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-  for (int i = 0; i < 8; ++i) {
-    const uint4 v = *reinterpret_cast<const uint4*>(base + off(i));
-    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  float s[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, q[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float d0 = bf_lo(u[j]) - k, d1 = bf_hi(u[j]) - k;
-      s[j] += d0 + d1;
-      q[j] = fmaf(d0, d0, fmaf(d1, d1, q[j]));
-    }
-  }
-  float ss = (s[0] + s[1]) + (s[2] + s[3]), qq = (q[0] + q[1]) + (q[2] + q[3]);
+  for (int i = 0; i < 8; ++i) ln_accumulate(*reinterpret_cast<const uint4*>(base + off(i)), k, s[i & 1], q[i & 1]);
+  float ss = (s[0][0] + s[0][1]) + (s[1][0] + s[1][1]), qq = (q[0][0] + q[0][1]) + (q[1][0] + q[1][1]);
   ss += __shfl_xor_sync(0xffffffffu, ss, 1);
   qq += __shfl_xor_sync(0xffffffffu, qq, 1);
   const float dm = ss * (1.0f / C);
   const float mean = k + dm, rstd = rsqrtf(fmaxf(qq * (1.0f / C) - dm * dm, 0.f) + eps);
-#pragma unroll 2
+  const float zero8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
   for (int i = 0; i < 8; ++i) {
     const int c8 = 64 * h + 8 * ((i + 4 * h) & 7);   // first channel of this chunk
-    uint4 v = *reinterpret_cast<const uint4*>(base + off(i));
-    uint32_t* u = reinterpret_cast<uint32_t*>(&v);
-    const float4 w0 = *reinterpret_cast<const float4*>(w_s + c8);
-    const float4 w1 = *reinterpret_cast<const float4*>(w_s + c8 + 4);
-    float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
-    if (b_s) {
-      b0 = *reinterpret_cast<const float4*>(b_s + c8);
-      b1 = *reinterpret_cast<const float4*>(b_s + c8 + 4);
-    }
-    u[0] = pack_bf2((bf_lo(u[0]) - mean) * rstd * w0.x + b0.x, (bf_hi(u[0]) - mean) * rstd * w0.y + b0.y);
-    u[1] = pack_bf2((bf_lo(u[1]) - mean) * rstd * w0.z + b0.z, (bf_hi(u[1]) - mean) * rstd * w0.w + b0.w);
-    u[2] = pack_bf2((bf_lo(u[2]) - mean) * rstd * w1.x + b1.x, (bf_hi(u[2]) - mean) * rstd * w1.y + b1.y);
-    u[3] = pack_bf2((bf_lo(u[3]) - mean) * rstd * w1.z + b1.z, (bf_hi(u[3]) - mean) * rstd * w1.w + b1.w);
-    *reinterpret_cast<uint4*>(base + off(i)) = v;
+    uint4* p = reinterpret_cast<uint4*>(base + off(i));
+    *p = ln_apply(*p, mean, rstd, w_s + c8, b_s ? b_s + c8 : zero8);
   }
 }
 

@@ -78,30 +78,21 @@ constexpr int OFF_JBAR = OFF_JLN + C * 4;
 constexpr int SMEM_PROJ = OFF_JBAR + 256 + 1024;
 static_assert(SMEM_PROJ <= 232448, "projection shared memory");
 
-// Scale-only LayerNorm of tile row r in place (three passes over shared memory)
-// and the four pair-bias logits of the bf16-rounded normalised row.
 // Scale-only LayerNorm of tile row r in place (one thread per row) and the row's
 // pair bias LN(z) . W_b[h] (bf16 operands, fp32 sums): statistics in one pass,
 // shifted by the row's first value so E[(x-k)^2] - E[x-k]^2 keeps its precision,
-// independent accumulators throughout; the scale and W_b come from shared memory.
+// packed fp32 pair arithmetic; the scale and W_b come from shared memory.
 __device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* w_s, const bf16* wb_s, float (&bias)[H]) {
   auto off = [&](int i) -> uint32_t { return (uint32_t)(i >> 3) * ATOM + tc::sw128_off(r, i & 7); };
   const float k = bf_lo(*reinterpret_cast<const uint32_t*>(tile + off(0)));
-  float s[4] = {0.f, 0.f, 0.f, 0.f}, q[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-  for (int i = 0; i < 16; ++i) {
-    const uint4 v = *reinterpret_cast<const uint4*>(tile + off(i));
-    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+  float s[2][2] = {{0.f, 0.f}, {0.f, 0.f}}, q[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float d0 = bf_lo(u[j]) - k, d1 = bf_hi(u[j]) - k;
-      s[j] += d0 + d1;
-      q[j] = fmaf(d0, d0, fmaf(d1, d1, q[j]));
-    }
-  }
-  const float dm = ((s[0] + s[1]) + (s[2] + s[3])) * (1.0f / C);
+  for (int i = 0; i < 16; ++i)
+    ln_accumulate(*reinterpret_cast<const uint4*>(tile + off(i)), k, s[i & 1], q[i & 1]);
+  const float dm = ((s[0][0] + s[0][1]) + (s[1][0] + s[1][1])) * (1.0f / C);
   const float mean = k + dm;
-  const float rstd = rsqrtf(fmaxf(((q[0] + q[1]) + (q[2] + q[3])) * (1.0f / C) - dm * dm, 0.f) + 1e-5f);
+  const float rstd =
+      rsqrtf(fmaxf(((q[0][0] + q[0][1]) + (q[1][0] + q[1][1])) * (1.0f / C) - dm * dm, 0.f) + 1e-5f);
   float b2[2][H];
 #pragma unroll
   for (int h = 0; h < H; ++h) b2[0][h] = b2[1][h] = 0.f;
@@ -117,7 +108,11 @@ __device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* w
     for (int h = 0; h < H; ++h) wv[h] = *reinterpret_cast<const uint4*>(wb_s + h * C + 8 * i);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      u[j] = pack_bf2((bf_lo(u[j]) - mean) * rstd * wl[2 * j], (bf_hi(u[j]) - mean) * rstd * wl[2 * j + 1]);
+      float x0 = bf_lo(u[j]), x1 = bf_hi(u[j]);
+      sub2(x0, x1, mean, mean);
+      mul2(x0, x1, rstd, rstd);
+      mul2(x0, x1, wl[2 * j], wl[2 * j + 1]);
+      u[j] = pack_bf2(x0, x1);
       // the bias uses the bf16-rounded normalised row: bf16 x bf16 products accumulated in fp32
 #pragma unroll
       for (int h = 0; h < H; ++h)
