@@ -195,14 +195,44 @@ def tri_mult_mode(p: int) -> str:
   return "channels" if p >= CHANNELS_FROM_RANKS else "rows"
 
 
+# Channel sub-chunks per rank in the "channels" mode: the all-to-alls of chunk s+1 run on NCCL's
+# stream while chunk s contracts, and chunk s's product goes back while chunk s+1 contracts
+# (SF_TRIMULT_CHUNKS overrides; 1 = no pipelining).
+TRIMULT_CHUNKS = 2
+
+
+def _trimult_chunks(cl: int) -> int:
+  import os
+  want = int(os.environ.get("SF_TRIMULT_CHUNKS", TRIMULT_CHUNKS))
+  return want if want >= 1 and cl % want == 0 else 1
+
+
+def channel_blocks_out_async(op: torch.Tensor, p: int, s: int, sub: int, group=None):
+  """Start the all-to-all that takes channels [q C/P + s sub, q C/P + (s+1) sub) of every rank's op
+  [m][C][kp] to rank q.  Returns (work, recv [P][m_src][sub][kp], send); keep send alive until the work
+  is waited for."""
+  m, c, kp = op.shape
+  cl = c // p
+  op = op.contiguous()
+  send = torch.empty(p, m, sub, kp, dtype=op.dtype, device=op.device)
+  _pack_blocks(send, op.view(-1)[s * sub * kp:], p, m, sub * kp, cl * kp, c * kp, m * sub * kp, sub * kp)
+  recv = torch.empty_like(send)
+  work = dist.all_to_all_single(recv.view(p * m, sub, kp), send.view(p * m, sub, kp), group=group, async_op=True)
+  return work, recv, send
+
+
 def channel_blocks_out(op: torch.Tensor, p: int, group=None) -> torch.Tensor:
   """op [m][C][kp] (this rank's rows of a contraction operand) -> [P][m_src][C/P][kp]: channel block r
   of every rank's op on rank r (all-to-all; block q of the send buffer = channels q C/P ..)."""
-  m, c, kp = op.shape
-  cl = c // p
-  send = torch.empty(p, m, cl, kp, dtype=op.dtype, device=op.device)
-  _pack_blocks(send, op.contiguous(), p, m, cl * kp, cl * kp, c * kp, m * cl * kp, cl * kp)
-  return all_to_all_rows(send.view(p * m, cl, kp), group).view(p, m, cl, kp)
+  work, recv, _send = channel_blocks_out_async(op, p, 0, op.shape[1] // p, group)
+  work.wait()
+  return recv
+
+
+def _unpack_product(out: torch.Tensor, recv: torch.Tensor, p: int, s: int, sub: int) -> None:
+  """recv [P (channel block q)][rows][sub][pn] -> out[:, q C/P + s sub .. + sub, :] of out [rows][C][pn]."""
+  rows, c, pn = out.shape
+  _pack_blocks(out.view(-1)[s * sub * pn:], recv, p, rows, sub * pn, rows * sub * pn, sub * pn, (c // p) * pn, c * pn)
 
 
 def channel_blocks_back(prod_c: torch.Tensor, p: int, rows: int, c: int, group=None) -> torch.Tensor:
@@ -210,8 +240,41 @@ def channel_blocks_back(prod_c: torch.Tensor, p: int, rows: int, c: int, group=N
   n, cl, pn = prod_c.shape
   recv = all_to_all_rows(prod_c.contiguous().view(n, cl, pn), group)      # [P (channel block)][rows][cl][pn]
   out = torch.empty(rows, c, pn, dtype=prod_c.dtype, device=prod_c.device)
-  _pack_blocks(out, recv, p, rows, cl * pn, rows * cl * pn, cl * pn, cl * pn, c * pn)
+  _unpack_product(out, recv.view(p, rows, cl, pn), p, 0, cl)
   return out
+
+
+def channel_pipeline(a_op: torch.Tensor, b_op: torch.Tensor, p: int, rows: int, pn: int, contract, group=None,
+                     chunks: int | None = None) -> torch.Tensor:
+  """The data movement of the "channels" mode, in channel sub-chunks.
+
+  a_op, b_op [m][C][kp] are this rank's contraction operands; rank q contracts channels
+  [q C/P, (q+1) C/P).  For sub-chunk s (sub = C/P / chunks channels) the operands go out
+  by one all-to-all each, ``contract(a_s, b_s, sub)`` (a_s, b_s [P][m_src][sub][kp]) returns
+  the sub-chunk's product [N][sub][pn] over all rows, and that goes back by row block.  The
+  all-to-alls are asynchronous (NCCL's stream): chunk s+1's operands move while chunk s
+  contracts, and chunk s's product returns while chunk s+1 contracts.  Returns this rank's
+  rows of the product for every channel, [rows][C][pn]."""
+  m, c, kp = a_op.shape
+  cl = c // p
+  chunks = _trimult_chunks(cl) if chunks is None else chunks
+  sub = cl // chunks
+  outs = [(channel_blocks_out_async(a_op, p, s, sub, group), channel_blocks_out_async(b_op, p, s, sub, group))
+          for s in range(chunks)]
+  prod = torch.empty(rows, c, pn, dtype=a_op.dtype, device=a_op.device)
+  backs = []
+  for s in range(chunks):
+    (wa, ra, _sa), (wb, rb, _sb) = outs[s]
+    wa.wait()
+    wb.wait()
+    prod_s = contract(ra, rb, sub).contiguous()                                   # [N][sub][pn]
+    recv = torch.empty_like(prod_s)
+    work = dist.all_to_all_single(recv, prod_s, group=group, async_op=True)
+    backs.append((work, recv, prod_s))
+  for s, (work, recv, _ps) in enumerate(backs):
+    work.wait()
+    _unpack_product(prod, recv.view(p, rows, sub, pn), p, s, sub)
+  return prod
 
 
 def _tri_mult_channels(mod, z_loc, mask_u8, shard: Shard, w, group=None) -> torch.Tensor:
@@ -220,29 +283,30 @@ def _tri_mult_channels(mod, z_loc, mask_u8, shard: Shard, w, group=None) -> torc
   if not shard.is_even or c % p:
     raise ValueError("channel-sharded triangle multiplication needs an even row split and C divisible by P")
   dt = N.SF_BF16
-  cl = c // p
   if not mod.incoming:
     pitch = ops.pitch(n)
     a_op = torch.empty(rows, c, pitch, dtype=z_loc.dtype, device=z_loc.device)
     b_op = torch.empty_like(a_op)
     N.call("sf_tri_mult_project_rows", dt, _p(z_loc), _p(mask_u8), rows, n, shard.offset(), 0, C.byref(w), _p(a_op),
            _p(b_op), _stream())
-    a_c = channel_blocks_out(a_op, p, group)               # [P][rows][cl][pitch] = all rows i of my channels
-    b_c = channel_blocks_out(b_op, p, group)
-    chunks = 1
+    kchunks = 1                    # each rank's a/b sub-chunk is [P][rows][sub][pitch] = all rows i, K whole
   else:
     if rows % 64 or ops.pitch(rows) != rows:
       raise ValueError(f"incoming triangle multiplication needs shard rows ({rows}) that are multiples of 64")
-    a_send = torch.empty(n, c, rows, dtype=z_loc.dtype, device=z_loc.device)   # b^T: [i][C][k_loc]
-    b_send = torch.empty_like(a_send)                                          # a^T: [j][C][k_loc]
+    a_op = torch.empty(n, c, rows, dtype=z_loc.dtype, device=z_loc.device)   # b^T: [i][C][k_loc]
+    b_op = torch.empty_like(a_op)                                             # a^T: [j][C][k_loc]
     N.call("sf_tri_mult_project_rows", dt, _p(z_loc), _p(mask_u8), rows, n, shard.offset(), 1, C.byref(w),
-           _p(a_send), _p(b_send), _stream())
-    a_c = channel_blocks_out(a_send, p, group)             # [P (k chunk)][N][cl][k_loc]
-    b_c = channel_blocks_out(b_send, p, group)
-    chunks = p
-  prod_c = torch.empty(n, cl, ops.pitch(n), dtype=z_loc.dtype, device=z_loc.device)
-  N.call("sf_tri_mult_contract_chunked", dt, _p(a_c), chunks, _p(b_c), chunks, _p(prod_c), cl, n, n, n, _stream())
-  prod = channel_blocks_back(prod_c, p, rows, c, group)
+           _p(a_op), _p(b_op), _stream())
+    kchunks = p                    # [P (k chunk)][N][sub][k_loc]: K arrives in per-rank chunks
+  pn = ops.pitch(n)
+
+  def contract(a_s, b_s, sub):
+    prod_s = torch.empty(n, sub, pn, dtype=z_loc.dtype, device=z_loc.device)
+    N.call("sf_tri_mult_contract_chunked", dt, _p(a_s), kchunks, _p(b_s), kchunks, _p(prod_s), sub, n, n, n,
+           _stream())
+    return prod_s
+
+  prod = channel_pipeline(a_op, b_op, p, rows, pn, contract, group)
   out = torch.empty_like(z_loc)
   N.call("sf_tri_mult_output", dt, _p(z_loc), _p(prod), rows, n, C.byref(w), _p(out), None, 0, _stream())
   return out

@@ -137,3 +137,40 @@ def _channel_choreography(rank, world):
 @pytest.mark.parametrize("world", [2, 4])
 def test_channel_sharded_triangle_multiplication_choreography(world):
   _run(_channel_choreography, world)
+
+
+def _channel_pipeline_choreography(rank, world):
+  """The pipelined "channels" mode (sharding.channel_pipeline): operands out and products back in
+  channel sub-chunks with asynchronous all-to-alls, for 1, 2 and 4 sub-chunks, outgoing (K whole on
+  every rank) and incoming (K in per-rank chunks); the contraction is emulated with einsum."""
+  from sparsefold_b200.sharding import channel_pipeline
+  g = torch.Generator().manual_seed(3)
+  n, c = 8, 4 * world
+  sh = Shard(n, world, rank)
+  rows, off = sh.size(), sh.offset()
+  a = torch.randn(n, c, n, generator=g)           # A[i][c][k]
+  b = torch.randn(n, c, n, generator=g)           # B[j][c][k]
+  ref = torch.einsum("ick,jck->icj", a, b)[off:off + rows]
+
+  def contract_out(a_s, b_s, sub):                # [P][rows][sub][k] -> [N][sub][N]
+    return torch.einsum("ick,jck->icj", a_s.reshape(n, sub, n), b_s.reshape(n, sub, n))
+
+  # incoming layout: each rank holds every i with its own K chunk, [i][C][k_loc]
+  at, bt = a[:, :, off:off + rows].contiguous(), b[:, :, off:off + rows].contiguous()
+
+  def contract_in(a_s, b_s, sub):                 # [P (k chunk)][N][sub][k_loc] -> [N][sub][N]
+    af = a_s.permute(1, 2, 0, 3).reshape(n, sub, n)
+    bf = b_s.permute(1, 2, 0, 3).reshape(n, sub, n)
+    return torch.einsum("ick,jck->icj", af, bf)
+
+  for chunks in (1, 2, 4):
+    got = channel_pipeline(a[off:off + rows].contiguous(), b[off:off + rows].contiguous(), world, rows, n,
+                           contract_out, chunks=chunks)
+    assert torch.allclose(got, ref, atol=1e-5), chunks
+    got = channel_pipeline(at, bt, world, rows, n, contract_in, chunks=chunks)
+    assert torch.allclose(got, ref, atol=1e-5), chunks
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_channel_pipeline_choreography(world):
+  _run(_channel_pipeline_choreography, world)
