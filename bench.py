@@ -63,7 +63,15 @@ class ClockSampler:
             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
   def __init__(self, index: int):
+    # nvidia-smi numbers GPUs physically; with CUDA_VISIBLE_DEVICES set, local device `index`
+    # is another one, so the GPU is named by its UUID when torch reports it
     self.index = index
+    try:
+      import torch
+      uuid = str(torch.cuda.get_device_properties(index).uuid)
+      self.index = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+    except Exception:
+      pass
     self.proc = None
 
   def __enter__(self):
@@ -362,6 +370,8 @@ def run_b200(args) -> None:
     print(json.dumps(line), flush=True)
   if world > 1:
     import torch.distributed as dist
+    from sparsefold_b200 import sharding
+    sharding.close_peer_exchanges()
     dist.destroy_process_group()
 
 

@@ -290,6 +290,27 @@ int sf_pair_outer_sum(int dtype, const void* left, const void* right, const void
  * (a zero feature skips its term), in increasing k, fp32 sums rounded once to dtype. */
 int sf_pair_sparse_linear(int dtype, const void* x, const float* w, const void* residual, void* out,
                           int64_t positions, int64_t k, int64_t channels, sf_stream_t stream);
+/* ---- Peer exchanges over NVLink (the all-to-all / all-gather of the row-sharded path,
+ * runtime/dist.py:477-565, between the ranks of one box, one process per GPU) ----
+ * sf_ipc_export: the CUDA IPC handle (CUDA_IPC_HANDLE_SIZE = 64 bytes) of the device
+ * allocation holding ptr, and ptr's offset in it.  sf_ipc_import: ptr = a peer's allocation
+ * mapped into this process (cudaIpcOpenMemHandle, peer access enabled; one mapping per
+ * handle and device, reused) + offset.  sf_ipc_close_all unmaps every imported allocation. */
+int sf_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+int sf_ipc_import(const void* handle, uint64_t offset, void** ptr);
+int sf_ipc_close_all(void);
+/* Block q of src (block_bytes each, src_stride_bytes apart, q = 0 .. n-1) is written to
+ * dsts_dev[q] + dst_offset_bytes with 16-byte stores from the SMs; dsts_dev is a device array
+ * of n pointers (local or peer-mapped).  Everything a multiple of 16 bytes. */
+int sf_scatter_peers(const void* src, void* const* dsts_dev, int32_t n, int64_t block_bytes,
+                     int64_t src_stride_bytes, int64_t dst_offset_bytes, sf_stream_t stream);
+/* After everything earlier on the stream: *flag = value (a peer's flag word, system-scope
+ * release).  sf_peer_wait: the stream waits until flags[q] >= value (wrapping compare) for every
+ * q != self, q < n <= 32, polling at most `polls` times (about 0.25 us apart); on timeout the
+ * kernel records SF_ERR_TIMEOUT in sf_device_status() and returns. */
+int sf_peer_signal(uint32_t* flag, uint32_t value, sf_stream_t stream);
+int sf_peer_wait(const uint32_t* flags, int32_t n, int32_t self, uint32_t value, uint32_t polls,
+                 sf_stream_t stream);
 
 #ifdef __cplusplus
 }

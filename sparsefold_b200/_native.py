@@ -89,6 +89,12 @@ _SIGNATURES = {
     "sf_copy_blocks": (C.c_int, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
     "sf_pair_outer_sum": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "sf_pair_sparse_linear": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "sf_ipc_export": (C.c_int, [_vp, _vp, C.POINTER(C.c_uint64)]),
+    "sf_ipc_import": (C.c_int, [_vp, C.c_uint64, C.POINTER(C.c_void_p)]),
+    "sf_ipc_close_all": (C.c_int, []),
+    "sf_scatter_peers": (C.c_int, [_vp, _vp, C.c_int32, _i64, _i64, _i64, _vp]),
+    "sf_peer_signal": (C.c_int, [_vp, C.c_uint32, _vp]),
+    "sf_peer_wait": (C.c_int, [_vp, C.c_int32, C.c_int32, C.c_uint32, C.c_uint32, _vp]),
     "sf_tri_mult_project_rows": (C.c_int, [C.c_int, _vp, _vp, _i64, _i64, _i64, C.c_int, C.POINTER(TriMultWeights),
                                            _vp, _vp, _vp]),
     "sf_tri_mult_contract_chunked": (C.c_int, [C.c_int, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp]),

@@ -107,10 +107,47 @@ def world_size(group=None) -> int:
   return dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
 
 
+# CUDA ranks exchange through sparsefold_b200.p2p (NVLink peer stores, CUDA IPC mappings made
+# once per buffer); SF_PEER_EXCHANGE=0 keeps NCCL's all-gather / all-to-all.  A result of the
+# peer path lives in the exchange's buffer pool and stays valid for at least two more exchanges
+# of its size, which every caller here consumes before.
+_PEER: dict = {}
+
+
+def peer_exchange(group=None):
+  """The PeerExchange of a process group (made on first use by every rank), or None when disabled."""
+  import os
+  if os.environ.get("SF_PEER_EXCHANGE", "1").strip() == "0":
+    return None
+  key = id(group) if group is not None else 0
+  if key not in _PEER:
+    from sparsefold_b200 import p2p
+    _PEER[key] = p2p.PeerExchange(group)
+  return _PEER[key]
+
+
+def close_peer_exchanges() -> None:
+  """Unmap every peer buffer (all ranks, before the process group goes away)."""
+  for ex in list(_PEER.values()):
+    ex.close()
+  _PEER.clear()
+
+
+def _peer_for(t: torch.Tensor, group, block_bytes: int):
+  """The peer exchange for t's blocks of block_bytes each (16-byte multiples), or None (NCCL / gloo)."""
+  return peer_exchange(group) if t.is_cuda and block_bytes % 16 == 0 else None
+
+
 def all_gather_rows(x: torch.Tensor, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
   """Concatenate every rank's x along dim 0 (equal shards)."""
   world = world_size(group)
   x = x.contiguous()
+  if world > 1 and (px := _peer_for(x, group, x.numel() * x.element_size())) is not None:
+    res = px.all_gather(x)
+    if out is None:
+      return res
+    out.copy_(res)
+    return out
   if out is None:
     out = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
   if world == 1:
@@ -123,6 +160,9 @@ def all_gather_rows(x: torch.Tensor, group=None, out: torch.Tensor | None = None
 def all_to_all_rows(send: torch.Tensor, group=None) -> torch.Tensor:
   """send [P * m, ...] -> recv [P * m, ...]: block p of send goes to rank p, block p of recv came from rank p."""
   send = send.contiguous()
+  world = world_size(group)
+  if world > 1 and (px := _peer_for(send, group, send.numel() * send.element_size() // world)) is not None:
+    return px.all_to_all(send)
   recv = torch.empty_like(send)
   dist.all_to_all_single(recv, send, group=group)
   return recv
@@ -207,15 +247,22 @@ def _trimult_chunks(cl: int) -> int:
   return want if want >= 1 and cl % want == 0 else 1
 
 
-def channel_blocks_out_async(op: torch.Tensor, p: int, s: int, sub: int, group=None):
-  """Start the all-to-all that takes channels [q C/P + s sub, q C/P + (s+1) sub) of every rank's op
-  [m][C][kp] to rank q.  Returns (work, recv [P][m_src][sub][kp], send); keep send alive until the work
-  is waited for."""
+def _channel_send(op: torch.Tensor, p: int, s: int, sub: int) -> torch.Tensor:
+  """[P][m][sub][kp]: block q = channels [q C/P + s sub, + sub) of op [m][C][kp]."""
   m, c, kp = op.shape
   cl = c // p
   op = op.contiguous()
   send = torch.empty(p, m, sub, kp, dtype=op.dtype, device=op.device)
   _pack_blocks(send, op.view(-1)[s * sub * kp:], p, m, sub * kp, cl * kp, c * kp, m * sub * kp, sub * kp)
+  return send
+
+
+def channel_blocks_out_async(op: torch.Tensor, p: int, s: int, sub: int, group=None):
+  """Start the all-to-all that takes channels [q C/P + s sub, q C/P + (s+1) sub) of every rank's op
+  [m][C][kp] to rank q.  Returns (work, recv [P][m_src][sub][kp], send); keep send alive until the work
+  is waited for."""
+  m, c, kp = op.shape
+  send = _channel_send(op, p, s, sub)
   recv = torch.empty_like(send)
   work = dist.all_to_all_single(recv.view(p * m, sub, kp), send.view(p * m, sub, kp), group=group, async_op=True)
   return work, recv, send
@@ -257,6 +304,15 @@ def channel_pipeline(a_op: torch.Tensor, b_op: torch.Tensor, p: int, rows: int, 
   rows of the product for every channel, [rows][C][pn]."""
   m, c, kp = a_op.shape
   cl = c // p
+  if a_op.is_cuda and peer_exchange(group) is not None:
+    # the peer exchanges are synchronous on the stream (and faster than NCCL's all-to-all):
+    # operands out, contraction, product back, one chunk
+    a_s = all_to_all_rows(_channel_send(a_op, p, 0, cl).view(p * m, cl, kp), group).view(p, m, cl, kp)
+    b_s = all_to_all_rows(_channel_send(b_op, p, 0, cl).view(p * m, cl, kp), group).view(p, m, cl, kp)
+    prod_s = contract(a_s, b_s, cl).contiguous()
+    prod = torch.empty(rows, c, pn, dtype=a_op.dtype, device=a_op.device)
+    _unpack_product(prod, all_to_all_rows(prod_s, group).view(p, rows, cl, pn), p, 0, cl)
+    return prod
   chunks = _trimult_chunks(cl) if chunks is None else chunks
   sub = cl // chunks
   outs = [(channel_blocks_out_async(a_op, p, s, sub, group), channel_blocks_out_async(b_op, p, s, sub, group))

@@ -70,6 +70,7 @@ def _rank(rank, world, port, q):
       es = max_rel_err(sg.float().cpu(), sr.float().cpu())
       q.put("ok" if ez < 1e-2 and es < 1e-2 else f"mismatch z {ez:.3e} s {es:.3e}")
     torch.distributed.barrier()
+    sharding.close_peer_exchanges()
   except Exception as e:
     q.put(repr(e))
     raise

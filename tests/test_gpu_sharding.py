@@ -1,8 +1,9 @@
 """Row-sharded Pairformer block on GPUs vs the single-device block (bf16).
 
-The sharded path runs the same kernels on each rank's rows with NCCL exchanges
-(all-gathers of b / a / bias / k,v, all-to-alls for the incoming operand and the
-ending-node transpose); its gathered output must match the single-device block.
+The sharded path runs the same kernels on each rank's rows with the exchanges of the
+reference (all-gathers of b / a / bias / k,v, all-to-alls for the incoming operand and the
+ending-node transpose), through NVLink peer stores (sparsefold_b200.p2p) or NCCL; its
+gathered output must match the single-device block.
 """
 import os
 import socket
@@ -54,10 +55,11 @@ def _free_port():
     return sk.getsockname()[1]
 
 
-def _rank(rank, world, port, q, mode="rows"):
+def _rank(rank, world, port, q, mode="rows", peer="1"):
   import datetime
   import torch.distributed as dist
-  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", SF_TRIMULT_SHARDING=mode)
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0", SF_TRIMULT_SHARDING=mode,
+                    SF_PEER_EXCHANGE=peer)
   torch.cuda.set_device(rank)
   dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                           device_id=torch.device("cuda", rank))
@@ -74,8 +76,10 @@ def _rank(rank, world, port, q, mode="rows"):
       torch.cuda.synchronize()
       ez = max_rel_err(zg.float().cpu(), zr.float().cpu())
       es = max_rel_err(sg.float().cpu(), sr.float().cpu())
-      q.put(("ok" if ez < 1e-2 and es < 1e-2 else f"mismatch z {ez:.3e} s {es:.3e}"))
+      st = _native.device_status()
+      q.put(("ok" if ez < 1e-2 and es < 1e-2 and st == 0 else f"mismatch z {ez:.3e} s {es:.3e} status {st}"))
     dist.barrier()
+    sharding.close_peer_exchanges()
   except Exception as e:
     q.put(repr(e))
     raise
@@ -84,14 +88,16 @@ def _rank(rank, world, port, q, mode="rows"):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("peer", ["1", "0"], ids=["nvlink-peer-stores", "nccl"])
 @pytest.mark.parametrize("mode", ["rows", "channels"])
-def test_two_gpu_sharded_block_matches_block(mode):
+def test_two_gpu_sharded_block_matches_block(mode, peer):
   """Both ways of moving the triangle-multiplication operands: all-gathers of whole operands ("rows", the
-  reference's choreography) and channel blocks out / product rows back ("channels")."""
+  reference's choreography) and channel blocks out / product rows back ("channels"); each over the
+  NVLink peer exchange and over NCCL."""
   ctx = mp.get_context("spawn")
   q = ctx.Queue()
   port = _free_port()
-  procs = [ctx.Process(target=_rank, args=(r, 2, port, q, mode)) for r in range(2)]
+  procs = [ctx.Process(target=_rank, args=(r, 2, port, q, mode, peer)) for r in range(2)]
   for p in procs:
     p.start()
   for p in procs:
