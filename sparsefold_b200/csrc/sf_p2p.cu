@@ -21,12 +21,31 @@
 namespace sf {
 namespace {
 
+// Each thread moves SP_UNROLL chunks per step (their loads issued before any store), so
+// enough stores are in flight to keep the NVLink of every peer busy.
+constexpr int SP_UNROLL = 4;
 __global__ void k_scatter_peers(const uint4* __restrict__ src, uint4* const* __restrict__ dsts, int n, int64_t chunks,
                                 int64_t src_stride, int64_t dst_offset) {
   const int64_t total = (int64_t)n * chunks;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t q = e / chunks, c = e - q * chunks;
-    dsts[q][dst_offset + c] = __ldg(src + q * src_stride + c);
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e0 < total; e0 += step * SP_UNROLL) {
+    uint4 v[SP_UNROLL];
+#pragma unroll
+    for (int u = 0; u < SP_UNROLL; ++u) {
+      const int64_t e = e0 + u * step;
+      if (e < total) {
+        const int64_t q = e / chunks, c = e - q * chunks;
+        v[u] = __ldg(src + q * src_stride + c);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < SP_UNROLL; ++u) {
+      const int64_t e = e0 + u * step;
+      if (e < total) {
+        const int64_t q = e / chunks, c = e - q * chunks;
+        dsts[q][dst_offset + c] = v[u];
+      }
+    }
   }
 }
 
