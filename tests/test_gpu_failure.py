@@ -67,3 +67,23 @@ def test_selftest_rejects_unbounded_polls():
   assert lib.sf_selftest_wait(0, 0, None) == N.SF_ERR_ARG
   assert lib.sf_selftest_wait(0xFFFFFFFF, 0, None) == N.SF_ERR_ARG
   assert "polls" in N.last_error()
+
+
+def test_peer_wait_on_a_flag_nothing_raises_times_out():
+  """The flag wait of the NVLink peer exchange (sf_peer_wait), on one GPU: a 'peer' flag nobody raises
+  (a local array of zeros) makes the bounded wait run out; the kernel returns and reports SF_ERR_TIMEOUT.
+  A flag that is already raised passes at once and leaves the status clear."""
+  lib = N.load()
+  flags = torch.zeros(4, dtype=torch.int32, device="cuda")
+  assert N.device_status(clear=True) == 0
+  t0 = time.monotonic()
+  N.call("sf_peer_wait", flags.data_ptr(), 4, 0, 1, 1 << 12, _stream())
+  torch.cuda.synchronize()
+  assert time.monotonic() - t0 < 5.0
+  assert N.device_status(clear=True) == N.SF_ERR_TIMEOUT
+  flags.fill_(7)
+  N.call("sf_peer_wait", flags.data_ptr(), 4, 0, 7, 1 << 12, _stream())
+  torch.cuda.synchronize()
+  assert N.device_status() == 0
+  assert lib.sf_peer_wait(flags.data_ptr(), 0, 0, 1, 1, None) == N.SF_ERR_ARG       # no ranks
+  assert lib.sf_peer_wait(flags.data_ptr(), 4, 0, 1, 0, None) == N.SF_ERR_ARG       # unbounded
