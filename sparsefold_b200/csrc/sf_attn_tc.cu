@@ -71,6 +71,8 @@ template <int KSW, int G>
 __global__ void __launch_bounds__(MH_THREADS, 1) k_mha_tc(const __grid_constant__ CUtensorMap tmK,
                                                           const __grid_constant__ CUtensorMap tmV,
                                                           const __grid_constant__ CUtensorMap tmB, MhaParams P) {
+  tc::griddep_wait();     // the previous kernel's outputs are complete and visible from here on
+  tc::griddep_launch();
   constexpr int DK = KSW / 2;                     // padded head dim of K (32 or 64)
   constexpr int KBG = MH_KB / G;                  // keys of one entry in a 64-key block
   constexpr int QG = TILE / G;                    // query rows of one entry
@@ -446,7 +448,7 @@ int attention_tc(const sf_attention_args* a, cudaStream_t stream) {
   MhaParams p{*a, batched, status};
   dim3 grid(G == 1 ? (unsigned)((a->q_len + TILE - 1) / TILE) : 1u, (unsigned)a->heads,
             (unsigned)((a->batch + G - 1) / G));
-  kern<<<grid, MH_THREADS, MH_SMEM, stream>>>(mk, mv, mb, p);
+  launch_pdl(kern, grid, dim3(MH_THREADS), MH_SMEM, stream, mk, mv, mb, p);
   count_launch();
   return check_launch("attention_tc");
 }

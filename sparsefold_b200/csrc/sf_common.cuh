@@ -52,6 +52,26 @@ int check_launch(const char* what);  // cudaGetLastError -> status
 // a kernel whose bounded wait gave up stores SF_ERR_TIMEOUT).  nullptr on error.
 uint32_t* device_status_ptr();
 
+// Launch with programmatic stream serialisation, so that the kernel's set-up overlaps the tail of
+// the kernel before it (the kernel itself waits with tc::griddep_wait() before touching any
+// activation); SF_PDL=0 in the environment launches plainly.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // tcgen05 kernels (bf16 track), host launchers defined in sf_*_tc.cu.
 int num_sms();
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,

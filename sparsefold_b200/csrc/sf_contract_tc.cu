@@ -82,6 +82,8 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
+  tc::griddep_wait();     // the previous kernel's outputs are complete and visible from here on
+  tc::griddep_launch();
   const uint32_t tbase = *tmem_slot;
   bool aborted = false;
   uint32_t loads = 0;   // TMA loads issued by the producer (abort-path drain)
@@ -272,7 +274,7 @@ static int launch_gemm_tc(const CUtensorMap& ma, const bf16* b_op, int64_t chunk
     attr_set[dev & 63] = true;
   }
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  k_contract_tc<BN><<<grid, 192, Tile<BN>::SMEM, stream>>>(ma, mb, p);
+  launch_pdl(k_contract_tc<BN>, dim3(grid), dim3(192), Tile<BN>::SMEM, stream, ma, mb, p);
   count_launch();
   return check_launch("contract_tc");
 }

@@ -31,6 +31,8 @@ struct PlParams {
 
 __global__ void __launch_bounds__(128) k_pair_logits_tc(const __grid_constant__ CUtensorMap tmZ, PlParams p) {
   extern __shared__ uint8_t smem_raw[];
+  tc::griddep_wait();     // the previous kernel's outputs are complete and visible from here on
+  tc::griddep_launch();
   uint8_t* smem = align1024(smem_raw);
   uint64_t* ldbar = reinterpret_cast<uint64_t*>(smem + OFF_PLBAR);
   uint64_t* mmabar = ldbar + 1;
@@ -144,7 +146,7 @@ static int pair_logits_launch(const bf16* z, const float* ln_w, const float* ln_
     attr[dev & 63] = true;
   }
   PlParams pp{ln_w, ln_b, w, logits, M, heads, status, ncols, ldb, scale};
-  k_pair_logits_tc<<<(unsigned)((M + TILE - 1) / TILE), 128, SMEM_PL, stream>>>(mz, pp);
+  launch_pdl(k_pair_logits_tc, dim3((unsigned)((M + TILE - 1) / TILE)), dim3(128), SMEM_PL, stream, mz, pp);
   count_launch();
   return check_launch("pair_logits_tc");
 }

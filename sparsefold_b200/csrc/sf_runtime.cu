@@ -1,5 +1,6 @@
 // Runtime plumbing of the C ABI: per-thread error messages, launch accounting,
 // device check, version.
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -23,6 +24,14 @@ void set_error(const char* fmt, ...) {
 }
 
 void count_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("SF_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();

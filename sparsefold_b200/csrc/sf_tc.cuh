@@ -95,6 +95,15 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   return false;
 }
 
+// ---- programmatic dependent launch ------------------------------------------------
+// A kernel launched with launch_pdl may start while the kernel before it on the stream is
+// still running: it sets up (TMEM, barriers, weights in shared memory) and then waits here
+// until the previous grid has completed and its memory is visible, before it reads any
+// activation or writes any global memory.  (Without the launch attribute this is a no-op.)
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel on the stream launch once every CTA of this grid has passed here.
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- fences --------------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }

@@ -118,6 +118,8 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
+  tc::griddep_wait();     // the previous kernel's outputs are complete and visible from here on
+  tc::griddep_launch();
   const uint32_t tbase = *tmem_slot;
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
@@ -378,7 +380,7 @@ int transition_tc(const bf16* x, const float* ln_w, const float* ln_b, const bf1
   TrParams p{x, y, ln_w, ln_b, M, status};
   const int64_t npairs = (M + 2 * TILE - 1) / (2 * TILE);
   const int grid = (int)(npairs < num_sms() ? npairs : num_sms());
-  k_transition_tc<<<grid, TR_THREADS, SMEM_TR, stream>>>(mx, mw1, mw2, my, p);
+  launch_pdl(k_transition_tc, dim3(grid), dim3(TR_THREADS), SMEM_TR, stream, mx, mw1, mw2, my, p);
   count_launch();
   return check_launch("transition_tc");
 }

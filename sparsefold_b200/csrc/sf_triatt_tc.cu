@@ -170,6 +170,8 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
+  tc::griddep_wait();     // the previous kernel's outputs are complete and visible from here on
+  tc::griddep_launch();
   const uint32_t tbase = *tmem_slot;
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
@@ -452,6 +454,8 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
                                                            const __grid_constant__ CUtensorMap tmR,
                                                            const __grid_constant__ CUtensorMap tmO, AttCoreParams p) {
   extern __shared__ uint8_t smem_raw[];
+  tc::griddep_wait();     // the previous kernel's outputs are complete and visible from here on
+  tc::griddep_launch();
   uint8_t* smem = align1024(smem_raw);
   // Block-indexed barriers come in pairs (block j uses [j & 1], phase j >> 1): a parity
   // wait only tells phases apart within one phase of the barrier, and the softmax warps,
@@ -903,7 +907,7 @@ int triatt_project_tc(const bf16* z, int64_t rows, int64_t cols, int transpose, 
   AttProjParams pp{ln_w, w_bias, bias, nb, nq, qp, transpose, compute_bias, status};
   const int64_t ntiles = nb * (qp / TILE);
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  k_triatt_project_tc<<<grid, PJ_THREADS, SMEM_PROJ, stream>>>(mz, mq, mk, mv, mg, w_qkvg, pp);
+  launch_pdl(k_triatt_project_tc, dim3(grid), dim3(PJ_THREADS), SMEM_PROJ, stream, mz, mq, mk, mv, mg, w_qkvg, pp);
   count_launch();
   return check_launch("triatt_project_tc");
 }
@@ -980,7 +984,7 @@ int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, 
   AttCoreParams cp{q, g, bias, w_out, mask, z, z_out, cols, nq, qp, batch_offset, transpose,
                    (1.0f / sqrtf((float)D)) * kLog2e, status};
   dim3 cgrid((unsigned)(qp / TILE), (unsigned)nb);
-  k_triatt_core_tc<<<cgrid, CORE_THREADS, SMEM_CORE, stream>>>(mk, mv, mb, mw, mr, mo, cp);
+  launch_pdl(k_triatt_core_tc, cgrid, dim3(CORE_THREADS), SMEM_CORE, stream, mk, mv, mb, mw, mr, mo, cp);
   count_launch();
   return check_launch("triatt_core_tc");
 }

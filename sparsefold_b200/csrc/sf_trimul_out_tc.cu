@@ -98,6 +98,8 @@ __global__ void __launch_bounds__(OUT_THREADS, 1) k_trimul_output_tc(const __gri
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
+  tc::griddep_wait();     // the previous kernel's outputs are complete and visible from here on
+  tc::griddep_launch();
   const uint32_t tbase = *tmem_slot;
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
@@ -379,7 +381,7 @@ int trimul_output_tc(const bf16* z, const bf16* P, int64_t rows, int64_t n, cons
   OutParams p{ln_w, ln_b, center_w, center_b, rows, n, status};
   const int64_t ntiles = rows * ((n + TILE - 1) / TILE);
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  k_trimul_output_tc<<<grid, OUT_THREADS, SMEM_OUT, stream>>>(mz, mp, mo, w_gate, w_out, p);
+  launch_pdl(k_trimul_output_tc, dim3(grid), dim3(OUT_THREADS), SMEM_OUT, stream, mz, mp, mo, w_gate, w_out, p);
   count_launch();
   return check_launch("trimul_output_tc");
 }

@@ -91,6 +91,8 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
+  tc::griddep_wait();     // the previous kernel's outputs are complete and visible from here on
+  tc::griddep_launch();
   const uint32_t tbase = *tmem_slot;
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
@@ -348,7 +350,7 @@ int trimul_project_tc(const bf16* z, const uint8_t* mask, int64_t rows, int64_t 
   const int64_t span = incoming ? rows : n;
   const int64_t ntiles = majors * ((span + pt::TILE - 1) / pt::TILE);
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  k_trimul_project_tc<<<grid, PROJ_THREADS, SMEM_PROJ, stream>>>(mz, ma, mb, w_glu, p);
+  launch_pdl(k_trimul_project_tc, dim3(grid), dim3(PROJ_THREADS), SMEM_PROJ, stream, mz, ma, mb, w_glu, p);
   count_launch();
   return check_launch("trimul_project_tc");
 }
