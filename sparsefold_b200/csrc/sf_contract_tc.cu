@@ -5,17 +5,22 @@
 // collective an operand may arrive as [rank][row][channel][k-chunk], which the
 // 4-D tensor maps read in place.
 //
-// Persistent, warp-specialised: warp 4 streams 128x64 A and 256x64 B tiles by
-// TMA through a 4-stage shared-memory ring; one thread of warp 5 issues
+// Persistent, warp-specialised: warp 8 streams 128x64 A and 256x64 B tiles by
+// TMA through a 4-stage shared-memory ring; one thread of warp 9 issues
 // tcgen05.mma (M=128, N=256, K=16) into one of two TMEM accumulators
-// (2 x 256 fp32 columns); warps 0-3 drain the other accumulator (tcgen05.ld,
-// one row per thread) and store bf16 rows of P while the next tile computes.
+// (2 x 256 fp32 columns); warps 0-7 drain the other accumulator (tcgen05.ld of
+// 32 columns at a time, one row per thread, each warp half of the columns) and
+// store bf16 rows of P while the next tile computes.
 #include "sf_pair_tc.cuh"
 
 namespace sf {
 namespace {
 
 constexpr int BM = 128, BK = 64, STAGES = 4;
+// warps 0-7 epilogue (warp w: TMEM lanes 32 (w % 4).., columns (w / 4) BN/2 ..), warp 8 TMA
+// producer, warp 9 MMA issuer
+constexpr int CT_EPI_WARPS = 8;
+constexpr int CT_THREADS = (CT_EPI_WARPS + 2) * 32;
 constexpr int SA_BYTES = BM * BK * 2;              // 16 KB
 template <int BN>
 struct Tile {
@@ -43,7 +48,7 @@ __device__ __forceinline__ float post(float v, int op) {
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ CUtensorMap tmA,
+__global__ void __launch_bounds__(CT_THREADS, 1) k_contract_tc(const __grid_constant__ CUtensorMap tmA,
                                                         const __grid_constant__ CUtensorMap tmB,
                                                         ContractParams p) {
   constexpr int STAGE_BYTES = Tile<BN>::STAGE_BYTES;
@@ -72,7 +77,7 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(&accf[a], 1);
-      tc::mbar_init(&acce[a], 128);
+      tc::mbar_init(&acce[a], CT_EPI_WARPS * 32);
     }
     tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
@@ -88,7 +93,7 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
   bool aborted = false;
   uint32_t loads = 0;   // TMA loads issued by the producer (abort-path drain)
 
-  if (warp == 4 && lane == 0) {
+  if (warp == CT_EPI_WARPS && lane == 0) {
     // ---- TMA producer (stops at its first failed wait) ----
     uint32_t& q = loads;
     for (int64_t t = blockIdx.x; t < ntiles && !aborted; t += gridDim.x) {
@@ -105,7 +110,7 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
         tc::tma_load_4d(st + SA_BYTES, &tmB, &full[s], (int)(k % p.kl_b), (int)c, j0, (int)(k / p.kl_b));
       }
     }
-  } else if (warp == 5 && lane == 0) {
+  } else if (warp == CT_EPI_WARPS + 1 && lane == 0) {
     // ---- MMA issuer (stops at its first failed wait) ----
     constexpr uint32_t IDESC = tc::idesc_bf16(BM, BN);
     const uint32_t sbase = tc::smem_u32(smem);
@@ -130,26 +135,29 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
       if (aborted) break;
       tc::mma_commit(&accf[acc]);
     }
-  } else if (warp < 4) {
-    // ---- epilogue ----
+  } else if (warp < CT_EPI_WARPS) {
+    // ---- epilogue: 32 columns per TMEM load, one wait each ----
+    constexpr int HALF = BN / 2, CW = HALF < 32 ? HALF : 32;
     const int64_t cp = pair_pitch(p.cols);
-    const uint32_t lane_addr = tbase + ((uint32_t)(warp * 32) << 16);
+    const int quad = warp & 3, half = warp >> 2;
+    const uint32_t lane_addr = tbase + ((uint32_t)(quad * 32) << 16);
     uint32_t u = 0;
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++u) {
       const uint32_t acc = u & 1;
       const int64_t c = t / (mt * nt), rem = t % (mt * nt);
-      const int64_t i = (rem / nt) * BM + tid, j0 = (rem % nt) * BN;
+      const int64_t i = (rem / nt) * BM + quad * 32 + lane, j0 = (rem % nt) * BN + half * HALF;
       tc::mbar_wait(&accf[acc], (u >> 1) & 1, p.status, aborted);
       tc::tc_fence_after();
       bf16* prow = p.P + (i * p.channels + c) * cp;
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 16; ++ch) {
-        float v[16];
-        tc::tmem_ld16(lane_addr + acc * BN + ch * 16, v);
+      for (int ch = 0; ch < HALF / CW; ++ch) {
+        float v[CW];
+        if constexpr (CW == 32) tc::tmem_ld32(lane_addr + acc * BN + half * HALF + ch * CW, v);
+        else tc::tmem_ld16(lane_addr + acc * BN + half * HALF + ch * CW, v);
         if (i < p.rows) {
 #pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            const int64_t j = j0 + ch * 16 + g * 8;
+          for (int g = 0; g < CW / 8; ++g) {
+            const int64_t j = j0 + ch * CW + g * 8;
             if (j + 8 <= cp) {
               if (p.bias || p.residual || p.post_op) {
                 float bv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -191,8 +199,8 @@ __global__ void __launch_bounds__(192, 1) k_contract_tc(const __grid_constant__ 
   }
   tc::tc_fence_before();
   if (__syncthreads_or(aborted)) {   // abort path: drain the producer's loads and the issuer's MMAs
-    if (warp == 4 && lane == 0) tc::drain_ring(full, STAGES, loads, p.status);
-    if (warp == 5 && lane == 0) tc::drain_mma(drain, p.status);
+    if (warp == CT_EPI_WARPS && lane == 0) tc::drain_ring(full, STAGES, loads, p.status);
+    if (warp == CT_EPI_WARPS + 1 && lane == 0) tc::drain_mma(drain, p.status);
     __syncthreads();
   }
   if (warp == 0) {
@@ -274,7 +282,7 @@ static int launch_gemm_tc(const CUtensorMap& ma, const bf16* b_op, int64_t chunk
     attr_set[dev & 63] = true;
   }
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  launch_pdl(k_contract_tc<BN>, dim3(grid), dim3(192), Tile<BN>::SMEM, stream, ma, mb, p);
+  launch_pdl(k_contract_tc<BN>, dim3(grid), dim3(CT_THREADS), Tile<BN>::SMEM, stream, ma, mb, p);
   count_launch();
   return check_launch("contract_tc");
 }
