@@ -182,8 +182,9 @@ int sf_tri_mult_project_rows(int dtype, const void* z, const uint8_t* mask, int6
 int sf_tri_mult_contract_chunked(int dtype, const void* a_op, int64_t chunks_a, const void* b_op,
                                  int64_t chunks_b, void* p, int64_t channels, int64_t rows, int64_t cols,
                                  int64_t kdim, sf_stream_t stream);
-/* Query pitch qp of the attention buffers: Q (stored times log2(e)/sqrt(32)), K, Vt [nb][4][qp][32],
- * G [nb][qp][128], bias [qp][4][qp] (bias[q][h][k], rows gathered across ranks). */
+/* Query pitch qp of the attention buffers: K [nb][4][qp][32], Vt [nb][4][32][qp], Q (stored times
+ * log2(e)/sqrt(32)) and G = sigmoid(gate) [nb][4][qp/32][4][32][8] (per group of 32 queries, four
+ * [32 queries][8 channels] chunks), bias [qp][4][qp] (bias[q][h][k], rows gathered across ranks). */
 int64_t sf_tri_attention_query_pitch(int64_t nq);
 /* Pair bias of the local rows: bias[(r*4 + h)*ldb + s] = log2(e) * LN(z[r,s]) . W_b[h] in bf16
  * (blocks.py:317-320; stored in base-2 logit units, the form the attention core adds its scaled

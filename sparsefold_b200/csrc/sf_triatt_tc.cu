@@ -22,7 +22,10 @@
 //                       output projection, whose epilogue adds the residual.
 //
 // Intermediate layouts (qp = n rounded up to 128; padded query rows are zero):
-//   Q, K  [b][h][qp][32] (Q times log2(e)/sqrt(32))    Vt [b][h][32][qp]    G = sigmoid(gate) [b][qp][128]
+//   K [b][h][qp][32]    Vt [b][h][32][qp]
+//   Q (times log2(e)/sqrt(32)) and G = sigmoid(gate) [b][h][qp / 32][4][32][8]: per group of 32
+//         queries, four chunks of 8 channels, each [32 queries][8 channels] (2 KB per group), so
+//         that a warp holding one query per lane reads each chunk as 512 contiguous bytes
 //   bias  [q][h][qp] (bias[q][h][k] = log2(e) LN(z)[q,k] . W_b[h] in bf16, untransposed;
 //         rows q all-gathered from the row shards when the pair tensor is distributed)
 #include <cfloat>
@@ -42,6 +45,8 @@ constexpr float kBiasScale = kLog2e;
 constexpr float kQScale = 0.25503486f;   // log2(e) / sqrt(32)
 
 struct AttProjParams {
+  bf16* q;                // Q and G in 32-query groups (see the layouts above)
+  bf16* g;
   const float* ln_w;      // act_norm scale [128]
   const bf16* w_bias;     // [4][128]
   bf16* bias;             // [.][H][qp]
@@ -125,10 +130,8 @@ __device__ __forceinline__ void ln_row_bias(uint8_t* tile, int r, const float* w
 }
 
 __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __grid_constant__ CUtensorMap tmZ,
-                                                                     const __grid_constant__ CUtensorMap tmQ,
                                                                      const __grid_constant__ CUtensorMap tmK,
                                                                      const __grid_constant__ CUtensorMap tmV,
-                                                                     const __grid_constant__ CUtensorMap tmG,
                                                                      const bf16* __restrict__ w_qkvg, AttProjParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -157,10 +160,8 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
     tc::mbar_init(drain, 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmZ);
-    tc::prefetch_tmap(&tmQ);
     tc::prefetch_tmap(&tmK);
     tc::prefetch_tmap(&tmV);
-    tc::prefetch_tmap(&tmG);
   }
   for (int e = tid; e < H * C / 8; e += PJ_THREADS)
     reinterpret_cast<uint4*>(smem + OFF_JWB)[e] = __ldg(reinterpret_cast<const uint4*>(p.w_bias) + e);
@@ -255,8 +256,10 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
     uint8_t* stg = smem + OFF_JST + warp * PJ_ST_BYTES;
     int sh = 0;              // staging half for the next [32 queries][32 channels] store
     bool full_used = false;  // the last store read the whole staging tile (v^T)
-    // one [32 queries][32 channels] tile (this lane = query row, 64B swizzle) into the next half, then stored
-    auto store_rows = [&](const float* v, const CUtensorMap* map, int c0, int c1) {
+    // one [32 queries][32 channels] tile (this lane = query row) into the next half, then stored:
+    // K by TMA as rows (64B swizzle), Q and G as one 2 KB group of four [32 queries][8 channels]
+    // chunks by a plain bulk copy (map == nullptr, dst the group)
+    auto store_rows = [&](const float* v, const CUtensorMap* map, int c0, int c1, bf16* dst) {
       if (lane == 0) {
         if (full_used) tc::bulk_wait_read0();
         else tc::bulk_wait_read1();   // the store that used this half (two stores ago) has read it
@@ -265,13 +268,14 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
       uint8_t* half = stg + sh * 2048;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<uint4*>(half + tc::sw64_off(lane, c)) =
+        *reinterpret_cast<uint4*>(half + (map ? tc::sw64_off(lane, c) : (uint32_t)(c * 512 + lane * 16))) =
             make_uint4(pack_bf2(v[8 * c], v[8 * c + 1]), pack_bf2(v[8 * c + 2], v[8 * c + 3]),
                        pack_bf2(v[8 * c + 4], v[8 * c + 5]), pack_bf2(v[8 * c + 6], v[8 * c + 7]));
       tc::fence_proxy_async();
       __syncwarp();
       if (lane == 0) {
-        tc::tma_store_2d(map, half, c0, c1);
+        if (map) tc::tma_store_2d(map, half, c0, c1);
+        else tc::bulk_store(dst, half, 2048);
         tc::bulk_commit();
       }
       sh ^= 1;
@@ -298,7 +302,8 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] *= kQScale;   // q stored pre-scaled for the base-2 softmax
         }
-        store_rows(v, t == 0 ? &tmQ : &tmK, 0, (int)(((int64_t)b * H + hd) * p.qp + qrow));
+        const int64_t grow0 = ((int64_t)b * H + hd) * p.qp + qrow;   // first row of the 32-query group
+        store_rows(v, t == 0 ? nullptr : &tmK, 0, (int)grow0, p.q + grow0 * D);
       }
       // ---- half 1: gate (heads 2 hf, 2 hf + 1) and v^T (head quad, queries 64 hf ..) ----
       tc::mbar_wait(&tfull[1], it & 1, p.status, aborted);
@@ -310,7 +315,7 @@ __global__ void __launch_bounds__(PJ_THREADS, 1) k_triatt_project_tc(const __gri
         tc::tmem_ld32(lane_addr + 256 + hd * D, v);
 #pragma unroll
         for (int e = 0; e < 32; ++e) v[e] = sigmoid_tanh(v[e]);
-        store_rows(v, &tmG, hd * D, (int)((int64_t)b * p.qp + qrow));
+        store_rows(v, nullptr, 0, 0, p.g + (((int64_t)b * H + hd) * p.qp + qrow) * D);
       }
       {
         float v[64];
@@ -477,7 +482,6 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   const int64_t q0 = (int64_t)blockIdx.x * TILE, b = blockIdx.y;
   const int nkb = (int)(p.qp / KB);   // >= 4
   const int64_t bh = b * H + g;
-  const int64_t q = q0 + t;
   uint8_t* ring = smem + OFF_RING + g * HEAD_BYTES;
   auto k_of = [&](int jj) { return ring + (jj % RING) * K_BYTES; };
   auto bt_of = [&](int jj) { return ring + RING * K_BYTES + (jj % RING) * BT_BYTES; };
@@ -489,9 +493,9 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
   // this thread's query row of Q (64 B), for TMEM: requested first, it is the longest wait
   uint4 qrow[4];
   if (!issuer) {
-    const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (bh * p.qp + q) * D);
+    const uint4* qsrc = reinterpret_cast<const uint4*>(p.q + (bh * p.qp + q0 + (t & ~31)) * D) + (t & 31);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) qrow[c] = __ldg(qsrc + c);
+    for (int c = 0; c < 4; ++c) qrow[c] = __ldg(qsrc + 32 * c);
   }
   auto issue_load = [&](int jj) {   // K, V^T and bias[q0..q0+127][g][32 jj .. 32 jj + 31] of block jj (jj == loads)
     ++loads;
@@ -640,7 +644,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
       }
     }
   } else {
-    const uint4* grow = reinterpret_cast<const uint4*>(p.g + (b * p.qp + q) * C + g * D);
+    const uint4* grow = reinterpret_cast<const uint4*>(p.g + (bh * p.qp + q0 + (t & ~31)) * D) + (t & 31);
     for (int j = 0; j < nkb; ++j) {
       // S_j is written and block j (its bias tile) has landed
       tc::mbar_wait(&sbar[g * 2 + (j & 1)], (j >> 1) & 1, p.status, aborted);
@@ -778,7 +782,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core_tc(const __grid
     // ---- normalise, gate, stage O_h (K-major 128 x 32, 64B swizzle) in the last bias slot ----
     uint4 graw[D / 8];
 #pragma unroll
-    for (int c = 0; c < D / 8; ++c) graw[c] = __ldg(grow + c);
+    for (int c = 0; c < D / 8; ++c) graw[c] = __ldg(grow + 32 * c);
     // the last two P V (S_{nkb-1} complete only means P V up to block nkb-3 is)
     tc::mbar_wait(&pvbar[g * 2 + ((nkb - 2) & 1)], ((nkb - 2) >> 1) & 1, p.status, aborted);
     tc::mbar_wait(&pvbar[g * 2 + ((nkb - 1) & 1)], ((nkb - 1) >> 1) & 1, p.status, aborted);
@@ -896,18 +900,18 @@ int triatt_project_tc(const bf16* z, int64_t rows, int64_t cols, int transpose, 
              (long long)nb, (long long)qp);
   static bool attr[64] = {false};
   SF_TRY(set_smem(k_triatt_project_tc, SMEM_PROJ, attr));
-  CUtensorMap mz, mq, mk, mv, mg;
+  CUtensorMap mz, mk, mv;
   SF_TRY(make_pair_tmap(&mz, z, rows, cols, transpose != 0));
-  // epilogue stores: Q, K [nb*H*qp][32] and G [nb*qp][128] as 32 queries x 32 channels (64B swizzle),
-  // V^T [nb*H*32][qp] as 32 channels x 64 queries (128B swizzle)
-  SF_TRY(make_2d_tmap(&mq, q, D, nb * H * qp, D, 32, 64));
+  // epilogue stores: K [nb*H*qp][32] as 32 queries x 32 channels (64B swizzle), V^T [nb*H*32][qp] as
+  // 32 channels x 64 queries (128B swizzle); Q and G as 2 KB groups by plain bulk copies
+  SF_REQUIRE(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(g)) & 15) == 0,
+             "triatt_project: q and g must be 16-byte aligned");
   SF_TRY(make_2d_tmap(&mk, k, D, nb * H * qp, D, 32, 64));
   SF_TRY(make_2d_tmap(&mv, vt, qp, nb * H * D, 64, D, 128));
-  SF_TRY(make_2d_tmap(&mg, g, C, nb * qp, D, 32, 64));
-  AttProjParams pp{ln_w, w_bias, bias, nb, nq, qp, transpose, compute_bias, status};
+  AttProjParams pp{q, g, ln_w, w_bias, bias, nb, nq, qp, transpose, compute_bias, status};
   const int64_t ntiles = nb * (qp / TILE);
   const int grid = (int)(ntiles < num_sms() ? ntiles : num_sms());
-  launch_pdl(k_triatt_project_tc, dim3(grid), dim3(PJ_THREADS), SMEM_PROJ, stream, mz, mq, mk, mv, mg, w_qkvg, pp);
+  launch_pdl(k_triatt_project_tc, dim3(grid), dim3(PJ_THREADS), SMEM_PROJ, stream, mz, mk, mv, w_qkvg, pp);
   count_launch();
   return check_launch("triatt_project_tc");
 }
@@ -989,7 +993,8 @@ int triatt_core_tc(const bf16* q, const bf16* k, const bf16* vt, const bf16* g, 
   return check_launch("triatt_core_tc");
 }
 
-// Buffer sizes of one attention call: Q, K, Vt [nb][H][qp][32], G [nb][qp][128], bias [qp][H][qp].
+// Buffer sizes of one attention call: Q, K, Vt, G [nb][H][qp][32] (Q and G in 32-query groups),
+// bias [qp][H][qp].
 size_t triatt_tc_workspace(int64_t n) {
   const int64_t qp = triatt_query_pitch(n);
   const size_t per = (size_t)n * H * qp * D * 2;

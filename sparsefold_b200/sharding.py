@@ -406,7 +406,7 @@ def tri_mult(mod, z_loc: torch.Tensor, mask_u8: torch.Tensor, shard: Shard, grou
 def _att_buffers(nb: int, nq: int, dtype, device):
   qp = int(N.load().sf_tri_attention_query_pitch(nq))
   q = torch.empty(nb, 4, qp, 32, dtype=dtype, device=device)
-  return qp, q, torch.empty_like(q), torch.empty_like(q), torch.empty(nb, qp, 128, dtype=dtype, device=device)
+  return qp, q, torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)   # Q, K, V^T, G
 
 
 def tri_attention(mod, z_loc: torch.Tensor, mask_u8: torch.Tensor, shard: Shard, group=None) -> torch.Tensor:
