@@ -17,8 +17,14 @@
 //   warps 0-7   thread = position (warps 0-3 tile 0, 4-7 tile 1): LayerNorm of
 //               the pass in place (statistics in one shifted pass, scale and
 //               shift from shared memory), then per chunk swish(a) * b from TMEM
-//               into the 64B-swizzled hidden tile, and finally y = x + acc, staged
-//               by 64-channel halves in the free hidden buffers and TMA-stored.
+//               into the 64B-swizzled hidden tile; then straight on to the next
+//               pass's LayerNorm
+//   warps 12-15 residual epilogue (warp 12+q reads TMEM lanes 32q..): y = x + acc in
+//               eight units of [128 rows][32 channels], the x rows of each brought
+//               by TMA into one of two 8 KB staging buffers, the sum written over
+//               them and TMA-stored; this runs while warps 0-7 normalise the next
+//               pass and the GEMMs start on it (GEMM2 waits only for the
+//               accumulators to have been read)
 #include "sf_pair_tc.cuh"
 
 namespace sf {
@@ -38,13 +44,16 @@ constexpr int HBUF = 3;                                      // hidden tiles in 
 constexpr int OFF_H = OFF_X + X_BYTES;                       // [HBUF buffers][2 tiles]
 constexpr int OFF_W1 = OFF_H + HBUF * 2 * H_BYTES;           // [stage]
 constexpr int OFF_W2 = OFF_W1 + W1_STAGES * W1C_BYTES;       // [stage]
-constexpr int OFF_LNP = OFF_W2 + W2_STAGES * W2C_BYTES;      // LayerNorm scale [128] and shift [128], fp32
+constexpr int Y_BYTES = TILE * 32 * 2;                       // one epilogue unit: 128 rows x 32 channels (64B swizzle)
+constexpr int OFF_Y = OFF_W2 + W2_STAGES * W2C_BYTES;        // [2] residual / output staging
+constexpr int OFF_LNP = OFF_Y + 2 * Y_BYTES;                 // LayerNorm scale [128] and shift [128], fp32
 constexpr int OFF_BAR = OFF_LNP + 2 * C * 4;
 constexpr int SMEM_TR = OFF_BAR + 512 + 1024;
 static_assert(SMEM_TR <= 232448, "transition shared memory");
 
-__device__ __forceinline__ void tile_sync(int t2) { asm volatile("bar.sync %0, 128;" ::"r"(1 + t2) : "memory"); }
-constexpr int TR_THREADS = 12 * 32;
+// the four epilogue warps (named barrier 1)
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+constexpr int TR_THREADS = 16 * 32;
 
 struct TrParams {
   const bf16* x;
@@ -58,7 +67,8 @@ struct TrParams {
 __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_constant__ CUtensorMap tmX,
                                                                  const __grid_constant__ CUtensorMap tmW1,
                                                                  const __grid_constant__ CUtensorMap tmW2,
-                                                                 const __grid_constant__ CUtensorMap tmY, TrParams p) {
+                                                                 const __grid_constant__ CUtensorMap tmY,
+                                                                 const __grid_constant__ CUtensorMap tmR, TrParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -66,7 +76,7 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   uint64_t* xready = bars + 1;                   // LN done (256)
   uint64_t* xfree = bars + 2;                    // last GEMM1 of the pass done (both issuers)
   uint64_t* accfull = bars + 3;                  // last GEMM2 of the pass done
-  uint64_t* accfree = bars + 4;                  // accumulators read (8 warps)
+  uint64_t* accfree = bars + 4;                  // accumulators read (4 epilogue warps)
   uint64_t* w1full = bars + 5;                   // [W1_STAGES]
   uint64_t* w1free = w1full + W1_STAGES;         // both GEMM1 issuers done with the chunk
   uint64_t* w2full = w1free + W1_STAGES;
@@ -76,7 +86,8 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   uint64_t* hfull = s1free + 4;                  // [HBUF] (8 warps)
   uint64_t* hfree = hfull + HBUF;                // [HBUF]
   uint64_t* drain = hfree + HBUF;                // [3] drain barriers of the MMA issuers, warps 9-11 (abort path)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 3);
+  uint64_t* ybar = drain + 3;                    // [2] residual rows of an epilogue unit landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ybar + 2);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t npasses = (p.M + 2 * TILE - 1) / (2 * TILE);
   float* lnp = reinterpret_cast<float*>(smem + OFF_LNP);
@@ -91,7 +102,7 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
     tc::mbar_init(xready, 256);
     tc::mbar_init(xfree, 2);
     tc::mbar_init(accfull, 1);
-    tc::mbar_init(accfree, 8);
+    tc::mbar_init(accfree, 4);
     for (int s = 0; s < W1_STAGES; ++s) {
       tc::mbar_init(&w1full[s], 1);
       tc::mbar_init(&w1free[s], 2);
@@ -109,11 +120,13 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       tc::mbar_init(&hfree[s], 1);
     }
     for (int s = 0; s < 3; ++s) tc::mbar_init(&drain[s], 1);
+    for (int s = 0; s < 2; ++s) tc::mbar_init(&ybar[s], 1);
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmX);
     tc::prefetch_tmap(&tmW1);
     tc::prefetch_tmap(&tmW2);
     tc::prefetch_tmap(&tmY);
+    tc::prefetch_tmap(&tmR);
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -123,7 +136,7 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
   const uint32_t tbase = *tmem_slot;
   const uint32_t sb = tc::smem_u32(smem);
   bool aborted = false;
-  uint32_t xloads = 0, w1loads = 0, w2loads = 0;   // TMA loads issued per ring (abort-path drain)
+  uint32_t xloads = 0, w1loads = 0, w2loads = 0, yloads = 0;   // TMA loads issued per ring (abort-path drain)
 
   if (warp == 8) {
     // ---- TMA producer (stops at its first failed wait) ----
@@ -218,27 +231,72 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
         tc::mma_commit(accfull);
       }
     }
+  } else if (warp >= 12) {
+    // ---- residual epilogue: y = x + acc in units u = 4 t2 + cq (tile t2, channels 32 cq ..) ----
+    const int quad = warp & 3, r = tid - 12 * 32;   // r: row of the tile = TMEM lane
+    const bool leader = r == 0;                     // issues the unit loads and stores
+    const uint32_t lane_addr = tbase + ((uint32_t)(32 * quad) << 16);
+    // x[m0 + 128 t2 ..][32 cq ..] of unit u into staging buffer u & 1 (by the leader)
+    auto load_unit = [&](int64_t m0, int u) {
+      tc::mbar_expect_tx(&ybar[u & 1], Y_BYTES);
+      tc::tma_load_2d(smem + OFF_Y + (u & 1) * Y_BYTES, &tmR, &ybar[u & 1], (u & 3) * 32, (int)(m0 + (u >> 2) * TILE));
+      ++yloads;
+    };
+    uint32_t pi = 0;
+    for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
+      const int64_t m0 = ps * 2 * TILE;
+      // the staging buffers are free: the leader waited for the last pass's stores to read them
+      if (leader && !aborted) {
+        load_unit(m0, 0);
+        load_unit(m0, 1);
+      }
+      tc::mbar_wait(accfull, pi & 1, p.status, aborted);
+      tc::tc_fence_after();
+      for (int u = 0; u < 8; ++u) {
+        const int t2 = u >> 2, cq = u & 3;
+        uint8_t* ys = smem + OFF_Y + (u & 1) * Y_BYTES;
+        float v[32];
+        tc::tmem_ld32(lane_addr + 256 + t2 * 128 + 32 * cq, v);
+        if (u == 7) {   // every accumulator column has been read: the next pass's GEMM2 may start
+          tc::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(accfree);
+        }
+        // unit u's x rows are in buffer u & 1 (its use (u >> 1) of this pass, four per pass)
+        tc::mbar_wait(&ybar[u & 1], (u >> 1) & 1, p.status, aborted);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4* yp = reinterpret_cast<uint4*>(ys + tc::sw64_off(r, c));
+          const uint4 xx = *yp;
+          const uint32_t xu[4] = {xx.x, xx.y, xx.z, xx.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[e] = pack_bf2(bf_lo(xu[e]) + v[8 * c + 2 * e], bf_hi(xu[e]) + v[8 * c + 2 * e + 1]);
+          *yp = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        tc::fence_proxy_async();
+        epi_sync();
+        if (leader) {
+          tc::tma_store_2d(&tmY, ys, cq * 32, (int)(m0 + t2 * TILE));   // rows past M are clipped
+          tc::bulk_commit();
+          tc::bulk_wait_read0();   // buffer u & 1 may take unit u + 2 (or the next pass's units)
+          if (u + 2 < 8 && !aborted) load_unit(m0, u + 2);
+        }
+      }
+    }
+    if (leader) tc::bulk_wait0();
   } else {
     // ---- 8 warps, thread = position: warps 0-3 tile 0, 4-7 tile 1 ----
     const int t2 = warp >> 2, r = tid & 127;
     const uint32_t lane_addr = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
     uint32_t q = 0, pi = 0;
     for (int64_t ps = blockIdx.x; ps < npasses; ps += gridDim.x, ++pi) {
-      const int64_t m0 = ps * 2 * TILE;
       tc::mbar_wait(xfull, pi & 1, p.status, aborted);
       ln_row_shifted(smem + OFF_X + t2 * A_BYTES, r, lnp, lnp + C, 1e-5f);
       tc::fence_proxy_async();
       tc::mbar_arrive(xready);
-      const int64_t m = m0 + t2 * TILE + r;
-      const bool live = m < p.M;
-      const uint4* xr = reinterpret_cast<const uint4*>(p.x + (live ? m : 0) * C);
-      uint4 xpre[16];
       for (int hc = 0; hc < NCHUNK; ++hc, ++q) {
         const int sbuf = q & 1;
-        if (hc == NCHUNK - 4) {
-#pragma unroll
-          for (int c = 0; c < 16; ++c) xpre[c] = xr[c];   // raw x row for the residual (the tile in smem is normalised)
-        }
         tc::mbar_wait(&s1full[sbuf * 2 + t2], (q >> 1) & 1, p.status, aborted);
         tc::tc_fence_after();
         float ab[2 * HC];   // a (swish input) then b, adjacent columns: one load, one wait
@@ -264,41 +322,6 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&hfull[hbuf]);
       }
-      // ---- residual epilogue: y = x + acc (the x row was prefetched during the last chunks), one
-      // 64-channel half at a time staged in the free hidden buffers (16 KB per tile, 128B swizzle)
-      // and TMA-stored: rows 256 B apart make per-thread 16-byte stores 32 transactions each ----
-      tc::mbar_wait(accfull, pi & 1, p.status, aborted);
-      tc::tc_fence_after();
-      uint8_t* ystage = smem + OFF_H + t2 * 2 * H_BYTES;
-      for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-        for (int i2 = 0; i2 < 2; ++i2) {
-          const int i = 2 * hh + i2;   // channels 32i .. 32i+31
-          float v[32];
-          tc::tmem_ld32(lane_addr + 256 + t2 * 128 + 32 * i, v);
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 xx = xpre[4 * i + c];
-            const uint32_t xu[4] = {xx.x, xx.y, xx.z, xx.w};
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              o[e] = pack_bf2(bf_lo(xu[e]) + v[8 * c + 2 * e], bf_hi(xu[e]) + v[8 * c + 2 * e + 1]);
-            *reinterpret_cast<uint4*>(ystage + tc::sw128_off(r, 4 * i2 + c)) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-        }
-        tc::fence_proxy_async();
-        tile_sync(t2);
-        if (r == 0) {
-          tc::tma_store_2d(&tmY, ystage, hh * 64, (int)(m0 + t2 * TILE));   // rows past M are clipped
-          tc::bulk_commit();
-          tc::bulk_wait_read0();
-        }
-        tile_sync(t2);
-      }
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(accfree);
     }
   }
   tc::tc_fence_before();
@@ -307,7 +330,9 @@ __global__ void __launch_bounds__(TR_THREADS, 1) k_transition_tc(const __grid_co
       if (warp == 8) {
         tc::drain_ring(xfull, 1, xloads, p.status);
         tc::drain_ring(w1full, W1_STAGES, w1loads, p.status);
-      } else if (warp >= 9 && warp <= 11) {
+      }
+      if (warp == 12) tc::drain_ring(ybar, 2, yloads, p.status);
+      if (warp >= 9 && warp <= 11) {
         if (warp == 10) tc::drain_ring(w2full, W2_STAGES, w2loads, p.status);
         tc::drain_mma(&drain[warp - 9], p.status);
       }
@@ -361,7 +386,9 @@ int transition_tc(const bf16* x, const float* ln_w, const float* ln_b, const bf1
              "transition_tc: layer-norm parameters must be 16-byte aligned");
   CUtensorMap mx, mw1, mw2, my;
   SF_TRY(make_2d_tmap(&mx, x, C, M, 64, TILE));
-  SF_TRY(make_2d_tmap(&my, y, C, M, 64, TILE));
+  SF_TRY(make_2d_tmap(&my, y, C, M, 32, TILE, 64));          // residual epilogue units: 32 channels x 128 rows
+  CUtensorMap mr;
+  SF_TRY(make_2d_tmap(&mr, x, C, M, 32, TILE, 64));
   SF_TRY(make_2d_tmap(&mw1, w1, C, 2 * I, 64, HC));         // W1 [1024][128]: 64 k x 32 rows
   SF_TRY(make_2d_tmap(&mw2, w2, I, C, HC, C, 64));          // W2 [128][512]: 32 k x 128 rows, 64B swizzle
   uint32_t* status = device_status_ptr();
@@ -380,7 +407,7 @@ int transition_tc(const bf16* x, const float* ln_w, const float* ln_b, const bf1
   TrParams p{x, y, ln_w, ln_b, M, status};
   const int64_t npairs = (M + 2 * TILE - 1) / (2 * TILE);
   const int grid = (int)(npairs < num_sms() ? npairs : num_sms());
-  launch_pdl(k_transition_tc, dim3(grid), dim3(TR_THREADS), SMEM_TR, stream, mx, mw1, mw2, my, p);
+  launch_pdl(k_transition_tc, dim3(grid), dim3(TR_THREADS), SMEM_TR, stream, mx, mw1, mw2, my, mr, p);
   count_launch();
   return check_launch("transition_tc");
 }
