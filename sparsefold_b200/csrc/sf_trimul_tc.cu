@@ -6,9 +6,13 @@
 // rows in place (two threads per row), one thread issues the GLU GEMMs transposed,
 // D[out channel][position] = W . LN(z)^T (M=128, N=128, K=128, four weight
 // matrices kept resident), into two TMEM halves so the epilogue of one operand
-// overlaps the GEMM of the other, and eight epilogue warps apply
+// overlaps the GEMM of the other, and sixteen epilogue warps apply
 // sigmoid(gate) * value * mask and TMA-store the contraction operands as
-// [row][channel][pitch] (each TMEM lane is one channel row of the output).
+// [row][channel][pitch] (each TMEM lane is one channel row of the output).  The
+// next tile's GEMM of a half waits for every epilogue warp to have read it, so the
+// epilogue is split thin (a clock64 trace with eight warps: a tile every ~7.1k
+// cycles against ~5.2k of LayerNorm, each half's hand-off waiting 1-3k cycles on
+// the slowest epilogue warp).
 #include "sf_pair_tc.cuh"
 
 namespace sf {
@@ -25,23 +29,23 @@ struct ProjParams {
   uint32_t* status;
 };
 
-// Warp roles (576 threads):
-//   warps 0-7   epilogue: warp w reads TMEM lanes 32(w%4).. (output channels) and
-//               positions 64(w/4)..+63 of the tile; stages sigmoid(gate) * value *
-//               mask as [32 channels][64 positions] (128B swizzle) and TMA-stores it
-//   warps 8-15  layer norm of the tile rows in place (two threads per position)
-//   warp 16     TMA producer of z tiles (two stages)
-//   warp 17     MMA issuer: D[out channel][position] = W_x . LN(z)^T for the four
+// Warp roles (832 threads):
+//   warps 0-15  epilogue: warp w reads TMEM lanes 32(w%4).. (output channels) and
+//               positions 32(w/4)..+31 of the tile; stages sigmoid(gate) * value *
+//               mask as [32 channels][32 positions] (64B swizzle) and TMA-stores it
+//   warps 16-23 layer norm of the tile rows in place (two threads per position)
+//   warp 24     TMA producer of z tiles (two stages)
+//   warp 25     MMA issuer: D[out channel][position] = W_x . LN(z)^T for the four
 //               GLU matrices, two at a time (TMEM halves a = cols 0-255, b = 256-511)
 constexpr int NOUT = 512;
 constexpr int W_BYTES = NOUT * C * 2;                       // 128 KB, rows = gate_a, val_a, gate_b, val_b
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 16;
 constexpr int LN_WARPS = 8;
 constexpr int PROJ_THREADS = (EPI_WARPS + LN_WARPS + 2) * 32;
-constexpr int ST_BYTES = 32 * 128;                          // one epilogue warp's staging: 32 channels x 64 positions
+constexpr int ST_BYTES = 32 * 64;                           // one epilogue warp's staging: 32 channels x 32 positions
 constexpr int OFF_PW = 0;
 constexpr int OFF_PZ = W_BYTES;                             // two z stages
-constexpr int OFF_PST = OFF_PZ + 2 * A_BYTES;               // 8 staging tiles
+constexpr int OFF_PST = OFF_PZ + 2 * A_BYTES;               // EPI_WARPS staging tiles
 constexpr int OFF_PLN = OFF_PST + EPI_WARPS * ST_BYTES;    // LayerNorm scale and shift, 2 x 128 fp32
 constexpr int OFF_PBAR = OFF_PLN + 2 * C * 4;
 constexpr int SMEM_PROJ = OFF_PBAR + 256 + 1024;
@@ -57,7 +61,7 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
   uint64_t* normed = full + 2;                                      // [2] z tile normalised (128 arrivals)
   uint64_t* zfree = normed + 2;                                     // [2] MMAs of the stage done
   uint64_t* tfull = zfree + 2;                                      // [2] TMEM half written
-  uint64_t* tfree = tfull + 2;                                      // [2] TMEM half read (8 warps)
+  uint64_t* tfree = tfull + 2;                                      // [2] TMEM half read (16 warps)
   uint64_t* drain = tfree + 2;                                      // MMA drain barrier (abort path)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -158,27 +162,22 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
     }
   } else {
     // ---- epilogue ----
-    const int quad = warp & 3, hf = warp >> 2;
+    const int quad = warp & 3, pg = warp >> 2;   // channels 32 quad .., positions 32 pg ..
     const uint32_t lane_addr = tbase + ((uint32_t)(32 * quad) << 16);
     uint8_t* stg = smem + OFF_PST + warp * ST_BYTES;
     uint32_t it = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
-      const int64_t major = tile / nb, minor0 = (tile % nb) * TILE + hf * 64;
-      // keep[pos] = valid && mask[row] && mask[col] for the warp's 64 positions
-      uint64_t keep;
+      const int64_t major = tile / nb, minor0 = (tile % nb) * TILE + 32 * pg;
+      // keep[pos] = valid && mask[row] && mask[col] for the warp's 32 positions
+      uint32_t keep;
       {
-        uint32_t kw[2];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const int64_t minor = minor0 + 32 * i + lane;
-          bool k = minor < span;
-          if (k) {
-            const int64_t rr = p.incoming ? minor : major, ss = p.incoming ? major : minor;
-            k = p.mask[p.row_offset + rr] != 0 && p.mask[ss] != 0;
-          }
-          kw[i] = __ballot_sync(0xffffffffu, k);
+        const int64_t minor = minor0 + lane;
+        bool k = minor < span;
+        if (k) {
+          const int64_t rr = p.incoming ? minor : major, ss = p.incoming ? major : minor;
+          k = p.mask[p.row_offset + rr] != 0 && p.mask[ss] != 0;
         }
-        keep = (uint64_t)kw[0] | ((uint64_t)kw[1] << 32);
+        keep = __ballot_sync(0xffffffffu, k);
       }
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
@@ -187,13 +186,13 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
         if (lane == 0) tc::bulk_wait_read0();   // previous store from this staging tile has read it
         __syncwarp();
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 2; ++k) {
           float gt[16], vl[16];
-          tc::tmem_ld16(lane_addr + hh * 256 + hf * 64 + 16 * k, gt);
-          tc::tmem_ld16(lane_addr + hh * 256 + 128 + hf * 64 + 16 * k, vl);
+          tc::tmem_ld16(lane_addr + hh * 256 + 32 * pg + 16 * k, gt);
+          tc::tmem_ld16(lane_addr + hh * 256 + 128 + 32 * pg + 16 * k, vl);
           uint32_t pk[8];
           // a column is one position, the same for every lane: the mask test is warp-uniform
-          const uint32_t kw = (uint32_t)(keep >> (16 * k)) & 0xFFFFu;
+          const uint32_t kw = (keep >> (16 * k)) & 0xFFFFu;
           if (kw == 0xFFFFu) {
 #pragma unroll
             for (int e = 0; e < 8; ++e)
@@ -206,8 +205,8 @@ __global__ void __launch_bounds__(PROJ_THREADS, 1) k_trimul_project_tc(const __g
               pk[e] = pack_bf2(o0, o1);
             }
           }
-          *reinterpret_cast<uint4*>(stg + tc::sw128_off(lane, 2 * k)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          *reinterpret_cast<uint4*>(stg + tc::sw128_off(lane, 2 * k + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          *reinterpret_cast<uint4*>(stg + tc::sw64_off(lane, 2 * k)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(stg + tc::sw64_off(lane, 2 * k + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
         tc::tc_fence_before();
         tc::fence_proxy_async();
@@ -321,10 +320,10 @@ int trimul_project_tc(const bf16* z, const uint8_t* mask, int64_t rows, int64_t 
       }
       cuuint64_t dims[3] = {(cuuint64_t)pitch, (cuuint64_t)pt::C, (cuuint64_t)majors};
       cuuint64_t strides[2] = {(cuuint64_t)pitch * 2, (cuuint64_t)(pt::C * pitch * 2)};
-      cuuint32_t box[3] = {64, 32, 1};
+      cuuint32_t box[3] = {32, 32, 1};   // one epilogue warp's [32 channels][32 positions]
       cuuint32_t estr[3] = {1, 1, 1};
       CUresult r = encode(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dst[i], dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
       if (r != CUDA_SUCCESS) {
         set_error("cuTensorMapEncodeTiled failed (%d) for operand [%lld][128][%lld]", (int)r, (long long)majors,
