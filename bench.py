@@ -173,7 +173,7 @@ def tri_attention_op_flops(n: int) -> float:
 
 # DRAM bytes of one triangle attention (projection + core) at N=512, from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum; profiles/k_triatt_tc_n512.md).
-TRI_ATT_TRAFFIC_N512 = int((67.31 + 214.41 + 337.75 + 55.92) * 1e6)
+TRI_ATT_TRAFFIC_N512 = int((67.32 + 215.30 + 337.74 + 55.81) * 1e6)
 
 
 def tri_attention_exp2_count(n: int) -> float:
