@@ -87,3 +87,42 @@ def test_prepare_after_move_keeps_every_buffer_on_the_parameter_device():
   modules.prepare(b)
   for name, buf in b.named_buffers():
     assert buf.device.type == "meta", name
+
+
+def test_diffusion_pair_logit_pack_reused_for_an_unchanged_pair_cond():
+  """The diffusion transformer computes its pair-logit pack once while the denoising loop passes the
+  same, unchanged pair_cond (generator.py:338-346), and again after an in-place change, for another
+  dtype or another tensor; inference tensors (no version counter) are never memoised, and the memo
+  goes when its pair_cond is freed."""
+  import gc
+
+  t = modules.DiffusionTransformerB200.__new__(modules.DiffusionTransformerB200)
+  t._pack_memo = None
+  calls = []
+
+  def fake_pack(pair_cond, dtype):
+    calls.append((pair_cond, dtype))
+    return torch.full((1,), float(len(calls)))
+
+  t.pair_logits_pack = fake_pack
+  pc = torch.zeros(4, 4, 8)
+  p1 = t._pack_of(pc, torch.bfloat16)
+  assert t._pack_of(pc, torch.bfloat16) is p1 and len(calls) == 1
+  pc.add_(1.0)                                   # in place: the version counter moves
+  p2 = t._pack_of(pc, torch.bfloat16)
+  assert p2 is not p1 and len(calls) == 2
+  assert t._pack_of(pc, torch.float32) is not p2 and len(calls) == 3
+  other = pc.clone()
+  t._pack_of(other, torch.float32)
+  assert len(calls) == 4
+  with torch.inference_mode():
+    inf = torch.zeros(4, 4, 8)
+  t._pack_of(inf, torch.bfloat16)
+  t._pack_of(inf, torch.bfloat16)
+  assert len(calls) == 6
+  t._pack_of(other, torch.bfloat16)
+  assert t._pack_memo is not None
+  calls.clear()
+  del other
+  gc.collect()
+  assert t._pack_memo is None

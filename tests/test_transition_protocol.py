@@ -3,9 +3,11 @@ sparsefold_b200/csrc/sf_transition_tc.cu), run under many random interleavings o
 
 Actors of one CTA over several 256-position passes: the TMA producer (x tiles, W1 ring), the
 two GEMM1 issuers (one per 128-position tile), the GEMM2 issuer (which also refills the W2
-ring), the eight epilogue warps (four per tile), the tensor core (MMAs run one at a time in
-issue order; a commit arrives once everything issued before it has run) and the TMA engine
-(loads land in any order; a store reads its staging some time before its wait returns).
+ring), the eight element-wise warps (four per tile: LayerNorm, then SwiGLU per chunk), the four
+residual-epilogue warps (eight units per pass through two staging buffers, the first warp's
+leader thread loading each unit's x rows and storing the sum), the tensor core (MMAs run one at
+a time in issue order; a commit arrives once everything issued before it has run) and the TMA
+engine (loads land in any order; a store reads its staging some time before its wait returns).
 Every parity wait checks that its barrier is within one phase of the phase it waits for, and
 every shared-memory stage, TMEM buffer and hidden buffer records what it holds, so a reader
 that would see the wrong chunk, or a writer that would overwrite data still in use, fails.
@@ -33,13 +35,17 @@ class Bar:
 
 
 class Cta:
-  def __init__(self, passes, rng, w2_early=False):
+  def __init__(self, passes, rng, w2_early=False, early_reload=False):
     # w2_early plants a mistake in the model (a W2 stage refilled without waiting for the GEMM2
-    # that reads it), to show that the model catches it
-    self.P, self.rng, self.w2_early = passes, rng, w2_early
+    # that reads it), early_reload another (a staging buffer reloaded before the store of its last
+    # unit has read it), to show that the model catches them
+    self.P, self.rng, self.w2_early, self.early_reload = passes, rng, w2_early, early_reload
     B = Bar
     self.xfull, self.xready, self.xfree = B("xfull", 2), B("xready", 8), B("xfree", 2)
-    self.accfull, self.accfree = B("accfull", 1), B("accfree", 8)
+    self.accfull, self.accfree = B("accfull", 1), B("accfree", 4)
+    self.ybar = [B(f"ybar{i}", 2) for i in range(2)]
+    self.ystage = [None, None]             # ("loading" | "x" | "sum" | "ydone", pass, unit)
+    self.ysync = {}                        # (pass, unit) -> epilogue warps that wrote their rows
     self.w1full = [B(f"w1full{i}", 2) for i in range(W1S)]
     self.w1free = [B(f"w1free{i}", 2) for i in range(W1S)]
     self.w2full = [B(f"w2full{i}", 2) for i in range(W2S)]
@@ -52,7 +58,7 @@ class Cta:
     self.w1 = [None] * W1S                 # chunk index held
     self.w2 = [None] * W2S
     self.s1 = [None] * 4                   # (buffer, tile) -> chunk q
-    self.h = [None] * (2 * HBUF)           # (buffer, tile) -> chunk q, or "y" while staging the output
+    self.h = [None] * (2 * HBUF)           # (buffer, tile) -> chunk q
     self.acc_pass = None
     self.mma, self.tma = [], []
     self.ln_done = {}
@@ -138,8 +144,8 @@ class Cta:
       self.mma.append(("commit", self.accfull))
       yield None
 
-  # ---- an epilogue warp (warps 4 t2 .. 4 t2 + 3 hold the rows of tile t2) ----
-  def epilogue(self, w):
+  # ---- an element-wise warp (warps 4 t2 .. 4 t2 + 3 hold the rows of tile t2) ----
+  def elementwise(self, w):
     t2 = w // 4
     q = 0
     for pi in range(self.P):
@@ -155,7 +161,7 @@ class Cta:
         sbuf = q & 1
         while not self.s1full[sbuf * 2 + t2].ready(q >> 1):
           yield "s1full"
-        assert self.s1[sbuf * 2 + t2] == q, f"epilogue reads S1 {self.s1[sbuf * 2 + t2]} for chunk {q}"
+        assert self.s1[sbuf * 2 + t2] == q, f"element-wise warp reads S1 {self.s1[sbuf * 2 + t2]} for chunk {q}"
         self.s1free[sbuf * 2 + t2].arrive()
         yield None
         hbuf = q % HBUF
@@ -163,38 +169,57 @@ class Cta:
           while not self.hfree[hbuf].ready(q // HBUF - 1):
             yield "hfree"
         cur = self.h[hbuf * 2 + t2]
-        # free: never used, an output tile whose store has read it, or a hidden tile GEMM2 is done with
-        # (or this chunk, written by another warp of the tile: each warp writes its own rows)
-        assert cur is None or cur[0] == "ydone" or (cur[0] == "h" and (cur[1] <= q - HBUF or cur[1] == q)), \
-            f"chunk {q} hidden write over {cur}"
+        # free: never used, or a hidden tile GEMM2 is done with (or this chunk, written by another
+        # warp of the tile: each warp writes its own rows)
+        assert cur is None or cur[1] <= q - HBUF or cur[1] == q, f"chunk {q} hidden write over {cur}"
         self.h[hbuf * 2 + t2] = ("h", q)
         self.hfull[hbuf].arrive()
         q += 1
         yield None
+
+  # ---- a residual-epilogue warp; warp 0's leader also loads and stores the units ----
+  def load_unit(self, pi, u):
+    b = u & 1
+    assert self.ystage[b] is None or self.ystage[b][0] == "ydone", f"unit ({pi}, {u}) loaded over {self.ystage[b]}"
+    self.ybar[b].arrive()
+    self.ystage[b] = ("loading", pi, u)
+    self.tma.append(("yload", (b, pi, u), self.ybar[b]))
+
+  def epilogue(self, e):
+    for pi in range(self.P):
+      if e == 0:
+        self.load_unit(pi, 0)
+        self.load_unit(pi, 1)
+        yield None
       while not self.accfull.ready(pi):
         yield "accfull"
-      assert self.acc_pass == pi
-      self.accfree.arrive()
-      # the output tile of the pass is staged in hidden buffers 2 t2, 2 t2 + 1 and TMA-stored
-      for idx in (2 * t2, 2 * t2 + 1):
-        assert self.h[idx] is None or self.h[idx][0] != "h" or self.h[idx][1] < q - HBUF or self.hfree_done(idx // 2, self.h[idx][1]), \
-            f"output staging over {self.h[idx]}"
-        self.h[idx] = ("y", pi)
-      yield None
-      # the tile's store has read the staging (bulk wait, then the tile's named barrier)
-      for idx in (2 * t2, 2 * t2 + 1):
-        if self.h[idx] == ("y", pi):
-          self.h[idx] = ("ydone", pi)
-      yield None
-
-  def hfree_done(self, buf, q):
-    return self.hfree[buf].done > q // HBUF
-
+      for u in range(8):
+        assert self.acc_pass == pi, f"epilogue of pass {pi} reads the accumulators of {self.acc_pass}"
+        if u == 7:
+          self.accfree.arrive()
+        b = u & 1
+        while not self.ybar[b].ready(pi * 4 + (u >> 1)):
+          yield "ybar"
+        assert self.ystage[b] in (("x", pi, u), ("sum", pi, u)), f"unit ({pi}, {u}) reads staging {self.ystage[b]}"
+        self.ysync.setdefault((pi, u), set()).add(e)
+        yield None
+        while len(self.ysync[(pi, u)]) < 4:     # the epilogue warps' named barrier
+          yield "ysync"
+        if e == 0:
+          self.ystage[b] = ("sum", pi, u)
+          self.tma.append(("ystore", (b, pi, u), None))
+          yield None
+          if not self.early_reload:
+            while self.ystage[b] != ("ydone", pi, u):   # bulk wait: the store has read the staging
+              yield "ystore"
+          if u + 2 < 8:
+            self.load_unit(pi, u + 2)
+          yield None
 
 class Sim:
-  def __init__(self, passes, seed, w2_early=False):
+  def __init__(self, passes, seed, w2_early=False, early_reload=False):
     self.rng = random.Random(seed)
-    self.c = Cta(passes, self.rng, w2_early)
+    self.c = Cta(passes, self.rng, w2_early, early_reload)
 
   def run_mma(self):
     c = self.c
@@ -218,7 +243,16 @@ class Sim:
   def land(self):
     c = self.c
     kind, arg, bar = c.tma.pop(self.rng.randrange(len(c.tma)))
-    if kind == "x":
+    if kind == "yload":
+      b, pi, u = arg
+      assert c.ystage[b] == ("loading", pi, u), f"unit ({pi}, {u}) lands over {c.ystage[b]}"
+      c.ystage[b] = ("x", pi, u)
+    elif kind == "ystore":
+      b, pi, u = arg
+      assert c.ystage[b] == ("sum", pi, u), f"the store of unit ({pi}, {u}) reads {c.ystage[b]}"
+      c.ystage[b] = ("ydone", pi, u)
+      return
+    elif kind == "x":
       c.x = ("raw", arg)
     elif kind == "w1":
       st, q = arg
@@ -229,10 +263,11 @@ class Sim:
     bar.arrive()
 
 
-def simulate(passes, seed, w2_early=False):
-  s = Sim(passes, seed, w2_early)
+def simulate(passes, seed, w2_early=False, early_reload=False):
+  s = Sim(passes, seed, w2_early, early_reload)
   c = s.c
-  gens = [c.producer(), c.gemm1(0), c.gemm1(1), c.gemm2()] + [c.epilogue(w) for w in range(8)]
+  gens = ([c.producer(), c.gemm1(0), c.gemm1(1), c.gemm2()] + [c.elementwise(w) for w in range(8)] +
+          [c.epilogue(e) for e in range(4)])
   actors = dict(enumerate(gens))
 
   def step(a):
@@ -272,3 +307,14 @@ def test_model_catches_early_w2_refill():
     except AssertionError:
       failures += 1
   assert failures >= 8
+
+
+def test_model_catches_a_staging_reload_before_its_store_has_read_it():
+  """The residual epilogue with its bulk wait removed must fail."""
+  failures = 0
+  for seed in range(20):
+    try:
+      simulate(2, seed, early_reload=True)
+    except AssertionError:
+      failures += 1
+  assert failures >= 5, failures
