@@ -378,7 +378,11 @@ class DiffusionTransformerB200(B200Module):
     conditioning (``torch.asarray`` of a tensor already in the compute dtype returns the tensor
     itself), so through the plugin the pack is computed once per loop, not once per step.  The
     memo is dropped when that tensor is freed and when the weights are prepared again; inference
-    tensors keep no version counter and are not memoised."""
+    tensors keep no version counter and are not memoised.  Under CUDA-graph capture the memo is
+    neither used nor filled: the graph must record the pack's own computation, since a replay
+    re-reads pair_cond's buffer without running this code."""
+    if pair_cond.is_cuda and torch.cuda.is_current_stream_capturing():
+      return self.pair_logits_pack(pair_cond, dtype)
     try:
       version = pair_cond._version
     except RuntimeError:

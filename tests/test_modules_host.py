@@ -7,6 +7,8 @@ buffers are added, and re-preparation is idempotent.  The packing tests
 recompute an op's first stage on the CPU from the *packed* weights and compare
 it with the oracle, which pins the row orders the kernels rely on.
 """
+import types
+
 import pytest
 import torch
 
@@ -126,3 +128,17 @@ def test_diffusion_pair_logit_pack_reused_for_an_unchanged_pair_cond():
   del other
   gc.collect()
   assert t._pack_memo is None
+
+
+def test_diffusion_pair_logit_pack_not_memoised_under_graph_capture(monkeypatch):
+  """A CUDA graph must record the pack's computation (a replay re-reads pair_cond without running
+  Python), so while the current stream captures, every call computes the pack and none is kept."""
+  t = modules.DiffusionTransformerB200.__new__(modules.DiffusionTransformerB200)
+  t._pack_memo = None
+  calls = []
+  t.pair_logits_pack = lambda pc, dt: calls.append(dt) or torch.zeros(1)
+  pc = types.SimpleNamespace(is_cuda=True)   # a CUDA pair_cond, as far as the memo looks
+  monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+  t._pack_of(pc, torch.bfloat16)
+  t._pack_of(pc, torch.bfloat16)
+  assert len(calls) == 2 and t._pack_memo is None
